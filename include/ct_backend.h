@@ -1,0 +1,118 @@
+/* ct_backend.h -- the drop-in C ABI exported by libct_b200.so.
+ *
+ * libct_b200.so exports exactly the 40 `backend_*` symbols that the reference
+ * engine's host code (transcribe.c, model.h, tests/test_kernels.c) calls, with
+ * identical signatures and semantics.  Each declaration cites the reference
+ * declaration it replaces (backends/backend.h:<line>) and the reference CPU
+ * implementation whose results it must reproduce (backends/cpu/backend.c:<line>).
+ *
+ * Conventions (same as the reference CUDA backend, backends/cuda/backend.cu):
+ *   - weight pointers are HOST pointers into the blob handed to
+ *     backend_weights_upload_blob; the library maps them by byte offset onto
+ *     its device copy (one copy per visible GPU);
+ *   - activation pointers are device pointers inside the arena returned by
+ *     backend_arena_alloc (fp32);
+ *   - `tokens`, `S_dev`, `active`, `T_enc` and argmax `out` are host arrays;
+ *   - all mutable state (stream, arena, graph cache, per-item counters) is
+ *     per host thread; one host thread drives one GPU;
+ *   - functions return void; a CUDA failure prints to stderr and exits(1).
+ *
+ * All compute runs on sm_100a kernels of this library; there is no CPU path.
+ */
+#ifndef CT_BACKEND_H
+#define CT_BACKEND_H
+
+#include "ct_model_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- lifecycle / memory (backend.h:20-46) ---------------------------- */
+void  backend_init(int device_id);                                  /* backend.h:20 */
+void  backend_destroy(void);                                        /* backend.h:21 */
+int   backend_num_devices(void);                                    /* backend.h:25 */
+void  backend_thread_cleanup(void);                                 /* backend.h:30 */
+void  backend_weights_upload_blob(const void *host_base, size_t bytes); /* backend.h:34 */
+void *backend_device_ptr(const void *host_ptr);                     /* backend.h:38 */
+float *backend_arena_alloc(size_t floats);                          /* backend.h:41 */
+void   backend_arena_free(float *arena);                            /* backend.h:42 */
+void backend_htod(float *dev_dst, const float *host_src, size_t floats); /* backend.h:45 */
+void backend_dtoh(void *host_dst, const void *dev_src, size_t bytes);    /* backend.h:46 */
+
+/* ---- compute primitives (backend.h:52-106; cpu/backend.c:109-387) ----- */
+void backend_layernorm(float *dst, const float *src,
+                       const uint16_t *w, const uint16_t *b, int T, int D);        /* backend.h:52 */
+void backend_linear(float *y, const float *x,
+                    const uint16_t *W, const uint16_t *b, int T, int in_d, int out_d); /* backend.h:56 */
+void backend_linear_silu(float *y, const float *x,
+                         const uint16_t *W, const uint16_t *b, int T, int in_d, int out_d); /* backend.h:58 */
+void backend_linear_relu(float *y, const float *x,
+                         const uint16_t *W, const uint16_t *b, int T, int in_d, int out_d); /* backend.h:60 */
+void backend_linear_fmadd(float *acc, float scale, const float *x,
+                          const uint16_t *W, const uint16_t *b, int T, int in_d, int out_d); /* backend.h:63 */
+void backend_add_inplace(float *dst, const float *src, int n);                       /* backend.h:67 */
+void backend_encoder_subsampling(const float *mel, int T_mel, int T_mel_stride,
+                                 float *x_enc, int T_enc, float *work,
+                                 const Weights *W);                                    /* backend.h:72 */
+void backend_make_rel_pos_emb(float *pe, int T);                                      /* backend.h:77 */
+void backend_rel_pos_mhsa(float *x, const float *pos_emb,
+                          int T, const ELayer *L, float *work);                        /* backend.h:81 */
+void backend_conformer_conv(float *x, int T, const ELayer *L, float *work);           /* backend.h:86 */
+void backend_sdp_attn(float *out, const float *q, const float *k, const float *v,
+                      const float *mask, int T_q, int T_k, float *work);               /* backend.h:90 */
+void backend_embed(float *h, const int *tokens, int S, int pos_start,
+                   const uint16_t *etw, const uint16_t *epw,
+                   const uint16_t *elnw, const uint16_t *elnb);                       /* backend.h:96 */
+void backend_fill_causal_mask(float *mask, int S);                                    /* backend.h:101 */
+void backend_lm_head(float *logits_out, const float *last,
+                     const uint16_t *etw, const uint16_t *hdb);                       /* backend.h:105 */
+
+/* ---- graph hooks (backend.h:113-138) ---------------------------------- */
+#define GRAPH_TAG_ENCODER    0
+#define GRAPH_TAG_PRECOMPUTE 1
+#define GRAPH_TAG_DECODER    2
+void backend_upload_tokens(const int *host_tokens, int S);                            /* backend.h:121 */
+int  backend_graph_replay(int tag, int T_enc, int S, int B);                          /* backend.h:128 */
+void backend_graph_begin_capture(int tag);                                            /* backend.h:133 */
+void backend_graph_end_capture(int tag, int T_enc, int S, int B);                     /* backend.h:138 */
+
+/* ---- device-side sequence counter, B=1 decode (backend.h:147-175) ----- */
+void backend_decode_set_S(int n);                                                     /* backend.h:147 */
+void backend_decode_inc_S(void);                                                      /* backend.h:152 */
+void backend_linear_to_kvcache(float *cache, const float *x,
+                               const uint16_t *W, const uint16_t *b,
+                               int in_d, int out_d);                                   /* backend.h:159 */
+void backend_sdp_attn_devS(float *out, const float *q,
+                           const float *k, const float *v, float *work);               /* backend.h:166 */
+void backend_embed_decode(float *h,
+                          const uint16_t *etw, const uint16_t *epw,
+                          const uint16_t *elnw, const uint16_t *elnb);                 /* backend.h:173 */
+
+/* ---- batched decode step (backend.h:185-228; cpu/backend.c:425-500) --- */
+void backend_embed_decode_batch(float *h, const int *tokens,
+                                const int *S_dev, const int *active, int B,
+                                const uint16_t *etw, const uint16_t *epw,
+                                const uint16_t *elnw, const uint16_t *elnb);           /* backend.h:185 */
+void backend_lm_head_batch(float *logits, const float *h,
+                           const uint16_t *etw, const uint16_t *hdb,
+                           const int *active, int B);                                  /* backend.h:192 */
+void backend_argmax_batch(int *out, const float *logits,
+                          const int *active, int B);                                   /* backend.h:198 */
+void backend_upload_T_enc(const int *T_enc, int B);                                   /* backend.h:207 */
+void backend_linear_to_kvcache_batch(float *cache, const float *x,
+                                     const uint16_t *W, const uint16_t *b,
+                                     int B, int cache_seq_stride,
+                                     int in_d, int out_d);                             /* backend.h:214 */
+void backend_sdp_attn_batch_decode_sa(float *out, const float *Q,
+                                      const float *K, const float *V,
+                                      int T_k_stride, int B, float *work);             /* backend.h:223 */
+void backend_sdp_attn_batch_decode_ca(float *out, const float *Q,
+                                      const float *K, const float *V,
+                                      int T_k_stride, int B, float *work);             /* backend.h:226 */
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CT_BACKEND_H */

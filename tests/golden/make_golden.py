@@ -1,0 +1,99 @@
+#!/usr/bin/env python3
+"""Regenerate the golden fixtures in this directory from the REFERENCE code.
+
+Needs the reference source tree (argument or $CT_REFERENCE_DIR); it compiles
+the reference's own CPU backend, kernel test program and model graph (through
+oracle/Makefile into oracle/_ref/) and records their outputs:
+
+  test_kernels_ref_cpu.bin   tests/test_kernels.c of the reference on its CPU
+                             backend (LCG seed 0xdeadbeef; 9 kernels)
+  struct_offsets_ref.txt     field offsets of the reference weight-table structs
+  tiny_e2e_ref.npz           configuration 1 end to end (log-mel -> tokens) on the
+                             reference model.h + CPU backend at the tiny dims
+  full_decode_ref.npz        full-size decoder: prefill + batched greedy decode of
+                             two sequences from seeded encoder outputs
+
+Inputs are regenerated from seeds by tests/golden/inputs.py; a checksum of
+each input is stored with the outputs so drift is detected.
+"""
+import ctypes
+import os
+import subprocess
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+sys.path.insert(0, HERE)
+
+import importlib  # noqa: E402
+
+import inputs  # noqa: E402
+import pyoracle  # noqa: E402
+
+ctb = importlib.import_module("cohere-transcribe_b200")
+W = importlib.import_module("cohere-transcribe_b200.weights")
+
+
+def main(ref: str) -> None:
+    pyoracle.build(ref)
+    rdir = pyoracle.REF_DIR
+
+    # 1. the reference kernel test program
+    subprocess.run([os.path.join(rdir, "test_kernels_ref"), os.path.join(HERE, "test_kernels_ref_cpu.bin")],
+                   check=True, stderr=subprocess.DEVNULL)
+
+    # 2. struct layout of the reference header
+    exe = os.path.join(rdir, "struct_offsets_ref")
+    subprocess.run(["gcc", "-O0", f"-DMODEL_TYPES_HEADER=\"{ref}/backends/model_types.h\"",
+                    "-o", exe, os.path.join(HERE, "struct_offsets.c")], check=True)
+    with open(os.path.join(HERE, "struct_offsets_ref.txt"), "w") as fh:
+        fh.write(subprocess.run([exe], check=True, capture_output=True, text=True).stdout)
+
+    # 3. configuration 1, tiny, end to end on the reference
+    case = inputs.tiny_e2e_case()
+    L = pyoracle.bind_ref_decode(pyoracle.ref_lib("libref_decode_tiny.so"))
+    wb = W.make_blob(W.TINY_DIMS, seed=case["weight_seed"])
+    ws = W.weights_struct(wb, enc_n=2, dec_n=2)
+    L.refh_bind_weights(ctypes.addressof(ws))
+    L.backend_init(0)
+    B = case["mel"].shape[0]
+    tokens = np.zeros((B, 1024), np.int32)
+    n_tok = np.zeros(B, np.int32)
+    am = np.full((B, 1024), -1, np.int32)
+    mg = np.full((B, 1024), np.nan, np.float32)
+    enc_h = np.zeros((B, ctb.t_enc_of(case["T_mel_max"]), 256), np.float32)
+    L.refh_transcribe_batch(B, pyoracle.fp(case["mel"]), case["T_mel_max"], pyoracle.ip(case["T_mel"]),
+                            pyoracle.ip(case["prompt"]), len(case["prompt"]), pyoracle.ip(case["forced_len"]),
+                            pyoracle.null_i(), pyoracle.ip(tokens), pyoracle.ip(n_tok), pyoracle.ip(am),
+                            pyoracle.fp(mg), pyoracle.fp(enc_h))
+    np.savez_compressed(os.path.join(HERE, "tiny_e2e_ref.npz"), tokens=tokens, n_tok=n_tok, argmax=am,
+                        margin=mg, enc_h=enc_h, mel_checksum=np.float64(case["mel"].astype(np.float64).sum()))
+
+    # 4. full-size decoder slice on the reference
+    case = inputs.full_decode_case()
+    L = pyoracle.bind_ref_decode(pyoracle.ref_lib("libref_decode_cpu.so"))
+    wb = W.make_blob(W.FULL_DIMS, seed=case["weight_seed"], parts=("dec",))
+    ws = W.weights_struct(wb)
+    L.refh_bind_weights(ctypes.addressof(ws))
+    L.backend_init(0)
+    enc = case["enc_h"]
+    B, T_max, _ = enc.shape
+    tokens = np.zeros((B, 1024), np.int32)
+    n_tok = np.zeros(B, np.int32)
+    am = np.full((B, 1024), -1, np.int32)
+    mg = np.full((B, 1024), np.nan, np.float32)
+    L.refh_decode_from_enc(B, pyoracle.fp(enc), pyoracle.ip(case["T_enc"]), T_max,
+                           pyoracle.ip(case["prompt"]), len(case["prompt"]), pyoracle.ip(case["forced_len"]),
+                           pyoracle.null_i(), pyoracle.ip(tokens), pyoracle.ip(n_tok), pyoracle.ip(am),
+                           pyoracle.fp(mg))
+    np.savez_compressed(os.path.join(HERE, "full_decode_ref.npz"), tokens=tokens, n_tok=n_tok, argmax=am,
+                        margin=mg, enc_checksum=np.float64(enc.astype(np.float64).sum()))
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CT_REFERENCE_DIR", "/root/reference"))
