@@ -1,0 +1,118 @@
+"""ctypes prototypes of libct_b200.so (the C ABI of include/ct_backend.h).
+
+`load()` fails loudly when the library is missing: there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from . import LIB_PATH
+
+_f = ctypes.POINTER(ctypes.c_float)
+_i = ctypes.POINTER(ctypes.c_int)
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_int = ctypes.c_int
+_flt = ctypes.c_float
+
+# name -> (restype, argtypes); weight pointers are passed as void* (host addresses)
+SIGNATURES = {
+    "backend_init": (None, [_int]),
+    "backend_destroy": (None, []),
+    "backend_num_devices": (_int, []),
+    "backend_thread_cleanup": (None, []),
+    "backend_weights_upload_blob": (None, [_vp, _sz]),
+    "backend_device_ptr": (_vp, [_vp]),
+    "backend_arena_alloc": (_vp, [_sz]),
+    "backend_arena_free": (None, [_vp]),
+    "backend_htod": (None, [_vp, _vp, _sz]),
+    "backend_dtoh": (None, [_vp, _vp, _sz]),
+    "backend_layernorm": (None, [_vp, _vp, _vp, _vp, _int, _int]),
+    "backend_linear": (None, [_vp, _vp, _vp, _vp, _int, _int, _int]),
+    "backend_linear_silu": (None, [_vp, _vp, _vp, _vp, _int, _int, _int]),
+    "backend_linear_relu": (None, [_vp, _vp, _vp, _vp, _int, _int, _int]),
+    "backend_linear_fmadd": (None, [_vp, _flt, _vp, _vp, _vp, _int, _int, _int]),
+    "backend_add_inplace": (None, [_vp, _vp, _int]),
+    "backend_encoder_subsampling": (None, [_vp, _int, _int, _vp, _int, _vp, _vp]),
+    "backend_make_rel_pos_emb": (None, [_vp, _int]),
+    "backend_rel_pos_mhsa": (None, [_vp, _vp, _int, _vp, _vp]),
+    "backend_conformer_conv": (None, [_vp, _int, _vp, _vp]),
+    "backend_sdp_attn": (None, [_vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
+    "backend_embed": (None, [_vp, _vp, _int, _int, _vp, _vp, _vp, _vp]),
+    "backend_fill_causal_mask": (None, [_vp, _int]),
+    "backend_lm_head": (None, [_vp, _vp, _vp, _vp]),
+    "backend_upload_tokens": (None, [_vp, _int]),
+    "backend_graph_replay": (_int, [_int, _int, _int, _int]),
+    "backend_graph_begin_capture": (None, [_int]),
+    "backend_graph_end_capture": (None, [_int, _int, _int, _int]),
+    "backend_decode_set_S": (None, [_int]),
+    "backend_decode_inc_S": (None, []),
+    "backend_linear_to_kvcache": (None, [_vp, _vp, _vp, _vp, _int, _int]),
+    "backend_sdp_attn_devS": (None, [_vp, _vp, _vp, _vp, _vp]),
+    "backend_embed_decode": (None, [_vp, _vp, _vp, _vp, _vp]),
+    "backend_embed_decode_batch": (None, [_vp, _vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
+    "backend_lm_head_batch": (None, [_vp, _vp, _vp, _vp, _vp, _int]),
+    "backend_argmax_batch": (None, [_vp, _vp, _vp, _int]),
+    "backend_upload_T_enc": (None, [_vp, _int]),
+    "backend_linear_to_kvcache_batch": (None, [_vp, _vp, _vp, _vp, _int, _int, _int, _int]),
+    "backend_sdp_attn_batch_decode_sa": (None, [_vp, _vp, _vp, _vp, _int, _int, _vp]),
+    "backend_sdp_attn_batch_decode_ca": (None, [_vp, _vp, _vp, _vp, _int, _int, _vp]),
+    # extension
+    "ct_device_status": (_int, []),
+}
+
+BACKEND_SYMBOLS = [n for n in SIGNATURES if n.startswith("backend_")]
+
+_lib = None
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load libct_b200.so and set its prototypes (raises if it is not built)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise RuntimeError(f"{p} is missing: run __graft_entry__.build() (there is no CPU fallback)")
+    L = ctypes.CDLL(p)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = L
+    return L
+
+
+class DeviceArena:
+    """Device float buffers carved from the backend arena (backend_arena_alloc),
+    mirroring how transcribe.c lays out its arena."""
+
+    def __init__(self, lib: ctypes.CDLL, floats: int):
+        self.lib = lib
+        self.base = lib.backend_arena_alloc(floats)
+        self.cap = floats
+        self.off = 0
+
+    def take(self, n: int) -> int:
+        n = int(n)
+        n = (n + 63) // 64 * 64          # keep every buffer 256-byte aligned
+        if self.off + n > self.cap:
+            raise MemoryError("arena exhausted")
+        p = self.base + 4 * self.off
+        self.off += n
+        return p
+
+    def put(self, arr: np.ndarray) -> int:
+        a = np.ascontiguousarray(arr, dtype=np.float32)
+        p = self.take(a.size)
+        self.lib.backend_htod(p, a.ctypes.data, a.size)
+        return p
+
+    def get(self, ptr: int, shape, dtype=np.float32) -> np.ndarray:
+        out = np.empty(shape, dtype)
+        self.lib.backend_dtoh(out.ctypes.data, ptr, out.nbytes)
+        return out

@@ -1,0 +1,440 @@
+// gemm.cu -- tcgen05 / TMA GEMM (see gemm.cuh).
+//
+// One CTA computes a 128 (features) x BN (tokens) output tile over a K range:
+//   warp 0      TMA producer: W tile [128 x 64] and X tile(s) [BN x 64] per stage
+//   warp 1      MMA issuer: 4 (or 8 with X_lo) tcgen05.mma K=16 per stage,
+//               TMEM allocation owner
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, bias/activation/
+//               residual/scatter, coalesced stores (lanes = consecutive features)
+// Stages are released by tcgen05.commit on the stage's "empty" mbarrier.
+// Split-K (grid.z) writes fp32 partials that a second kernel sums in split
+// order, so the result is deterministic and independent of T.
+#include <memory>
+#include <unordered_map>
+
+#include "gemm.cuh"
+
+namespace ct {
+
+static constexpr int BM = 128;
+static constexpr int BK = 64;
+static constexpr int kThreads = 192;
+static constexpr int kSmemBudget = 220 * 1024;
+
+struct KernelParams {
+    int N, K, T;
+    int kbps;      // k-blocks (of 64) per split
+    int kb_total;
+    int stages;
+    float *ws;     // split partials [nsplit][T][N] (null when not split)
+    GemmEpilogue ep;
+};
+
+__device__ __forceinline__ void apply_epilogue(const GemmEpilogue &ep, int t, int n, float v) {
+    if (ep.row_mask && !ep.row_mask[t]) return;
+    switch (ep.epi) {
+    case EPI_STORE: ep.Y[(size_t)t * ep.ldy + n] = v; break;
+    case EPI_SILU: ep.Y[(size_t)t * ep.ldy + n] = v / (1.0f + expf(-v)); break;
+    case EPI_RELU: ep.Y[(size_t)t * ep.ldy + n] = v > 0.0f ? v : 0.0f; break;
+    case EPI_FMADD: ep.Y[(size_t)t * ep.ldy + n] += ep.scale * v; break;
+    case EPI_KVCACHE: {
+        const int slot = ep.pos[t] - 1;
+        if (slot < 0 || slot >= ep.kv_stride) { set_status(CT_STATUS_BAD_ARG); break; }
+        ep.Y[((size_t)t * ep.kv_stride + slot) * ep.ldy + n] = v;
+        break;
+    }
+    case EPI_BF16: {
+        float a = v;
+        if (ep.act == 1) a = v / (1.0f + expf(-v));
+        else if (ep.act == 2) a = v > 0.0f ? v : 0.0f;
+        const bf16 hb = __float2bfloat16_rn(a);
+        ep.Ybf[(size_t)t * ep.ldy + n] = hb;
+        if (ep.Ybf_lo) ep.Ybf_lo[(size_t)t * ep.ldy + n] = __float2bfloat16_rn(a - __bfloat162float(hb));
+        break;
+    }
+    case EPI_QKV_PAGED: {
+        if (n < ep.qdim) { ep.Y[(size_t)t * ep.ldy + n] = v; break; }
+        const long long off = ep.row_off[t];
+        if (off < 0) break;
+        const int n2 = n - ep.qdim, kv = n2 / ep.kv_width, c = n2 % ep.kv_width;
+        ep.kv_pool[off + (long long)(ep.layer * 2 + kv) * kPageRows * ep.kv_width + c] = __float2bfloat16_rn(v);
+        break;
+    }
+    case EPI_CAKV_PAGED: {
+        const long long off = ep.row_off[t];
+        if (off < 0) break;
+        const int lk = n / ep.kv_width, c = n % ep.kv_width;   // lk = layer*2 + kv
+        ep.kv_pool[off + (long long)lk * kPageRows * ep.kv_width + c] = __float2bfloat16_rn(v);
+        break;
+    }
+    case EPI_RELU_FLAT:
+        ep.Y[(size_t)(t / ep.flat_f) * ep.ldy + (size_t)n * ep.flat_f + (t % ep.flat_f)] = v > 0.0f ? v : 0.0f;
+        break;
+    default: break;
+    }
+}
+
+template <int BN, bool TWO>
+__global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                           const __grid_constant__ CUtensorMap tmXh,
+                                                           const __grid_constant__ CUtensorMap tmXl,
+                                                           const KernelParams p) {
+    constexpr uint32_t A_BYTES = BM * BK * 2;
+    constexpr uint32_t B_BYTES = BN * BK * 2;
+    constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES * (TWO ? 2 : 1);
+    constexpr uint32_t NCOLS = BN < 32 ? 32 : BN;
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int stages = p.stages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)stages * STAGE_BYTES);
+    uint64_t *empty = full + stages;
+    uint64_t *accb = empty + stages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accb + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BM, t0 = blockIdx.y * BN, z = blockIdx.z;
+    const int T_eff = p.ep.T_dev ? min(p.T, *p.ep.T_dev) : p.T;
+    if (t0 >= T_eff) return;   // uniform per CTA, before any barrier or TMEM allocation
+    const int kb0 = z * p.kbps;
+    const int kb1 = min(kb0 + p.kbps, p.kb_total);
+    const int nkb = kb1 - kb0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(accb, 1);
+        fence_mbar_init();
+        prefetch_tmap(&tmW);
+        prefetch_tmap(&tmXh);
+        if (TWO) prefetch_tmap(&tmXl);
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, NCOLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % stages;
+                const uint32_t ph = (uint32_t)(i / stages) & 1u;
+                if (i >= stages && !mbar_wait(&empty[s], ph ^ 1u, CT_STATUS_TIMEOUT_FREE)) break;
+                uint8_t *a = smem + (size_t)s * STAGE_BYTES;
+                mbar_expect_tx(&full[s], STAGE_BYTES);
+                const int kc = (kb0 + i) * BK;
+                tma_load_2d(a, &tmW, &full[s], kc, n0);
+                tma_load_2d(a + A_BYTES, &tmXh, &full[s], kc, t0);
+                if (TWO) tma_load_2d(a + A_BYTES + B_BYTES, &tmXl, &full[s], kc, t0);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(BM, BN);
+            bool ok = true;
+            for (int i = 0; i < nkb && ok; ++i) {
+                const int s = i % stages;
+                const uint32_t ph = (uint32_t)(i / stages) & 1u;
+                ok = mbar_wait(&full[s], ph, CT_STATUS_TIMEOUT_TMA);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t a = smem_u32(smem + (size_t)s * STAGE_BYTES);
+                const uint64_t ad = sw128_desc(a);
+                const uint64_t bd = sw128_desc(a + A_BYTES);
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)
+                    mma_bf16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+                if (TWO) {
+                    const uint64_t ld = sw128_desc(a + A_BYTES + B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) mma_bf16(tmem, ad + 2 * k, ld + 2 * k, idesc, 1u);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(accb);
+        }
+    } else {
+        // epilogue warps 2..5 -> TMEM lane quarters 2,3,0,1
+        const int q = warp & 3;
+        const int n = n0 + q * 32 + lane;
+        const bool nvalid = n < p.N;
+        const bool split = p.ws != nullptr;
+        const float bias = (!split && nvalid && p.ep.bias) ? bf2f(p.ep.bias[n]) : 0.0f;
+        bool ok = mbar_wait(accb, 0, CT_STATUS_TIMEOUT_MMA);
+        ok = __all_sync(0xffffffffu, ok);
+        tc_fence_after();
+        if (ok) {
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                if (t0 + c >= T_eff) break;   // warp-uniform
+                float v[32];
+                tmem_ld32(tbase + (uint32_t)c, v);
+                if (nvalid) {
+                    const int tl = min(32, T_eff - (t0 + c));
+                    if (split) {
+                        float *w = p.ws + ((size_t)z * p.T + t0 + c) * p.N + n;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < tl) w[(size_t)j * p.N] = v[j];
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < tl) apply_epilogue(p.ep, t0 + c + j, n, v[j] + bias);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, NCOLS);
+}
+
+__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int nsplit, int T, int N, GemmEpilogue ep) {
+    const size_t TN = (size_t)T * N;
+    const size_t lim = ep.T_dev ? (size_t)min(T, *ep.T_dev) * N : TN;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < lim; i += (size_t)gridDim.x * blockDim.x) {
+        float s = ws[i];
+        for (int z = 1; z < nsplit; ++z) s += ws[(size_t)z * TN + i];
+        const int t = (int)(i / N), n = (int)(i % N);
+        if (ep.bias) s += bf2f(ep.bias[n]);
+        apply_epilogue(ep, t, n, s);
+    }
+}
+
+__global__ void split_fp32_kernel(const float *__restrict__ x, int T, int K, int ldx, bf16 *__restrict__ hi,
+                                  bf16 *__restrict__ lo, int Kp) {
+    const size_t total = (size_t)T * Kp;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / Kp), k = (int)(i % Kp);
+        const float v = k < K ? x[(size_t)t * ldx + k] : 0.0f;
+        const bf16 h = __float2bfloat16_rn(v);
+        hi[i] = h;
+        if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+}
+
+// ---------------------------------------------------------------- host ------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        CT_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !p) CT_FATAL("cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+struct MapKey {
+    const void *p;
+    long rows, cols, box;
+    bool operator==(const MapKey &o) const { return p == o.p && rows == o.rows && cols == o.cols && box == o.box; }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const {
+        return std::hash<const void *>()(k.p) ^ (std::hash<long>()(k.rows) * 31) ^ (std::hash<long>()(k.cols) * 131) ^
+               (std::hash<long>()(k.box) * 7919);
+    }
+};
+
+struct WCopy {
+    bf16 *p;
+    int Kp;
+};
+
+struct GemmCtx {
+    int device = -1;
+    float *ws = nullptr;
+    size_t ws_bytes = 0;
+    bf16 *xhi = nullptr, *xlo = nullptr;
+    size_t x_elems = 0;
+    std::unordered_map<MapKey, CUtensorMap, MapKeyHash> maps;
+    std::unordered_map<const void *, WCopy> wcopies;
+};
+
+static thread_local std::unique_ptr<GemmCtx> t_ctx;
+
+static bool capturing(cudaStream_t st) {
+    cudaStreamCaptureStatus s = cudaStreamCaptureStatusNone;
+    CT_CHECK(cudaStreamIsCapturing(st, &s));
+    return s != cudaStreamCaptureStatusNone;
+}
+
+GemmCtx *gemm_ctx() {
+    int dev = 0;
+    CT_CHECK(cudaGetDevice(&dev));
+    if (t_ctx && t_ctx->device != dev) gemm_ctx_release();
+    if (!t_ctx) {
+        t_ctx.reset(new GemmCtx());
+        t_ctx->device = dev;
+        t_ctx->ws_bytes = 64ull << 20;
+        CT_CHECK(cudaMalloc(&t_ctx->ws, t_ctx->ws_bytes));
+        t_ctx->x_elems = 16ull << 20;
+        CT_CHECK(cudaMalloc(&t_ctx->xhi, t_ctx->x_elems * sizeof(bf16)));
+        CT_CHECK(cudaMalloc(&t_ctx->xlo, t_ctx->x_elems * sizeof(bf16)));
+    }
+    return t_ctx.get();
+}
+
+void gemm_ctx_release() {
+    if (!t_ctx) return;
+    int cur = 0;
+    CT_CHECK(cudaGetDevice(&cur));
+    CT_CHECK(cudaSetDevice(t_ctx->device));
+    CT_CHECK(cudaDeviceSynchronize());
+    cudaFree(t_ctx->ws);
+    cudaFree(t_ctx->xhi);
+    cudaFree(t_ctx->xlo);
+    for (auto &kv : t_ctx->wcopies) cudaFree(kv.second.p);
+    t_ctx.reset();
+    CT_CHECK(cudaSetDevice(cur));
+}
+
+void gemm_reserve_ws(size_t bytes) {
+    GemmCtx *c = gemm_ctx();
+    if (bytes <= c->ws_bytes) return;
+    CT_CHECK(cudaDeviceSynchronize());
+    scratch_moved();
+    cudaFree(c->ws);
+    c->ws_bytes = bytes;
+    CT_CHECK(cudaMalloc(&c->ws, bytes));
+}
+
+static const CUtensorMap &tmap_bf16(GemmCtx *c, const void *ptr, long rows, long cols, long box_rows) {
+    MapKey key{ptr, rows, cols, box_rows};
+    auto it = c->maps.find(key);
+    if (it != c->maps.end()) return it->second;
+    if (((uintptr_t)ptr & 15) || (cols & 7)) CT_FATAL("TMA operand not 16-byte aligned (ptr %p, cols %ld)", ptr, cols);
+    CUtensorMap m;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) CT_FATAL("cuTensorMapEncodeTiled failed (%d) rows %ld cols %ld box %ld", (int)r, rows, cols, box_rows);
+    return c->maps.emplace(key, m).first->second;
+}
+
+int split_factor(int N, int K) {
+    const int tiles = (N + BM - 1) / BM;
+    const int kb = (K + BK - 1) / BK;
+    if ((long)N * K > 4l * 1024 * 1024) return 1;
+    int s = 1;
+    while (tiles * s * 2 <= 128 && kb / (s * 2) >= 2) s *= 2;
+    return s;
+}
+
+template <int BN, bool TWO>
+static void launch_tc(cudaStream_t st, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml,
+                      KernelParams p, int nsplit) {
+    constexpr int STAGE = BM * BK * 2 + BN * BK * 2 * (TWO ? 2 : 1);
+    const int max_stages = (kSmemBudget - 2048) / STAGE;
+    p.stages = p.kbps < max_stages ? p.kbps : max_stages;
+    if (p.stages > 8) p.stages = 8;
+    const size_t smem = (size_t)p.stages * STAGE + 1024 + 16 * (2 * p.stages + 2);
+    static thread_local bool configured = false;   // per instantiation and thread
+    if (!configured) {
+        CT_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN, TWO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kSmemBudget));
+        configured = true;
+    }
+    dim3 grid((p.N + BM - 1) / BM, (p.T + BN - 1) / BN, nsplit);
+    gemm_tc_kernel<BN, TWO><<<grid, kThreads, smem, st>>>(mw, mh, ml, p);
+    CT_CHECK(cudaGetLastError());
+}
+
+void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, const bf16 *X_lo, int T,
+               const GemmEpilogue &ep_in, bool allow_split) {
+    if (T <= 0 || N <= 0) return;
+    GemmCtx *c = gemm_ctx();
+    GemmEpilogue ep = ep_in;
+    if (ep.ldy == 0) ep.ldy = N;
+    const bool two = X_lo != nullptr;
+    int BN = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : (two ? 128 : 256);
+    const int kb_total = (K + BK - 1) / BK;
+    int nsplit = allow_split ? split_factor(N, K) : 1;
+    if (nsplit > 1 && (size_t)nsplit * T * N * sizeof(float) > c->ws_bytes) nsplit = 1;
+    const int kbps = (kb_total + nsplit - 1) / nsplit;
+    nsplit = (kb_total + kbps - 1) / kbps;   // every split gets >= 1 block
+    // X maps use the scratch capacity (or T) as the row count; rows >= T are never stored
+    const long xrows = (X_hi == c->xhi || X_hi == c->xlo) ? (long)(c->x_elems / K) : (long)T;
+    const CUtensorMap &mw = tmap_bf16(c, W, N, K, BM);
+    const CUtensorMap &mh = tmap_bf16(c, X_hi, xrows, K, BN);
+    const CUtensorMap &ml = two ? tmap_bf16(c, X_lo, xrows, K, BN) : mh;
+    KernelParams p;
+    p.N = N; p.K = K; p.T = T; p.kbps = kbps; p.kb_total = kb_total; p.stages = 1;
+    p.ws = nsplit > 1 ? c->ws : nullptr;
+    p.ep = ep;
+#define CT_LAUNCH(bn)                                                                            \
+    (two ? launch_tc<bn, true>(st, mw, mh, ml, p, nsplit) : launch_tc<bn, false>(st, mw, mh, ml, p, nsplit))
+    switch (BN) {
+    case 32: CT_LAUNCH(32); break;
+    case 64: CT_LAUNCH(64); break;
+    case 128: CT_LAUNCH(128); break;
+    default: launch_tc<256, false>(st, mw, mh, ml, p, nsplit); break;
+    }
+#undef CT_LAUNCH
+    if (nsplit > 1) {
+        const size_t TN = (size_t)T * N;
+        int blocks = (int)((TN + 255) / 256);
+        if (blocks > 148 * 8) blocks = 148 * 8;
+        splitk_reduce_kernel<<<blocks, 256, 0, st>>>(c->ws, nsplit, T, N, ep);
+        CT_CHECK(cudaGetLastError());
+    }
+}
+
+void split_fp32_to_bf16(cudaStream_t st, const float *x, int T, int K, int ldx, bf16 *hi, bf16 *lo, int Kp) {
+    const size_t total = (size_t)T * Kp;
+    if (!total) return;
+    int blocks = (int)((total + 255) / 256);
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    split_fp32_kernel<<<blocks, 256, 0, st>>>(x, T, K, ldx, hi, lo, Kp);
+    CT_CHECK(cudaGetLastError());
+}
+
+static const bf16 *usable_weight(GemmCtx *c, cudaStream_t st, const bf16 *W, int N, int K, int Kp) {
+    if (((uintptr_t)W & 15) == 0 && Kp == K) return W;
+    auto it = c->wcopies.find(W);
+    if (it != c->wcopies.end() && it->second.Kp == Kp) return it->second.p;
+    if (capturing(st)) CT_FATAL("weight at %p needs an aligned copy; first use may not be inside graph capture", (const void *)W);
+    bf16 *cp = nullptr;
+    CT_CHECK(cudaMalloc(&cp, (size_t)N * Kp * sizeof(bf16)));
+    CT_CHECK(cudaMemsetAsync(cp, 0, (size_t)N * Kp * sizeof(bf16), st));
+    CT_CHECK(cudaMemcpy2DAsync(cp, (size_t)Kp * 2, W, (size_t)K * 2, (size_t)K * 2, N, cudaMemcpyDeviceToDevice, st));
+    c->wcopies[W] = WCopy{cp, Kp};
+    return cp;
+}
+
+void linear_fp32(cudaStream_t st, const bf16 *W, int N, int K, const float *X, int T, int ldx,
+                 const GemmEpilogue &ep, bool allow_split, bool two_term) {
+    if (T <= 0 || N <= 0) return;
+    GemmCtx *c = gemm_ctx();
+    const int Kp = (K + 7) & ~7;
+    const bf16 *Wu = usable_weight(c, st, W, N, K, Kp);
+    if ((size_t)T * Kp > c->x_elems) {
+        if (capturing(st)) CT_FATAL("activation scratch too small inside graph capture (T %d, K %d)", T, K);
+        CT_CHECK(cudaStreamSynchronize(st));
+        scratch_moved();
+        cudaFree(c->xhi);
+        cudaFree(c->xlo);
+        for (auto it = c->maps.begin(); it != c->maps.end();)
+            it = (it->first.p == c->xhi || it->first.p == c->xlo) ? c->maps.erase(it) : std::next(it);
+        c->x_elems = (size_t)T * Kp * 2;
+        CT_CHECK(cudaMalloc(&c->xhi, c->x_elems * sizeof(bf16)));
+        CT_CHECK(cudaMalloc(&c->xlo, c->x_elems * sizeof(bf16)));
+    }
+    split_fp32_to_bf16(st, X, T, K, ldx, c->xhi, two_term ? c->xlo : nullptr, Kp);
+    gemm_bf16(st, Wu, N, Kp, c->xhi, two_term ? c->xlo : nullptr, T, ep, allow_split);
+}
+
+}  // namespace ct

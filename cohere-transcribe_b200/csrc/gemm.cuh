@@ -1,0 +1,81 @@
+// gemm.cuh -- tcgen05 GEMM of libct_b200.so: Y[t, n] = epi( X[t, :] . W[n, :] + b[n] ).
+//
+// W is a bf16 weight matrix [N, K] (row-major, the layout of every linear in
+// the model file), X is bf16 activations [T, K].  The kernel tiles the
+// weights as the MMA's M side (128 output features per tile) and the tokens as
+// the N side (BN = 32..256 tokens per tile), so small decode batches still
+// fill the 128-row MMA ("swap-AB").  Optional second activation plane (X_lo)
+// carries the bf16 residual of fp32 activations: X ~= X_hi + X_lo to ~2^-17
+// relative, which lets fp32 inputs reach near-fp32 accuracy on bf16 tensor
+// cores (two MMAs into the same TMEM accumulator).
+#pragma once
+#include "ct_common.cuh"
+
+namespace ct {
+
+enum Epi : int {
+    EPI_STORE = 0,    // Y = acc + b
+    EPI_SILU = 1,     // Y = silu(acc + b)
+    EPI_RELU = 2,     // Y = relu(acc + b)
+    EPI_FMADD = 3,    // Y += scale * (acc + b)
+    EPI_KVCACHE = 4,  // Y[(t*kv_stride + pos[t]-1) * ldy + n] = acc + b
+    EPI_BF16 = 5,     // Ybf[t * ldy + n] = bf16(act(acc + b)), act = p.act (0 none, 1 silu, 2 relu)
+    EPI_RELU_FLAT = 6,  // token t = frame * flat_f + f:  Y[frame * ldy + n * flat_f + f] = relu(acc + b)
+    EPI_QKV_PAGED = 7,  // n < qdim: Y[t*ldy+n] = v (fp32 Q); else K/V -> kv_pool at row_off[t] (layer `layer`)
+    EPI_CAKV_PAGED = 8, // n = (l*2 + kv)*1024 + c -> kv_pool[row_off[t] + (l*2+kv)*PAGE*1024 + c]
+};
+
+// Paged KV pool geometry: page = [DEC_N layers][K,V][kPageRows rows][1024].
+constexpr int kPageRows = 16;
+
+struct GemmEpilogue {
+    int epi = EPI_STORE;
+    float scale = 1.0f;
+    const bf16 *bias = nullptr;   // [N] or null
+    float *Y = nullptr;           // fp32 output
+    bf16 *Ybf = nullptr;          // bf16 output (EPI_BF16)
+    int ldy = 0;                  // output row stride in elements (default N)
+    const int *pos = nullptr;     // EPI_KVCACHE: per-token sequence length (slot = pos-1)
+    int kv_stride = 0;            // EPI_KVCACHE: rows per item
+    int act = 0;                  // EPI_BF16 activation
+    int flat_f = 0;               // EPI_RELU_FLAT: frequency bins per frame
+    const int *row_mask = nullptr;  // optional: rows t with row_mask[t] == 0 are not stored
+    bf16 *Ybf_lo = nullptr;       // EPI_BF16: optional residual plane (v - hi), same layout
+    bf16 *kv_pool = nullptr;      // EPI_QKV_PAGED / EPI_CAKV_PAGED
+    const long long *row_off = nullptr;  // per-row element offset of (page, row-in-page); < 0 skips
+    int layer = 0;
+    int qdim = 0;
+    int kv_width = 1024;          // K/V row width in the pool
+    const int *T_dev = nullptr;   // optional device row count (rows >= *T_dev are skipped)
+};
+
+// Per-thread GEMM context: stream, workspaces, tensor-map cache.
+struct GemmCtx;
+GemmCtx *gemm_ctx();   // the calling thread's context (created on first use)
+void gemm_ctx_release();
+
+// Launch on `st`.  X_lo may be null (single bf16 plane).  allow_split enables
+// the deterministic split-K used for decode-sized problems; the split factor
+// depends only on (N, K), never on T.
+void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, const bf16 *X_lo, int T,
+               const GemmEpilogue &ep, bool allow_split);
+
+// fp32 activations [T, K] (row stride ldx) -> bf16 hi/lo planes [T, Kp], zero-padded to Kp.
+void split_fp32_to_bf16(cudaStream_t st, const float *x, int T, int K, int ldx, bf16 *hi, bf16 *lo, int Kp);
+
+// Convenience for the fp32 ABI: converts X into the thread's scratch planes,
+// pads K to a multiple of 8 (TMA row pitch) and makes an aligned weight copy
+// when the blob pointer is not 16-byte aligned.
+void linear_fp32(cudaStream_t st, const bf16 *W, int N, int K, const float *X, int T, int ldx,
+                 const GemmEpilogue &ep, bool allow_split = true, bool two_term = true);
+
+int split_factor(int N, int K);
+
+// Called whenever a per-thread scratch buffer moves, so that cached CUDA graphs
+// holding its old address are dropped (defined by the ABI layer).
+void scratch_moved();
+
+// Make sure the split-K workspace of the calling thread holds `bytes`.
+void gemm_reserve_ws(size_t bytes);
+
+}  // namespace ct

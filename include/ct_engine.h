@@ -1,0 +1,92 @@
+/* ct_engine.h -- continuous-batching decode engine of libct_b200.so.
+ *
+ * Additive to the drop-in ABI of ct_backend.h: that ABI cannot express a
+ * paged KV cache or admission of new sequences into a running batch (its KV
+ * cache is a dense fp32 [B, MAX_SEQ, DEC_D] arena region, backends/backend.h:214-217,
+ * and transcribe_batch admits nothing mid-flight, transcribe.c:752-795).  The
+ * engine replaces the per-item prefill + joint decode loop of transcribe_batch
+ * (transcribe.c:692-795) and decoder_step_decode_batch (model.h:721-744):
+ *
+ *   - one engine per GPU, driven by one host thread;
+ *   - sequences are admitted into slots; every step packs the query rows of all
+ *     live slots (10 prompt rows for a slot's first step, then 1 row) with
+ *     prefix sums on the GPU, so prefill and decode share one batched pass;
+ *   - self-attention K/V and cross-attention K/V live in a bf16 page pool
+ *     (16 token rows per page, all layers); cross K/V are projected once at
+ *     admission (model.h:620-635) straight into pages;
+ *   - greedy argmax, EOS / forced-length retirement and token append happen on
+ *     the GPU; the host only admits, launches the captured step graph and
+ *     harvests finished sequences.
+ *
+ * All functions return 0 on success or a negative CT_E* code; none exits.
+ */
+#ifndef CT_ENGINE_H
+#define CT_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "ct_model_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CT_OK 0
+#define CT_EINVAL (-1)      /* bad argument */
+#define CT_ENOMEM (-2)      /* device or page-pool allocation failed */
+#define CT_EBUSY (-3)       /* no free slot / pages: retry after harvesting */
+#define CT_EDEVICE (-4)     /* a CUDA call failed */
+#define CT_ETIMEDOUT (-5)   /* a bounded device wait gave up (status word set) */
+
+typedef struct ct_engine ct_engine;
+
+typedef struct {
+    int max_slots;       /* concurrent sequences (default 256, max 1024) */
+    int max_rows;        /* packed query rows per step (default 1024) */
+    int kv_pages;        /* pages in the pool; 0 = size for max_slots full-length sequences */
+    int precision;       /* 1 = activations as bf16 hi+lo planes (near fp32, default), 0 = bf16 */
+    int n_prompt;        /* prompt length (default 10) */
+    const int *prompt;   /* prompt tokens (default: transcribe.c:1320-1330 with a synthetic language id) */
+} ct_engine_config;
+
+typedef struct {
+    long long utt_id;
+    int n_tokens;        /* generated tokens, EOS included */
+    int status;          /* 0 ok */
+} ct_result;
+
+/* w_host: the reference weight table (host pointers into host_blob). */
+int ct_engine_create(ct_engine **out, int device, const void *host_blob, size_t bytes, const Weights *w_host,
+                     const ct_engine_config *cfg);
+void ct_engine_destroy(ct_engine *e);
+
+/* Queue one utterance from its encoder output enc_h (host, fp32 [T_enc, DEC_D],
+ * the rows model.h's encoder_forward_batch produces).  forced_len > 0 forces EOS
+ * as the forced_len-th generated token (natural EOS before it is ignored);
+ * forced_len == 0 decodes until EOS or MAX_SEQ. */
+int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const float *enc_h, int T_enc, int forced_len);
+
+/* Run up to n_steps packed steps (admitting queued utterances when slots and
+ * pages allow).  Returns the number of sequences still queued or live, or a
+ * negative error. */
+int ct_engine_step(ct_engine *e, int n_steps);
+
+/* Run until every submitted utterance has finished. */
+int ct_engine_run(ct_engine *e);
+
+/* Finished utterances (up to max), oldest first.  tokens (optional) receives
+ * each result's generated tokens at tokens + i * tok_stride. */
+int ct_engine_poll(ct_engine *e, ct_result *out, int max, int *tokens, int tok_stride);
+
+/* Counters: steps run, rows processed, tokens generated, device time of the
+ * step graphs in milliseconds (CUDA events). */
+int ct_engine_stats(ct_engine *e, long long *steps, long long *rows, long long *tokens, double *step_ms);
+
+/* Read (and clear) the device status word; 0 when no kernel reported a problem. */
+int ct_engine_status(ct_engine *e);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
