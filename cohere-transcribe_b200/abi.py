@@ -62,7 +62,88 @@ SIGNATURES = {
     "backend_sdp_attn_batch_decode_ca": (None, [_vp, _vp, _vp, _vp, _int, _int, _vp]),
     # extension
     "ct_device_status": (_int, []),
+    # engine (include/ct_engine.h)
+    "ct_engine_create": (_int, [_vp, _int, _vp, _sz, _vp, _vp]),
+    "ct_engine_destroy": (None, [_vp]),
+    "ct_engine_submit_encoded": (_int, [_vp, ctypes.c_longlong, _vp, _int, _int]),
+    "ct_engine_step": (_int, [_vp, _int]),
+    "ct_engine_run": (_int, [_vp]),
+    "ct_engine_poll": (_int, [_vp, _vp, _int, _vp, _int]),
+    "ct_engine_stats": (_int, [_vp, _vp]),
+    "ct_engine_status": (_int, [_vp]),
 }
+
+
+class EngineConfig(ctypes.Structure):
+    _fields_ = [("max_slots", _int), ("max_rows", _int), ("kv_pages", _int), ("precision", _int),
+                ("n_prompt", _int), ("prompt", _vp)]
+
+
+class EngineStats(ctypes.Structure):
+    _fields_ = [("steps", ctypes.c_longlong), ("rows", ctypes.c_longlong), ("tokens", ctypes.c_longlong),
+                ("admitted", ctypes.c_longlong), ("step_ms", ctypes.c_double), ("admit_ms", ctypes.c_double),
+                ("self_attn_ms", ctypes.c_double), ("cross_attn_ms", ctypes.c_double), ("ffn_ms", ctypes.c_double),
+                ("self_kv_bytes", ctypes.c_double), ("cross_kv_bytes", ctypes.c_double),
+                ("ffn_bytes", ctypes.c_double), ("attn_launches", ctypes.c_longlong),
+                ("ffn_launches", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong)]
+
+
+class Result(ctypes.Structure):
+    _fields_ = [("utt_id", ctypes.c_longlong), ("n_tokens", _int), ("status", _int)]
+
+
+class Engine:
+    """Thin owner of a ct_engine* (one per GPU, driven by one thread)."""
+
+    def __init__(self, lib, device, wb, wstruct, max_slots=256, max_rows=1024, precision=1, kv_pages=0):
+        self.lib = lib
+        self.wb = wb            # keeps the host blob alive (the engine copies it at creation)
+        self.ws = wstruct
+        cfg = EngineConfig(max_slots, max_rows, kv_pages, precision, 0, None)
+        h = ctypes.c_void_p()
+        rc = lib.ct_engine_create(ctypes.byref(h), device, wb.ptr(), wb.nbytes, ctypes.addressof(wstruct),
+                                  ctypes.byref(cfg))
+        if rc != 0:
+            raise RuntimeError(f"ct_engine_create failed: {rc}")
+        self.h = h
+
+    def submit(self, utt_id, enc_h, forced_len):
+        a = np.ascontiguousarray(enc_h, dtype=np.float32)
+        rc = self.lib.ct_engine_submit_encoded(self.h, utt_id, a.ctypes.data, a.shape[0], int(forced_len))
+        if rc != 0:
+            raise RuntimeError(f"submit failed: {rc}")
+
+    def step(self, n=1):
+        rc = self.lib.ct_engine_step(self.h, n)
+        if rc < 0:
+            raise RuntimeError(f"step failed: {rc}")
+        return rc
+
+    def run(self):
+        rc = self.lib.ct_engine_run(self.h)
+        if rc < 0:
+            raise RuntimeError(f"run failed: {rc}")
+
+    def poll(self, max_results=4096, tok_stride=1024):
+        res = (Result * max_results)()
+        toks = np.zeros((max_results, tok_stride), np.int32)
+        n = self.lib.ct_engine_poll(self.h, res, max_results, toks.ctypes.data, tok_stride)
+        if n < 0:
+            raise RuntimeError(f"poll failed: {n}")
+        return {res[i].utt_id: toks[i, :res[i].n_tokens].copy() for i in range(n)}
+
+    def stats(self):
+        s = EngineStats()
+        self.lib.ct_engine_stats(self.h, ctypes.byref(s))
+        return {f: getattr(s, f) for f, _ in EngineStats._fields_}
+
+    def status(self):
+        return self.lib.ct_engine_status(self.h)
+
+    def close(self):
+        if self.h:
+            self.lib.ct_engine_destroy(self.h)
+            self.h = None
 
 BACKEND_SYMBOLS = [n for n in SIGNATURES if n.startswith("backend_")]
 

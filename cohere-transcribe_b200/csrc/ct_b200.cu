@@ -3,3 +3,4 @@
 #include "gemm.cu"
 #include "kernels.cu"
 #include "backend_abi.cu"
+#include "engine.cu"

@@ -1,0 +1,897 @@
+// engine.cu -- continuous-batching decode engine (include/ct_engine.h).
+//
+// Device state per engine (one GPU, one host thread):
+//   slot table (SoA): state, current token, filled KV rows, generated count,
+//                     forced length, T_enc, self/cross page tables, output tokens
+//   page pool (bf16): [page][DEC_N][K,V][16 rows][DEC_D]
+//   step buffers sized for max_rows packed query rows
+// One step = build rows (block prefix sum over slots) -> embed+LN ->
+// DEC_N x [LN, QKV GEMM (K/V scattered into pages), paged self-attention,
+// O GEMM + residual, LN, Q GEMM, paged cross-attention, O GEMM + residual,
+// LN, FFN1 (ReLU), FFN2 + residual] -> final LN of each sequence's last row ->
+// LM head GEMM -> argmax -> retire / append on the GPU.  Kernels read the row
+// and sequence counts from device memory, so one captured graph per capacity
+// bucket serves every step.
+#include <algorithm>
+#include <deque>
+#include <string.h>
+#include <vector>
+
+#include "../../include/ct_engine.h"
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+namespace ct {
+namespace eng {
+
+constexpr int D = DEC_D, FF = DEC_FF, H = DEC_H, DK = DEC_DK, NL = DEC_N, V = VOCAB;
+constexpr int PR = kPageRows;
+constexpr int SELF_PAGES = MAX_SEQ / PR;     // 64
+constexpr int CROSS_PAGES = 64;              // T_enc <= 1024
+constexpr long long PAGE_ELEMS = (long long)NL * 2 * PR * D;
+constexpr int PCH = 128;                     // attention keys per chunk
+enum { S_FREE = 0, S_PREFILL = 1, S_DECODE = 2, S_DONE = 3 };
+
+struct DevState {
+    int *state, *tok, *pos, *gen, *forced, *tenc;
+    int *self_pt, *cross_pt;     // [slots][64]
+    int *out_tok;                // [slots][MAX_SEQ]
+    int *prompt;                 // [n_prompt]
+    int *done_map;               // host-mapped [slots]: n_gen when finished (device pointer)
+    // per-step rows
+    int *r_slot, *r_pos, *r_tok;
+    long long *r_off;            // self page offset of each row
+    int *q_row, *q_slot;         // per sequence: last row, slot
+    int *n_rows, *n_seqs;        // device counts
+    int max_slots, max_rows, n_prompt;
+};
+
+// ------------------------------------------------------------ kernels -----
+// Block-wide exclusive scan (blockDim = 1024).
+__device__ int block_excl_scan(int v, int *tmp, int *total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) tmp[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int s = lane < (int)(blockDim.x >> 5) ? tmp[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        tmp[32 + lane] = s;   // inclusive per-warp prefix
+    }
+    __syncthreads();
+    const int warp_base = w > 0 ? tmp[32 + w - 1] : 0;
+    *total = tmp[32 + (blockDim.x >> 5) - 1];
+    return warp_base + x - v;
+}
+
+__global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_cap, int seq_cap) {
+    __shared__ int tmp[64];
+    __shared__ int tmp2[64];
+    const int i = threadIdx.x;
+    const int st = i < s.max_slots ? s.state[i] : S_FREE;
+    int nr = st == S_PREFILL ? s.n_prompt : st == S_DECODE ? 1 : 0;
+    int total = 0, nseq = 0;
+    const int base = block_excl_scan(nr, tmp, &total);
+    __syncthreads();
+    const int sidx = block_excl_scan(nr > 0 ? 1 : 0, tmp2, &nseq);
+    if (total > row_cap || nseq > seq_cap) {   // the host bounds admissions; never expected
+        if (i == 0) { set_status(CT_STATUS_BAD_ARG); *s.n_rows = 0; *s.n_seqs = 0; }
+        return;
+    }
+    for (int j = 0; j < nr; ++j) {
+        const int r = base + j;
+        const int p = st == S_PREFILL ? j : s.pos[i];
+        s.r_slot[r] = i;
+        s.r_pos[r] = p;
+        s.r_tok[r] = st == S_PREFILL ? s.prompt[j] : s.tok[i];
+        const int page = (p >= 0 && p < MAX_SEQ) ? s.self_pt[i * SELF_PAGES + p / PR] : -1;
+        s.r_off[r] = page >= 0 ? (long long)page * PAGE_ELEMS + (long long)(p % PR) * D : -1;
+    }
+    if (nr > 0) { s.q_row[sidx] = base + nr - 1; s.q_slot[sidx] = i; }
+    if (i == 0) { *s.n_rows = total; *s.n_seqs = nseq; }
+}
+
+__device__ __forceinline__ void store_planes(float v, bf16 *hi, bf16 *lo, size_t idx) {
+    const bf16 h = __float2bfloat16_rn(v);
+    hi[idx] = h;
+    if (lo) lo[idx] = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
+__device__ __forceinline__ float block_sum256e(float v, float *red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k];
+    return t;
+}
+
+// h[r] = LN(etw[tok] + epw[pos]) (fp32) and its bf16 planes; rows r < *n.
+__global__ void __launch_bounds__(256) embed_rows_kernel(DevState s, const bf16 *etw, const bf16 *epw,
+                                                         const bf16 *lnw, const bf16 *lnb, float *h, bf16 *hi,
+                                                         bf16 *lo) {
+    __shared__ float row[D];
+    __shared__ float red[8];
+    const int r = blockIdx.x;
+    if (r >= *s.n_rows) return;
+    const int id = s.r_tok[r], p = s.r_pos[r];
+    if (id < 0 || id >= V || p < 0 || p >= MAX_SEQ) { if (threadIdx.x == 0) set_status(CT_STATUS_BAD_ARG); return; }
+    float sum = 0.0f;
+    for (int k = threadIdx.x; k < D; k += 256) {
+        const float v = bf2f(etw[(size_t)id * D + k]) + bf2f(epw[(size_t)p * D + k]);
+        row[k] = v;
+        sum += v;
+    }
+    const float mean = block_sum256e(sum, red) / D;
+    float var = 0.0f;
+    for (int k = threadIdx.x; k < D; k += 256) { const float c = row[k] - mean; var += c * c; }
+    const float inv = 1.0f / sqrtf(block_sum256e(var, red) / D + 1e-5f);
+    for (int k = threadIdx.x; k < D; k += 256) {
+        const float o = (row[k] - mean) * inv * bf2f(lnw[k]) + bf2f(lnb[k]);
+        h[(size_t)r * D + k] = o;
+        store_planes(o, hi, lo, (size_t)r * D + k);
+    }
+}
+
+// planes[r] = LN(h[src(r)]) for r < *n; src(r) = rows ? rows[r] : r.
+__global__ void __launch_bounds__(256) ln_rows_kernel(const int *n, const int *rows, const float *h, const bf16 *w,
+                                                      const bf16 *b, bf16 *hi, bf16 *lo) {
+    __shared__ float red[8];
+    const int r = blockIdx.x;
+    if (r >= *n) return;
+    const float *x = h + (size_t)(rows ? rows[r] : r) * D;
+    float v[D / 256];
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < D / 256; ++j) { v[j] = x[threadIdx.x + 256 * j]; sum += v[j]; }
+    const float mean = block_sum256e(sum, red) / D;
+    float var = 0.0f;
+#pragma unroll
+    for (int j = 0; j < D / 256; ++j) { const float c = v[j] - mean; var += c * c; }
+    const float inv = 1.0f / sqrtf(block_sum256e(var, red) / D + 1e-5f);
+#pragma unroll
+    for (int j = 0; j < D / 256; ++j) {
+        const int k = threadIdx.x + 256 * j;
+        store_planes((v[j] - mean) * inv * bf2f(w[k]) + bf2f(b[k]), hi, lo, (size_t)r * D + k);
+    }
+}
+
+// Paged attention over bf16 K/V.  Row r of slot s = r_slot[r]: self mode
+// attends to rows [0, r_pos[r]] of the slot's self pages (causal prefix; a
+// decode row is its last position), cross mode to rows [0, T_enc[s]).
+// Split-KV with 128-key chunks; single-chunk rows write the output planes
+// directly, others leave (m, l, o) partials for attn_paged_combine.
+__global__ void __launch_bounds__(PCH) attn_paged_kernel(DevState s, const float *Q, const bf16 *pool, int layer,
+                                                         int cross, bf16 *hi, bf16 *lo, float *ws, int nck_max) {
+    __shared__ __align__(16) float qs[DK];
+    __shared__ float ps[PCH];
+    __shared__ float red[4];
+    __shared__ float ored[4][DK];
+    const int r = blockIdx.z, hh = blockIdx.y, c = blockIdx.x;
+    if (r >= *s.n_rows) return;
+    const int slot = s.r_slot[r];
+    const int L = cross ? s.tenc[slot] : s.r_pos[r] + 1;
+    const int nck = (L + PCH - 1) / PCH;
+    if (c >= nck) return;
+    if (nck > nck_max) { if (threadIdx.x == 0) set_status(CT_STATUS_BAD_ARG); return; }
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int *pt = (cross ? s.cross_pt : s.self_pt) + slot * (cross ? CROSS_PAGES : SELF_PAGES);
+    qs[tid] = Q[(size_t)r * D + hh * DK + tid];   // DK == PCH == 128
+    __syncthreads();
+    const float scale = 1.0f / sqrtf((float)DK);
+    const int k = c * PCH + tid;
+    float sc = -INFINITY;
+    if (k < L && pt[k / PR] < 0) { set_status(CT_STATUS_BAD_ARG); return; }
+    if (k < L) {
+        const int page = pt[k / PR];
+        const bf16 *kr = pool + (long long)page * PAGE_ELEMS + (long long)(layer * 2 + 0) * PR * D +
+                         (long long)(k % PR) * D + hh * DK;
+        const uint4 *kp = reinterpret_cast<const uint4 *>(kr);
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int i = 0; i < DK / 8; ++i) {
+            const uint4 u = kp[i];
+            const bf16 *e = reinterpret_cast<const bf16 *>(&u);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc += qs[i * 8 + j] * __bfloat162float(e[j]);
+        }
+        sc = acc * scale;
+    }
+    float m = warp_max(sc);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float p = k < L ? expf(sc - m) : 0.0f;
+    ps[tid] = p;
+    float l = warp_sum(p);
+    __syncthreads();
+    if (lane == 0) red[warp] = l;
+    __syncthreads();
+    l = red[0] + red[1] + red[2] + red[3];
+    // o[d] over this warp's 32 keys; lane owns dims 4*lane .. 4*lane+3
+    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+    const int kw0 = c * PCH + warp * 32;
+    const int kn = min(32, L - kw0);
+    for (int kk = 0; kk < kn; ++kk) {
+        const int key = kw0 + kk;
+        const int page = max(pt[key / PR], 0);   // unallocated pages were reported above
+        const bf16 *vr = pool + (long long)page * PAGE_ELEMS + (long long)(layer * 2 + 1) * PR * D +
+                         (long long)(key % PR) * D + hh * DK + 4 * lane;
+        const uint2 u = *reinterpret_cast<const uint2 *>(vr);
+        const bf16 *e = reinterpret_cast<const bf16 *>(&u);
+        const float pk = ps[warp * 32 + kk];
+        o0 += pk * __bfloat162float(e[0]);
+        o1 += pk * __bfloat162float(e[1]);
+        o2 += pk * __bfloat162float(e[2]);
+        o3 += pk * __bfloat162float(e[3]);
+    }
+    ored[warp][4 * lane + 0] = o0;
+    ored[warp][4 * lane + 1] = o1;
+    ored[warp][4 * lane + 2] = o2;
+    ored[warp][4 * lane + 3] = o3;
+    __syncthreads();
+    const float od = ored[0][tid] + ored[1][tid] + ored[2][tid] + ored[3][tid];
+    if (nck == 1) {
+        store_planes(od / l, hi, lo, (size_t)r * D + hh * DK + tid);
+    } else {
+        float *w = ws + (((size_t)r * H + hh) * nck_max + c) * (DK + 2);
+        if (tid == 0) { w[0] = m; w[1] = l; }
+        w[2 + tid] = od;
+    }
+}
+
+__global__ void __launch_bounds__(DK) attn_paged_combine(DevState s, int cross, bf16 *hi, bf16 *lo, const float *ws,
+                                                         int nck_max) {
+    const int r = blockIdx.x, hh = blockIdx.y;
+    if (r >= *s.n_rows) return;
+    const int L = cross ? s.tenc[s.r_slot[r]] : s.r_pos[r] + 1;
+    const int nck = (L + PCH - 1) / PCH;
+    if (nck <= 1 || nck > nck_max) return;
+    const float *w = ws + ((size_t)r * H + hh) * nck_max * (DK + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nck; ++c) M = fmaxf(M, w[(size_t)c * (DK + 2)]);
+    float Ls = 0.0f, o = 0.0f;
+    for (int c = 0; c < nck; ++c) {
+        const float f = expf(w[(size_t)c * (DK + 2)] - M);
+        Ls += w[(size_t)c * (DK + 2) + 1] * f;
+        o += w[(size_t)c * (DK + 2) + 2 + threadIdx.x] * f;
+    }
+    store_planes(o / Ls, hi, lo, (size_t)r * D + hh * DK + threadIdx.x);
+}
+
+// next[q] = argmax over the vocabulary of sequence q's logits (first max).
+__global__ void __launch_bounds__(256) argmax_seq_kernel(DevState s, const float *logits, int *next) {
+    __shared__ float bv[256];
+    __shared__ int bi[256];
+    const int q = blockIdx.x;
+    if (q >= *s.n_seqs) return;
+    const float *x = logits + (size_t)q * V;
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += 256) {
+        const float v = x[i];
+        if (v > best) { best = v; idx = i; }
+    }
+    bv[threadIdx.x] = best;
+    bi[threadIdx.x] = idx;
+    __syncthreads();
+    for (int st = 128; st > 0; st >>= 1) {
+        if (threadIdx.x < st) {
+            const float ov = bv[threadIdx.x + st];
+            const int oi = bi[threadIdx.x + st];
+            if (ov > bv[threadIdx.x] || (ov == bv[threadIdx.x] && oi < bi[threadIdx.x])) {
+                bv[threadIdx.x] = ov;
+                bi[threadIdx.x] = oi;
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) next[q] = bi[0] == 0x7fffffff ? 0 : bi[0];
+}
+
+// Append the step's token to every live sequence, advance its KV length and
+// retire it on forced length / EOS / MAX_SEQ (transcribe.c:771-794).
+__global__ void update_kernel(DevState s, const int *next) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= *s.n_seqs) return;
+    const int slot = s.q_slot[q];
+    const int st = s.state[slot];
+    int tok = next[q];
+    const int gen = s.gen[slot] + 1;
+    const int forced = s.forced[slot];
+    if (forced > 0 && gen >= forced) tok = CT_TOK_EOS;
+    if (gen - 1 < MAX_SEQ) s.out_tok[(size_t)slot * MAX_SEQ + gen - 1] = tok;
+    s.gen[slot] = gen;
+    s.pos[slot] += st == S_PREFILL ? s.n_prompt : 1;
+    s.tok[slot] = tok;
+    const bool done = (forced > 0 ? gen >= forced : tok == CT_TOK_EOS) || s.n_prompt + gen >= MAX_SEQ;
+    if (done) {
+        s.state[slot] = S_DONE;
+        volatile int *dm = s.done_map;
+        dm[slot] = gen;
+        __threadfence_system();
+    } else {
+        s.state[slot] = S_DECODE;
+    }
+}
+
+// ------------------------------------------------------------ host --------
+struct Pending {
+    long long id;
+    std::vector<float> enc;
+    int T_enc, forced;
+};
+
+struct Bucket {
+    int rows = 0;
+    int kernels = 0;   // kernel nodes in the captured step graph
+    cudaGraphExec_t exec = nullptr;
+    cudaGraph_t graph = nullptr;
+};
+
+}  // namespace eng
+}  // namespace ct
+
+using namespace ct;
+using namespace ct::eng;
+
+struct ct_engine {
+    int device = -1;
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    ct_engine_config cfg;
+    std::vector<int> prompt;
+    // weights
+    void *blob = nullptr;
+    size_t blob_bytes = 0;
+    const uint8_t *host_base = nullptr;
+    const bf16 *etw, *epw, *elnw, *elnb, *dlnw, *dlnb, *hdb;
+    struct Layer {
+        const bf16 *sa_lnw, *sa_lnb, *sa_ow, *sa_ob, *ca_lnw, *ca_lnb, *ca_qw, *ca_qb, *ca_ow, *ca_ob;
+        const bf16 *ffn_lnw, *ffn_lnb, *ffn_w1, *ffn_b1, *ffn_w2, *ffn_b2;
+        bf16 *qkv_w, *qkv_b;
+    } L[NL];
+    bf16 *cakv_w = nullptr, *cakv_b = nullptr;
+    // pool
+    bf16 *pool = nullptr;
+    int n_pages = 0;
+    std::vector<int> free_pages;
+    // device state
+    DevState ds;
+    int *h_done = nullptr;   // host view of done_map
+    // step buffers
+    float *h = nullptr, *q = nullptr, *attn_ws = nullptr, *logits = nullptr;
+    bf16 *xa[2], *xb[2], *xm[2], *lm[2];
+    int *next = nullptr;
+    size_t attn_ws_floats = 0;
+    // admission staging
+    float *enc_dev = nullptr;
+    bf16 *enc_pl[2];
+    long long *enc_off = nullptr;
+    int enc_rows_cap = 0;
+    float *enc_stage = nullptr;      // pinned
+    long long *off_stage = nullptr;  // pinned
+    int *slot_stage = nullptr;       // pinned slot records
+    // host slot bookkeeping
+    std::vector<int> slot_live;      // 0 free, 1 live
+    std::vector<int> slot_first;     // 1 until its first (prefill) step has been launched
+    std::vector<long long> slot_id;
+    std::vector<std::vector<int>> slot_pages;
+    std::deque<Pending> pending;
+    std::deque<ct_result> results;
+    std::deque<std::vector<int>> result_tokens;
+    std::vector<Bucket> buckets;
+    long long n_steps = 0, n_rows = 0, n_tokens = 0;
+    double step_ms = 0.0;
+    int n_live = 0;
+    ct_engine_stats_t st_acc;
+    cudaEvent_t pev[NL][6];          // captured around self-attn, cross-attn, FFN of every layer
+    cudaEvent_t aev0 = nullptr, aev1 = nullptr;
+    std::vector<int> slot_steps;     // steps run since admission (host mirror of the KV length)
+    std::vector<int> slot_tenc;
+    float *gws = nullptr;            // split-K workspace owned by this engine
+    size_t gws_bytes = 0;
+    std::vector<void *> owned;       // aligned copies of misaligned weights
+};
+
+#define EK(x)                                                                                     \
+    do {                                                                                          \
+        cudaError_t e_ = (x);                                                                     \
+        if (e_ != cudaSuccess) {                                                                  \
+            fprintf(stderr, "ct_engine: %s: %s\n", #x, cudaGetErrorString(e_));                   \
+            return CT_EDEVICE;                                                                    \
+        }                                                                                         \
+    } while (0)
+
+static const bf16 *ew(ct_engine *e, const uint16_t *hp) {
+    if (!hp) return nullptr;
+    const uint8_t *p = reinterpret_cast<const uint8_t *>(hp);
+    if (p < e->host_base || p >= e->host_base + e->blob_bytes) return nullptr;
+    return reinterpret_cast<const bf16 *>(static_cast<uint8_t *>(e->blob) + (p - e->host_base));
+}
+
+// A weight matrix used as a TMA operand must start on a 16-byte boundary;
+// tensors of a safetensors file need not, so those get an aligned copy.
+static const bf16 *ew_matrix(ct_engine *e, const uint16_t *hp, size_t elems) {
+    const bf16 *d = ew(e, hp);
+    if (!d || ((uintptr_t)d & 15) == 0) return d;
+    bf16 *c = nullptr;
+    if (cudaMalloc(&c, elems * sizeof(bf16)) != cudaSuccess) return nullptr;
+    e->owned.push_back(c);
+    if (cudaMemcpy(c, d, elems * sizeof(bf16), cudaMemcpyDeviceToDevice) != cudaSuccess) return nullptr;
+    return c;
+}
+
+static bool two_planes(const ct_engine *e) { return e->cfg.precision != 0; }
+
+// GEMM on the engine's stream with the engine's own split-K workspace and
+// buffer-capacity tensor maps (so captured graphs never refer to another
+// owner's scratch).
+static void egemm(ct_engine *e, const bf16 *W, int N, int K, const bf16 *xh, const bf16 *xl, int T, long x_rows,
+                  GemmEpilogue ep, bool split) {
+    ep.ws = e->gws;
+    ep.ws_bytes = e->gws_bytes;
+    ep.x_rows = x_rows;
+    gemm_bf16(e->st, W, N, K, xh, xl, T, ep, split);
+}
+
+// Encode one step for capacity `rows` (seqs capacity = min(rows, max_slots)) on e->st.
+static void encode_step(ct_engine *e, int rows) {
+    const int seqs = std::min(rows, e->cfg.max_slots);
+    DevState s = e->ds;
+    cudaStream_t st = e->st;
+    const bool two = two_planes(e);
+    bf16 *xa_lo = two ? e->xa[1] : nullptr, *xb_lo = two ? e->xb[1] : nullptr, *xm_lo = two ? e->xm[1] : nullptr;
+    bf16 *lm_lo = two ? e->lm[1] : nullptr;
+    build_rows_kernel<<<1, 1024, 0, st>>>(s, rows, seqs);
+    embed_rows_kernel<<<rows, 256, 0, st>>>(s, e->etw, e->epw, e->elnw, e->elnb, e->h, e->xa[0], xa_lo);
+    const int nck = (MAX_SEQ + PCH - 1) / PCH;
+    for (int l = 0; l < NL; ++l) {
+        const auto &Ly = e->L[l];
+        ln_rows_kernel<<<rows, 256, 0, st>>>(s.n_rows, nullptr, e->h, Ly.sa_lnw, Ly.sa_lnb, e->xa[0], xa_lo);
+        GemmEpilogue qkv;
+        qkv.epi = EPI_QKV_PAGED; qkv.bias = Ly.qkv_b; qkv.Y = e->q; qkv.ldy = D; qkv.qdim = D;
+        qkv.kv_pool = e->pool; qkv.row_off = s.r_off; qkv.layer = l; qkv.T_dev = s.n_rows;
+        egemm(e, Ly.qkv_w, 3 * D, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, qkv, true);
+        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][0], st, cudaEventRecordExternal));
+        attn_paged_kernel<<<dim3(nck, H, rows), PCH, 0, st>>>(s, e->q, e->pool, l, 0, e->xb[0], xb_lo, e->attn_ws, nck);
+        attn_paged_combine<<<dim3(rows, H), DK, 0, st>>>(s, 0, e->xb[0], xb_lo, e->attn_ws, nck);
+        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][1], st, cudaEventRecordExternal));
+        GemmEpilogue o;
+        o.epi = EPI_FMADD; o.scale = 1.0f; o.bias = Ly.sa_ob; o.Y = e->h; o.ldy = D; o.T_dev = s.n_rows;
+        egemm(e, Ly.sa_ow, D, D, e->xb[0], xb_lo, rows, e->cfg.max_rows, o, true);
+        ln_rows_kernel<<<rows, 256, 0, st>>>(s.n_rows, nullptr, e->h, Ly.ca_lnw, Ly.ca_lnb, e->xa[0], xa_lo);
+        GemmEpilogue qc;
+        qc.bias = Ly.ca_qb; qc.Y = e->q; qc.ldy = D; qc.T_dev = s.n_rows;
+        egemm(e, Ly.ca_qw, D, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, qc, true);
+        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][2], st, cudaEventRecordExternal));
+        attn_paged_kernel<<<dim3(CROSS_PAGES * PR / PCH, H, rows), PCH, 0, st>>>(s, e->q, e->pool, l, 1, e->xb[0],
+                                                                                 xb_lo, e->attn_ws, nck);
+        attn_paged_combine<<<dim3(rows, H), DK, 0, st>>>(s, 1, e->xb[0], xb_lo, e->attn_ws, nck);
+        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][3], st, cudaEventRecordExternal));
+        GemmEpilogue oc = o;
+        oc.bias = Ly.ca_ob;
+        egemm(e, Ly.ca_ow, D, D, e->xb[0], xb_lo, rows, e->cfg.max_rows, oc, true);
+        ln_rows_kernel<<<rows, 256, 0, st>>>(s.n_rows, nullptr, e->h, Ly.ffn_lnw, Ly.ffn_lnb, e->xa[0], xa_lo);
+        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][4], st, cudaEventRecordExternal));
+        GemmEpilogue f1;
+        f1.epi = EPI_BF16; f1.act = 2; f1.bias = Ly.ffn_b1; f1.Ybf = e->xm[0]; f1.Ybf_lo = xm_lo; f1.ldy = FF;
+        f1.T_dev = s.n_rows;
+        egemm(e, Ly.ffn_w1, FF, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, f1, true);
+        GemmEpilogue f2 = o;
+        f2.bias = Ly.ffn_b2;
+        egemm(e, Ly.ffn_w2, D, FF, e->xm[0], xm_lo, rows, e->cfg.max_rows, f2, true);
+        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][5], st, cudaEventRecordExternal));
+    }
+    ln_rows_kernel<<<seqs, 256, 0, st>>>(s.n_seqs, s.q_row, e->h, e->dlnw, e->dlnb, e->lm[0], lm_lo);
+    GemmEpilogue lh;
+    lh.bias = e->hdb; lh.Y = e->logits; lh.ldy = V; lh.T_dev = s.n_seqs;
+    egemm(e, e->etw, V, D, e->lm[0], lm_lo, seqs, e->cfg.max_slots, lh, true);
+    argmax_seq_kernel<<<seqs, 256, 0, st>>>(s, e->logits, e->next);
+    update_kernel<<<(seqs + 255) / 256, 256, 0, st>>>(s, e->next);
+}
+
+static Bucket *bucket_for(ct_engine *e, int rows_needed) {
+    int cap = 32;
+    while (cap < rows_needed) cap *= 2;
+    cap = std::min(cap, e->cfg.max_rows);
+    for (auto &b : e->buckets)
+        if (b.rows == cap) return &b;
+    Bucket b;
+    b.rows = cap;
+    CT_CHECK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeRelaxed));
+    encode_step(e, cap);
+    CT_CHECK(cudaStreamEndCapture(e->st, &b.graph));
+    CT_CHECK(cudaGraphInstantiate(&b.exec, b.graph, 0));
+    size_t nn = 0;
+    CT_CHECK(cudaGraphGetNodes(b.graph, nullptr, &nn));
+    std::vector<cudaGraphNode_t> nodes(nn);
+    CT_CHECK(cudaGraphGetNodes(b.graph, nodes.data(), &nn));
+    for (auto nd : nodes) {
+        cudaGraphNodeType ty;
+        CT_CHECK(cudaGraphNodeGetType(nd, &ty));
+        if (ty == cudaGraphNodeTypeKernel) ++b.kernels;
+    }
+    e->buckets.push_back(b);
+    return &e->buckets.back();
+}
+
+// Host mirror of the device slot record written at admission.
+enum { REC_STATE, REC_TOK, REC_POS, REC_GEN, REC_FORCED, REC_TENC, REC_N };
+
+static int admit(ct_engine *e) {
+    // pick admissions: free slot, pages, rows budget, encoder-row staging budget
+    int live_rows = 0;
+    for (int i = 0; i < e->cfg.max_slots; ++i) live_rows += e->slot_live[i] ? 1 : 0;
+    std::vector<int> slots;
+    std::vector<Pending> adm;
+    int enc_rows = 0;
+    while (!e->pending.empty()) {
+        Pending &p = e->pending.front();
+        if (enc_rows + p.T_enc > e->enc_rows_cap) break;
+        if (live_rows + e->cfg.n_prompt > e->cfg.max_rows) break;
+        const int gen_max = p.forced > 0 ? p.forced : MAX_SEQ - e->cfg.n_prompt;
+        const int self_need = (std::min(MAX_SEQ, e->cfg.n_prompt + gen_max) + PR - 1) / PR;
+        const int cross_need = (p.T_enc + PR - 1) / PR;
+        if ((int)e->free_pages.size() < self_need + cross_need) break;
+        int slot = -1;
+        for (int i = 0; i < e->cfg.max_slots; ++i)
+            if (!e->slot_live[i]) { slot = i; break; }
+        if (slot < 0) break;
+        std::vector<int> pages(e->free_pages.end() - (self_need + cross_need), e->free_pages.end());
+        e->free_pages.resize(e->free_pages.size() - (self_need + cross_need));
+        e->slot_live[slot] = 1;
+        e->slot_first[slot] = 1;
+        e->slot_id[slot] = p.id;
+        e->slot_pages[slot] = pages;
+        e->slot_steps[slot] = 0;
+        e->slot_tenc[slot] = p.T_enc;
+        ++e->st_acc.admitted;
+        // slot record + page tables
+        int *rec = e->slot_stage;
+        rec[REC_STATE] = S_PREFILL; rec[REC_TOK] = 0; rec[REC_POS] = 0; rec[REC_GEN] = 0;
+        rec[REC_FORCED] = p.forced; rec[REC_TENC] = p.T_enc;
+        int *spt = rec + REC_N, *cpt = spt + SELF_PAGES;
+        for (int j = 0; j < SELF_PAGES; ++j) spt[j] = j < self_need ? pages[j] : -1;
+        for (int j = 0; j < CROSS_PAGES; ++j) cpt[j] = j < cross_need ? pages[self_need + j] : -1;
+        int *const fields[REC_N] = {e->ds.state, e->ds.tok, e->ds.pos, e->ds.gen, e->ds.forced, e->ds.tenc};
+        for (int f = 0; f < REC_N; ++f)
+            EK(cudaMemcpyAsync(fields[f] + slot, rec + f, sizeof(int), cudaMemcpyHostToDevice, e->st));
+        EK(cudaMemcpyAsync(e->ds.self_pt + (size_t)slot * SELF_PAGES, spt, sizeof(int) * SELF_PAGES,
+                           cudaMemcpyHostToDevice, e->st));
+        EK(cudaMemcpyAsync(e->ds.cross_pt + (size_t)slot * CROSS_PAGES, cpt, sizeof(int) * CROSS_PAGES,
+                           cudaMemcpyHostToDevice, e->st));
+        // these staging copies must land before the staging area is rewritten
+        EK(cudaStreamSynchronize(e->st));
+        // encoder rows of this utterance -> staging, with their cross page offsets
+        memcpy(e->enc_stage + (size_t)enc_rows * D, p.enc.data(), sizeof(float) * (size_t)p.T_enc * D);
+        for (int t = 0; t < p.T_enc; ++t)
+            e->off_stage[enc_rows + t] = (long long)pages[self_need + t / PR] * PAGE_ELEMS + (long long)(t % PR) * D;
+        enc_rows += p.T_enc;
+        live_rows += e->cfg.n_prompt;
+        ++e->n_live;
+        e->pending.pop_front();
+    }
+    if (enc_rows == 0) return 0;
+    // cross-attention K/V of all admitted utterances: one GEMM into their pages
+    EK(cudaMemcpyAsync(e->enc_dev, e->enc_stage, sizeof(float) * (size_t)enc_rows * D, cudaMemcpyHostToDevice, e->st));
+    EK(cudaMemcpyAsync(e->enc_off, e->off_stage, sizeof(long long) * enc_rows, cudaMemcpyHostToDevice, e->st));
+    EK(cudaEventRecord(e->aev0, e->st));
+    const bool two = two_planes(e);
+    split_fp32_to_bf16(e->st, e->enc_dev, enc_rows, D, D, e->enc_pl[0], two ? e->enc_pl[1] : nullptr, D);
+    GemmEpilogue ep;
+    ep.epi = EPI_CAKV_PAGED; ep.bias = e->cakv_b; ep.kv_pool = e->pool; ep.row_off = e->enc_off;
+    egemm(e, e->cakv_w, NL * 2 * D, D, e->enc_pl[0], two ? e->enc_pl[1] : nullptr, enc_rows, e->enc_rows_cap, ep, false);
+    EK(cudaEventRecord(e->aev1, e->st));
+    EK(cudaStreamSynchronize(e->st));   // staging reuse
+    float ams = 0.0f;
+    EK(cudaEventElapsedTime(&ams, e->aev0, e->aev1));
+    e->st_acc.admit_ms += ams;
+    e->st_acc.kernel_launches += 2;   // plane split + cross K/V GEMM
+    return 0;
+}
+
+static int harvest(ct_engine *e) {
+    for (int i = 0; i < e->cfg.max_slots; ++i) {
+        if (!e->slot_live[i]) continue;
+        const int ng = ((volatile int *)e->h_done)[i];
+        if (ng <= 0) continue;
+        std::vector<int> toks(ng);
+        EK(cudaMemcpyAsync(toks.data(), e->ds.out_tok + (size_t)i * MAX_SEQ, sizeof(int) * ng,
+                           cudaMemcpyDeviceToHost, e->st));
+        const int zero = S_FREE;
+        EK(cudaMemcpyAsync(e->ds.state + i, &zero, sizeof(int), cudaMemcpyHostToDevice, e->st));
+        EK(cudaStreamSynchronize(e->st));
+        ((volatile int *)e->h_done)[i] = 0;
+        ct_result r;
+        r.utt_id = e->slot_id[i];
+        r.n_tokens = ng;
+        r.status = 0;
+        e->results.push_back(r);
+        e->result_tokens.push_back(std::move(toks));
+        for (int pg : e->slot_pages[i]) e->free_pages.push_back(pg);
+        e->slot_pages[i].clear();
+        e->slot_live[i] = 0;
+        --e->n_live;
+        e->n_tokens += ng;
+    }
+    return 0;
+}
+
+extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
+    if (!e) return CT_EINVAL;
+    EK(cudaSetDevice(e->device));
+    for (int it = 0; it < n_steps; ++it) {
+        int rc = harvest(e);
+        if (rc) return rc;
+        rc = admit(e);
+        if (rc) return rc;
+        if (e->n_live == 0) {
+            if (!e->pending.empty()) return CT_EBUSY;   // nothing live and nothing admissible
+            break;
+        }
+        int rows = 0;
+        double self_b = 0.0, cross_b = 0.0;
+        const double kv_row = 2.0 * D * sizeof(bf16);   // K + V bytes of one cached row, one layer
+        for (int i = 0; i < e->cfg.max_slots; ++i) {
+            if (!e->slot_live[i]) continue;
+            if (e->slot_first[i]) {
+                rows += e->cfg.n_prompt;
+                for (int p = 0; p < e->cfg.n_prompt; ++p) self_b += (p + 1) * kv_row;
+                cross_b += (double)e->cfg.n_prompt * e->slot_tenc[i] * kv_row;
+            } else {
+                rows += 1;
+                self_b += (double)(e->cfg.n_prompt + e->slot_steps[i]) * kv_row;
+                cross_b += (double)e->slot_tenc[i] * kv_row;
+            }
+        }
+        Bucket *b = bucket_for(e, std::max(rows, 1));
+        EK(cudaEventRecord(e->ev0, e->st));
+        EK(cudaGraphLaunch(b->exec, e->st));
+        EK(cudaEventRecord(e->ev1, e->st));
+        EK(cudaEventSynchronize(e->ev1));
+        float ms = 0.0f;
+        EK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
+        e->step_ms += ms;
+        e->st_acc.kernel_launches += b->kernels;
+        ++e->n_steps;
+        e->n_rows += rows;
+        for (int l = 0; l < NL; ++l) {
+            float a = 0.f, c = 0.f, f = 0.f;
+            EK(cudaEventElapsedTime(&a, e->pev[l][0], e->pev[l][1]));
+            EK(cudaEventElapsedTime(&c, e->pev[l][2], e->pev[l][3]));
+            EK(cudaEventElapsedTime(&f, e->pev[l][4], e->pev[l][5]));
+            e->st_acc.self_attn_ms += a;
+            e->st_acc.cross_attn_ms += c;
+            e->st_acc.ffn_ms += f;
+        }
+        e->st_acc.self_kv_bytes += NL * self_b;
+        e->st_acc.cross_kv_bytes += NL * cross_b;
+        e->st_acc.ffn_bytes += NL * (2.0 * 2.0 * FF * D + (double)rows * (D + FF) * 2.0 * (two_planes(e) ? 2 : 1));
+        e->st_acc.attn_launches += 2 * NL;
+        e->st_acc.ffn_launches += 2 * NL;
+        for (int i = 0; i < e->cfg.max_slots; ++i) {
+            if (e->slot_live[i]) ++e->slot_steps[i];
+            e->slot_first[i] = 0;
+        }
+    }
+    int rc = harvest(e);
+    if (rc) return rc;
+    return (int)e->pending.size() + e->n_live;
+}
+
+extern "C" int ct_engine_run(ct_engine *e) {
+    for (;;) {
+        const int r = ct_engine_step(e, 64);
+        if (r <= 0) return r;
+    }
+}
+
+extern "C" int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const float *enc_h, int T_enc, int forced_len) {
+    if (!e || !enc_h || T_enc <= 0 || T_enc > CROSS_PAGES * PR || forced_len < 0) return CT_EINVAL;
+    if (T_enc > e->enc_rows_cap) return CT_EINVAL;
+    const int gen_max = forced_len > 0 ? forced_len : MAX_SEQ - e->cfg.n_prompt;
+    const int need = (std::min(MAX_SEQ, e->cfg.n_prompt + gen_max) + PR - 1) / PR + (T_enc + PR - 1) / PR;
+    if (need > e->n_pages) return CT_EINVAL;   // could never be admitted
+    Pending p;
+    p.id = utt_id;
+    p.enc.assign(enc_h, enc_h + (size_t)T_enc * D);
+    p.T_enc = T_enc;
+    p.forced = forced_len;
+    e->pending.push_back(std::move(p));
+    return CT_OK;
+}
+
+extern "C" int ct_engine_poll(ct_engine *e, ct_result *out, int max, int *tokens, int tok_stride) {
+    if (!e || (max > 0 && !out)) return CT_EINVAL;
+    int n = 0;
+    while (n < max && !e->results.empty()) {
+        out[n] = e->results.front();
+        if (tokens) {
+            const auto &tk = e->result_tokens.front();
+            memcpy(tokens + (size_t)n * tok_stride, tk.data(), sizeof(int) * std::min<size_t>(tk.size(), tok_stride));
+        }
+        e->results.pop_front();
+        e->result_tokens.pop_front();
+        ++n;
+    }
+    return n;
+}
+
+extern "C" int ct_engine_stats(ct_engine *e, ct_engine_stats_t *out) {
+    if (!e || !out) return CT_EINVAL;
+    *out = e->st_acc;
+    out->steps = e->n_steps;
+    out->rows = e->n_rows;
+    out->tokens = e->n_tokens;
+    out->step_ms = e->step_ms;
+    return CT_OK;
+}
+
+extern "C" int ct_engine_status(ct_engine *e) {
+    if (!e) return CT_EINVAL;
+    EK(cudaSetDevice(e->device));
+    EK(cudaStreamSynchronize(e->st));
+    int v = 0, zero = 0;
+    EK(cudaMemcpyFromSymbol(&v, g_ct_status, sizeof(int)));
+    EK(cudaMemcpyToSymbol(g_ct_status, &zero, sizeof(int)));
+    return v;
+}
+
+extern "C" void ct_engine_destroy(ct_engine *e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    cudaStreamSynchronize(e->st);
+    for (auto &b : e->buckets) { cudaGraphExecDestroy(b.exec); cudaGraphDestroy(b.graph); }
+    void *ptrs[] = {e->blob, e->pool, e->cakv_w, e->cakv_b, e->h, e->q, e->attn_ws, e->logits, e->xa[0], e->xa[1],
+                    e->xb[0], e->xb[1], e->xm[0], e->xm[1], e->lm[0], e->lm[1], e->next, e->enc_dev, e->enc_pl[0],
+                    e->enc_pl[1], e->enc_off, e->ds.state, e->ds.tok, e->ds.pos, e->ds.gen, e->ds.forced,
+                    e->ds.tenc, e->ds.self_pt, e->ds.cross_pt, e->ds.out_tok, e->ds.prompt, e->ds.r_slot,
+                    e->ds.r_pos, e->ds.r_tok, e->ds.r_off, e->ds.q_row, e->ds.q_slot, e->ds.n_rows, e->ds.n_seqs,
+                    e->gws};
+    for (void *p : ptrs) cudaFree(p);
+    for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
+    cudaFreeHost(e->h_done);
+    cudaFreeHost(e->enc_stage);
+    cudaFreeHost(e->off_stage);
+    cudaFreeHost(e->slot_stage);
+    cudaEventDestroy(e->ev0);
+    cudaEventDestroy(e->ev1);
+    cudaEventDestroy(e->aev0);
+    cudaEventDestroy(e->aev1);
+    for (int l = 0; l < NL; ++l)
+        for (int j = 0; j < 6; ++j) cudaEventDestroy(e->pev[l][j]);
+    cudaStreamDestroy(e->st);
+    for (void *p : e->owned) cudaFree(p);
+    delete e;
+}
+
+template <typename T>
+static int dalloc(T **p, size_t n) {
+    if (cudaMalloc(reinterpret_cast<void **>(p), sizeof(T) * (n ? n : 1)) != cudaSuccess) return CT_ENOMEM;
+    return CT_OK;
+}
+
+extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_blob, size_t bytes, const Weights *w,
+                                const ct_engine_config *cfg_in) {
+    if (!out || !host_blob || !w) return CT_EINVAL;
+    *out = nullptr;
+    ct_engine_config cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    if (cfg_in) cfg = *cfg_in;
+    if (cfg.max_slots <= 0) cfg.max_slots = 256;
+    if (cfg.max_rows <= 0) cfg.max_rows = 1024;
+    if (cfg.n_prompt <= 0) cfg.n_prompt = 10;
+    if (cfg.max_slots > 1024 || cfg.n_prompt > 64 || cfg.max_rows < cfg.n_prompt) return CT_EINVAL;
+    static const int kPrompt[10] = {13764, 7, 4, 16, 62, 62, 5, 9, 11, 13};
+    ct_engine *e = new ct_engine();
+    e->cfg = cfg;
+    e->prompt.assign(cfg.prompt ? cfg.prompt : kPrompt, (cfg.prompt ? cfg.prompt : kPrompt) + cfg.n_prompt);
+    if (!cfg.prompt && cfg.n_prompt != 10) { delete e; return CT_EINVAL; }
+    e->device = device;
+    if (cudaSetDevice(device) != cudaSuccess) { delete e; return CT_EDEVICE; }
+    EK(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
+    EK(cudaEventCreate(&e->ev0));
+    EK(cudaEventCreate(&e->ev1));
+    EK(cudaEventCreate(&e->aev0));
+    EK(cudaEventCreate(&e->aev1));
+    for (int l = 0; l < NL; ++l)
+        for (int j = 0; j < 6; ++j) EK(cudaEventCreate(&e->pev[l][j]));
+    memset(&e->st_acc, 0, sizeof(e->st_acc));
+    // weights: one device copy of the blob, then derived concatenations
+    e->host_base = static_cast<const uint8_t *>(host_blob);
+    e->blob_bytes = bytes;
+    if (dalloc((uint8_t **)&e->blob, bytes)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    EK(cudaMemcpy(e->blob, host_blob, bytes, cudaMemcpyHostToDevice));
+    e->etw = ew_matrix(e, w->etw, (size_t)V * D); e->epw = ew(e, w->epw); e->elnw = ew(e, w->elnw); e->elnb = ew(e, w->elnb);
+    e->dlnw = ew(e, w->dlnw); e->dlnb = ew(e, w->dlnb); e->hdb = ew(e, w->hdb);
+    if (!e->etw || !e->epw || !e->elnw || !e->elnb || !e->dlnw || !e->dlnb || !e->hdb) { ct_engine_destroy(e); return CT_EINVAL; }
+    if (dalloc(&e->cakv_w, (size_t)NL * 2 * D * D) || dalloc(&e->cakv_b, (size_t)NL * 2 * D)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    for (int l = 0; l < NL; ++l) {
+        const DLayer &d = w->dec[l];
+        auto &Ly = e->L[l];
+        Ly.sa_lnw = ew(e, d.sa_lnw); Ly.sa_lnb = ew(e, d.sa_lnb); Ly.sa_ob = ew(e, d.sa_ob);
+        Ly.sa_ow = ew_matrix(e, d.sa_ow, (size_t)D * D);
+        Ly.ca_lnw = ew(e, d.ca_lnw); Ly.ca_lnb = ew(e, d.ca_lnb); Ly.ca_qb = ew(e, d.ca_qb);
+        Ly.ca_qw = ew_matrix(e, d.ca_qw, (size_t)D * D);
+        Ly.ca_ow = ew_matrix(e, d.ca_ow, (size_t)D * D); Ly.ca_ob = ew(e, d.ca_ob);
+        Ly.ffn_lnw = ew(e, d.ffn_lnw); Ly.ffn_lnb = ew(e, d.ffn_lnb);
+        Ly.ffn_w1 = ew_matrix(e, d.ffn_w1, (size_t)FF * D);
+        Ly.ffn_b1 = ew(e, d.ffn_b1); Ly.ffn_w2 = ew_matrix(e, d.ffn_w2, (size_t)D * FF); Ly.ffn_b2 = ew(e, d.ffn_b2);
+        const bf16 *parts[3] = {ew(e, d.sa_qw), ew(e, d.sa_kw), ew(e, d.sa_vw)};
+        const bf16 *bparts[3] = {ew(e, d.sa_qb), ew(e, d.sa_kb), ew(e, d.sa_vb)};
+        if (dalloc(&Ly.qkv_w, (size_t)3 * D * D) || dalloc(&Ly.qkv_b, (size_t)3 * D)) { ct_engine_destroy(e); return CT_ENOMEM; }
+        for (int j = 0; j < 3; ++j) {
+            if (!parts[j] || !bparts[j]) { ct_engine_destroy(e); return CT_EINVAL; }
+            EK(cudaMemcpy(Ly.qkv_w + (size_t)j * D * D, parts[j], sizeof(bf16) * D * D, cudaMemcpyDeviceToDevice));
+            EK(cudaMemcpy(Ly.qkv_b + (size_t)j * D, bparts[j], sizeof(bf16) * D, cudaMemcpyDeviceToDevice));
+        }
+        const bf16 *ck = ew(e, d.ca_kw), *cv = ew(e, d.ca_vw), *ckb = ew(e, d.ca_kb), *cvb = ew(e, d.ca_vb);
+        if (!ck || !cv || !ckb || !cvb || !Ly.sa_ow || !Ly.ca_qw || !Ly.ffn_w1 || !Ly.ffn_w2) { ct_engine_destroy(e); return CT_EINVAL; }
+        EK(cudaMemcpy(e->cakv_w + (size_t)(2 * l) * D * D, ck, sizeof(bf16) * D * D, cudaMemcpyDeviceToDevice));
+        EK(cudaMemcpy(e->cakv_w + (size_t)(2 * l + 1) * D * D, cv, sizeof(bf16) * D * D, cudaMemcpyDeviceToDevice));
+        EK(cudaMemcpy(e->cakv_b + (size_t)(2 * l) * D, ckb, sizeof(bf16) * D, cudaMemcpyDeviceToDevice));
+        EK(cudaMemcpy(e->cakv_b + (size_t)(2 * l + 1) * D, cvb, sizeof(bf16) * D, cudaMemcpyDeviceToDevice));
+    }
+    // page pool
+    const int S = cfg.max_slots, R = cfg.max_rows;
+    e->n_pages = cfg.kv_pages > 0 ? cfg.kv_pages : S * (SELF_PAGES + 24);
+    if (dalloc(&e->pool, (size_t)e->n_pages * PAGE_ELEMS)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    for (int i = e->n_pages - 1; i >= 0; --i) e->free_pages.push_back(i);
+    // device slot table
+    DevState &s = e->ds;
+    s.max_slots = S; s.max_rows = R; s.n_prompt = cfg.n_prompt;
+    if (dalloc(&s.state, S) || dalloc(&s.tok, S) || dalloc(&s.pos, S) || dalloc(&s.gen, S) || dalloc(&s.forced, S) ||
+        dalloc(&s.tenc, S) || dalloc(&s.self_pt, (size_t)S * SELF_PAGES) || dalloc(&s.cross_pt, (size_t)S * CROSS_PAGES) ||
+        dalloc(&s.out_tok, (size_t)S * MAX_SEQ) || dalloc(&s.prompt, cfg.n_prompt) || dalloc(&s.r_slot, R) ||
+        dalloc(&s.r_pos, R) || dalloc(&s.r_tok, R) || dalloc(&s.r_off, R) || dalloc(&s.q_row, S) ||
+        dalloc(&s.q_slot, S) || dalloc(&s.n_rows, 1) || dalloc(&s.n_seqs, 1)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    EK(cudaMemset(s.state, 0, sizeof(int) * S));
+    EK(cudaMemset(s.n_rows, 0, sizeof(int)));
+    EK(cudaMemset(s.n_seqs, 0, sizeof(int)));
+    EK(cudaMemcpy(s.prompt, e->prompt.data(), sizeof(int) * cfg.n_prompt, cudaMemcpyHostToDevice));
+    EK(cudaHostAlloc(&e->h_done, sizeof(int) * S, cudaHostAllocMapped));
+    memset(e->h_done, 0, sizeof(int) * S);
+    EK(cudaHostGetDevicePointer(&s.done_map, e->h_done, 0));
+    // step buffers
+    if (dalloc(&e->h, (size_t)R * D) || dalloc(&e->q, (size_t)R * D) || dalloc(&e->xa[0], (size_t)R * D) ||
+        dalloc(&e->xa[1], (size_t)R * D) || dalloc(&e->xb[0], (size_t)R * D) || dalloc(&e->xb[1], (size_t)R * D) ||
+        dalloc(&e->xm[0], (size_t)R * FF) || dalloc(&e->xm[1], (size_t)R * FF) || dalloc(&e->lm[0], (size_t)S * D) ||
+        dalloc(&e->lm[1], (size_t)S * D) || dalloc(&e->logits, (size_t)S * V) || dalloc(&e->next, S)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    e->attn_ws_floats = (size_t)R * H * ((MAX_SEQ + PCH - 1) / PCH) * (DK + 2);
+    if (dalloc(&e->attn_ws, e->attn_ws_floats)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    // admission staging: up to 64 utterances of 30 s worth of encoder rows
+    e->enc_rows_cap = 64 * 400;
+    if (dalloc(&e->enc_dev, (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_pl[0], (size_t)e->enc_rows_cap * D) ||
+        dalloc(&e->enc_pl[1], (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_off, e->enc_rows_cap)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    EK(cudaHostAlloc(&e->enc_stage, sizeof(float) * (size_t)e->enc_rows_cap * D, cudaHostAllocDefault));
+    EK(cudaHostAlloc(&e->off_stage, sizeof(long long) * e->enc_rows_cap, cudaHostAllocDefault));
+    EK(cudaHostAlloc(&e->slot_stage, sizeof(int) * (REC_N + SELF_PAGES + CROSS_PAGES), cudaHostAllocDefault));
+    e->slot_live.assign(S, 0);
+    e->slot_first.assign(S, 0);
+    e->slot_id.assign(S, -1);
+    e->slot_pages.assign(S, {});
+    e->slot_steps.assign(S, 0);
+    e->slot_tenc.assign(S, 0);
+    // split-K workspace for the largest step (nsplit * rows * N floats)
+    size_t ws = 0;
+    const int shapes[4][2] = {{3 * D, D}, {D, D}, {FF, D}, {D, FF}};
+    for (auto &sh : shapes) ws = std::max(ws, (size_t)split_factor(sh[0], sh[1]) * R * sh[0] * sizeof(float));
+    e->gws_bytes = ws;
+    if (dalloc((uint8_t **)&e->gws, ws)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    EK(cudaDeviceSynchronize());
+    *out = e;
+    return CT_OK;
+}

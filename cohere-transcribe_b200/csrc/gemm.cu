@@ -362,18 +362,20 @@ void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, c
     const bool two = X_lo != nullptr;
     int BN = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : (two ? 128 : 256);
     const int kb_total = (K + BK - 1) / BK;
+    float *ws = ep.ws ? ep.ws : c->ws;
+    const size_t ws_bytes = ep.ws ? ep.ws_bytes : c->ws_bytes;
     int nsplit = allow_split ? split_factor(N, K) : 1;
-    if (nsplit > 1 && (size_t)nsplit * T * N * sizeof(float) > c->ws_bytes) nsplit = 1;
+    if (nsplit > 1 && (size_t)nsplit * T * N * sizeof(float) > ws_bytes) nsplit = 1;
     const int kbps = (kb_total + nsplit - 1) / nsplit;
     nsplit = (kb_total + kbps - 1) / kbps;   // every split gets >= 1 block
     // X maps use the scratch capacity (or T) as the row count; rows >= T are never stored
-    const long xrows = (X_hi == c->xhi || X_hi == c->xlo) ? (long)(c->x_elems / K) : (long)T;
+    const long xrows = (X_hi == c->xhi || X_hi == c->xlo) ? (long)(c->x_elems / K) : (ep.x_rows > 0 ? ep.x_rows : (long)T);
     const CUtensorMap &mw = tmap_bf16(c, W, N, K, BM);
     const CUtensorMap &mh = tmap_bf16(c, X_hi, xrows, K, BN);
     const CUtensorMap &ml = two ? tmap_bf16(c, X_lo, xrows, K, BN) : mh;
     KernelParams p;
     p.N = N; p.K = K; p.T = T; p.kbps = kbps; p.kb_total = kb_total; p.stages = 1;
-    p.ws = nsplit > 1 ? c->ws : nullptr;
+    p.ws = nsplit > 1 ? ws : nullptr;
     p.ep = ep;
 #define CT_LAUNCH(bn)                                                                            \
     (two ? launch_tc<bn, true>(st, mw, mh, ml, p, nsplit) : launch_tc<bn, false>(st, mw, mh, ml, p, nsplit))
@@ -388,7 +390,7 @@ void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, c
         const size_t TN = (size_t)T * N;
         int blocks = (int)((TN + 255) / 256);
         if (blocks > 148 * 8) blocks = 148 * 8;
-        splitk_reduce_kernel<<<blocks, 256, 0, st>>>(c->ws, nsplit, T, N, ep);
+        splitk_reduce_kernel<<<blocks, 256, 0, st>>>(ws, nsplit, T, N, ep);
         CT_CHECK(cudaGetLastError());
     }
 }

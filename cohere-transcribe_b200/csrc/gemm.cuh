@@ -47,6 +47,9 @@ struct GemmEpilogue {
     int qdim = 0;
     int kv_width = 1024;          // K/V row width in the pool
     const int *T_dev = nullptr;   // optional device row count (rows >= *T_dev are skipped)
+    float *ws = nullptr;          // optional caller-owned split-K workspace (else the thread's)
+    size_t ws_bytes = 0;
+    long x_rows = 0;              // rows of the X buffers (tensor-map extent); 0 = T
 };
 
 // Per-thread GEMM context: stream, workspaces, tensor-map cache.

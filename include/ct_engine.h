@@ -79,9 +79,24 @@ int ct_engine_run(ct_engine *e);
  * each result's generated tokens at tokens + i * tok_stride. */
 int ct_engine_poll(ct_engine *e, ct_result *out, int max, int *tokens, int tok_stride);
 
-/* Counters: steps run, rows processed, tokens generated, device time of the
- * step graphs in milliseconds (CUDA events). */
-int ct_engine_stats(ct_engine *e, long long *steps, long long *rows, long long *tokens, double *step_ms);
+/* Counters since creation.  Device times come from CUDA events on the engine's
+ * stream; the per-kernel-class times from event nodes captured inside the step
+ * graphs around those launches. */
+typedef struct {
+    long long steps, rows, tokens, admitted;
+    double step_ms;          /* step graphs */
+    double admit_ms;         /* admission compute: cross K/V projection into pages */
+    double self_attn_ms;     /* paged self-attention kernels (all layers) */
+    double cross_attn_ms;    /* paged cross-attention kernels (all layers) */
+    double ffn_ms;           /* FFN1 + FFN2 GEMMs (all layers) */
+    double self_kv_bytes;    /* algorithmic K/V bytes the self-attention launches read */
+    double cross_kv_bytes;   /* algorithmic K/V bytes the cross-attention launches read */
+    double ffn_bytes;        /* algorithmic bytes of the FFN GEMMs (weights + activations) */
+    long long attn_launches; /* self + cross attention launches (main kernel, per layer) */
+    long long ffn_launches;
+    long long kernel_launches; /* kernels of this library launched (graph kernel nodes + admission) */
+} ct_engine_stats_t;
+int ct_engine_stats(ct_engine *e, ct_engine_stats_t *out);
 
 /* Read (and clear) the device status word; 0 when no kernel reported a problem. */
 int ct_engine_status(ct_engine *e);
