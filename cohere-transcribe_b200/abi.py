@@ -60,8 +60,9 @@ SIGNATURES = {
     "backend_linear_to_kvcache_batch": (None, [_vp, _vp, _vp, _vp, _int, _int, _int, _int]),
     "backend_sdp_attn_batch_decode_sa": (None, [_vp, _vp, _vp, _vp, _int, _int, _vp]),
     "backend_sdp_attn_batch_decode_ca": (None, [_vp, _vp, _vp, _vp, _int, _int, _vp]),
-    # extension
+    # extensions
     "ct_device_status": (_int, []),
+    "ct_sdp_attn_batch_decode_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
     # engine (include/ct_engine.h)
     "ct_engine_create": (_int, [_vp, _int, _vp, _sz, _vp, _vp]),
     "ct_engine_destroy": (None, [_vp]),

@@ -4,3 +4,4 @@
 #include "kernels.cu"
 #include "backend_abi.cu"
 #include "engine.cu"
+#include "noalloc.cu"

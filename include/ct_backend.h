@@ -111,6 +111,38 @@ void backend_sdp_attn_batch_decode_ca(float *out, const float *Q,
                                       const float *K, const float *V,
                                       int T_k_stride, int B, float *work);             /* backend.h:226 */
 
+/* ---- extensions (no counterpart in the reference ABI) -------------------- */
+
+/* Read and clear the device status word that this library's bounded waits and
+ * index checks set instead of trapping (0 = nothing reported).  No counterpart
+ * in the reference. */
+int ct_device_status(void);
+
+/* Batched decode attention that allocates nothing.  No counterpart in the
+ * reference: it is the no-allocation form of backend_sdp_attn_batch_decode_sa
+ * / _ca for callers that cannot call cudaMalloc -- code running under CUDA
+ * graph stream capture (allocation is rejected in global / thread-local
+ * capture mode), real-time threads and callbacks that must not take the device
+ * synchronisation an allocation can imply, and hosts with a fixed memory
+ * budget.  Every argument is caller memory: out/Q [B, DEC_D], K/V
+ * [B, T_k_stride, DEC_D] (fp32, device), lens [B] (int, device) = keys per
+ * item; stream is a cudaStream_t (NULL = the default stream).  Does not need
+ * backend_init.  Its split-KV scratch is a static device array of
+ * CT_NOALLOC_ATTN_SCRATCH_FLOATS floats (2 MiB, held by every GPU that loads
+ * the library until exit); B * DEC_H * ceil(T_k_stride / 128) * (DEC_DK + 2)
+ * must fit in it (e.g. B <= 64 with T_k_stride <= MAX_SEQ), else the call
+ * returns CT_NOALLOC_ETOOBIG and launches nothing.  The first call on a device
+ * looks up the array's device address (once per device, with that device
+ * current), so make that first call before any stream capture.  Calls share
+ * the array: calls that overlap on the GPU race and must be serialised.
+ * Returns 0, CT_NOALLOC_EINVAL, CT_NOALLOC_ETOOBIG or CT_NOALLOC_ECUDA. */
+#define CT_NOALLOC_ATTN_SCRATCH_FLOATS (64 * DEC_H * ((MAX_SEQ + 127) / 128) * (DEC_DK + 2))
+#define CT_NOALLOC_EINVAL (-1)
+#define CT_NOALLOC_ETOOBIG (-2)
+#define CT_NOALLOC_ECUDA (-4)
+int ct_sdp_attn_batch_decode_noalloc(float *out, const float *Q, const float *K, const float *V,
+                                     const int *lens, int T_k_stride, int B, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
