@@ -42,9 +42,9 @@ METRIC = "decode tokens/s (ragged continuous batch, greedy)"
 BATCH = 64
 
 
-def workload(seed: int = 0):
+def workload(seed: int = 0, batch: int = BATCH):
     import inputs
-    case = inputs.ragged_decode_case(BATCH, seed=seed, t_lo=5.0, t_hi=30.0, l_lo=20, l_hi=220)
+    case = inputs.ragged_decode_case(batch, seed=seed, t_lo=5.0, t_hi=30.0, l_lo=20, l_hi=220)
     enc = inputs.enc_outputs(case["T_enc"], case["enc_seed"])
     return case, enc
 
@@ -161,7 +161,7 @@ class ReferenceCPU:
         self.ws = W.weights_struct(self.wb)
         self.L.refh_bind_weights(ctypes.addressof(self.ws))
         n = n_threads
-        idx = np.arange(n) % BATCH
+        idx = np.arange(n) % len(case["T_enc"])
         self.n = n
         self.T_enc = np.ascontiguousarray(case["T_enc"][idx], dtype=np.int32)
         self.Tm = int(self.T_enc.max())
@@ -191,16 +191,24 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=32, help="token cap per utterance of the CPU sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--precision", type=int, default=1)
+    ap.add_argument("--batch", type=int, default=BATCH, help="utterances per GPU per step (profiling cases)")
+    ap.add_argument("--kv-pages", type=int, default=0, help="page-pool size (0 = engine default)")
+    ap.add_argument("--max-len", type=int, default=0, help="cap the forced lengths (profiling cases)")
+    ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel-class profiling pass")
+    ap.add_argument("--no-pdl", action="store_true", help="launch step kernels without programmatic dependent launch")
     args = ap.parse_args()
 
     world, rank, local = dist_setup(args.gpus)
     pk, pk_kind = peaks()
-    case, enc = workload(0)
+    case, enc = workload(0, args.batch)
+    if args.max_len > 0:
+        case["forced_len"] = np.minimum(case["forced_len"], args.max_len).astype(np.int32)
+    nb = args.batch
     tokens_per_step = int(case["forced_len"].sum())
     ncores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
-    cfg = {"workload": "config 3 shape: 64 ragged utterances/GPU, T_enc from U(5,30) s, EOS forced at U{20..220}",
-           "global_batch": BATCH * world, "decoder": "8 x 1024, 8 heads, FFN 4096, vocab 16384 (model.h dims)",
+    cfg = {"workload": f"config 3 shape: {nb} ragged utterances/GPU, T_enc from U(5,30) s, EOS forced at U{{20..220}}",
+           "global_batch": nb * world, "decoder": "8 x 1024, 8 heads, FFN 4096, vocab 16384 (model.h dims)",
            "tokens_per_step_per_gpu": tokens_per_step, "prompt_tokens": 10,
            "kv": "bf16 pages of 16 rows", "l2": "not flushed: per-step working set (268 MB weights + KV) > 126 MB L2",
            "parallelism": f"replicas x{world} (utterance sharding, no collective)"}
@@ -232,28 +240,29 @@ def main():
     lib = abi.load()
     wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("dec",))
     ws = W.weights_struct(wb)
-    eng = abi.Engine(lib, local if world > 1 else 0, wb, ws, max_slots=256, max_rows=1024, precision=args.precision)
-    # host inputs in pinned memory (page-locked through the CUDA runtime of the library's process)
-    enc_rows = [np.ascontiguousarray(enc[b, :case["T_enc"][b]]) for b in range(BATCH)]
+    dev = local if world > 1 else 0
+    eng = abi.Engine(lib, dev, wb, ws, max_slots=256, max_rows=1024, precision=args.precision,
+                     kv_pages=args.kv_pages, no_pdl=int(args.no_pdl))
+    # host inputs: the encoder rows of every utterance (fp32, host memory)
+    enc_rows = [np.ascontiguousarray(enc[b, :case["T_enc"][b]]) for b in range(nb)]
     h2d = int(sum(x.nbytes for x in enc_rows))
     d2h = int(4 * tokens_per_step)
 
-    def one_step(step_times):
-        for b in range(BATCH):
-            eng.submit(b, enc_rows[b], int(case["forced_len"][b]))
-        before = eng.stats()["step_ms"]
+    def one_step(e, step_times):
+        for b in range(nb):
+            e.submit(b, enc_rows[b], int(case["forced_len"][b]))
         while True:
-            s0 = eng.stats()["step_ms"]
-            left = eng.step(1)
-            step_times.append(eng.stats()["step_ms"] - s0)
+            s0 = e.stats()["step_ms"]
+            left = e.step(1)
+            step_times.append(e.stats()["step_ms"] - s0)
             if left <= 0:
                 break
-        out = eng.poll()
-        assert len(out) == BATCH
+        out = e.poll()
+        assert len(out) == nb
         return out
 
     for _ in range(args.warmup):
-        one_step([])
+        one_step(eng, [])
     if eng.status() != 0:
         raise RuntimeError("device status set during warm-up")
     barrier(world)
@@ -262,20 +271,40 @@ def main():
     with ClockSampler(local) as clk:
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            one_step(step_times)
+            one_step(eng, step_times)
         wall = time.perf_counter() - t0
     s1 = eng.stats()
     barrier(world)
     status = eng.status()
+    eng.close()
     dev_ms = (s1["step_ms"] - s0["step_ms"]) + (s1["admit_ms"] - s0["admit_ms"])
     dev_ms_max = barrier_max(world, dev_ms)
     wall_max = barrier_max(world, wall)
     tokens = tokens_per_step * args.steps * world
     value = tokens / (dev_ms_max / 1000.0)
     e2e = tokens / wall_max
+    dt = {k: s1[k] - s0[k] for k in s1}
 
-    # roofline of the dominant kernel class (from event nodes inside the step graphs)
-    d = {k: s1[k] - s0[k] for k in s1}
+    # Per-kernel-class device times: one more bench step on an engine whose step
+    # graphs carry CUDA event nodes around the attention and FFN launches of
+    # every layer (kept out of the timed run: event nodes serialise neighbours).
+    if not args.no_profile:
+        prof = abi.Engine(lib, dev, wb, ws, max_slots=256, max_rows=1024, precision=args.precision,
+                          kv_pages=args.kv_pages, profile=1)
+        one_step(prof, [])
+        p0 = prof.stats()
+        r0 = prof.profile_report()
+        one_step(prof, [])
+        p1 = prof.stats()
+        r1 = prof.profile_report()
+        prof.close()
+        breakdown = {k: {"ms_per_step": (v[0] - r0.get(k, [0, 0])[0]) / max(1, p1["steps"] - p0["steps"]),
+                         "launch_groups_per_step": (v[1] - r0.get(k, [0, 0])[1]) / max(1, p1["steps"] - p0["steps"])}
+                     for k, v in r1.items()}
+        d = {k: p1[k] - p0[k] for k in p1}
+    else:
+        d = {k: 0.0 for k in dt}
+        breakdown = {}
     classes = {
         "paged cross-attention": (d["cross_attn_ms"], d["cross_kv_bytes"]),
         "paged self-attention": (d["self_attn_ms"], d["self_kv_bytes"]),
@@ -293,7 +322,7 @@ def main():
     roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
             "frac": achieved / pk["hbm_gbs"], "peak_kind": pk_kind, "traffic": traffic,
             "algorithmic_bytes_per_launch": byts / max(1, launches), "avg_launch_ms": ms / max(1, launches),
-            "share_of_step": ms / max(1e-9, d["step_ms"])}
+            "measured": "CUDA event nodes around every launch of the class in one profiled bench step"}
     shares = {k: v[0] / max(1e-9, d["step_ms"]) for k, v in classes.items()}
 
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -301,9 +330,10 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "p50_step_ms": statistics.median(step_times) if step_times else None,
-            "decode_steps_per_bench_step": d["steps"] / args.steps,
-            "gpu_launches": int(d["kernel_launches"]) if "kernel_launches" in d else None,
-            "roofline": roof, "time_shares": shares, "clocks": clk.summary(), "device_status": status,
+            "decode_steps_per_bench_step": dt["steps"] / args.steps,
+            "admit_ms_per_step": dt["admit_ms"] / args.steps,
+            "gpu_launches": int(dt["kernel_launches"]),
+            "roofline": roof, "time_shares": shares, "profiled_step_breakdown": breakdown, "clocks": clk.summary(), "device_status": status,
             "precision": "bf16 weights, activations as bf16 hi+lo planes, fp32 accumulate" if args.precision else
             "bf16 weights and activations, fp32 accumulate"}
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -311,7 +341,6 @@ def main():
         t, s = ref.run()
         line["cpu_baseline"] = {"value": t / s, "unit": "tokens/s", "cores": ncores, "kind": "reference",
                                 "sample": ref.sample}
-    eng.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

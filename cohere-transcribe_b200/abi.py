@@ -72,12 +72,13 @@ SIGNATURES = {
     "ct_engine_poll": (_int, [_vp, _vp, _int, _vp, _int]),
     "ct_engine_stats": (_int, [_vp, _vp]),
     "ct_engine_status": (_int, [_vp]),
+    "ct_engine_profile_report": (_int, [_vp, _vp, _int]),
 }
 
 
 class EngineConfig(ctypes.Structure):
     _fields_ = [("max_slots", _int), ("max_rows", _int), ("kv_pages", _int), ("precision", _int),
-                ("n_prompt", _int), ("prompt", _vp)]
+                ("n_prompt", _int), ("prompt", _vp), ("profile", _int), ("no_pdl", _int)]
 
 
 class EngineStats(ctypes.Structure):
@@ -96,11 +97,12 @@ class Result(ctypes.Structure):
 class Engine:
     """Thin owner of a ct_engine* (one per GPU, driven by one thread)."""
 
-    def __init__(self, lib, device, wb, wstruct, max_slots=256, max_rows=1024, precision=1, kv_pages=0):
+    def __init__(self, lib, device, wb, wstruct, max_slots=256, max_rows=1024, precision=1, kv_pages=0, profile=0,
+                 no_pdl=0):
         self.lib = lib
         self.wb = wb            # keeps the host blob alive (the engine copies it at creation)
         self.ws = wstruct
-        cfg = EngineConfig(max_slots, max_rows, kv_pages, precision, 0, None)
+        cfg = EngineConfig(max_slots, max_rows, kv_pages, precision, 0, None, profile, no_pdl)
         h = ctypes.c_void_p()
         rc = lib.ct_engine_create(ctypes.byref(h), device, wb.ptr(), wb.nbytes, ctypes.addressof(wstruct),
                                   ctypes.byref(cfg))
@@ -140,6 +142,12 @@ class Engine:
 
     def status(self):
         return self.lib.ct_engine_status(self.h)
+
+    def profile_report(self):
+        import json
+        buf = ctypes.create_string_buffer(1 << 16)
+        self.lib.ct_engine_profile_report(self.h, buf, len(buf))
+        return json.loads(buf.value.decode())
 
     def close(self):
         if self.h:

@@ -14,6 +14,8 @@
 // bucket serves every step.
 #include <algorithm>
 #include <deque>
+#include <map>
+#include <string>
 #include <string.h>
 #include <vector>
 
@@ -29,8 +31,11 @@ constexpr int PR = kPageRows;
 constexpr int SELF_PAGES = MAX_SEQ / PR;     // 64
 constexpr int CROSS_PAGES = 64;              // T_enc <= 1024
 constexpr long long PAGE_ELEMS = (long long)NL * 2 * PR * D;
-constexpr int PCH = 128;                     // attention keys per chunk
 enum { S_FREE = 0, S_PREFILL = 1, S_DECODE = 2, S_DONE = 3 };
+constexpr int KCH = 64;                        // attention keys per work item (4 pages)
+constexpr int AW = 8;                          // consumer warps per attention CTA (one per head)
+constexpr int KCH_MAX = (MAX_SEQ + KCH - 1) / KCH;   // chunks per row (self and cross)
+constexpr int ANST = 3;                        // page stages in the attention pipeline
 
 struct DevState {
     int *state, *tok, *pos, *gen, *forced, *tenc;
@@ -43,6 +48,8 @@ struct DevState {
     long long *r_off;            // self page offset of each row
     int *q_row, *q_slot;         // per sequence: last row, slot
     int *n_rows, *n_seqs;        // device counts
+    int *w_self, *w_cross;       // attention work items: row << 8 | chunk
+    int *n_wself, *n_wcross;     // item counts
     int max_slots, max_rows, n_prompt;
 };
 
@@ -79,10 +86,19 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     const int i = threadIdx.x;
     const int st = i < s.max_slots ? s.state[i] : S_FREE;
     int nr = st == S_PREFILL ? s.n_prompt : st == S_DECODE ? 1 : 0;
-    int total = 0, nseq = 0;
+    const int te = nr > 0 ? s.tenc[i] : 0;
+    const int cross_ck = (te + KCH - 1) / KCH;
+    int self_items = 0;
+    if (st == S_PREFILL) for (int j = 0; j < nr; ++j) self_items += (j + 1 + KCH - 1) / KCH;
+    else if (st == S_DECODE) self_items = (s.pos[i] + 1 + KCH - 1) / KCH;
+    int total = 0, nseq = 0, n_ws = 0, n_wc = 0;
     const int base = block_excl_scan(nr, tmp, &total);
     __syncthreads();
     const int sidx = block_excl_scan(nr > 0 ? 1 : 0, tmp2, &nseq);
+    __syncthreads();
+    const int wsb = block_excl_scan(self_items, tmp, &n_ws);
+    __syncthreads();
+    const int wcb = block_excl_scan(nr * cross_ck, tmp2, &n_wc);
     if (total > row_cap || nseq > seq_cap) {   // the host bounds admissions; never expected
         if (i == 0) { set_status(CT_STATUS_BAD_ARG); *s.n_rows = 0; *s.n_seqs = 0; }
         return;
@@ -97,7 +113,16 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
         s.r_off[r] = page >= 0 ? (long long)page * PAGE_ELEMS + (long long)(p % PR) * D : -1;
     }
     if (nr > 0) { s.q_row[sidx] = base + nr - 1; s.q_slot[sidx] = i; }
-    if (i == 0) { *s.n_rows = total; *s.n_seqs = nseq; }
+    // attention work lists: (row, 32-key chunk) pairs, rows in order
+    int ws_i = wsb, wc_i = wcb;
+    for (int j = 0; j < nr; ++j) {
+        const int r = base + j;
+        const int p = st == S_PREFILL ? j : s.pos[i];
+        const int nck = (p + 1 + KCH - 1) / KCH;
+        for (int c = 0; c < nck && ws_i < row_cap * KCH_MAX; ++c) s.w_self[ws_i++] = (r << 8) | c;
+        for (int c = 0; c < cross_ck && wc_i < row_cap * KCH_MAX; ++c) s.w_cross[wc_i++] = (r << 8) | c;
+    }
+    if (i == 0) { *s.n_rows = total; *s.n_seqs = nseq; *s.n_wself = n_ws; *s.n_wcross = n_wc; }
 }
 
 __device__ __forceinline__ void store_planes(float v, bf16 *hi, bf16 *lo, size_t idx) {
@@ -118,10 +143,13 @@ __device__ __forceinline__ float block_sum256e(float v, float *red) {
     return t;
 }
 
-// h[r] = LN(etw[tok] + epw[pos]) (fp32) and its bf16 planes; rows r < *n.
+// h[r] = LN_e(etw[tok] + epw[pos]) (fp32) and the bf16 planes of LN_1(h[r])
+// (the first decoder layer's self-attention LayerNorm); rows r < *n.
 __global__ void __launch_bounds__(256) embed_rows_kernel(DevState s, const bf16 *etw, const bf16 *epw,
-                                                         const bf16 *lnw, const bf16 *lnb, float *h, bf16 *hi,
-                                                         bf16 *lo) {
+                                                         const bf16 *lnw, const bf16 *lnb, const bf16 *ln1w,
+                                                         const bf16 *ln1b, float *h, bf16 *hi, bf16 *lo) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float row[D];
     __shared__ float red[8];
     const int r = blockIdx.x;
@@ -138,16 +166,26 @@ __global__ void __launch_bounds__(256) embed_rows_kernel(DevState s, const bf16 
     float var = 0.0f;
     for (int k = threadIdx.x; k < D; k += 256) { const float c = row[k] - mean; var += c * c; }
     const float inv = 1.0f / sqrtf(block_sum256e(var, red) / D + 1e-5f);
+    float s2 = 0.0f;
     for (int k = threadIdx.x; k < D; k += 256) {
         const float o = (row[k] - mean) * inv * bf2f(lnw[k]) + bf2f(lnb[k]);
         h[(size_t)r * D + k] = o;
-        store_planes(o, hi, lo, (size_t)r * D + k);
+        row[k] = o;
+        s2 += o;
     }
+    const float mean2 = block_sum256e(s2, red) / D;
+    float var2 = 0.0f;
+    for (int k = threadIdx.x; k < D; k += 256) { const float c = row[k] - mean2; var2 += c * c; }
+    const float inv2 = 1.0f / sqrtf(block_sum256e(var2, red) / D + 1e-5f);
+    for (int k = threadIdx.x; k < D; k += 256)
+        store_planes((row[k] - mean2) * inv2 * bf2f(ln1w[k]) + bf2f(ln1b[k]), hi, lo, (size_t)r * D + k);
 }
 
 // planes[r] = LN(h[src(r)]) for r < *n; src(r) = rows ? rows[r] : r.
 __global__ void __launch_bounds__(256) ln_rows_kernel(const int *n, const int *rows, const float *h, const bf16 *w,
                                                       const bf16 *b, bf16 *hi, bf16 *lo) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[8];
     const int r = blockIdx.x;
     if (r >= *n) return;
@@ -168,111 +206,201 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const int *n, const int *r
     }
 }
 
-// Paged attention over bf16 K/V.  Row r of slot s = r_slot[r]: self mode
-// attends to rows [0, r_pos[r]] of the slot's self pages (causal prefix; a
-// decode row is its last position), cross mode to rows [0, T_enc[s]).
-// Split-KV with 128-key chunks; single-chunk rows write the output planes
-// directly, others leave (m, l, o) partials for attn_paged_combine.
-__global__ void __launch_bounds__(PCH) attn_paged_kernel(DevState s, const float *Q, const bf16 *pool, int layer,
-                                                         int cross, bf16 *hi, bf16 *lo, float *ws, int nck_max) {
-    __shared__ __align__(16) float qs[DK];
-    __shared__ float ps[PCH];
-    __shared__ float red[4];
-    __shared__ float ored[4][DK];
-    const int r = blockIdx.z, hh = blockIdx.y, c = blockIdx.x;
-    if (r >= *s.n_rows) return;
+// Paged attention over bf16 K/V with TMA-staged pages.  Work items are
+// (row, 64-key chunk) pairs listed by build_rows.  Row r of slot s attends, in
+// self mode, to positions [0, r_pos[r]] of the slot's self pages (the causal
+// prefix; a decode row is its last position), in cross mode to rows
+// [0, T_enc[s]) of its cross pages.  A persistent CTA walks its items; warp 8
+// streams every page the items touch -- the layer's 16 K rows (32 KB) and 16 V
+// rows (32 KB), contiguous in the pool -- into a ring of ANST shared-memory
+// stages with cp.async.bulk; warps 0..7 (head = warp) read their head's 256-byte
+// slices from shared memory, reduce the 16 scores of a page with a butterfly
+// over the lanes and keep an online softmax per head.  A row split over several
+// items leaves (m, l, o) per head in ws; the row's last item (atomic ticket)
+// merges them in chunk order.
+struct AttnSmem {
+    bf16 kv[ANST][2][PR * D];                  // [stage][K,V][16 rows x 1024]
+    uint64_t full[ANST], empty[ANST];
+    int last_flag;
+};
+
+__device__ __forceinline__ void item_span(const DevState &s, int cross, int w, int &r, int &c, int &L, int &p0,
+                                          int &p1, const int *&pt) {
+    r = w >> 8;
+    c = w & 255;
     const int slot = s.r_slot[r];
-    const int L = cross ? s.tenc[slot] : s.r_pos[r] + 1;
-    const int nck = (L + PCH - 1) / PCH;
-    if (c >= nck) return;
-    if (nck > nck_max) { if (threadIdx.x == 0) set_status(CT_STATUS_BAD_ARG); return; }
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int *pt = (cross ? s.cross_pt : s.self_pt) + slot * (cross ? CROSS_PAGES : SELF_PAGES);
-    qs[tid] = Q[(size_t)r * D + hh * DK + tid];   // DK == PCH == 128
-    __syncthreads();
-    const float scale = 1.0f / sqrtf((float)DK);
-    const int k = c * PCH + tid;
-    float sc = -INFINITY;
-    if (k < L && pt[k / PR] < 0) { set_status(CT_STATUS_BAD_ARG); return; }
-    if (k < L) {
-        const int page = pt[k / PR];
-        const bf16 *kr = pool + (long long)page * PAGE_ELEMS + (long long)(layer * 2 + 0) * PR * D +
-                         (long long)(k % PR) * D + hh * DK;
-        const uint4 *kp = reinterpret_cast<const uint4 *>(kr);
-        float acc = 0.0f;
-#pragma unroll 4
-        for (int i = 0; i < DK / 8; ++i) {
-            const uint4 u = kp[i];
-            const bf16 *e = reinterpret_cast<const bf16 *>(&u);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc += qs[i * 8 + j] * __bfloat162float(e[j]);
-        }
-        sc = acc * scale;
-    }
-    float m = warp_max(sc);
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    const float p = k < L ? expf(sc - m) : 0.0f;
-    ps[tid] = p;
-    float l = warp_sum(p);
-    __syncthreads();
-    if (lane == 0) red[warp] = l;
-    __syncthreads();
-    l = red[0] + red[1] + red[2] + red[3];
-    // o[d] over this warp's 32 keys; lane owns dims 4*lane .. 4*lane+3
-    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-    const int kw0 = c * PCH + warp * 32;
-    const int kn = min(32, L - kw0);
-    for (int kk = 0; kk < kn; ++kk) {
-        const int key = kw0 + kk;
-        const int page = max(pt[key / PR], 0);   // unallocated pages were reported above
-        const bf16 *vr = pool + (long long)page * PAGE_ELEMS + (long long)(layer * 2 + 1) * PR * D +
-                         (long long)(key % PR) * D + hh * DK + 4 * lane;
-        const uint2 u = *reinterpret_cast<const uint2 *>(vr);
-        const bf16 *e = reinterpret_cast<const bf16 *>(&u);
-        const float pk = ps[warp * 32 + kk];
-        o0 += pk * __bfloat162float(e[0]);
-        o1 += pk * __bfloat162float(e[1]);
-        o2 += pk * __bfloat162float(e[2]);
-        o3 += pk * __bfloat162float(e[3]);
-    }
-    ored[warp][4 * lane + 0] = o0;
-    ored[warp][4 * lane + 1] = o1;
-    ored[warp][4 * lane + 2] = o2;
-    ored[warp][4 * lane + 3] = o3;
-    __syncthreads();
-    const float od = ored[0][tid] + ored[1][tid] + ored[2][tid] + ored[3][tid];
-    if (nck == 1) {
-        store_planes(od / l, hi, lo, (size_t)r * D + hh * DK + tid);
-    } else {
-        float *w = ws + (((size_t)r * H + hh) * nck_max + c) * (DK + 2);
-        if (tid == 0) { w[0] = m; w[1] = l; }
-        w[2 + tid] = od;
-    }
+    L = cross ? s.tenc[slot] : s.r_pos[r] + 1;
+    pt = (cross ? s.cross_pt : s.self_pt) + slot * (cross ? CROSS_PAGES : SELF_PAGES);
+    const int k0 = c * KCH, k1 = min(L, k0 + KCH);
+    p0 = k0 / PR;
+    p1 = k1 > k0 ? (k1 - 1) / PR + 1 : p0;     // pages [p0, p1)
 }
 
-__global__ void __launch_bounds__(DK) attn_paged_combine(DevState s, int cross, bf16 *hi, bf16 *lo, const float *ws,
-                                                         int nck_max) {
-    const int r = blockIdx.x, hh = blockIdx.y;
-    if (r >= *s.n_rows) return;
-    const int L = cross ? s.tenc[s.r_slot[r]] : s.r_pos[r] + 1;
-    const int nck = (L + PCH - 1) / PCH;
-    if (nck <= 1 || nck > nck_max) return;
-    const float *w = ws + ((size_t)r * H + hh) * nck_max * (DK + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nck; ++c) M = fmaxf(M, w[(size_t)c * (DK + 2)]);
-    float Ls = 0.0f, o = 0.0f;
-    for (int c = 0; c < nck; ++c) {
-        const float f = expf(w[(size_t)c * (DK + 2)] - M);
-        Ls += w[(size_t)c * (DK + 2) + 1] * f;
-        o += w[(size_t)c * (DK + 2) + 2 + threadIdx.x] * f;
+__global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s, const float *Q, const bf16 *pool,
+                                                                      int layer, int cross, bf16 *hi, bf16 *lo,
+                                                                      float *ws, int *tickets) {
+    extern __shared__ __align__(128) uint8_t asmem_raw[];
+    AttnSmem &sm = *reinterpret_cast<AttnSmem *>(asmem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < ANST; ++i) { mbar_init(&sm.full[i], 1); mbar_init(&sm.empty[i], AW); }
+        fence_mbar_init();
     }
-    store_planes(o / Ls, hi, lo, (size_t)r * D + hh * DK + threadIdx.x);
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    const int n_items = cross ? *s.n_wcross : *s.n_wself;
+    const int *items = cross ? s.w_cross : s.w_self;
+    const long long kvoff = (long long)layer * 2 * PR * D;
+
+    if (warp == AW) {
+        // ---------------------------------------------------------- producer
+        if (lane == 0) {
+            int g = 0;   // pages issued so far (ring position)
+            for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+                int r, c, L, p0, p1;
+                const int *pt;
+                item_span(s, cross, items[it], r, c, L, p0, p1, pt);
+                for (int p = p0; p < p1; ++p, ++g) {
+                    const int st = g % ANST;
+                    if (g >= ANST && !mbar_wait(&sm.empty[st], ((g / ANST) & 1) ^ 1, CT_STATUS_TIMEOUT_FREE)) return;
+                    const int page = max(pt[p], 0);
+                    const bf16 *src = pool + (long long)page * PAGE_ELEMS + kvoff;
+                    mbar_expect_tx(&sm.full[st], 2 * PR * D * sizeof(bf16));
+                    bulk_load(sm.kv[st][0], src, PR * D * sizeof(bf16), &sm.full[st]);
+                    bulk_load(sm.kv[st][1], src + PR * D, PR * D * sizeof(bf16), &sm.full[st]);
+                }
+            }
+        }
+        return;
+    }
+    // -------------------------------------------------------------- consumers
+    const int hh = warp;
+    const float scale = 1.0f / sqrtf((float)DK);
+    int g = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+        int r, c, L, p0, p1;
+        const int *pt;
+        item_span(s, cross, items[it], r, c, L, p0, p1, pt);
+        const int nck = (L + KCH - 1) / KCH;
+        for (int p = p0; p < p1; ++p)
+            if (pt[p] < 0) { if (lane == 0) set_status(CT_STATUS_BAD_ARG); }
+        const float4 qv = *reinterpret_cast<const float4 *>(Q + (size_t)r * D + hh * DK + 4 * lane);
+        float m = -INFINITY, l = 0.0f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+        for (int p = p0; p < p1; ++p, ++g) {
+            const int st = g % ANST;
+            if (!mbar_wait(&sm.full[st], (g / ANST) & 1, CT_STATUS_TIMEOUT_TMA)) return;
+            const bf16 *Ks = sm.kv[st][0] + hh * DK + 4 * lane;
+            const bf16 *Vs = sm.kv[st][1] + hh * DK + 4 * lane;
+            // partial dot products of the page's 16 keys over this lane's 4 dims
+            float sc[PR];
+#pragma unroll
+            for (int k = 0; k < PR; ++k) {
+                const uint2 u = *reinterpret_cast<const uint2 *>(Ks + k * D);
+                const bf16 *e = reinterpret_cast<const bf16 *>(&u);
+                sc[k] = qv.x * __bfloat162float(e[0]) + qv.y * __bfloat162float(e[1]) +
+                        qv.z * __bfloat162float(e[2]) + qv.w * __bfloat162float(e[3]);
+            }
+            // butterfly reduce-scatter: after it lane l holds key (l >> 1)'s full score
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const bool up = lane & 16;
+                const float send = up ? sc[k] : sc[k + 8];
+                const float keep = up ? sc[k + 8] : sc[k];
+                sc[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const bool up = lane & 8;
+                const float send = up ? sc[k] : sc[k + 4];
+                const float keep = up ? sc[k + 4] : sc[k];
+                sc[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+            }
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const bool up = lane & 4;
+                const float send = up ? sc[k] : sc[k + 2];
+                const float keep = up ? sc[k + 2] : sc[k];
+                sc[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+            {
+                const bool up = lane & 2;
+                const float send = up ? sc[0] : sc[1];
+                const float keep = up ? sc[1] : sc[0];
+                sc[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+            }
+            sc[0] += __shfl_xor_sync(0xffffffffu, sc[0], 1);
+            // lane l now holds the score of key j = bit-reversed index built above
+            const int j = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+            const int key = p * PR + j;
+            const bool valid = key >= c * KCH && key < min(L, (c + 1) * KCH);
+            const float sj = valid ? sc[0] * scale : -INFINITY;
+            const float mn = fmaxf(m, warp_max(sj));
+            const float corr = expf(m - mn);   // m = -inf before the first valid key -> 0
+            const float pj = valid ? expf(sj - mn) : 0.0f;
+            l = l * corr + warp_sum(pj) * 0.5f;   // every key is held by two lanes
+            o0 *= corr; o1 *= corr; o2 *= corr; o3 *= corr;
+#pragma unroll
+            for (int k = 0; k < PR; ++k) {
+                // key k sits on lanes whose bits 4..1 spell k
+                const int src = ((k >> 3) & 1) << 4 | ((k >> 2) & 1) << 3 | ((k >> 1) & 1) << 2 | (k & 1) << 1;
+                const float pk = __shfl_sync(0xffffffffu, pj, src);
+                if (pk == 0.0f) continue;   // masked (or underflowed) key: its V row may be stale or unset
+                const uint2 u = *reinterpret_cast<const uint2 *>(Vs + k * D);
+                const bf16 *e = reinterpret_cast<const bf16 *>(&u);
+                o0 += pk * __bfloat162float(e[0]);
+                o1 += pk * __bfloat162float(e[1]);
+                o2 += pk * __bfloat162float(e[2]);
+                o3 += pk * __bfloat162float(e[3]);
+            }
+            m = mn;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[st]);
+        }
+        const size_t idx = (size_t)r * D + hh * DK + 4 * lane;
+        if (nck == 1) {
+            const float inv = 1.0f / l;
+            store_planes(o0 * inv, hi, lo, idx);
+            store_planes(o1 * inv, hi, lo, idx + 1);
+            store_planes(o2 * inv, hi, lo, idx + 2);
+            store_planes(o3 * inv, hi, lo, idx + 3);
+            continue;
+        }
+        float *wp = ws + ((size_t)r * KCH_MAX + c) * (2 * H + D);
+        if (lane == 0) { wp[hh] = m; wp[H + hh] = l; }
+        *reinterpret_cast<float4 *>(wp + 2 * H + hh * DK + 4 * lane) = make_float4(o0, o1, o2, o3);
+        __threadfence();
+        asm volatile("bar.sync 1, %0;" ::"n"(AW * 32));   // consumer warps only
+        if (threadIdx.x == 0) sm.last_flag = atomicAdd(&tickets[r], 1) == nck - 1;
+        asm volatile("bar.sync 1, %0;" ::"n"(AW * 32));
+        if (!sm.last_flag) continue;
+        __threadfence();
+        const float *wr = ws + (size_t)r * KCH_MAX * (2 * H + D);
+        float Mg = -INFINITY;
+        for (int cc = 0; cc < nck; ++cc) Mg = fmaxf(Mg, wr[(size_t)cc * (2 * H + D) + hh]);
+        float Lg = 0.0f;
+        float4 og = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int cc = 0; cc < nck; ++cc) {
+            const float *pc = wr + (size_t)cc * (2 * H + D);
+            const float f = expf(pc[hh] - Mg);
+            Lg += pc[H + hh] * f;
+            const float4 v = *reinterpret_cast<const float4 *>(pc + 2 * H + hh * DK + 4 * lane);
+            og.x += v.x * f; og.y += v.y * f; og.z += v.z * f; og.w += v.w * f;
+        }
+        const float inv = 1.0f / Lg;
+        store_planes(og.x * inv, hi, lo, idx);
+        store_planes(og.y * inv, hi, lo, idx + 1);
+        store_planes(og.z * inv, hi, lo, idx + 2);
+        store_planes(og.w * inv, hi, lo, idx + 3);
+        asm volatile("bar.sync 1, %0;" ::"n"(AW * 32));   // everyone has read last_flag
+        if (threadIdx.x == 0) tickets[r] = 0;                // ready for the next launch
+    }
 }
 
 // next[q] = argmax over the vocabulary of sequence q's logits (first max).
 __global__ void __launch_bounds__(256) argmax_seq_kernel(DevState s, const float *logits, int *next) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float bv[256];
     __shared__ int bi[256];
     const int q = blockIdx.x;
@@ -304,6 +432,8 @@ __global__ void __launch_bounds__(256) argmax_seq_kernel(DevState s, const float
 // Append the step's token to every live sequence, advance its KV length and
 // retire it on forced length / EOS / MAX_SEQ (transcribe.c:771-794).
 __global__ void update_kernel(DevState s, const int *next) {
+    pdl_wait();
+    pdl_trigger();
     const int q = blockIdx.x * blockDim.x + threadIdx.x;
     if (q >= *s.n_seqs) return;
     const int slot = s.q_slot[q];
@@ -335,6 +465,7 @@ struct Pending {
 };
 
 struct Bucket {
+    std::vector<std::string> labels;   // profile mode: label of each event node, in order
     int rows = 0;
     int kernels = 0;   // kernel nodes in the captured step graph
     cudaGraphExec_t exec = nullptr;
@@ -373,6 +504,8 @@ struct ct_engine {
     int *h_done = nullptr;   // host view of done_map
     // step buffers
     float *h = nullptr, *q = nullptr, *attn_ws = nullptr, *logits = nullptr;
+    int *tickets = nullptr;          // per-row chunk counters of the attention kernel
+    int attn_ctas = 296;             // persistent attention grid (2 per SM)
     bf16 *xa[2], *xb[2], *xm[2], *lm[2];
     int *next = nullptr;
     size_t attn_ws_floats = 0;
@@ -397,12 +530,12 @@ struct ct_engine {
     double step_ms = 0.0;
     int n_live = 0;
     ct_engine_stats_t st_acc;
-    cudaEvent_t pev[NL][6];          // captured around self-attn, cross-attn, FFN of every layer
+    std::vector<cudaEvent_t> marks;  // profile mode: event nodes between the step's launch groups
+    std::vector<std::string> mark_label;
+    std::map<std::string, std::pair<double, long long>> mark_ms;   // label -> (total ms, count)
     cudaEvent_t aev0 = nullptr, aev1 = nullptr;
     std::vector<int> slot_steps;     // steps run since admission (host mirror of the KV length)
     std::vector<int> slot_tenc;
-    float *gws = nullptr;            // split-K workspace owned by this engine
-    size_t gws_bytes = 0;
     std::vector<void *> owned;       // aligned copies of misaligned weights
 };
 
@@ -436,15 +569,69 @@ static const bf16 *ew_matrix(ct_engine *e, const uint16_t *hp, size_t elems) {
 
 static bool two_planes(const ct_engine *e) { return e->cfg.precision != 0; }
 
-// GEMM on the engine's stream with the engine's own split-K workspace and
-// buffer-capacity tensor maps (so captured graphs never refer to another
-// owner's scratch).
+static thread_local bool t_pdl = true;   // set from the engine's config while a step is captured
+
+// Profile mode: record an external event node after a launch group; the time
+// from the previous mark is attributed to `label`.
+static void mark(ct_engine *e, const char *label) {
+    if (!e->cfg.profile) return;
+    const size_t i = e->mark_label.size();
+    if (i >= e->marks.size()) {
+        cudaEvent_t ev;
+        CT_CHECK(cudaEventCreate(&ev));
+        e->marks.push_back(ev);
+    }
+    e->mark_label.push_back(label);
+    CT_CHECK(cudaEventRecordWithFlags(e->marks[i], e->st, cudaEventRecordExternal));
+}
+
+// GEMM on the engine's stream with buffer-capacity tensor maps; step GEMMs use
+// programmatic dependent launch.
 static void egemm(ct_engine *e, const bf16 *W, int N, int K, const bf16 *xh, const bf16 *xl, int T, long x_rows,
-                  GemmEpilogue ep, bool split) {
-    ep.ws = e->gws;
-    ep.ws_bytes = e->gws_bytes;
+                  GemmEpilogue ep, bool split, bool pdl = true) {
     ep.x_rows = x_rows;
+    ep.pdl = pdl && t_pdl;
     gemm_bf16(e->st, W, N, K, xh, xl, T, ep, split);
+}
+
+// Launch with programmatic stream serialization (the kernel calls pdl_wait()
+// before it reads anything its predecessor writes).
+template <typename... KArgs, typename... Args>
+static void launch_pdl(cudaStream_t st, dim3 grid, dim3 block, void (*k)(KArgs...), Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = t_pdl ? 1 : 0;
+    CT_CHECK(cudaLaunchKernelEx(&cfg, k, args...));
+}
+
+static void launch_attn(cudaStream_t st, int ctas, const DevState &s, const float *q, const bf16 *pool, int layer,
+                        int cross, bf16 *hi, bf16 *lo, float *ws, int *tickets) {
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    CT_CHECK(cudaGetDevice(&dev));
+    if (configured_dev != dev) {
+        CT_CHECK(cudaFuncSetAttribute(attn_paged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)sizeof(AttnSmem)));
+        configured_dev = dev;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3((AW + 1) * 32);
+    cfg.dynamicSmemBytes = sizeof(AttnSmem);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = t_pdl ? 1 : 0;
+    CT_CHECK(cudaLaunchKernelEx(&cfg, attn_paged_kernel, s, q, pool, layer, cross, hi, lo, ws, tickets));
 }
 
 // Encode one step for capacity `rows` (seqs capacity = min(rows, max_slots)) on e->st.
@@ -455,52 +642,68 @@ static void encode_step(ct_engine *e, int rows) {
     const bool two = two_planes(e);
     bf16 *xa_lo = two ? e->xa[1] : nullptr, *xb_lo = two ? e->xb[1] : nullptr, *xm_lo = two ? e->xm[1] : nullptr;
     bf16 *lm_lo = two ? e->lm[1] : nullptr;
+    e->mark_label.clear();
+    mark(e, "start");
     build_rows_kernel<<<1, 1024, 0, st>>>(s, rows, seqs);
-    embed_rows_kernel<<<rows, 256, 0, st>>>(s, e->etw, e->epw, e->elnw, e->elnb, e->h, e->xa[0], xa_lo);
-    const int nck = (MAX_SEQ + PCH - 1) / PCH;
+    mark(e, "build_rows");
+    launch_pdl(st, dim3(rows), dim3(256), embed_rows_kernel, s, e->etw, e->epw, e->elnw, e->elnb, e->L[0].sa_lnw,
+               e->L[0].sa_lnb, e->h, e->xa[0], xa_lo);
+    mark(e, "embed_ln");
     for (int l = 0; l < NL; ++l) {
         const auto &Ly = e->L[l];
-        ln_rows_kernel<<<rows, 256, 0, st>>>(s.n_rows, nullptr, e->h, Ly.sa_lnw, Ly.sa_lnb, e->xa[0], xa_lo);
         GemmEpilogue qkv;
         qkv.epi = EPI_QKV_PAGED; qkv.bias = Ly.qkv_b; qkv.Y = e->q; qkv.ldy = D; qkv.qdim = D;
         qkv.kv_pool = e->pool; qkv.row_off = s.r_off; qkv.layer = l; qkv.T_dev = s.n_rows;
         egemm(e, Ly.qkv_w, 3 * D, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, qkv, true);
-        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][0], st, cudaEventRecordExternal));
-        attn_paged_kernel<<<dim3(nck, H, rows), PCH, 0, st>>>(s, e->q, e->pool, l, 0, e->xb[0], xb_lo, e->attn_ws, nck);
-        attn_paged_combine<<<dim3(rows, H), DK, 0, st>>>(s, 0, e->xb[0], xb_lo, e->attn_ws, nck);
-        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][1], st, cudaEventRecordExternal));
+        mark(e, "gemm_qkv");
+        launch_attn(st, e->attn_ctas, s, e->q, e->pool, l, 0, e->xb[0], xb_lo, e->attn_ws, e->tickets);
+        mark(e, "attn_self");
         GemmEpilogue o;
         o.epi = EPI_FMADD; o.scale = 1.0f; o.bias = Ly.sa_ob; o.Y = e->h; o.ldy = D; o.T_dev = s.n_rows;
         egemm(e, Ly.sa_ow, D, D, e->xb[0], xb_lo, rows, e->cfg.max_rows, o, true);
-        ln_rows_kernel<<<rows, 256, 0, st>>>(s.n_rows, nullptr, e->h, Ly.ca_lnw, Ly.ca_lnb, e->xa[0], xa_lo);
+        mark(e, "gemm_o");
+        launch_pdl(st, dim3(rows), dim3(256), ln_rows_kernel, (const int *)s.n_rows, (const int *)nullptr, (const float *)e->h,
+                   Ly.ca_lnw, Ly.ca_lnb, e->xa[0], xa_lo);
+        mark(e, "layernorm");
         GemmEpilogue qc;
         qc.bias = Ly.ca_qb; qc.Y = e->q; qc.ldy = D; qc.T_dev = s.n_rows;
         egemm(e, Ly.ca_qw, D, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, qc, true);
-        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][2], st, cudaEventRecordExternal));
-        attn_paged_kernel<<<dim3(CROSS_PAGES * PR / PCH, H, rows), PCH, 0, st>>>(s, e->q, e->pool, l, 1, e->xb[0],
-                                                                                 xb_lo, e->attn_ws, nck);
-        attn_paged_combine<<<dim3(rows, H), DK, 0, st>>>(s, 1, e->xb[0], xb_lo, e->attn_ws, nck);
-        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][3], st, cudaEventRecordExternal));
+        mark(e, "gemm_q_cross");
+        launch_attn(st, e->attn_ctas, s, e->q, e->pool, l, 1, e->xb[0], xb_lo, e->attn_ws, e->tickets);
+        mark(e, "attn_cross");
         GemmEpilogue oc = o;
         oc.bias = Ly.ca_ob;
         egemm(e, Ly.ca_ow, D, D, e->xb[0], xb_lo, rows, e->cfg.max_rows, oc, true);
-        ln_rows_kernel<<<rows, 256, 0, st>>>(s.n_rows, nullptr, e->h, Ly.ffn_lnw, Ly.ffn_lnb, e->xa[0], xa_lo);
-        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][4], st, cudaEventRecordExternal));
+        mark(e, "gemm_o");
+        launch_pdl(st, dim3(rows), dim3(256), ln_rows_kernel, (const int *)s.n_rows, (const int *)nullptr, (const float *)e->h,
+                   Ly.ffn_lnw, Ly.ffn_lnb, e->xa[0], xa_lo);
+        mark(e, "layernorm");
         GemmEpilogue f1;
         f1.epi = EPI_BF16; f1.act = 2; f1.bias = Ly.ffn_b1; f1.Ybf = e->xm[0]; f1.Ybf_lo = xm_lo; f1.ldy = FF;
         f1.T_dev = s.n_rows;
         egemm(e, Ly.ffn_w1, FF, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, f1, true);
+        mark(e, "gemm_ffn1");
         GemmEpilogue f2 = o;
         f2.bias = Ly.ffn_b2;
         egemm(e, Ly.ffn_w2, D, FF, e->xm[0], xm_lo, rows, e->cfg.max_rows, f2, true);
-        CT_CHECK(cudaEventRecordWithFlags(e->pev[l][5], st, cudaEventRecordExternal));
+        mark(e, "gemm_ffn2");
+        if (l + 1 < NL) {   // the next layer's self-attention LayerNorm (layer 0's is fused into the embedding)
+            launch_pdl(st, dim3(rows), dim3(256), ln_rows_kernel, (const int *)s.n_rows, (const int *)nullptr,
+                       (const float *)e->h, e->L[l + 1].sa_lnw, e->L[l + 1].sa_lnb, e->xa[0], xa_lo);
+            mark(e, "layernorm");
+        }
     }
-    ln_rows_kernel<<<seqs, 256, 0, st>>>(s.n_seqs, s.q_row, e->h, e->dlnw, e->dlnb, e->lm[0], lm_lo);
+    launch_pdl(st, dim3(seqs), dim3(256), ln_rows_kernel, (const int *)s.n_seqs, (const int *)s.q_row, (const float *)e->h,
+               e->dlnw, e->dlnb, e->lm[0], lm_lo);
+    mark(e, "layernorm_final");
     GemmEpilogue lh;
     lh.bias = e->hdb; lh.Y = e->logits; lh.ldy = V; lh.T_dev = s.n_seqs;
+    lh.split = 4;   // 128 vocabulary tiles x 4 K-splits: enough CTAs to stream the 32 MB table
     egemm(e, e->etw, V, D, e->lm[0], lm_lo, seqs, e->cfg.max_slots, lh, true);
-    argmax_seq_kernel<<<seqs, 256, 0, st>>>(s, e->logits, e->next);
-    update_kernel<<<(seqs + 255) / 256, 256, 0, st>>>(s, e->next);
+    mark(e, "gemm_lm_head");
+    launch_pdl(st, dim3(seqs), dim3(256), argmax_seq_kernel, s, (const float *)e->logits, e->next);
+    launch_pdl(st, dim3((seqs + 255) / 256), dim3(256), update_kernel, s, (const int *)e->next);
+    mark(e, "argmax_update");
 }
 
 static Bucket *bucket_for(ct_engine *e, int rows_needed) {
@@ -512,7 +715,10 @@ static Bucket *bucket_for(ct_engine *e, int rows_needed) {
     Bucket b;
     b.rows = cap;
     CT_CHECK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeRelaxed));
+    t_pdl = !e->cfg.no_pdl;
     encode_step(e, cap);
+    t_pdl = true;
+    b.labels = e->mark_label;
     CT_CHECK(cudaStreamEndCapture(e->st, &b.graph));
     CT_CHECK(cudaGraphInstantiate(&b.exec, b.graph, 0));
     size_t nn = 0;
@@ -593,7 +799,8 @@ static int admit(ct_engine *e) {
     split_fp32_to_bf16(e->st, e->enc_dev, enc_rows, D, D, e->enc_pl[0], two ? e->enc_pl[1] : nullptr, D);
     GemmEpilogue ep;
     ep.epi = EPI_CAKV_PAGED; ep.bias = e->cakv_b; ep.kv_pool = e->pool; ep.row_off = e->enc_off;
-    egemm(e, e->cakv_w, NL * 2 * D, D, e->enc_pl[0], two ? e->enc_pl[1] : nullptr, enc_rows, e->enc_rows_cap, ep, false);
+    egemm(e, e->cakv_w, NL * 2 * D, D, e->enc_pl[0], two ? e->enc_pl[1] : nullptr, enc_rows, e->enc_rows_cap, ep, false,
+          false);
     EK(cudaEventRecord(e->aev1, e->st));
     EK(cudaStreamSynchronize(e->st));   // staging reuse
     float ams = 0.0f;
@@ -668,14 +875,17 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
         e->st_acc.kernel_launches += b->kernels;
         ++e->n_steps;
         e->n_rows += rows;
-        for (int l = 0; l < NL; ++l) {
-            float a = 0.f, c = 0.f, f = 0.f;
-            EK(cudaEventElapsedTime(&a, e->pev[l][0], e->pev[l][1]));
-            EK(cudaEventElapsedTime(&c, e->pev[l][2], e->pev[l][3]));
-            EK(cudaEventElapsedTime(&f, e->pev[l][4], e->pev[l][5]));
-            e->st_acc.self_attn_ms += a;
-            e->st_acc.cross_attn_ms += c;
-            e->st_acc.ffn_ms += f;
+        if (e->cfg.profile) {
+            for (size_t i = 1; i < b->labels.size(); ++i) {
+                float t = 0.f;
+                EK(cudaEventElapsedTime(&t, e->marks[i - 1], e->marks[i]));
+                auto &acc = e->mark_ms[b->labels[i]];
+                acc.first += t;
+                acc.second += 1;
+                if (b->labels[i] == "attn_self") e->st_acc.self_attn_ms += t;
+                else if (b->labels[i] == "attn_cross") e->st_acc.cross_attn_ms += t;
+                else if (b->labels[i].rfind("gemm_ffn", 0) == 0) e->st_acc.ffn_ms += t;
+            }
         }
         e->st_acc.self_kv_bytes += NL * self_b;
         e->st_acc.cross_kv_bytes += NL * cross_b;
@@ -740,6 +950,22 @@ extern "C" int ct_engine_stats(ct_engine *e, ct_engine_stats_t *out) {
     return CT_OK;
 }
 
+extern "C" int ct_engine_profile_report(ct_engine *e, char *buf, int cap) {
+    if (!e || !buf || cap <= 0) return CT_EINVAL;
+    std::string s = "{";
+    bool first = true;
+    for (auto &kv : e->mark_ms) {
+        char tmp[160];
+        snprintf(tmp, sizeof(tmp), "%s\"%s\": [%.6f, %lld]", first ? "" : ", ", kv.first.c_str(), kv.second.first,
+                 kv.second.second);
+        s += tmp;
+        first = false;
+    }
+    s += "}";
+    snprintf(buf, cap, "%s", s.c_str());
+    return (int)s.size();
+}
+
 extern "C" int ct_engine_status(ct_engine *e) {
     if (!e) return CT_EINVAL;
     EK(cudaSetDevice(e->device));
@@ -760,7 +986,7 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
                     e->enc_pl[1], e->enc_off, e->ds.state, e->ds.tok, e->ds.pos, e->ds.gen, e->ds.forced,
                     e->ds.tenc, e->ds.self_pt, e->ds.cross_pt, e->ds.out_tok, e->ds.prompt, e->ds.r_slot,
                     e->ds.r_pos, e->ds.r_tok, e->ds.r_off, e->ds.q_row, e->ds.q_slot, e->ds.n_rows, e->ds.n_seqs,
-                    e->gws};
+                    e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.n_wself, e->ds.n_wcross};
     for (void *p : ptrs) cudaFree(p);
     for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
     cudaFreeHost(e->h_done);
@@ -771,8 +997,7 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
     cudaEventDestroy(e->ev1);
     cudaEventDestroy(e->aev0);
     cudaEventDestroy(e->aev1);
-    for (int l = 0; l < NL; ++l)
-        for (int j = 0; j < 6; ++j) cudaEventDestroy(e->pev[l][j]);
+    for (auto ev : e->marks) cudaEventDestroy(ev);
     cudaStreamDestroy(e->st);
     for (void *p : e->owned) cudaFree(p);
     delete e;
@@ -807,8 +1032,6 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     EK(cudaEventCreate(&e->ev1));
     EK(cudaEventCreate(&e->aev0));
     EK(cudaEventCreate(&e->aev1));
-    for (int l = 0; l < NL; ++l)
-        for (int j = 0; j < 6; ++j) EK(cudaEventCreate(&e->pev[l][j]));
     memset(&e->st_acc, 0, sizeof(e->st_acc));
     // weights: one device copy of the blob, then derived concatenations
     e->host_base = static_cast<const uint8_t *>(host_blob);
@@ -849,6 +1072,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     const int S = cfg.max_slots, R = cfg.max_rows;
     e->n_pages = cfg.kv_pages > 0 ? cfg.kv_pages : S * (SELF_PAGES + 24);
     if (dalloc(&e->pool, (size_t)e->n_pages * PAGE_ELEMS)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    EK(cudaMemset(e->pool, 0, (size_t)e->n_pages * PAGE_ELEMS * sizeof(bf16)));   // no NaN bit patterns in unset rows
     for (int i = e->n_pages - 1; i >= 0; --i) e->free_pages.push_back(i);
     // device slot table
     DevState &s = e->ds;
@@ -857,7 +1081,14 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         dalloc(&s.tenc, S) || dalloc(&s.self_pt, (size_t)S * SELF_PAGES) || dalloc(&s.cross_pt, (size_t)S * CROSS_PAGES) ||
         dalloc(&s.out_tok, (size_t)S * MAX_SEQ) || dalloc(&s.prompt, cfg.n_prompt) || dalloc(&s.r_slot, R) ||
         dalloc(&s.r_pos, R) || dalloc(&s.r_tok, R) || dalloc(&s.r_off, R) || dalloc(&s.q_row, S) ||
-        dalloc(&s.q_slot, S) || dalloc(&s.n_rows, 1) || dalloc(&s.n_seqs, 1)) { ct_engine_destroy(e); return CT_ENOMEM; }
+        dalloc(&s.q_slot, S) || dalloc(&s.n_rows, 1) || dalloc(&s.n_seqs, 1) ||
+        dalloc(&s.w_self, (size_t)R * KCH_MAX) || dalloc(&s.w_cross, (size_t)R * KCH_MAX) || dalloc(&s.n_wself, 1) ||
+        dalloc(&s.n_wcross, 1)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    {
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        e->attn_ctas = sms;
+    }
     EK(cudaMemset(s.state, 0, sizeof(int) * S));
     EK(cudaMemset(s.n_rows, 0, sizeof(int)));
     EK(cudaMemset(s.n_seqs, 0, sizeof(int)));
@@ -870,8 +1101,12 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         dalloc(&e->xa[1], (size_t)R * D) || dalloc(&e->xb[0], (size_t)R * D) || dalloc(&e->xb[1], (size_t)R * D) ||
         dalloc(&e->xm[0], (size_t)R * FF) || dalloc(&e->xm[1], (size_t)R * FF) || dalloc(&e->lm[0], (size_t)S * D) ||
         dalloc(&e->lm[1], (size_t)S * D) || dalloc(&e->logits, (size_t)S * V) || dalloc(&e->next, S)) { ct_engine_destroy(e); return CT_ENOMEM; }
-    e->attn_ws_floats = (size_t)R * H * ((MAX_SEQ + PCH - 1) / PCH) * (DK + 2);
-    if (dalloc(&e->attn_ws, e->attn_ws_floats)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    e->attn_ws_floats = (size_t)R * KCH_MAX * (2 * H + D);
+    if (dalloc(&e->attn_ws, e->attn_ws_floats) || dalloc(&e->tickets, R)) {
+        ct_engine_destroy(e);
+        return CT_ENOMEM;
+    }
+    EK(cudaMemset(e->tickets, 0, sizeof(int) * R));
     // admission staging: up to 64 utterances of 30 s worth of encoder rows
     e->enc_rows_cap = 64 * 400;
     if (dalloc(&e->enc_dev, (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_pl[0], (size_t)e->enc_rows_cap * D) ||
@@ -885,12 +1120,6 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     e->slot_pages.assign(S, {});
     e->slot_steps.assign(S, 0);
     e->slot_tenc.assign(S, 0);
-    // split-K workspace for the largest step (nsplit * rows * N floats)
-    size_t ws = 0;
-    const int shapes[4][2] = {{3 * D, D}, {D, D}, {FF, D}, {D, FF}};
-    for (auto &sh : shapes) ws = std::max(ws, (size_t)split_factor(sh[0], sh[1]) * R * sh[0] * sizeof(float));
-    e->gws_bytes = ws;
-    if (dalloc((uint8_t **)&e->gws, ws)) { ct_engine_destroy(e); return CT_ENOMEM; }
     EK(cudaDeviceSynchronize());
     *out = e;
     return CT_OK;

@@ -9,6 +9,7 @@
 // Stages are released by tcgen05.commit on the stage's "empty" mbarrier.
 // Split-K (grid.z) writes fp32 partials that a second kernel sums in split
 // order, so the result is deterministic and independent of T.
+#include <algorithm>
 #include <memory>
 #include <unordered_map>
 
@@ -26,7 +27,8 @@ struct KernelParams {
     int kbps;      // k-blocks (of 64) per split
     int kb_total;
     int stages;
-    float *ws;     // split partials [nsplit][T][N] (null when not split)
+    int nsplit;    // K splits = cluster size along grid.z (1 = no split)
+    int bar_off;   // byte offset of the mbarriers in the aligned shared memory
     GemmEpilogue ep;
 };
 
@@ -87,15 +89,18 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int stages = p.stages;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)stages * STAGE_BYTES);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.bar_off);
     uint64_t *empty = full + stages;
     uint64_t *accb = empty + stages;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accb + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BM, t0 = blockIdx.y * BN, z = blockIdx.z;
+    // Rows beyond the device row count: every CTA of a cluster shares (n0, t0),
+    // so the whole cluster leaves together, before any TMA or TMEM work.  The
+    // count is produced at least two kernels upstream (see gemm.cuh).
     const int T_eff = p.ep.T_dev ? min(p.T, *p.ep.T_dev) : p.T;
-    if (t0 >= T_eff) return;   // uniform per CTA, before any barrier or TMEM allocation
+    if (t0 >= T_eff) return;
     const int kb0 = z * p.kbps;
     const int kb1 = min(kb0 + p.kbps, p.kb_total);
     const int nkb = kb1 - kb0;
@@ -114,16 +119,30 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Weights do not depend on the previous kernel: start streaming the first
+    // stages of this CTA's weight tiles before waiting for it.
+    const int pre = min(stages, nkb);
+    if (warp == 0 && lane == 0) {
+        for (int i = 0; i < pre; ++i) {
+            mbar_expect_tx(&full[i], STAGE_BYTES);
+            tma_load_2d(smem + (size_t)i * STAGE_BYTES, &tmW, &full[i], (kb0 + i) * BK, n0);
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+
     if (warp == 0) {
         if (lane == 0) {
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % stages;
                 const uint32_t ph = (uint32_t)(i / stages) & 1u;
-                if (i >= stages && !mbar_wait(&empty[s], ph ^ 1u, CT_STATUS_TIMEOUT_FREE)) break;
                 uint8_t *a = smem + (size_t)s * STAGE_BYTES;
-                mbar_expect_tx(&full[s], STAGE_BYTES);
                 const int kc = (kb0 + i) * BK;
-                tma_load_2d(a, &tmW, &full[s], kc, n0);
+                if (i >= pre) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, CT_STATUS_TIMEOUT_FREE)) break;
+                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    tma_load_2d(a, &tmW, &full[s], kc, n0);
+                }
                 tma_load_2d(a + A_BYTES, &tmXh, &full[s], kc, t0);
                 if (TWO) tma_load_2d(a + A_BYTES + B_BYTES, &tmXl, &full[s], kc, t0);
             }
@@ -131,12 +150,10 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16(BM, BN);
-            bool ok = true;
-            for (int i = 0; i < nkb && ok; ++i) {
+            for (int i = 0; i < nkb; ++i) {
                 const int s = i % stages;
                 const uint32_t ph = (uint32_t)(i / stages) & 1u;
-                ok = mbar_wait(&full[s], ph, CT_STATUS_TIMEOUT_TMA);
-                if (!ok) break;
+                if (!mbar_wait(&full[s], ph, CT_STATUS_TIMEOUT_TMA)) break;
                 tc_fence_after();
                 const uint32_t a = smem_u32(smem + (size_t)s * STAGE_BYTES);
                 const uint64_t ad = sw128_desc(a);
@@ -153,54 +170,88 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
             }
             mma_commit(accb);
         }
-    } else {
-        // epilogue warps 2..5 -> TMEM lane quarters 2,3,0,1
-        const int q = warp & 3;
-        const int n = n0 + q * 32 + lane;
-        const bool nvalid = n < p.N;
-        const bool split = p.ws != nullptr;
-        const float bias = (!split && nvalid && p.ep.bias) ? bf2f(p.ep.bias[n]) : 0.0f;
-        bool ok = mbar_wait(accb, 0, CT_STATUS_TIMEOUT_MMA);
+    }
+    // ---------------------------------------------------------------- epilogue
+    const bool split = p.nsplit > 1;
+    const int q = warp & 3;
+    const int n = n0 + q * 32 + lane;
+    const bool epi_warp = warp >= 2;
+    bool ok = true;
+    if (epi_warp) {
+        ok = mbar_wait(accb, 0, CT_STATUS_TIMEOUT_MMA);
         ok = __all_sync(0xffffffffu, ok);
         tc_fence_after();
-        if (ok) {
-            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    }
+    const float bias = (epi_warp && n < p.N && p.ep.bias) ? bf2f(p.ep.bias[n]) : 0.0f;
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    if (!split) {
+        if (epi_warp && ok) {
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 if (t0 + c >= T_eff) break;   // warp-uniform
                 float v[32];
                 tmem_ld32(tbase + (uint32_t)c, v);
-                if (nvalid) {
+                if (n < p.N) {
                     const int tl = min(32, T_eff - (t0 + c));
-                    if (split) {
-                        float *w = p.ws + ((size_t)z * p.T + t0 + c) * p.N + n;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (j < tl) w[(size_t)j * p.N] = v[j];
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (j < tl) apply_epilogue(p.ep, t0 + c + j, n, v[j] + bias);
-                    }
+                    for (int j = 0; j < 32; ++j)
+                        if (j < tl) apply_epilogue(p.ep, t0 + c + j, n, v[j] + bias);
                 }
             }
         }
+    } else {
+        // Split-K across the CTAs of one cluster (grid.z = cluster size): each
+        // CTA parks its fp32 accumulator tile in its own shared memory (the
+        // pipeline buffers are idle once the accumulator is complete), then CTA
+        // r sums tokens [r*BN/cs, (r+1)*BN/cs) of the tile over all CTAs in
+        // rank order through distributed shared memory.
+        float *acc_s = reinterpret_cast<float *>(smem);   // [BN][BM], feature fastest
+        if (epi_warp) {
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                float v[32];
+                if (ok) tmem_ld32(tbase + (uint32_t)c, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc_s[(c + j) * BM + q * 32 + lane] = ok ? v[j] : 0.0f;
+            }
+        }
+        cluster_sync();
+        if (epi_warp) {
+            // warp w2 = warp - 2 handles tokens tb + w2, tb + w2 + 4, ...; lane
+            // owns features 4*lane .. 4*lane+3 (one 16-byte remote load per CTA)
+            const int cs = p.nsplit;
+            const int slice = BN / cs;
+            const int tb = (int)cluster_ctarank() * slice;
+            const int w2 = warp - 2;
+            const uint32_t base = smem_u32(acc_s);
+            const int f0 = 4 * lane;
+            float b4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                b4[i] = (n0 + f0 + i < p.N && p.ep.bias) ? bf2f(p.ep.bias[n0 + f0 + i]) : 0.0f;
+            for (int j = w2; j < slice; j += 4) {
+                const int t = t0 + tb + j;
+                if (t >= T_eff) break;
+                const uint32_t off = base + (uint32_t)(((tb + j) * BM + f0) * 4);
+                float4 part[16];
+#pragma unroll
+                for (int r = 0; r < 16; ++r)
+                    if (r < cs) part[r] = dsmem_ld4(dsmem_addr(off, (uint32_t)r));
+                float4 sum = part[0];
+#pragma unroll
+                for (int r = 1; r < 16; ++r)
+                    if (r < cs) { sum.x += part[r].x; sum.y += part[r].y; sum.z += part[r].z; sum.w += part[r].w; }
+                const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (n0 + f0 + i < p.N) apply_epilogue(p.ep, t, n0 + f0 + i, vals[i] + b4[i]);
+            }
+        }
+        cluster_sync();   // no CTA leaves while another still reads its shared memory
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem, NCOLS);
-}
-
-__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int nsplit, int T, int N, GemmEpilogue ep) {
-    const size_t TN = (size_t)T * N;
-    const size_t lim = ep.T_dev ? (size_t)min(T, *ep.T_dev) * N : TN;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < lim; i += (size_t)gridDim.x * blockDim.x) {
-        float s = ws[i];
-        for (int z = 1; z < nsplit; ++z) s += ws[(size_t)z * TN + i];
-        const int t = (int)(i / N), n = (int)(i % N);
-        if (ep.bias) s += bf2f(ep.bias[n]);
-        apply_epilogue(ep, t, n, s);
-    }
 }
 
 __global__ void split_fp32_kernel(const float *__restrict__ x, int T, int K, int ldx, bf16 *__restrict__ hi,
@@ -252,8 +303,6 @@ struct WCopy {
 
 struct GemmCtx {
     int device = -1;
-    float *ws = nullptr;
-    size_t ws_bytes = 0;
     bf16 *xhi = nullptr, *xlo = nullptr;
     size_t x_elems = 0;
     std::unordered_map<MapKey, CUtensorMap, MapKeyHash> maps;
@@ -275,8 +324,6 @@ GemmCtx *gemm_ctx() {
     if (!t_ctx) {
         t_ctx.reset(new GemmCtx());
         t_ctx->device = dev;
-        t_ctx->ws_bytes = 64ull << 20;
-        CT_CHECK(cudaMalloc(&t_ctx->ws, t_ctx->ws_bytes));
         t_ctx->x_elems = 16ull << 20;
         CT_CHECK(cudaMalloc(&t_ctx->xhi, t_ctx->x_elems * sizeof(bf16)));
         CT_CHECK(cudaMalloc(&t_ctx->xlo, t_ctx->x_elems * sizeof(bf16)));
@@ -290,22 +337,11 @@ void gemm_ctx_release() {
     CT_CHECK(cudaGetDevice(&cur));
     CT_CHECK(cudaSetDevice(t_ctx->device));
     CT_CHECK(cudaDeviceSynchronize());
-    cudaFree(t_ctx->ws);
     cudaFree(t_ctx->xhi);
     cudaFree(t_ctx->xlo);
     for (auto &kv : t_ctx->wcopies) cudaFree(kv.second.p);
     t_ctx.reset();
     CT_CHECK(cudaSetDevice(cur));
-}
-
-void gemm_reserve_ws(size_t bytes) {
-    GemmCtx *c = gemm_ctx();
-    if (bytes <= c->ws_bytes) return;
-    CT_CHECK(cudaDeviceSynchronize());
-    scratch_moved();
-    cudaFree(c->ws);
-    c->ws_bytes = bytes;
-    CT_CHECK(cudaMalloc(&c->ws, bytes));
 }
 
 static const CUtensorMap &tmap_bf16(GemmCtx *c, const void *ptr, long rows, long cols, long box_rows) {
@@ -330,27 +366,70 @@ int split_factor(int N, int K) {
     const int kb = (K + BK - 1) / BK;
     if ((long)N * K > 4l * 1024 * 1024) return 1;
     int s = 1;
-    while (tiles * s * 2 <= 128 && kb / (s * 2) >= 2) s *= 2;
+    while (s < 16 && tiles * s * 2 <= 256 && kb / (s * 2) >= 1) s *= 2;
     return s;
 }
 
 template <int BN, bool TWO>
 static void launch_tc(cudaStream_t st, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml,
-                      KernelParams p, int nsplit) {
+                      KernelParams p, bool pdl) {
     constexpr int STAGE = BM * BK * 2 + BN * BK * 2 * (TWO ? 2 : 1);
-    const int max_stages = (kSmemBudget - 2048) / STAGE;
-    p.stages = p.kbps < max_stages ? p.kbps : max_stages;
-    if (p.stages > 8) p.stages = 8;
-    const size_t smem = (size_t)p.stages * STAGE + 1024 + 16 * (2 * p.stages + 2);
-    static thread_local bool configured = false;   // per instantiation and thread
-    if (!configured) {
+    // large clusters: keep two CTAs per SM so a 16-CTA cluster fits in a GPC
+    const int budget = p.nsplit > 8 ? 100 * 1024 : kSmemBudget;
+    const int max_stages = std::max(1, (budget - 2048) / STAGE);
+    p.stages = std::min(std::min(p.kbps, max_stages), 8);
+    size_t body = (size_t)p.stages * STAGE;
+    if (p.nsplit > 1) body = std::max(body, (size_t)BM * BN * sizeof(float));   // parked accumulator
+    p.bar_off = (int)((body + 15) & ~(size_t)15);
+    const size_t smem = 1024 + p.bar_off + 16 * (2 * p.stages + 2);
+    static thread_local int configured_dev = -1;   // per instantiation and thread
+    int dev = 0;
+    CT_CHECK(cudaGetDevice(&dev));
+    if (configured_dev != dev) {
         CT_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN, TWO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       kSmemBudget));
-        configured = true;
+        // K-split clusters of 16 CTAs exceed the portable limit of 8
+        CT_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN, TWO>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        configured_dev = dev;
     }
-    dim3 grid((p.N + BM - 1) / BM, (p.T + BN - 1) / BN, nsplit);
-    gemm_tc_kernel<BN, TWO><<<grid, kThreads, smem, st>>>(mw, mh, ml, p);
-    CT_CHECK(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((p.N + BM - 1) / BM, (p.T + BN - 1) / BN, p.nsplit);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (p.nsplit > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = 1;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = p.nsplit;
+        ++na;
+    }
+    if (pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    if (p.nsplit > 1) {
+        // a cluster shape the device cannot schedule would fail the launch
+        static thread_local std::unordered_map<long, int> fits;
+        const long key = ((long)dev << 40) | ((long)p.nsplit << 32) | (long)smem;
+        auto it = fits.find(key);
+        if (it == fits.end()) {
+            int n = 0;
+            cudaLaunchConfig_t q = cfg;
+            q.attrs = at;
+            q.numAttrs = 1;   // cluster attribute only
+            if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<BN, TWO>, &q) != cudaSuccess) n = 0;
+            cudaGetLastError();
+            it = fits.emplace(key, n).first;
+        }
+        if (it->second <= 0) CT_FATAL("GEMM cluster of %d CTAs with %zu B shared memory cannot be scheduled", p.nsplit, smem);
+    }
+    CT_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, TWO>, mw, mh, ml, p));
 }
 
 void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, const bf16 *X_lo, int T,
@@ -362,36 +441,25 @@ void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, c
     const bool two = X_lo != nullptr;
     int BN = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : (two ? 128 : 256);
     const int kb_total = (K + BK - 1) / BK;
-    float *ws = ep.ws ? ep.ws : c->ws;
-    const size_t ws_bytes = ep.ws ? ep.ws_bytes : c->ws_bytes;
-    int nsplit = allow_split ? split_factor(N, K) : 1;
-    if (nsplit > 1 && (size_t)nsplit * T * N * sizeof(float) > ws_bytes) nsplit = 1;
+    int nsplit = allow_split ? (ep.split > 0 ? std::min(ep.split, 16) : split_factor(N, K)) : 1;
+    while (nsplit > 1 && BN % nsplit) nsplit >>= 1;
     const int kbps = (kb_total + nsplit - 1) / nsplit;
-    nsplit = (kb_total + kbps - 1) / kbps;   // every split gets >= 1 block
-    // X maps use the scratch capacity (or T) as the row count; rows >= T are never stored
+    if ((kb_total + kbps - 1) / kbps != nsplit) nsplit = 1;   // every split must own >= 1 block
+    const int kbps_final = nsplit > 1 ? kbps : kb_total;
+    // X maps use the scratch capacity (or the caller's buffer rows) as the row count
     const long xrows = (X_hi == c->xhi || X_hi == c->xlo) ? (long)(c->x_elems / K) : (ep.x_rows > 0 ? ep.x_rows : (long)T);
     const CUtensorMap &mw = tmap_bf16(c, W, N, K, BM);
     const CUtensorMap &mh = tmap_bf16(c, X_hi, xrows, K, BN);
     const CUtensorMap &ml = two ? tmap_bf16(c, X_lo, xrows, K, BN) : mh;
     KernelParams p;
-    p.N = N; p.K = K; p.T = T; p.kbps = kbps; p.kb_total = kb_total; p.stages = 1;
-    p.ws = nsplit > 1 ? ws : nullptr;
+    p.N = N; p.K = K; p.T = T; p.kbps = kbps_final; p.kb_total = kb_total; p.stages = 1;
+    p.nsplit = nsplit; p.bar_off = 0;
     p.ep = ep;
-#define CT_LAUNCH(bn)                                                                            \
-    (two ? launch_tc<bn, true>(st, mw, mh, ml, p, nsplit) : launch_tc<bn, false>(st, mw, mh, ml, p, nsplit))
     switch (BN) {
-    case 32: CT_LAUNCH(32); break;
-    case 64: CT_LAUNCH(64); break;
-    case 128: CT_LAUNCH(128); break;
-    default: launch_tc<256, false>(st, mw, mh, ml, p, nsplit); break;
-    }
-#undef CT_LAUNCH
-    if (nsplit > 1) {
-        const size_t TN = (size_t)T * N;
-        int blocks = (int)((TN + 255) / 256);
-        if (blocks > 148 * 8) blocks = 148 * 8;
-        splitk_reduce_kernel<<<blocks, 256, 0, st>>>(ws, nsplit, T, N, ep);
-        CT_CHECK(cudaGetLastError());
+    case 32: two ? launch_tc<32, true>(st, mw, mh, ml, p, ep.pdl) : launch_tc<32, false>(st, mw, mh, ml, p, ep.pdl); break;
+    case 64: two ? launch_tc<64, true>(st, mw, mh, ml, p, ep.pdl) : launch_tc<64, false>(st, mw, mh, ml, p, ep.pdl); break;
+    case 128: two ? launch_tc<128, true>(st, mw, mh, ml, p, ep.pdl) : launch_tc<128, false>(st, mw, mh, ml, p, ep.pdl); break;
+    default: launch_tc<256, false>(st, mw, mh, ml, p, ep.pdl); break;
     }
 }
 

@@ -47,9 +47,10 @@ struct GemmEpilogue {
     int qdim = 0;
     int kv_width = 1024;          // K/V row width in the pool
     const int *T_dev = nullptr;   // optional device row count (rows >= *T_dev are skipped)
-    float *ws = nullptr;          // optional caller-owned split-K workspace (else the thread's)
-    size_t ws_bytes = 0;
     long x_rows = 0;              // rows of the X buffers (tensor-map extent); 0 = T
+    bool pdl = false;             // launch with programmatic stream serialization
+    int split = 0;                // K-split factor override (0 = split_factor(N, K)); a fixed
+                                  // per-call-site value keeps results independent of T
 };
 
 // Per-thread GEMM context: stream, workspaces, tensor-map cache.
@@ -58,8 +59,12 @@ GemmCtx *gemm_ctx();   // the calling thread's context (created on first use)
 void gemm_ctx_release();
 
 // Launch on `st`.  X_lo may be null (single bf16 plane).  allow_split enables
-// the deterministic split-K used for decode-sized problems; the split factor
-// depends only on (N, K), never on T.
+// the split-K used for decode-sized problems: the K-split CTAs of one output
+// tile form a thread-block cluster and reduce through distributed shared
+// memory in rank order, so the result is deterministic; the split factor
+// depends only on (N, K) (and BN divisibility), never on T.  With ep.T_dev the
+// kernel reads a device row count before its dependency wait, so that count
+// must come from a kernel at least two launches upstream.
 void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, const bf16 *X_lo, int T,
                const GemmEpilogue &ep, bool allow_split);
 
@@ -77,8 +82,5 @@ int split_factor(int N, int K);
 // Called whenever a per-thread scratch buffer moves, so that cached CUDA graphs
 // holding its old address are dropped (defined by the ABI layer).
 void scratch_moved();
-
-// Make sure the split-K workspace of the calling thread holds `bytes`.
-void gemm_reserve_ws(size_t bytes);
 
 }  // namespace ct

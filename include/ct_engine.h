@@ -48,6 +48,10 @@ typedef struct {
     int precision;       /* 1 = activations as bf16 hi+lo planes (near fp32, default), 0 = bf16 */
     int n_prompt;        /* prompt length (default 10) */
     const int *prompt;   /* prompt tokens (default: transcribe.c:1320-1330 with a synthetic language id) */
+    int profile;         /* 1 = capture CUDA event nodes around the attention and FFN launches of
+                            every layer (per-kernel-class device times in ct_engine_stats); the
+                            event nodes serialise their neighbours, so timed runs leave this 0 */
+    int no_pdl;          /* 1 = launch step kernels without programmatic dependent launch */
 } ct_engine_config;
 
 typedef struct {
@@ -86,9 +90,9 @@ typedef struct {
     long long steps, rows, tokens, admitted;
     double step_ms;          /* step graphs */
     double admit_ms;         /* admission compute: cross K/V projection into pages */
-    double self_attn_ms;     /* paged self-attention kernels (all layers) */
-    double cross_attn_ms;    /* paged cross-attention kernels (all layers) */
-    double ffn_ms;           /* FFN1 + FFN2 GEMMs (all layers) */
+    double self_attn_ms;     /* paged self-attention kernels (all layers; profile = 1 only) */
+    double cross_attn_ms;    /* paged cross-attention kernels (all layers; profile = 1 only) */
+    double ffn_ms;           /* FFN1 + FFN2 GEMMs (all layers; profile = 1 only) */
     double self_kv_bytes;    /* algorithmic K/V bytes the self-attention launches read */
     double cross_kv_bytes;   /* algorithmic K/V bytes the cross-attention launches read */
     double ffn_bytes;        /* algorithmic bytes of the FFN GEMMs (weights + activations) */
@@ -97,6 +101,11 @@ typedef struct {
     long long kernel_launches; /* kernels of this library launched (graph kernel nodes + admission) */
 } ct_engine_stats_t;
 int ct_engine_stats(ct_engine *e, ct_engine_stats_t *out);
+
+/* Profile mode: JSON object {label: [total device ms, launches]} of every
+ * launch group of the step graph, from the event nodes between them.
+ * Returns the JSON length (written truncated to cap - 1 bytes). */
+int ct_engine_profile_report(ct_engine *e, char *buf, int cap);
 
 /* Read (and clear) the device status word; 0 when no kernel reported a problem. */
 int ct_engine_status(ct_engine *e);
