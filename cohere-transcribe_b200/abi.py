@@ -73,12 +73,15 @@ SIGNATURES = {
     "ct_engine_stats": (_int, [_vp, _vp]),
     "ct_engine_status": (_int, [_vp]),
     "ct_engine_profile_report": (_int, [_vp, _vp, _int]),
+    "ct_engine_encode": (_int, [_vp, _int, _vp, _vp, _vp, _vp]),
+    "ct_engine_submit_mel": (_int, [_vp, ctypes.c_longlong, _vp, _int, _int]),
 }
 
 
 class EngineConfig(ctypes.Structure):
     _fields_ = [("max_slots", _int), ("max_rows", _int), ("kv_pages", _int), ("precision", _int),
-                ("n_prompt", _int), ("prompt", _vp), ("profile", _int), ("no_pdl", _int)]
+                ("n_prompt", _int), ("prompt", _vp), ("profile", _int), ("no_pdl", _int),
+                ("enc_max_utts", _int), ("enc_max_frames", _int)]
 
 
 class EngineStats(ctypes.Structure):
@@ -87,7 +90,8 @@ class EngineStats(ctypes.Structure):
                 ("self_attn_ms", ctypes.c_double), ("cross_attn_ms", ctypes.c_double), ("ffn_ms", ctypes.c_double),
                 ("self_kv_bytes", ctypes.c_double), ("cross_kv_bytes", ctypes.c_double),
                 ("ffn_bytes", ctypes.c_double), ("attn_launches", ctypes.c_longlong),
-                ("ffn_launches", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong)]
+                ("ffn_launches", ctypes.c_longlong), ("kernel_launches", ctypes.c_longlong),
+                ("enc_ms", ctypes.c_double), ("enc_utts", ctypes.c_longlong), ("enc_frames", ctypes.c_longlong)]
 
 
 class Result(ctypes.Structure):
@@ -98,11 +102,12 @@ class Engine:
     """Thin owner of a ct_engine* (one per GPU, driven by one thread)."""
 
     def __init__(self, lib, device, wb, wstruct, max_slots=256, max_rows=1024, precision=1, kv_pages=0, profile=0,
-                 no_pdl=0):
+                 no_pdl=0, enc_max_utts=0, enc_max_frames=0):
         self.lib = lib
         self.wb = wb            # keeps the host blob alive (the engine copies it at creation)
         self.ws = wstruct
-        cfg = EngineConfig(max_slots, max_rows, kv_pages, precision, 0, None, profile, no_pdl)
+        cfg = EngineConfig(max_slots, max_rows, kv_pages, precision, 0, None, profile, no_pdl, enc_max_utts,
+                           enc_max_frames)
         h = ctypes.c_void_p()
         rc = lib.ct_engine_create(ctypes.byref(h), device, wb.ptr(), wb.nbytes, ctypes.addressof(wstruct),
                                   ctypes.byref(cfg))
@@ -115,6 +120,27 @@ class Engine:
         rc = self.lib.ct_engine_submit_encoded(self.h, utt_id, a.ctypes.data, a.shape[0], int(forced_len))
         if rc != 0:
             raise RuntimeError(f"submit failed: {rc}")
+
+    def submit_mel(self, utt_id, mel, forced_len):
+        a = np.ascontiguousarray(mel, dtype=np.float32)          # [N_MELS, T_mel]
+        rc = self.lib.ct_engine_submit_mel(self.h, utt_id, a.ctypes.data, a.shape[1], int(forced_len))
+        if rc != 0:
+            raise RuntimeError(f"submit_mel failed: {rc}")
+
+    def encode(self, mels):
+        """mels: list of [N_MELS, T_mel] arrays -> list of [T_enc, DEC_D] encoder outputs."""
+        arrs = [np.ascontiguousarray(m, dtype=np.float32) for m in mels]
+        n = len(arrs)
+        ptrs = (ctypes.c_void_p * n)(*[x.ctypes.data for x in arrs])
+        T_mel = np.array([x.shape[1] for x in arrs], np.int32)
+        t3 = ((((T_mel + 1) // 2) + 1) // 2 + 1) // 2
+        out = np.zeros((int(t3.sum()), 1024), np.float32)
+        T_enc = np.zeros(n, np.int32)
+        rc = self.lib.ct_engine_encode(self.h, n, ptrs, T_mel.ctypes.data, out.ctypes.data, T_enc.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"encode failed: {rc}")
+        offs = np.concatenate([[0], np.cumsum(T_enc)])
+        return [out[offs[b]:offs[b + 1]] for b in range(n)]
 
     def step(self, n=1):
         rc = self.lib.ct_engine_step(self.h, n)

@@ -22,6 +22,7 @@
 #include "../../include/ct_engine.h"
 #include "gemm.cuh"
 #include "kernels.cuh"
+#include "encoder.cu"
 
 namespace ct {
 namespace eng {
@@ -535,6 +536,10 @@ struct ct_engine {
     std::map<std::string, std::pair<double, long long>> mark_ms;   // label -> (total ms, count)
     cudaEvent_t aev0 = nullptr, aev1 = nullptr;
     std::vector<int> slot_steps;     // steps run since admission (host mirror of the KV length)
+    enc::State *enc = nullptr;       // packed encoder (null when the blob has no encoder weights)
+    struct MelJob { long long id; std::vector<float> mel; int T_mel, forced; };
+    std::deque<MelJob> mel_pending;
+    cudaEvent_t eev0 = nullptr, eev1 = nullptr;
     std::vector<int> slot_tenc;
     std::vector<void *> owned;       // aligned copies of misaligned weights
 };
@@ -837,10 +842,57 @@ static int harvest(ct_engine *e) {
     return 0;
 }
 
+static bool admissible(const ct_engine *e, int T_enc, int forced_len);
+
+// Encode up to one encoder batch of queued log-mel utterances and queue their
+// encoder rows for admission.
+static int encode_pending(ct_engine *e) {
+    if (e->mel_pending.empty()) return 0;
+    if (!e->enc) return CT_EINVAL;
+    std::vector<const float *> mels;
+    std::vector<int> T_mel;
+    int frames = 0;
+    for (auto &j : e->mel_pending) {
+        if ((int)mels.size() >= e->enc->max_utts || frames + j.T_mel > e->enc->max_frames) break;
+        mels.push_back(j.mel.data());
+        T_mel.push_back(j.T_mel);
+        frames += j.T_mel;
+    }
+    const int n = (int)mels.size();
+    std::vector<int> off(n + 1);
+    EK(cudaEventRecord(e->eev0, e->st));
+    if (!enc::encode(e->st, *e->enc, n, mels.data(), T_mel.data(), off.data())) return CT_EINVAL;
+    EK(cudaEventRecord(e->eev1, e->st));
+    std::vector<float> host((size_t)off[n] * D);
+    EK(cudaMemcpyAsync(host.data(), e->enc->enc_h, sizeof(float) * host.size(), cudaMemcpyDeviceToHost, e->st));
+    EK(cudaStreamSynchronize(e->st));
+    float ms = 0.f;
+    EK(cudaEventElapsedTime(&ms, e->eev0, e->eev1));
+    e->st_acc.enc_ms += ms;
+    e->st_acc.enc_utts += n;
+    e->st_acc.enc_frames += frames;
+    e->st_acc.kernel_launches += 5 + 3 + 1 + 2 + NL * (5 + 2 + 2 + 2 + 1 + 2 + 2 + 1 + 3) + 1;
+    for (int b = 0; b < n; ++b) {
+        const auto &j = e->mel_pending.front();
+        Pending p;
+        p.id = j.id;
+        p.T_enc = off[b + 1] - off[b];
+        p.enc.assign(host.begin() + (size_t)off[b] * D, host.begin() + (size_t)off[b + 1] * D);
+        p.forced = j.forced;
+        e->pending.push_back(std::move(p));
+        e->mel_pending.pop_front();
+    }
+    return 0;
+}
+
 extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
     if (!e) return CT_EINVAL;
     EK(cudaSetDevice(e->device));
     for (int it = 0; it < n_steps; ++it) {
+        if (e->pending.empty() && !e->mel_pending.empty()) {
+            const int rc = encode_pending(e);
+            if (rc) return rc;
+        }
         int rc = harvest(e);
         if (rc) return rc;
         rc = admit(e);
@@ -899,7 +951,39 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
     }
     int rc = harvest(e);
     if (rc) return rc;
-    return (int)e->pending.size() + e->n_live;
+    return (int)e->pending.size() + (int)e->mel_pending.size() + e->n_live;
+}
+
+extern "C" int ct_engine_submit_mel(ct_engine *e, long long utt_id, const float *mel, int T_mel, int forced_len) {
+    if (!e || !mel || T_mel <= 0 || forced_len < 0) return CT_EINVAL;
+    if (!e->enc || T_mel > e->enc->max_frames) return CT_EINVAL;
+    const int t1 = (T_mel + 1) / 2, t2 = (t1 + 1) / 2, T_enc = (t2 + 1) / 2;
+    if (!admissible(e, T_enc, forced_len)) return CT_EINVAL;
+    ct_engine::MelJob j;
+    j.id = utt_id;
+    j.mel.assign(mel, mel + (size_t)N_MELS * T_mel);
+    j.T_mel = T_mel;
+    j.forced = forced_len;
+    e->mel_pending.push_back(std::move(j));
+    return CT_OK;
+}
+
+extern "C" int ct_engine_encode(ct_engine *e, int n, const float *const *mel, const int *T_mel, float *enc_h, int *T_enc) {
+    if (!e || n <= 0 || !mel || !T_mel || !enc_h || !T_enc) return CT_EINVAL;
+    if (!e->enc) return CT_EINVAL;
+    EK(cudaSetDevice(e->device));
+    std::vector<int> off(n + 1);
+    EK(cudaEventRecord(e->eev0, e->st));
+    if (!enc::encode(e->st, *e->enc, n, mel, T_mel, off.data())) return CT_EINVAL;
+    EK(cudaEventRecord(e->eev1, e->st));
+    EK(cudaMemcpyAsync(enc_h, e->enc->enc_h, sizeof(float) * (size_t)off[n] * D, cudaMemcpyDeviceToHost, e->st));
+    EK(cudaStreamSynchronize(e->st));
+    float ms = 0.f;
+    EK(cudaEventElapsedTime(&ms, e->eev0, e->eev1));
+    e->st_acc.enc_ms += ms;
+    e->st_acc.enc_utts += n;
+    for (int b = 0; b < n; ++b) { T_enc[b] = off[b + 1] - off[b]; e->st_acc.enc_frames += T_mel[b]; }
+    return CT_OK;
 }
 
 extern "C" int ct_engine_run(ct_engine *e) {
@@ -909,12 +993,16 @@ extern "C" int ct_engine_run(ct_engine *e) {
     }
 }
 
-extern "C" int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const float *enc_h, int T_enc, int forced_len) {
-    if (!e || !enc_h || T_enc <= 0 || T_enc > CROSS_PAGES * PR || forced_len < 0) return CT_EINVAL;
-    if (T_enc > e->enc_rows_cap) return CT_EINVAL;
+// An utterance of T_enc encoder rows that could ever be admitted.
+static bool admissible(const ct_engine *e, int T_enc, int forced_len) {
+    if (T_enc <= 0 || T_enc > CROSS_PAGES * PR || forced_len < 0 || T_enc > e->enc_rows_cap) return false;
     const int gen_max = forced_len > 0 ? forced_len : MAX_SEQ - e->cfg.n_prompt;
     const int need = (std::min(MAX_SEQ, e->cfg.n_prompt + gen_max) + PR - 1) / PR + (T_enc + PR - 1) / PR;
-    if (need > e->n_pages) return CT_EINVAL;   // could never be admitted
+    return need <= e->n_pages;
+}
+
+extern "C" int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const float *enc_h, int T_enc, int forced_len) {
+    if (!e || !enc_h || !admissible(e, T_enc, forced_len)) return CT_EINVAL;
     Pending p;
     p.id = utt_id;
     p.enc.assign(enc_h, enc_h + (size_t)T_enc * D);
@@ -998,6 +1086,13 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
     cudaEventDestroy(e->aev0);
     cudaEventDestroy(e->aev1);
     for (auto ev : e->marks) cudaEventDestroy(ev);
+    if (e->eev0) cudaEventDestroy(e->eev0);
+    if (e->eev1) cudaEventDestroy(e->eev1);
+    if (e->enc) {
+        for (int l = 0; l < ENC_N; ++l) { cudaFree(e->enc->w.L[l].qkv_w); cudaFree(e->enc->w.L[l].qkv_b); }
+        enc::state_free(*e->enc);
+        delete e->enc;
+    }
     cudaStreamDestroy(e->st);
     for (void *p : e->owned) cudaFree(p);
     delete e;
@@ -1120,6 +1215,57 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     e->slot_pages.assign(S, {});
     e->slot_steps.assign(S, 0);
     e->slot_tenc.assign(S, 0);
+    EK(cudaEventCreate(&e->eev0));
+    EK(cudaEventCreate(&e->eev1));
+    // packed encoder, when the blob carries the encoder weights
+    if (cfg.enc_max_utts >= 0 && ew(e, w->enc[0].ff1_w1) && ew(e, w->s0w) && ew(e, w->prw)) {
+        const int ED = ENC_D, EFF = ENC_FF;
+        enc::State *st = new enc::State();
+        e->enc = st;
+        enc::Weights_ &ww = st->w;
+        ww.s0w = ew(e, w->s0w); ww.s0b = ew(e, w->s0b); ww.s2w = ew(e, w->s2w); ww.s2b = ew(e, w->s2b);
+        ww.s3w = ew_matrix(e, w->s3w, (size_t)SUB_CH * SUB_CH); ww.s3b = ew(e, w->s3b);
+        ww.s5w = ew(e, w->s5w); ww.s5b = ew(e, w->s5b);
+        ww.s6w = ew_matrix(e, w->s6w, (size_t)SUB_CH * SUB_CH); ww.s6b = ew(e, w->s6b);
+        ww.sow = ew_matrix(e, w->sow, (size_t)ED * SUB_CH * 16); ww.sob = ew(e, w->sob);
+        ww.prw = ew_matrix(e, w->prw, (size_t)D * ED); ww.prb = ew(e, w->prb);
+        bool ok = ww.s0w && ww.s0b && ww.s2w && ww.s3w && ww.s5w && ww.s6w && ww.sow && ww.prw;
+        for (int l = 0; l < ENC_N && ok; ++l) {
+            const ELayer &s = w->enc[l];
+            enc::Layer &L = ww.L[l];
+            L.ff1_lnw = ew(e, s.ff1_lnw); L.ff1_lnb = ew(e, s.ff1_lnb);
+            L.ff1_w1 = ew_matrix(e, s.ff1_w1, (size_t)EFF * ED); L.ff1_b1 = ew(e, s.ff1_b1);
+            L.ff1_w2 = ew_matrix(e, s.ff1_w2, (size_t)ED * EFF); L.ff1_b2 = ew(e, s.ff1_b2);
+            L.sa_lnw = ew(e, s.sa_lnw); L.sa_lnb = ew(e, s.sa_lnb);
+            L.sa_pw = ew_matrix(e, s.sa_pw, (size_t)ED * ED);
+            L.sa_ow = ew_matrix(e, s.sa_ow, (size_t)ED * ED); L.sa_ob = ew(e, s.sa_ob);
+            L.sa_pbu = ew(e, s.sa_pbu); L.sa_pbv = ew(e, s.sa_pbv);
+            L.cv_lnw = ew(e, s.cv_lnw); L.cv_lnb = ew(e, s.cv_lnb);
+            L.cv_pw1w = ew_matrix(e, s.cv_pw1w, (size_t)2 * ED * ED); L.cv_pw1b = ew(e, s.cv_pw1b);
+            L.cv_dww = ew(e, s.cv_dww); L.cv_dwb = ew(e, s.cv_dwb);
+            L.cv_bnw = ew(e, s.cv_bnw); L.cv_bnb = ew(e, s.cv_bnb); L.cv_bnm = ew(e, s.cv_bnmean);
+            L.cv_bnv = ew(e, s.cv_bnvar);
+            L.cv_pw2w = ew_matrix(e, s.cv_pw2w, (size_t)ED * ED); L.cv_pw2b = ew(e, s.cv_pw2b);
+            L.ff2_lnw = ew(e, s.ff2_lnw); L.ff2_lnb = ew(e, s.ff2_lnb);
+            L.ff2_w1 = ew_matrix(e, s.ff2_w1, (size_t)EFF * ED); L.ff2_b1 = ew(e, s.ff2_b1);
+            L.ff2_w2 = ew_matrix(e, s.ff2_w2, (size_t)ED * EFF); L.ff2_b2 = ew(e, s.ff2_b2);
+            L.out_lnw = ew(e, s.out_lnw); L.out_lnb = ew(e, s.out_lnb);
+            const bf16 *q = ew(e, s.sa_qw), *k = ew(e, s.sa_kw), *v = ew(e, s.sa_vw);
+            const bf16 *qb = ew(e, s.sa_qb), *kb = ew(e, s.sa_kb), *vb = ew(e, s.sa_vb);
+            ok = q && k && v && qb && kb && vb && L.ff1_w1 && L.ff1_w2 && L.sa_pw && L.sa_ow && L.cv_pw1w &&
+                 L.cv_pw2w && L.ff2_w1 && L.ff2_w2 && L.out_lnw && L.cv_dww;
+            if (!ok) break;
+            if (dalloc(&L.qkv_w, (size_t)3 * ED * ED) || dalloc(&L.qkv_b, (size_t)3 * ED)) { ok = false; break; }
+            const bf16 *parts[3] = {q, k, v}, *bparts[3] = {qb, kb, vb};
+            for (int j = 0; j < 3; ++j) {
+                EK(cudaMemcpy(L.qkv_w + (size_t)j * ED * ED, parts[j], sizeof(bf16) * ED * ED, cudaMemcpyDeviceToDevice));
+                EK(cudaMemcpy(L.qkv_b + (size_t)j * ED, bparts[j], sizeof(bf16) * ED, cudaMemcpyDeviceToDevice));
+            }
+        }
+        const int mu = cfg.enc_max_utts > 0 ? cfg.enc_max_utts : 64;
+        const int mf = cfg.enc_max_frames > 0 ? cfg.enc_max_frames : 64 * 3001;
+        if (!ok || !enc::state_alloc(*st, mu, mf, cfg.precision != 0)) { ct_engine_destroy(e); return CT_ENOMEM; }
+    }
     EK(cudaDeviceSynchronize());
     *out = e;
     return CT_OK;

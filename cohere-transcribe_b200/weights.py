@@ -20,8 +20,10 @@ from __future__ import annotations
 
 import ctypes
 import json
+import os
 import struct
 import zlib
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -269,9 +271,16 @@ def make_blob(dims: dict = FULL_DIMS, seed: int = 0, parts=("enc", "dec")) -> We
     shift = (-raw.ctypes.data // 2) % 128          # align the base to 256 bytes
     blob = raw[shift:shift + total]
     wb = WeightBlob(dims=dims, blob=blob, parts=tuple(parts))
-    for (name, key, shape, init), off in zip(specs, offs):
-        n = int(np.prod(shape))
-        blob[off:off + n] = _draw(seed, name, shape, init, dims)
+
+    def fill(i):
+        name, key, shape, init = specs[i]
+        blob[offs[i]:offs[i] + int(np.prod(shape))] = _draw(seed, name, shape, init, dims)
+
+    # tensors are drawn independently (one generator per name), so threads
+    # give the same blob as a serial fill
+    with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as pool:
+        list(pool.map(fill, range(len(specs))))
+    for (name, key, shape, _init), off in zip(specs, offs):
         wb.index[name] = (off, tuple(shape), key)
     wb._raw = raw  # keep the allocation alive
     return wb

@@ -52,6 +52,8 @@ typedef struct {
                             every layer (per-kernel-class device times in ct_engine_stats); the
                             event nodes serialise their neighbours, so timed runs leave this 0 */
     int no_pdl;          /* 1 = launch step kernels without programmatic dependent launch */
+    int enc_max_utts;    /* encoder batch: utterances (default 64; < 0 = no encoder) */
+    int enc_max_frames;  /* encoder batch: log-mel frames in total (default 64 x 3001, 30 s each) */
 } ct_engine_config;
 
 typedef struct {
@@ -70,6 +72,18 @@ void ct_engine_destroy(ct_engine *e);
  * as the forced_len-th generated token (natural EOS before it is ignored);
  * forced_len == 0 decodes until EOS or MAX_SEQ. */
 int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const float *enc_h, int T_enc, int forced_len);
+
+/* Encode n utterances (host log-mel mel[b] = [N_MELS][T_mel[b]], the layout
+ * compute_mel writes, transcribe.c:177-214) with the packed Conformer encoder
+ * (model.h:573-609).  enc_h (host) receives the encoder outputs of all
+ * utterances back to back, fp32 [sum T_enc, DEC_D]; T_enc[b] their lengths
+ * (transcribe.c:268-271).  At most enc_max_utts / enc_max_frames per call. */
+int ct_engine_encode(ct_engine *e, int n, const float *const *mel, const int *T_mel, float *enc_h, int *T_enc);
+
+/* Queue one utterance from its log-mel [N_MELS][T_mel] (host).  Queued
+ * utterances are encoded in packed batches by ct_engine_step / ct_engine_run
+ * and then decoded like ct_engine_submit_encoded ones. */
+int ct_engine_submit_mel(ct_engine *e, long long utt_id, const float *mel, int T_mel, int forced_len);
 
 /* Run up to n_steps packed steps (admitting queued utterances when slots and
  * pages allow).  Returns the number of sequences still queued or live, or a
@@ -99,6 +113,8 @@ typedef struct {
     long long attn_launches; /* self + cross attention launches (main kernel, per layer) */
     long long ffn_launches;
     long long kernel_launches; /* kernels of this library launched (graph kernel nodes + admission) */
+    double enc_ms;           /* encoder batches (subsampling + 48 Conformer layers + projection) */
+    long long enc_utts, enc_frames;
 } ct_engine_stats_t;
 int ct_engine_stats(ct_engine *e, ct_engine_stats_t *out);
 
