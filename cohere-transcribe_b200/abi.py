@@ -74,6 +74,7 @@ SIGNATURES = {
     "ct_engine_status": (_int, [_vp]),
     "ct_engine_profile_report": (_int, [_vp, _vp, _int]),
     "ct_engine_encode": (_int, [_vp, _int, _vp, _vp, _vp, _vp]),
+    "ct_linear_bf16": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _vp]),
     "ct_engine_submit_mel": (_int, [_vp, ctypes.c_longlong, _vp, _int, _int]),
 }
 

@@ -527,3 +527,20 @@ extern "C" int ct_device_status(void) {
     CT_CHECK(cudaMemcpyToSymbol(g_ct_status, &zero, sizeof(int)));
     return v;
 }
+
+// Extension (not in the reference ABI): the library's tensor-core GEMM on
+// caller-held bf16 activation planes; Y = act(X W^T + b), fp32 out.
+extern "C" int ct_linear_bf16(float *Y, int ldy, const uint16_t *X_hi, const uint16_t *X_lo, const uint16_t *W,
+                              const uint16_t *bias, int T, int K, int N, int act, void *stream) {
+    if (!Y || !X_hi || !W || T <= 0 || N <= 0 || K <= 0 || (K & 7) || ldy < N || act < 0 || act > 2) return -1;
+    if (((uintptr_t)X_hi | (uintptr_t)X_lo | (uintptr_t)W) & 15) return -1;
+    GemmEpilogue ep;
+    ep.epi = act == 1 ? EPI_SILU : act == 2 ? EPI_RELU : EPI_STORE;
+    ep.bias = reinterpret_cast<const bf16 *>(bias);
+    ep.Y = Y;
+    ep.ldy = ldy;
+    ep.x_rows = T;
+    gemm_bf16(static_cast<cudaStream_t>(stream), reinterpret_cast<const bf16 *>(W), N, K,
+              reinterpret_cast<const bf16 *>(X_hi), reinterpret_cast<const bf16 *>(X_lo), T, ep, false);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}

@@ -50,6 +50,8 @@ struct Batch {
     int *row_utt1, *row_utt2, *row_utt3;   // packed row -> utterance, per stage
     int R1, R2, R3;                // total rows per stage
     int T_max;                     // max T_enc of the batch
+    const int *qtile;              // relative-position attention work list: utterance << 16 | first query row
+    int n_qtiles;
 };
 
 // ------------------------------------------------------------ kernels -----
@@ -144,85 +146,182 @@ __global__ void __launch_bounds__(256) ln_enc(const float *x, int R, const bf16 
     }
 }
 
-// Relative-position attention over packed rows (backends/cpu/backend.c:262-295):
-// one warp per (row, head), online softmax over 32-key chunks of the row's own
-// utterance.  QKV rows hold [Q | K | V] (stride 3D); P is the projected table
-// of 2*T_max - 1 rows; the key k / query q term reads P[k - q + T_max - 1].
-// Output: bf16 hi/lo planes [R, D].
-__global__ void __launch_bounds__(128) relpos_packed(const float *QKV, const float *P, Batch b, const bf16 *pbu,
-                                                     const bf16 *pbv, bf16 *hi, bf16 *lo) {
-    __shared__ __align__(16) float qu_s[4][DK];
-    __shared__ __align__(16) float qv_s[4][DK];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 4 + warp, h = blockIdx.y;
-    if (row >= b.R3) return;
-    const int u = b.row_utt3[row];
+// Relative-position attention over packed rows (backends/cpu/backend.c:262-295),
+// fp32 throughout.  One CTA per (query tile of RQ rows of one utterance, head);
+// key tiles of RQ keys; the DK = 160 dimensions are staged through shared
+// memory in chunks of RC.  Thread (ty, tx) of 16 x 16 owns a 4 x 4 block of
+// the score tile: queries ty*4 + i, keys tx*4 + j.  Both score terms
+//   AC[q][k] = (Q[q] + u) . K[k]          BD[q][k] = (Q[q] + v) . P[k - q + T_max - 1]
+// are accumulated together; the P rows a tile needs form a band of 2*RQ - 1
+// consecutive rows (relative offset k - q from -(RQ-1) to RQ-1), of which a
+// thread's block reads 7 consecutive ones.  Online softmax per query row (the
+// 16 threads of a row are 16 consecutive lanes), probabilities to shared
+// memory, then O[q][c] += p[q][k] V[k][c] with thread (ty, tx) owning rows
+// ty*4 + i and columns tx + 16*jj.  QKV rows hold [Q | K | V] (stride 3D); P
+// is the projected table of 2*T_max - 1 rows.  Output: bf16 hi/lo planes.
+constexpr int RQ = 64, RC = 32, RPAD = 4;
+constexpr int RP_ROWS = 2 * RQ;   // band of 2*RQ - 1 rows, padded to a multiple of 4
+struct RelposSmem {
+    union {
+        struct {
+            float qu[RC][RQ + RPAD], qv[RC][RQ + RPAD], k[RC][RQ + RPAD], p[RC][RP_ROWS + RPAD];
+        } c;                       // score phase: one chunk of dimensions, transposed (d-major)
+        float v[RQ][DK];           // value phase
+    } u;
+    float pr[RQ][RQ + RPAD];       // probabilities of the key tile
+};
+
+__global__ void __launch_bounds__(256) relpos_flash(const float *QKV, const float *P, Batch b, const bf16 *pbu,
+                                                    const bf16 *pbv, bf16 *hi, bf16 *lo) {
+    extern __shared__ __align__(16) uint8_t relpos_raw[];
+    RelposSmem &sm = *reinterpret_cast<RelposSmem *>(relpos_raw);
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int h = blockIdx.y;
+    const int wq = b.qtile[blockIdx.x];
+    const int u = wq >> 16, q0 = wq & 0xFFFF;
     const int base = b.r3_off[u];
     const int T = b.r3_off[u + 1] - base;
-    const int q = row - base;
-    float *qu = qu_s[warp], *qv = qv_s[warp];
-    for (int d = lane; d < DK; d += 32) {
-        const float x = QKV[(size_t)row * 3 * D + h * DK + d];
-        qu[d] = x + bf2f(pbu[h * DK + d]);
-        qv[d] = x + bf2f(pbv[h * DK + d]);
-    }
-    __syncwarp();
+    const int Tm = b.T_max, PL = 2 * Tm - 1;
     const float scale = 1.0f / sqrtf((float)DK);
-    float m = -INFINITY, l = 0.0f, o[DK / 32];
+    const size_t ld = (size_t)3 * D;
+
+    float o[4][DK / 16];
+    float m[4], l[4];
 #pragma unroll
-    for (int j = 0; j < DK / 32; ++j) o[j] = 0.0f;
-    for (int k0 = 0; k0 < T; k0 += 32) {
-        const int k = k0 + lane;
-        float sc = -INFINITY;
-        if (k < T) {
-            const float4 *kp = reinterpret_cast<const float4 *>(QKV + (size_t)(base + k) * 3 * D + D + h * DK);
-            const float4 *pp = reinterpret_cast<const float4 *>(P + (size_t)(k - q + b.T_max - 1) * D + h * DK);
-            const float4 *up = reinterpret_cast<const float4 *>(qu);
-            const float4 *vp = reinterpret_cast<const float4 *>(qv);
-            float ac = 0.0f, bd = 0.0f;
-#pragma unroll 8
-            for (int i = 0; i < DK / 4; ++i) {
-                const float4 kv = kp[i], pv = pp[i], a = up[i], c = vp[i];
-                ac += a.x * kv.x; ac += a.y * kv.y; ac += a.z * kv.z; ac += a.w * kv.w;
-                bd += c.x * pv.x; bd += c.y * pv.y; bd += c.z * pv.z; bd += c.w * pv.w;
-            }
-            sc = ac * scale + bd * scale;
-        }
-        const float mn = fmaxf(m, warp_max(sc));
-        const float corr = expf(m - mn);
-        const float p = k < T ? expf(sc - mn) : 0.0f;
-        l = l * corr + warp_sum(p);
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
 #pragma unroll
-        for (int j = 0; j < DK / 32; ++j) o[j] *= corr;
-        const int kn = min(32, T - k0);
-        for (int kk0 = 0; kk0 < kn; kk0 += 8) {
-            float vv[8][DK / 32];
+        for (int jj = 0; jj < DK / 16; ++jj) o[i][jj] = 0.0f;
+    }
+
+    for (int k0 = 0; k0 < T; k0 += RQ) {
+        float sc[4][4];
 #pragma unroll
-            for (int t8 = 0; t8 < 8; ++t8) {
-                const int kk = kk0 + t8;
-                const float *vrow = QKV + (size_t)(base + k0 + (kk < kn ? kk : 0)) * 3 * D + 2 * D + h * DK;
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < DK / 32; ++j) vv[t8][j] = vrow[lane + 32 * j];
-            }
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+        // band row m <-> relative offset (k - q) = (k0 - q0) - (RQ - 1) + m
+        const int rb = (k0 - q0) - (RQ - 1) + Tm - 1;
+        for (int d0 = 0; d0 < DK; d0 += RC) {
+            // ---- stage the chunk [d0, d0 + RC) of Q+u, Q+v, K (RQ rows) and the P band
+            {
+                const int r = tid >> 2, dd = (tid & 3) * 8;   // 64 rows x 4 groups of 8 dims
+                const int q = q0 + r, k = k0 + r;
+                float4 qa = make_float4(0.f, 0.f, 0.f, 0.f), qb = qa, ka = qa, kb2 = qa;
+                if (q < T) {
+                    const float4 *src = reinterpret_cast<const float4 *>(QKV + (size_t)(base + q) * ld + h * DK + d0 + dd);
+                    qa = src[0]; qb = src[1];
+                }
+                if (k < T) {
+                    const float4 *src = reinterpret_cast<const float4 *>(QKV + (size_t)(base + k) * ld + D + h * DK + d0 + dd);
+                    ka = src[0]; kb2 = src[1];
+                }
+                const float qv8[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                const float kv8[8] = {ka.x, ka.y, ka.z, ka.w, kb2.x, kb2.y, kb2.z, kb2.w};
 #pragma unroll
-            for (int t8 = 0; t8 < 8; ++t8) {
-                const int kk = kk0 + t8;
-                const float pk = __shfl_sync(0xffffffffu, p, kk < 32 ? kk : 0);
-                if (kk < kn) {
-#pragma unroll
-                    for (int j = 0; j < DK / 32; ++j) o[j] += pk * vv[t8][j];
+                for (int e = 0; e < 8; ++e) {
+                    const int d = dd + e;
+                    sm.u.c.qu[d][r] = qv8[e] + bf2f(pbu[h * DK + d0 + d]);
+                    sm.u.c.qv[d][r] = qv8[e] + bf2f(pbv[h * DK + d0 + d]);
+                    sm.u.c.k[d][r] = kv8[e];
+                }
+                // P band: 2*RQ - 1 rows; rows outside the table (only reached by
+                // padded queries or keys, whose scores are discarded) read as 0
+                for (int idx = tid; idx < RP_ROWS * (RC / 4); idx += 256) {
+                    const int mrow = idx / (RC / 4), d4 = (idx % (RC / 4)) * 4;
+                    const int pr = rb + mrow;
+                    float4 pv = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (mrow < 2 * RQ - 1 && pr >= 0 && pr < PL)
+                        pv = *reinterpret_cast<const float4 *>(P + (size_t)pr * D + h * DK + d0 + d4);
+                    sm.u.c.p[d4 + 0][mrow] = pv.x;
+                    sm.u.c.p[d4 + 1][mrow] = pv.y;
+                    sm.u.c.p[d4 + 2][mrow] = pv.z;
+                    sm.u.c.p[d4 + 3][mrow] = pv.w;
                 }
             }
+            __syncthreads();
+            // ---- scores: block rows ty*4+i, keys tx*4+j; band index
+            // (tx*4 + j) - (ty*4 + i) + RQ - 1 = mb + (j - i) + 3
+            const int mb = (tx - ty) * 4 + RQ - 4;
+#pragma unroll 4
+            for (int d = 0; d < RC; ++d) {
+                const float4 a = *reinterpret_cast<const float4 *>(&sm.u.c.qu[d][ty * 4]);
+                const float4 c = *reinterpret_cast<const float4 *>(&sm.u.c.qv[d][ty * 4]);
+                const float4 kk = *reinterpret_cast<const float4 *>(&sm.u.c.k[d][tx * 4]);
+                const float4 p0 = *reinterpret_cast<const float4 *>(&sm.u.c.p[d][mb]);
+                const float4 p1 = *reinterpret_cast<const float4 *>(&sm.u.c.p[d][mb + 4]);
+                const float av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
+                const float kv[4] = {kk.x, kk.y, kk.z, kk.w};
+                const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) sc[i][j] += av[i] * kv[j] + cv[i] * pv[j - i + 3];
+            }
+            __syncthreads();
         }
-        m = mn;
+        // ---- online softmax over this key tile
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float rmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const bool valid = k0 + tx * 4 + j < T;
+                sc[i][j] = valid ? sc[i][j] * scale : -INFINITY;
+                rmax = fmaxf(rmax, sc[i][j]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+            const float mn = fmaxf(m[i], rmax);   // finite: key k0 is valid
+            const float corr = expf(m[i] - mn);
+            float rs = 0.0f;
+            float pj[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) { pj[j] = expf(sc[i][j] - mn); rs += pj[j]; }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
+            l[i] = l[i] * corr + rs;
+            m[i] = mn;
+#pragma unroll
+            for (int jj = 0; jj < DK / 16; ++jj) o[i][jj] *= corr;
+            *reinterpret_cast<float4 *>(&sm.pr[ty * 4 + i][tx * 4]) = make_float4(pj[0], pj[1], pj[2], pj[3]);
+        }
+        // ---- value tile (aliases the chunk buffers, free after the last sync)
+        for (int idx = tid; idx < RQ * (DK / 4); idx += 256) {
+            const int r = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
+            float4 vv = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + r < T) vv = *reinterpret_cast<const float4 *>(QKV + (size_t)(base + k0 + r) * ld + 2 * D + h * DK + c4);
+            *reinterpret_cast<float4 *>(&sm.u.v[r][c4]) = vv;
+        }
+        __syncthreads();
+        const int kn = min(RQ, T - k0);
+        for (int kk = 0; kk < kn; ++kk) {
+            float pq[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pq[i] = sm.pr[ty * 4 + i][kk];
+#pragma unroll
+            for (int jj = 0; jj < DK / 16; ++jj) {
+                const float vv = sm.u.v[kk][tx + 16 * jj];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i][jj] += pq[i] * vv;
+            }
+        }
+        __syncthreads();
     }
 #pragma unroll
-    for (int j = 0; j < DK / 32; ++j) {
-        const float v = o[j] / l;
-        const size_t idx = (size_t)row * D + h * DK + lane + 32 * j;
-        const bf16 hb = __float2bfloat16_rn(v);
-        hi[idx] = hb;
-        if (lo) lo[idx] = __float2bfloat16_rn(v - __bfloat162float(hb));
+    for (int i = 0; i < 4; ++i) {
+        const int q = q0 + ty * 4 + i;
+        if (q >= T) continue;
+        const float inv = 1.0f / l[i];
+#pragma unroll
+        for (int jj = 0; jj < DK / 16; ++jj) {
+            const float v = o[i][jj] * inv;
+            const size_t idx = (size_t)(base + q) * D + h * DK + tx + 16 * jj;
+            const bf16 hb = __float2bfloat16_rn(v);
+            hi[idx] = hb;
+            if (lo) lo[idx] = __float2bfloat16_rn(v - __bfloat162float(hb));
+        }
     }
 }
 
@@ -267,7 +366,26 @@ struct State {
     int *tab = nullptr;                    // device tables
     std::vector<int> htab;
     std::vector<void *> owned;
+    // profile mode: events recorded between kernel groups, with the label of
+    // the group each closes (labels[0] is unused)
+    bool prof = false;
+    std::vector<cudaEvent_t> ev;
+    std::vector<const char *> labels;
+    int n_marks = 0;
 };
+
+static void mark(cudaStream_t s, State &st, const char *label) {
+    if (!st.prof) return;
+    if (st.n_marks >= (int)st.ev.size()) {
+        cudaEvent_t e;
+        CT_CHECK(cudaEventCreate(&e));
+        st.ev.push_back(e);
+        st.labels.push_back(nullptr);
+    }
+    st.labels[st.n_marks] = label;
+    CT_CHECK(cudaEventRecord(st.ev[st.n_marks], s));
+    ++st.n_marks;
+}
 
 static int t1_of(int t) { return (t + 1) / 2; }
 
@@ -296,7 +414,7 @@ static bool state_alloc(State &st, int max_utts, int max_frames, bool two) {
     bool ok = ealloc(st, &st.mel, (size_t)max_frames * F0) && ealloc(st, &st.s1, s1) && ealloc(st, &st.s2, s2) &&
               ealloc(st, &st.x, R * D) && ealloc(st, &st.qkv, R * 3 * D) && ealloc(st, &st.enc_h, R * DEC_D) &&
               ealloc(st, &st.pos, (size_t)(2 * st.T_cap) * D) && ealloc(st, &st.P, (size_t)(2 * st.T_cap) * D) &&
-              ealloc(st, &st.tab, (size_t)8 * max_utts + 8 + st.R1_max + st.R2_max + st.R3_max);
+              ealloc(st, &st.tab, (size_t)9 * max_utts + 8 + st.R1_max + st.R2_max + st.R3_max + st.R3_max / RQ + 1);
     const size_t hidn = std::max((size_t)R * FF, (size_t)st.R2_max * F2 * C);
     for (int k = 0; k < (two ? 2 : 1); ++k)
         ok = ok && ealloc(st, &st.xa[k], R * D) && ealloc(st, &st.hid[k], hidn) && ealloc(st, &st.ap[k], R * D) &&
@@ -307,6 +425,8 @@ static bool state_alloc(State &st, int max_utts, int max_frames, bool two) {
 static void state_free(State &st) {
     for (void *p : st.owned) cudaFree(p);
     st.owned.clear();
+    for (cudaEvent_t e : st.ev) cudaEventDestroy(e);
+    st.ev.clear();
 }
 
 static inline int grid_of(size_t n) {
@@ -345,8 +465,19 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         return false;
     const int R1 = r1[n], R2 = r2[n], R3 = r3[n];
     // device table layout: T_mel[n] mel_off[n] r1[n+1] r2[n+1] r3[n+1] utt1[R1] utt2[R2] utt3[R3]
+    // attention work list: query tiles, longest utterances first
+    std::vector<int> qt;
+    {
+        std::vector<int> order(n);
+        for (int b = 0; b < n; ++b) order[b] = b;
+        std::stable_sort(order.begin(), order.end(),
+                         [&](int a, int c) { return r3[a + 1] - r3[a] > r3[c + 1] - r3[c]; });
+        for (int b : order)
+            for (int q0 = 0; q0 < r3[b + 1] - r3[b]; q0 += RQ) qt.push_back(b << 16 | q0);
+    }
+    const int NQ = (int)qt.size();
     std::vector<int> &h = st.htab;
-    h.assign((size_t)5 * n + 3 + R1 + R2 + R3, 0);
+    h.assign((size_t)5 * n + 3 + R1 + R2 + R3 + NQ, 0);
     int *hp = h.data();
     memcpy(hp, T_mel, sizeof(int) * n);
     memcpy(hp + n, mel_off.data(), sizeof(int) * n);
@@ -359,6 +490,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         for (int r = r2[b]; r < r2[b + 1]; ++r) u2[r] = b;
         for (int r = r3[b]; r < r3[b + 1]; ++r) u3[r] = b;
     }
+    memcpy(u3 + R3, qt.data(), sizeof(int) * NQ);
     CT_CHECK(cudaMemcpyAsync(st.tab, hp, sizeof(int) * h.size(), cudaMemcpyHostToDevice, s));
     for (int b = 0; b < n; ++b)
         CT_CHECK(cudaMemcpyAsync(st.mel + mel_off[b], mel[b], sizeof(float) * F0 * T_mel[b], cudaMemcpyHostToDevice, s));
@@ -374,8 +506,19 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     bt.row_utt3 = bt.row_utt2 + R2;
     bt.R1 = R1; bt.R2 = R2; bt.R3 = R3;
     bt.T_max = T_max;
+    bt.qtile = bt.row_utt3 + R3;
+    bt.n_qtiles = NQ;
+    static thread_local int relpos_dev = -1;
+    int dev = 0;
+    CT_CHECK(cudaGetDevice(&dev));
+    if (relpos_dev != dev) {
+        CT_CHECK(cudaFuncSetAttribute(relpos_flash, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(RelposSmem)));
+        relpos_dev = dev;
+    }
     const Weights_ &w = st.w;
     bf16 *hidp[2] = {st.hid[0], st.hid[1]};
+    st.n_marks = 0;
+    mark(s, st, "");
     // ---- subsampling (backends/cpu/backend.c:188-229), channels last ----
     conv0_packed<<<grid_of((size_t)R1 * F1 * C), 256, 0, s>>>(st.mel, bt, w.s0w, w.s0b, st.s1);
     dw_packed<<<grid_of((size_t)R2 * F2 * C), 256, 0, s>>>(st.s1, F1, bt.r1_off, bt.r2_off, bt.row_utt2, R2, w.s2w,
@@ -394,10 +537,12 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     GemmEpilogue eo;
     eo.bias = w.sob; eo.Y = st.x; eo.ldy = D;
     egemm_enc(s, st, w.sow, D, C * F3, hidp, R3, st.R3_max, eo);
+    mark(s, st, "enc_subsampling");
     // ---- relative positional table for T_max (backends/cpu/backend.c:231-242) ----
     const int PL = 2 * T_max - 1;
     make_rel_pos_emb(s, st.pos, T_max, D);
     split_fp32_to_bf16(s, st.pos, PL, D, D, st.posp[0], st.two ? st.posp[1] : nullptr, D);
+    mark(s, st, "enc_pos_table");
     bf16 *xap[2] = {st.xa[0], st.xa[1]}, *app[2] = {st.ap[0], st.ap[1]};
     bf16 *lo_a = st.two ? st.xa[1] : nullptr, *lo_h = st.two ? st.hid[1] : nullptr, *lo_p = st.two ? st.ap[1] : nullptr;
     const int RT = st.R3_max;
@@ -406,49 +551,66 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         const Layer &L = w.L[l];
         // FFN1: x += 0.5 * W2 silu(W1 LN(x) + b1) + b2
         ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.ff1_lnw, L.ff1_lnb, nullptr, st.xa[0], lo_a);
+        mark(s, st, "enc_layernorm");
         GemmEpilogue f1;
         f1.epi = EPI_BF16; f1.act = 1; f1.bias = L.ff1_b1; f1.Ybf = st.hid[0]; f1.Ybf_lo = lo_h; f1.ldy = FF;
         egemm_enc(s, st, L.ff1_w1, FF, D, xap, R3, RT, f1);
+        mark(s, st, "enc_gemm_ffn1");
         GemmEpilogue f2;
         f2.epi = EPI_FMADD; f2.scale = 0.5f; f2.bias = L.ff1_b2; f2.Y = st.x; f2.ldy = D;
         egemm_enc(s, st, L.ff1_w2, D, FF, hidp, R3, RT, f2);
+        mark(s, st, "enc_gemm_ffn2");
         // relative-position self-attention: x += Wo attn(LN(x)) + bo
         ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.sa_lnw, L.sa_lnb, nullptr, st.xa[0], lo_a);
+        mark(s, st, "enc_layernorm");
         GemmEpilogue eq;
         eq.bias = L.qkv_b; eq.Y = st.qkv; eq.ldy = 3 * D;
         egemm_enc(s, st, L.qkv_w, 3 * D, D, xap, R3, RT, eq);
+        mark(s, st, "enc_gemm_qkv");
         GemmEpilogue ep;
         ep.Y = st.P; ep.ldy = D;
         egemm_enc(s, st, L.sa_pw, D, D, st.posp, PL, 2 * st.T_cap, ep);
-        relpos_packed<<<dim3((R3 + 3) / 4, H), 128, 0, s>>>(st.qkv, st.P, bt, L.sa_pbu, L.sa_pbv, st.ap[0], lo_p);
+        mark(s, st, "enc_gemm_pos");
+        relpos_flash<<<dim3(NQ, H), 256, sizeof(RelposSmem), s>>>(st.qkv, st.P, bt, L.sa_pbu, L.sa_pbv, st.ap[0], lo_p);
+        mark(s, st, "enc_relpos_attn");
         GemmEpilogue eo2;
         eo2.epi = EPI_FMADD; eo2.scale = 1.0f; eo2.bias = L.sa_ob; eo2.Y = st.x; eo2.ldy = D;
         egemm_enc(s, st, L.sa_ow, D, D, app, R3, RT, eo2);
+        mark(s, st, "enc_gemm_o");
         // conv module: x += pw2(silu(bn(dw(glu(pw1(LN(x)))))))
         ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.cv_lnw, L.cv_lnb, nullptr, st.xa[0], lo_a);
+        mark(s, st, "enc_layernorm");
         GemmEpilogue e1;
         e1.bias = L.cv_pw1b; e1.Y = st.qkv; e1.ldy = 2 * D;
         egemm_enc(s, st, L.cv_pw1w, 2 * D, D, xap, R3, RT, e1);
+        mark(s, st, "enc_gemm_pw1");
         glu_dw_packed<<<grid_of((size_t)R3 * D), 256, 0, s>>>(st.qkv, bt, L.cv_dww, L.cv_dwb, L.cv_bnw, L.cv_bnb,
                                                               L.cv_bnm, L.cv_bnv, st.ap[0], lo_p);
+        mark(s, st, "enc_glu_dwconv");
         GemmEpilogue e2;
         e2.epi = EPI_FMADD; e2.scale = 1.0f; e2.bias = L.cv_pw2b; e2.Y = st.x; e2.ldy = D;
         egemm_enc(s, st, L.cv_pw2w, D, D, app, R3, RT, e2);
+        mark(s, st, "enc_gemm_pw2");
         // FFN2
         ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.ff2_lnw, L.ff2_lnb, nullptr, st.xa[0], lo_a);
+        mark(s, st, "enc_layernorm");
         GemmEpilogue g1 = f1;
         g1.bias = L.ff2_b1;
         egemm_enc(s, st, L.ff2_w1, FF, D, xap, R3, RT, g1);
+        mark(s, st, "enc_gemm_ffn1");
         GemmEpilogue g2 = f2;
         g2.bias = L.ff2_b2;
         egemm_enc(s, st, L.ff2_w2, D, FF, hidp, R3, RT, g2);
+        mark(s, st, "enc_gemm_ffn2");
         // x = LN_out(x); its planes feed the next layer's nothing / the projection
         ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a);
+        mark(s, st, "enc_layernorm");
     }
     // ---- encoder -> decoder projection (model.h:607) ----
     GemmEpilogue pj;
     pj.bias = w.prb; pj.Y = st.enc_h; pj.ldy = DEC_D;
     egemm_enc(s, st, w.prw, DEC_D, D, xap, R3, RT, pj);
+    mark(s, st, "enc_gemm_proj");
     CT_CHECK(cudaGetLastError());
     memcpy(r3_off_out, r3.data(), sizeof(int) * (n + 1));
     return true;

@@ -842,6 +842,19 @@ static int harvest(ct_engine *e) {
     return 0;
 }
 
+// Profile mode: fold the encoder's event marks into the per-label totals.
+static void collect_enc_marks(ct_engine *e) {
+    enc::State &st = *e->enc;
+    if (!st.prof) return;
+    for (int i = 1; i < st.n_marks; ++i) {
+        float t = 0.f;
+        if (cudaEventElapsedTime(&t, st.ev[i - 1], st.ev[i]) != cudaSuccess) continue;
+        auto &acc = e->mark_ms[st.labels[i]];
+        acc.first += t;
+        acc.second += 1;
+    }
+}
+
 static bool admissible(const ct_engine *e, int T_enc, int forced_len);
 
 // Encode up to one encoder batch of queued log-mel utterances and queue their
@@ -868,6 +881,7 @@ static int encode_pending(ct_engine *e) {
     EK(cudaStreamSynchronize(e->st));
     float ms = 0.f;
     EK(cudaEventElapsedTime(&ms, e->eev0, e->eev1));
+    collect_enc_marks(e);
     e->st_acc.enc_ms += ms;
     e->st_acc.enc_utts += n;
     e->st_acc.enc_frames += frames;
@@ -980,6 +994,7 @@ extern "C" int ct_engine_encode(ct_engine *e, int n, const float *const *mel, co
     EK(cudaStreamSynchronize(e->st));
     float ms = 0.f;
     EK(cudaEventElapsedTime(&ms, e->eev0, e->eev1));
+    collect_enc_marks(e);
     e->st_acc.enc_ms += ms;
     e->st_acc.enc_utts += n;
     for (int b = 0; b < n; ++b) { T_enc[b] = off[b + 1] - off[b]; e->st_acc.enc_frames += T_mel[b]; }
@@ -1265,6 +1280,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         const int mu = cfg.enc_max_utts > 0 ? cfg.enc_max_utts : 64;
         const int mf = cfg.enc_max_frames > 0 ? cfg.enc_max_frames : 64 * 3001;
         if (!ok || !enc::state_alloc(*st, mu, mf, cfg.precision != 0)) { ct_engine_destroy(e); return CT_ENOMEM; }
+        st->prof = cfg.profile != 0;
     }
     EK(cudaDeviceSynchronize());
     *out = e;

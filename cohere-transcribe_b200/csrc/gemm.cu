@@ -32,19 +32,12 @@ struct KernelParams {
     GemmEpilogue ep;
 };
 
-__device__ __forceinline__ void apply_epilogue(const GemmEpilogue &ep, int t, int n, float v) {
-    if (ep.row_mask && !ep.row_mask[t]) return;
+// Store one output value for the store-only epilogues (no loads).
+__device__ __forceinline__ void store_epilogue(const GemmEpilogue &ep, int t, int n, float v) {
     switch (ep.epi) {
     case EPI_STORE: ep.Y[(size_t)t * ep.ldy + n] = v; break;
     case EPI_SILU: ep.Y[(size_t)t * ep.ldy + n] = v / (1.0f + expf(-v)); break;
     case EPI_RELU: ep.Y[(size_t)t * ep.ldy + n] = v > 0.0f ? v : 0.0f; break;
-    case EPI_FMADD: ep.Y[(size_t)t * ep.ldy + n] += ep.scale * v; break;
-    case EPI_KVCACHE: {
-        const int slot = ep.pos[t] - 1;
-        if (slot < 0 || slot >= ep.kv_stride) { set_status(CT_STATUS_BAD_ARG); break; }
-        ep.Y[((size_t)t * ep.kv_stride + slot) * ep.ldy + n] = v;
-        break;
-    }
     case EPI_BF16: {
         float a = v;
         if (ep.act == 1) a = v / (1.0f + expf(-v));
@@ -54,25 +47,119 @@ __device__ __forceinline__ void apply_epilogue(const GemmEpilogue &ep, int t, in
         if (ep.Ybf_lo) ep.Ybf_lo[(size_t)t * ep.ldy + n] = __float2bfloat16_rn(a - __bfloat162float(hb));
         break;
     }
-    case EPI_QKV_PAGED: {
-        if (n < ep.qdim) { ep.Y[(size_t)t * ep.ldy + n] = v; break; }
-        const long long off = ep.row_off[t];
-        if (off < 0) break;
-        const int n2 = n - ep.qdim, kv = n2 / ep.kv_width, c = n2 % ep.kv_width;
-        ep.kv_pool[off + (long long)(ep.layer * 2 + kv) * kPageRows * ep.kv_width + c] = __float2bfloat16_rn(v);
-        break;
-    }
-    case EPI_CAKV_PAGED: {
-        const long long off = ep.row_off[t];
-        if (off < 0) break;
-        const int lk = n / ep.kv_width, c = n % ep.kv_width;   // lk = layer*2 + kv
-        ep.kv_pool[off + (long long)lk * kPageRows * ep.kv_width + c] = __float2bfloat16_rn(v);
-        break;
-    }
     case EPI_RELU_FLAT:
         ep.Y[(size_t)(t / ep.flat_f) * ep.ldy + (size_t)n * ep.flat_f + (t % ep.flat_f)] = v > 0.0f ? v : 0.0f;
         break;
     default: break;
+    }
+}
+
+// Epilogue of feature n for tokens t0 .. t0 + tl - 1 (tl <= 16), values v[j]
+// (bias included).  Every load the chunk needs -- row mask, KV positions, page
+// offsets, the old values of an FMADD -- is issued before the first store:
+// the stores may alias those addresses as far as the compiler knows, so
+// interleaving loads and stores would serialise one memory round trip per token.
+__device__ __forceinline__ void epilogue16(const GemmEpilogue &ep, int t0, int tl, int n, const float *v) {
+    bool keep[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) keep[j] = j < tl && (!ep.row_mask || ep.row_mask[t0 + j]);
+    switch (ep.epi) {
+    case EPI_FMADD: {
+        float old[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) old[j] = keep[j] ? ep.Y[(size_t)(t0 + j) * ep.ldy + n] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (keep[j]) ep.Y[(size_t)(t0 + j) * ep.ldy + n] = old[j] + ep.scale * v[j];
+        break;
+    }
+    case EPI_KVCACHE: {
+        int slot[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) slot[j] = keep[j] ? ep.pos[t0 + j] - 1 : 0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (!keep[j]) continue;
+            if (slot[j] < 0 || slot[j] >= ep.kv_stride) { set_status(CT_STATUS_BAD_ARG); continue; }
+            ep.Y[((size_t)(t0 + j) * ep.kv_stride + slot[j]) * ep.ldy + n] = v[j];
+        }
+        break;
+    }
+    case EPI_QKV_PAGED:
+    case EPI_CAKV_PAGED: {
+        const bool qpart = ep.epi == EPI_QKV_PAGED && n < ep.qdim;
+        if (qpart) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (keep[j]) ep.Y[(size_t)(t0 + j) * ep.ldy + n] = v[j];
+            break;
+        }
+        long long off[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) off[j] = keep[j] ? ep.row_off[t0 + j] : -1;
+        // (layer*2 + kv) block of the page and the column inside it
+        const int n2 = ep.epi == EPI_QKV_PAGED ? n - ep.qdim : n;
+        const int lk = ep.epi == EPI_QKV_PAGED ? ep.layer * 2 + n2 / ep.kv_width : n2 / ep.kv_width;
+        const long long col = (long long)lk * kPageRows * ep.kv_width + n2 % ep.kv_width;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (off[j] >= 0) ep.kv_pool[off[j] + col] = __float2bfloat16_rn(v[j]);
+        break;
+    }
+    default:
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (keep[j]) store_epilogue(ep, t0 + j, n, v[j]);
+        break;
+    }
+}
+
+// Epilogue of token t for the four features nf .. nf + 3 (split-K path), the
+// same load-before-store order as epilogue16.
+__device__ __forceinline__ void epilogue_f4(const GemmEpilogue &ep, int t, int nf, int N, const float (&v)[4]) {
+    if (ep.row_mask && !ep.row_mask[t]) return;
+    switch (ep.epi) {
+    case EPI_FMADD: {
+        float old[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) old[i] = nf + i < N ? ep.Y[(size_t)t * ep.ldy + nf + i] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (nf + i < N) ep.Y[(size_t)t * ep.ldy + nf + i] = old[i] + ep.scale * v[i];
+        break;
+    }
+    case EPI_KVCACHE: {
+        const int slot = ep.pos[t] - 1;
+        if (slot < 0 || slot >= ep.kv_stride) { set_status(CT_STATUS_BAD_ARG); break; }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (nf + i < N) ep.Y[((size_t)t * ep.kv_stride + slot) * ep.ldy + nf + i] = v[i];
+        break;
+    }
+    case EPI_QKV_PAGED:
+    case EPI_CAKV_PAGED: {
+        long long off = -1;
+        bool any_kv = false;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) any_kv |= !(ep.epi == EPI_QKV_PAGED && nf + i < ep.qdim);
+        if (any_kv) off = ep.row_off[t];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int n = nf + i;
+            if (n >= N) continue;
+            if (ep.epi == EPI_QKV_PAGED && n < ep.qdim) { ep.Y[(size_t)t * ep.ldy + n] = v[i]; continue; }
+            if (off < 0) continue;
+            const int n2 = ep.epi == EPI_QKV_PAGED ? n - ep.qdim : n;
+            const int lk = ep.epi == EPI_QKV_PAGED ? ep.layer * 2 + n2 / ep.kv_width : n2 / ep.kv_width;
+            ep.kv_pool[off + (long long)lk * kPageRows * ep.kv_width + n2 % ep.kv_width] = __float2bfloat16_rn(v[i]);
+        }
+        break;
+    }
+    default:
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (nf + i < N) store_epilogue(ep, t, nf + i, v[i]);
+        break;
     }
 }
 
@@ -194,8 +281,9 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
                 if (n < p.N) {
                     const int tl = min(32, T_eff - (t0 + c));
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (j < tl) apply_epilogue(p.ep, t0 + c + j, n, v[j] + bias);
+                    for (int j = 0; j < 32; ++j) v[j] += bias;
+                    epilogue16(p.ep, t0 + c, min(16, tl), n, v);
+                    if (tl > 16) epilogue16(p.ep, t0 + c + 16, tl - 16, n, v + 16);
                 }
             }
         }
@@ -241,13 +329,145 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
 #pragma unroll
                 for (int r = 1; r < 16; ++r)
                     if (r < cs) { sum.x += part[r].x; sum.y += part[r].y; sum.z += part[r].z; sum.w += part[r].w; }
-                const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    if (n0 + f0 + i < p.N) apply_epilogue(p.ep, t, n0 + f0 + i, vals[i] + b4[i]);
+                const float vals[4] = {sum.x + b4[0], sum.y + b4[1], sum.z + b4[2], sum.w + b4[3]};
+                epilogue_f4(p.ep, t, n0 + f0, p.N, vals);
             }
         }
         cluster_sync();   // no CTA leaves while another still reads its shared memory
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, NCOLS);
+}
+
+// Persistent form for large T (no K split, no device row count): one CTA per
+// SM walks output tiles tile = blockIdx.x, blockIdx.x + gridDim.x, ...  The
+// TMA producer (warp 0) and the MMA issuer (warp 1) run ahead into the next
+// tile while the epilogue warps (2..5) drain the previous one: the TMEM holds
+// two BN-column accumulators, handed over through acc_full (MMA commit ->
+// epilogue) and acc_empty (4 epilogue warps -> MMA).  Per output element the
+// MMA sequence over K is the one of gemm_tc_kernel, so both forms give
+// bit-identical results.
+template <int BN, bool TWO>
+__global__ void __launch_bounds__(kThreads, 1) gemm_pers_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                                const __grid_constant__ CUtensorMap tmXh,
+                                                                const __grid_constant__ CUtensorMap tmXl,
+                                                                const KernelParams p) {
+    constexpr uint32_t A_BYTES = BM * BK * 2;
+    constexpr uint32_t B_BYTES = BN * BK * 2;
+    constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES * (TWO ? 2 : 1);
+    constexpr uint32_t NCOLS = 2 * BN;   // two accumulators
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int stages = p.stages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.bar_off);
+    uint64_t *empty = full + stages;
+    uint64_t *acc_full = empty + stages;     // [2]
+    uint64_t *acc_empty = acc_full + 2;      // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_n = (p.N + BM - 1) / BM;
+    const int n_tiles = tiles_n * ((p.T + BN - 1) / BN);
+    const int nkb = p.kb_total;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 4); }
+        fence_mbar_init();
+        prefetch_tmap(&tmW);
+        prefetch_tmap(&tmXh);
+        if (TWO) prefetch_tmap(&tmXl);
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, NCOLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+    pdl_trigger();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                const int n0 = (tile % tiles_n) * BM, t0 = (tile / tiles_n) * BN;
+                for (int i = 0; i < nkb; ++i, ++it) {
+                    const int s = (int)(it % (uint32_t)stages);
+                    const uint32_t ph = (it / (uint32_t)stages) & 1u;
+                    if (it >= (uint32_t)stages && !mbar_wait(&empty[s], ph ^ 1u, CT_STATUS_TIMEOUT_FREE)) { ok = false; break; }
+                    uint8_t *a = smem + (size_t)s * STAGE_BYTES;
+                    const int kc = i * BK;
+                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    tma_load_2d(a, &tmW, &full[s], kc, n0);
+                    tma_load_2d(a + A_BYTES, &tmXh, &full[s], kc, t0);
+                    if (TWO) tma_load_2d(a + A_BYTES + B_BYTES, &tmXl, &full[s], kc, t0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(BM, BN);
+            uint32_t it = 0, lt = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++lt) {
+                const uint32_t buf = lt & 1u, use = lt >> 1;
+                if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1u, CT_STATUS_TIMEOUT_FREE)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + buf * BN;
+                for (int i = 0; i < nkb; ++i, ++it) {
+                    const int s = (int)(it % (uint32_t)stages);
+                    const uint32_t ph = (it / (uint32_t)stages) & 1u;
+                    if (!mbar_wait(&full[s], ph, CT_STATUS_TIMEOUT_TMA)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(smem + (size_t)s * STAGE_BYTES);
+                    const uint64_t ad = sw128_desc(a);
+                    const uint64_t bd = sw128_desc(a + A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        mma_bf16(d, ad + 2 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+                    if (TWO) {
+                        const uint64_t ld = sw128_desc(a + A_BYTES + B_BYTES);
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k) mma_bf16(d, ad + 2 * k, ld + 2 * k, idesc, 1u);
+                    }
+                    mma_commit(&empty[s]);
+                }
+                if (ok) mma_commit(&acc_full[buf]);
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        uint32_t lt = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++lt) {
+            const uint32_t buf = lt & 1u, use = lt >> 1;
+            const int n0 = (tile % tiles_n) * BM, t0 = (tile / tiles_n) * BN;
+            bool ok = mbar_wait(&acc_full[buf], use & 1u, CT_STATUS_TIMEOUT_MMA);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+            const int n = n0 + q * 32 + lane;
+            const float bias = (n < p.N && p.ep.bias) ? bf2f(p.ep.bias[n]) : 0.0f;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                if (t0 + c >= p.T) break;   // warp-uniform
+                float v[32];
+                tmem_ld32(tbase + (uint32_t)c, v);
+                if (n < p.N) {
+                    const int tl = min(32, p.T - (t0 + c));
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] += bias;
+                    epilogue16(p.ep, t0 + c, min(16, tl), n, v);
+                    if (tl > 16) epilogue16(p.ep, t0 + c + 16, tl - 16, n, v + 16);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -432,6 +652,38 @@ static void launch_tc(cudaStream_t st, const CUtensorMap &mw, const CUtensorMap 
     CT_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, TWO>, mw, mh, ml, p));
 }
 
+template <int BN, bool TWO>
+static void launch_pers(cudaStream_t st, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml,
+                        KernelParams p, bool pdl) {
+    constexpr int STAGE = BM * BK * 2 + BN * BK * 2 * (TWO ? 2 : 1);
+    p.stages = std::min(std::max(1, (kSmemBudget - 2048) / STAGE), 8);
+    p.nsplit = 1;
+    p.bar_off = p.stages * STAGE;
+    const size_t smem = 1024 + p.bar_off + 8 * (2 * p.stages + 4) + 16;
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    CT_CHECK(cudaGetDevice(&dev));
+    static thread_local int n_sm = 0;
+    if (configured_dev != dev) {
+        CT_CHECK(cudaFuncSetAttribute(gemm_pers_kernel<BN, TWO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kSmemBudget));
+        CT_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+        configured_dev = dev;
+    }
+    const int n_tiles = ((p.N + BM - 1) / BM) * ((p.T + BN - 1) / BN);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min(n_tiles, n_sm));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    CT_CHECK(cudaLaunchKernelEx(&cfg, gemm_pers_kernel<BN, TWO>, mw, mh, ml, p));
+}
+
 void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, const bf16 *X_lo, int T,
                const GemmEpilogue &ep_in, bool allow_split) {
     if (T <= 0 || N <= 0) return;
@@ -448,6 +700,9 @@ void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, c
     const int kbps_final = nsplit > 1 ? kbps : kb_total;
     // X maps use the scratch capacity (or the caller's buffer rows) as the row count
     const long xrows = (X_hi == c->xhi || X_hi == c->xlo) ? (long)(c->x_elems / K) : (ep.x_rows > 0 ? ep.x_rows : (long)T);
+    // large problems without K split or device row count: persistent kernel
+    const bool pers = nsplit == 1 && !ep.T_dev && T > (two ? 64 : 128);
+    if (pers) BN = two ? 128 : 256;
     const CUtensorMap &mw = tmap_bf16(c, W, N, K, BM);
     const CUtensorMap &mh = tmap_bf16(c, X_hi, xrows, K, BN);
     const CUtensorMap &ml = two ? tmap_bf16(c, X_lo, xrows, K, BN) : mh;
@@ -455,6 +710,10 @@ void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, c
     p.N = N; p.K = K; p.T = T; p.kbps = kbps_final; p.kb_total = kb_total; p.stages = 1;
     p.nsplit = nsplit; p.bar_off = 0;
     p.ep = ep;
+    if (pers) {
+        two ? launch_pers<128, true>(st, mw, mh, ml, p, ep.pdl) : launch_pers<256, false>(st, mw, mh, ml, p, ep.pdl);
+        return;
+    }
     switch (BN) {
     case 32: two ? launch_tc<32, true>(st, mw, mh, ml, p, ep.pdl) : launch_tc<32, false>(st, mw, mh, ml, p, ep.pdl); break;
     case 64: two ? launch_tc<64, true>(st, mw, mh, ml, p, ep.pdl) : launch_tc<64, false>(st, mw, mh, ml, p, ep.pdl); break;

@@ -143,6 +143,17 @@ int ct_device_status(void);
 int ct_sdp_attn_batch_decode_noalloc(float *out, const float *Q, const float *K, const float *V,
                                      const int *lens, int T_k_stride, int B, void *stream);
 
+/* The library's tensor-core GEMM on caller-held bf16 activations.  No
+ * counterpart in the reference (its linears take fp32 activations,
+ * backends/backend.h:56-64): for callers that keep activations as bf16 planes.
+ * Y [T, N] fp32 (row stride ldy) = act(X W^T + b) with X = X_hi + X_lo
+ * (bf16 [T, K] each; X_lo may be NULL), W bf16 [N, K], b bf16 [N] or NULL;
+ * act 0 none, 1 SiLU, 2 ReLU.  All pointers device, 16-byte aligned; K a
+ * multiple of 8.  Launches on `stream` (a cudaStream_t, NULL = default) and
+ * returns 0, -1 (bad argument) or -4 (launch failed). */
+int ct_linear_bf16(float *Y, int ldy, const uint16_t *X_hi, const uint16_t *X_lo, const uint16_t *W,
+                   const uint16_t *bias, int T, int K, int N, int act, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

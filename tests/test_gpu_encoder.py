@@ -82,8 +82,10 @@ def test_encoder_batch_invariance(abi, full_model):
     """An utterance's encoder rows do not depend on the other utterances of
     the packed batch (row-wise GEMMs without K splits; attention and the
     convolutions stop at utterance boundaries; the position table depends only
-    on the relative position)."""
-    mel, T_mel = inputs.mel_batch([0.71, 1.9, 1.27, 0.15], seed=701)
+    on the relative position).  Together the batch has more than 64 rows (the
+    persistent GEMM kernel); alone each utterance has fewer (the tile kernel)."""
+    mel, T_mel = inputs.mel_batch([2.9, 1.9, 3.27, 0.15, 2.2], seed=701)
+    assert t_enc_of(T_mel).sum() > 64 and t_enc_of(T_mel).max() <= 64
     mels = mels_of(mel, T_mel)
     eng = make_engine(abi, full_model)
     try:
