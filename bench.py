@@ -1,24 +1,33 @@
 #!/usr/bin/env python3
-"""Benchmark: greedy decode tokens/s of the ragged continuous-batching engine.
+"""Benchmark: decode tokens/s, RTFx and p50 step latency of the engine.
 
-Workload (BASELINE configuration 3 shape, full-size decoder, one B200 per rank):
-64 utterances per GPU with T_enc drawn from 5-30 s of audio (8x-subsampled
-frames) and EOS forced at a drawn length of 20-220 generated tokens, from
-seeded N(0, 1) encoder outputs and seeded random-init bf16 decoder weights
-(there is no network for checkpoints or audio).  One bench step = submit the
-64 utterances, decode all of them to their forced EOS (prefill + packed decode
-steps), collect the tokens.
+Workload (full-size model, one B200 per rank): 64
+utterances per GPU of U(5, 30) s of seeded N(0, 1) log-mel (128 bins, 10 ms
+hop), EOS forced at U{20..220} generated tokens, seeded random-init bf16
+weights (there is no network for checkpoints or audio).  Rank r draws its own
+64 utterances (seed r): the job is sharded by utterance, with no collective.
 
-  value  generated tokens / device time of all engine GPU work (cross-K/V
-         projection + step graphs, CUDA events on the engine stream), inputs
-         resident; max over ranks; N ranks each run the same per-GPU workload.
-  e2e    the same count / wall time through the C ABI from host buffers:
-         ct_engine_submit_encoded (H2D of the fp32 encoder rows) + run + poll
-         (D2H of the tokens), every step.
+One bench step runs two legs over that batch:
+
+  A  decode: submit the 64 utterances' encoder rows (host fp32, seeded
+     N(0, 1)), decode all to their forced EOS, poll the tokens.
+       value  generated tokens / device time of the engine's GPU work (cross-K/V
+              projection into pages + packed step graphs; CUDA events on the
+              engine stream), inputs resident; summed over ranks / max time.
+       e2e    the same count / wall time of the C-ABI calls from host buffers
+              (H2D of the encoder rows, D2H of the tokens), every step.
+       p50_step_ms  median device time of one packed decode step.
+  B  transcribe: submit the 64 log-mel inputs (ct_engine_submit_mel), which
+     the engine encodes as one packed ragged batch (48 Conformer layers),
+     admits and decodes; poll the tokens.
+       rtfx.value  audio seconds / device time (encoder + admission + decode)
+       rtfx.e2e    audio seconds / wall time of the C-ABI calls from host log-mel
 
 `--impl reference` times the reference's own CPU implementation (its
 backends/cpu/backend.c driven by its model.h, prebuilt under oracle/_ref/) on
-a bounded sample of the same workload with one utterance per host thread.
+bounded samples of the same workload, one utterance per host thread: greedy
+decode from the same encoder rows (tokens/s), and full transcription
+(encoder + decode) of 1 s cuts of the log-mel inputs (RTFx).
 """
 from __future__ import annotations
 
@@ -38,15 +47,25 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 sys.path.insert(0, os.path.join(REPO, "tests", "golden"))
 
-METRIC = "decode tokens/s (ragged continuous batch, greedy)"
+METRIC = "decode tokens/s and RTFx per B200 (ragged continuous batch); p50 step latency"
 BATCH = 64
+CPU_CUT_S = 1.0        # seconds of log-mel per utterance in the CPU transcription sample
+CPU_CUT_TOKENS = 8     # generated-token cap per utterance in the CPU transcription sample
 
 
 def workload(seed: int = 0, batch: int = BATCH):
+    """Configuration 3: seconds ~ U(5, 30), forced lengths ~ U{20..220}; log-mel
+    N(0, 1) [128, 100 s + 1] per utterance; encoder rows N(0, 1) [T_enc, 1024]."""
     import inputs
     case = inputs.ragged_decode_case(batch, seed=seed, t_lo=5.0, t_hi=30.0, l_lo=20, l_hi=220)
     enc = inputs.enc_outputs(case["T_enc"], case["enc_seed"])
-    return case, enc
+    T_mel = np.array([inputs.ctb.t_mel_of_seconds(x) for x in case["seconds"]], np.int32)
+    mels = []
+    for b, t in enumerate(T_mel):
+        rng = np.random.default_rng([seed, 7, b])
+        mels.append(rng.standard_normal((128, int(t)), dtype=np.float32))
+    case["T_mel"] = T_mel
+    return case, enc, mels
 
 
 def peaks():
@@ -106,7 +125,7 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def dist_setup(n_gpus: int):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -121,13 +140,14 @@ def dist_setup(n_gpus: int):
     return world, rank, local
 
 
-def barrier_max(world, value: float) -> float:
+def all_reduce(world, value: float, op: str) -> float:
+    """Max or sum over ranks (host-side bookkeeping; no collective touches the data path)."""
     if world == 1:
         return value
     import torch
     import torch.distributed as dist
     t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return float(t.item())
 
 
@@ -140,14 +160,17 @@ def barrier(world):
 
 
 class ReferenceCPU:
-    """The reference's CPU decode (its model.h driving its backends/cpu/backend.c,
-    prebuilt as oracle/_ref/libref_decode_cpu.so) on a bounded sample of the
-    workload: the first n_threads utterances (one per host thread, as
-    run_files_parallel does with one CPU "device" per core), each decoded to
-    min(its forced length, cap) tokens, cross K/V precompute and 10-row
-    prefill included.  Rate = generated tokens / wall seconds."""
+    """The reference's CPU path (its model.h driving its backends/cpu/backend.c,
+    prebuilt as oracle/_ref/libref_decode_cpu.so) on bounded samples of the
+    workload, one utterance per host thread (as run_files_parallel does with one
+    CPU "device" per core), on the first n_threads utterances:
+      decode      cross K/V + 10-row prefill + greedy decode from the workload's
+                  encoder rows to min(forced length, cap) tokens -> tokens/s
+      transcribe  encoder + decode of the first CPU_CUT_S seconds of each
+                  utterance's log-mel, to min(forced, CPU_CUT_TOKENS) tokens
+                  -> RTFx (audio seconds / wall seconds)."""
 
-    def __init__(self, case, enc, n_threads: int, cap: int):
+    def __init__(self, case, enc, mels, n_threads: int, cap: int):
         sys.path.insert(0, os.path.join(REPO, "oracle"))
         import inputs as _in
         import pyoracle as po
@@ -157,7 +180,7 @@ class ReferenceCPU:
         if L is None:
             raise RuntimeError("oracle/_ref/libref_decode_cpu.so not built (build() with the reference tree)")
         self.L = po.bind_ref_decode(L)
-        self.wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("dec",))
+        self.wb = W.make_blob(W.FULL_DIMS, seed=0)
         self.ws = W.weights_struct(self.wb)
         self.L.refh_bind_weights(ctypes.addressof(self.ws))
         n = n_threads
@@ -168,11 +191,18 @@ class ReferenceCPU:
         self.enc = np.ascontiguousarray(enc[idx, :self.Tm], dtype=np.float32)
         self.forced = np.ascontiguousarray(np.minimum(case["forced_len"][idx], cap), dtype=np.int32)
         self.prompt = np.array(_in.ctb.PROMPT_FULL, np.int32)
+        cut = _in.ctb.t_mel_of_seconds(CPU_CUT_S)
+        self.T_mel_cut = np.full(n, cut, np.int32)
+        self.mel_cut = np.ascontiguousarray(np.stack([mels[i][:, :cut] for i in idx]), dtype=np.float32)
+        self.forced_cut = np.ascontiguousarray(np.minimum(case["forced_len"][idx], CPU_CUT_TOKENS), dtype=np.int32)
         self.sample = (f"first {n} utterances of the workload (T_enc {int(self.T_enc.min())}-{int(self.T_enc.max())}),"
                        f" each cross-K/V + 10-token prefill + greedy decode to min(forced length, {cap}) tokens"
                        f" ({int(self.forced.sum())} tokens), one utterance per host thread")
+        self.sample_rtfx = (f"first {n} utterances of the workload cut to their first {CPU_CUT_S:g} s of log-mel,"
+                            f" each encoder (48 layers) + prefill + greedy decode to {CPU_CUT_TOKENS} tokens,"
+                            f" one utterance per host thread")
 
-    def run(self):
+    def decode(self):
         po = self.po
         tokens = np.zeros((self.n, 1024), np.int32)
         n_tok = np.zeros(self.n, np.int32)
@@ -181,6 +211,15 @@ class ReferenceCPU:
                                            po.ip(tokens), po.ip(n_tok))
         return int(self.forced.sum()), secs
 
+    def transcribe(self):
+        po = self.po
+        tokens = np.zeros((self.n, 1024), np.int32)
+        n_tok = np.zeros(self.n, np.int32)
+        secs = self.L.refh_parallel_transcribe(self.n, self.n, po.fp(self.mel_cut), int(self.T_mel_cut[0]),
+                                               po.ip(self.T_mel_cut), po.ip(self.prompt), len(self.prompt),
+                                               po.ip(self.forced_cut), po.ip(tokens), po.ip(n_tok))
+        return self.n * CPU_CUT_S, secs
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -188,7 +227,7 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-tokens", type=int, default=32, help="token cap per utterance of the CPU sample")
+    ap.add_argument("--cpu-tokens", type=int, default=32, help="token cap per utterance of the CPU decode sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--precision", type=int, default=1)
     ap.add_argument("--batch", type=int, default=BATCH, help="utterances per GPU per step (profiling cases)")
@@ -196,59 +235,75 @@ def main():
     ap.add_argument("--max-len", type=int, default=0, help="cap the forced lengths (profiling cases)")
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel-class profiling pass")
     ap.add_argument("--no-pdl", action="store_true", help="launch step kernels without programmatic dependent launch")
+    ap.add_argument("--legs", default="AB", help="A = decode leg, B = transcription leg (profiling cases)")
     args = ap.parse_args()
 
-    world, rank, local = dist_setup(args.gpus)
+    world, rank, local = dist_setup()
     pk, pk_kind = peaks()
-    case, enc = workload(0, args.batch)
+    case, enc, mels = workload(rank, args.batch)
     if args.max_len > 0:
         case["forced_len"] = np.minimum(case["forced_len"], args.max_len).astype(np.int32)
     nb = args.batch
     tokens_per_step = int(case["forced_len"].sum())
+    audio_s = float(case["seconds"].sum())
     ncores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
-    cfg = {"workload": f"config 3 shape: {nb} ragged utterances/GPU, T_enc from U(5,30) s, EOS forced at U{{20..220}}",
-           "global_batch": nb * world, "decoder": "8 x 1024, 8 heads, FFN 4096, vocab 16384 (model.h dims)",
-           "tokens_per_step_per_gpu": tokens_per_step, "prompt_tokens": 10,
-           "kv": "bf16 pages of 16 rows", "l2": "not flushed: per-step working set (268 MB weights + KV) > 126 MB L2",
+    cfg = {"workload": f"config 3: {nb} ragged utterances/GPU of U(5,30) s log-mel, EOS forced at U{{20..220}}",
+           "global_batch": nb * world, "model": "encoder 48 x 1280 (8 heads, FFN 5120, dw-K 9), decoder 8 x 1024 "
+           "(8 heads, FFN 4096, vocab 16384): model.h dims, random-init bf16",
+           "prompt_tokens": 10, "kv": "bf16 pages of 16 rows",
+           "l2": "not flushed: per-step working sets (3.8 GB encoder weights, 268 MB decoder weights + KV) > 126 MB L2",
            "parallelism": f"replicas x{world} (utterance sharding, no collective)"}
 
     if args.impl == "reference":
         if rank != 0:
             return
-        ref = ReferenceCPU(case, enc, ncores, args.cpu_tokens)
+        ref = ReferenceCPU(case, enc, mels, ncores, args.cpu_tokens)
         for _ in range(args.warmup):
-            ref.run()
-        toks, secs = 0, 0.0
+            ref.decode()
+            ref.transcribe()
+        toks, secs, aud, tsecs = 0, 0.0, 0.0, 0.0
         for _ in range(args.steps):
-            t, s = ref.run()
+            t, s_ = ref.decode()
             toks += t
-            secs += s
+            secs += s_
+            a_, s2 = ref.transcribe()
+            aud += a_
+            tsecs += s2
         v = toks / secs
         line = {"metric": METRIC, "value": v, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1000.0 / args.steps,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": (secs + tsecs) * 1000.0 / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
                 "data": "synthetic", "config": cfg,
                 "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": ncores, "kind": "reference",
                                  "sample": ref.sample},
-                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "rtfx": {"value": aud / tsecs, "e2e": aud / tsecs, "unit": "audio s / s", "cores": ncores,
+                         "sample": ref.sample_rtfx}}
         print(json.dumps(line), flush=True)
         return
 
     abi = importlib.import_module("cohere-transcribe_b200.abi")
     W = importlib.import_module("cohere-transcribe_b200.weights")
     lib = abi.load()
-    wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("dec",))
+    wb = W.make_blob(W.FULL_DIMS, seed=0)
     ws = W.weights_struct(wb)
     dev = local if world > 1 else 0
-    eng = abi.Engine(lib, dev, wb, ws, max_slots=256, max_rows=1024, precision=args.precision,
-                     kv_pages=args.kv_pages, no_pdl=int(args.no_pdl))
-    # host inputs: the encoder rows of every utterance (fp32, host memory)
+    enc_frames = int(case["T_mel"].sum())
+
+    def make_engine(profile=0):
+        return abi.Engine(lib, dev, wb, ws, max_slots=256, max_rows=1024, precision=args.precision,
+                          kv_pages=args.kv_pages, no_pdl=int(args.no_pdl), profile=profile,
+                          enc_max_utts=nb, enc_max_frames=enc_frames)
+
+    eng = make_engine()
+    # host inputs: encoder rows (leg A) and log-mel (leg B), fp32 host memory
     enc_rows = [np.ascontiguousarray(enc[b, :case["T_enc"][b]]) for b in range(nb)]
-    h2d = int(sum(x.nbytes for x in enc_rows))
+    h2d_a = int(sum(x.nbytes for x in enc_rows))
+    h2d_b = int(sum(m.nbytes for m in mels))
     d2h = int(4 * tokens_per_step)
 
-    def one_step(e, step_times):
+    def leg_a(e, step_times):
         for b in range(nb):
             e.submit(b, enc_rows[b], int(case["forced_len"][b]))
         while True:
@@ -261,86 +316,139 @@ def main():
         assert len(out) == nb
         return out
 
+    def leg_b(e):
+        for b in range(nb):
+            e.submit_mel(b, mels[b], int(case["forced_len"][b]))
+        e.run()
+        out = e.poll()
+        assert len(out) == nb
+        return out
+
+    legs = args.legs.upper()
     for _ in range(args.warmup):
-        one_step(eng, [])
+        if "A" in legs:
+            leg_a(eng, [])
+        if "B" in legs:
+            leg_b(eng)
     if eng.status() != 0:
         raise RuntimeError("device status set during warm-up")
-    barrier(world)
-    s0 = eng.stats()
     step_times = []
-    with ClockSampler(local) as clk:
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            one_step(eng, step_times)
-        wall = time.perf_counter() - t0
-    s1 = eng.stats()
+    wall_a = wall_b = 0.0
+    dev_a = dev_b = enc_ms = 0.0
     barrier(world)
+    s_start = eng.stats()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            if "A" in legs:
+                s0 = eng.stats()
+                t0 = time.perf_counter()
+                leg_a(eng, step_times)
+                wall_a += time.perf_counter() - t0
+                s1 = eng.stats()
+                dev_a += (s1["step_ms"] - s0["step_ms"]) + (s1["admit_ms"] - s0["admit_ms"])
+            if "B" in legs:
+                s0 = eng.stats()
+                t0 = time.perf_counter()
+                leg_b(eng)
+                wall_b += time.perf_counter() - t0
+                s1 = eng.stats()
+                dev_b += (s1["step_ms"] - s0["step_ms"]) + (s1["admit_ms"] - s0["admit_ms"]) + \
+                    (s1["enc_ms"] - s0["enc_ms"])
+                enc_ms += s1["enc_ms"] - s0["enc_ms"]
+    barrier(world)
+    s_end = eng.stats()
     status = eng.status()
+    launches = int(s_end["kernel_launches"] - s_start["kernel_launches"])
     eng.close()
-    dev_ms = (s1["step_ms"] - s0["step_ms"]) + (s1["admit_ms"] - s0["admit_ms"])
-    dev_ms_max = barrier_max(world, dev_ms)
-    wall_max = barrier_max(world, wall)
-    tokens = tokens_per_step * args.steps * world
-    value = tokens / (dev_ms_max / 1000.0)
-    e2e = tokens / wall_max
-    dt = {k: s1[k] - s0[k] for k in s1}
 
-    # Per-kernel-class device times: one more bench step on an engine whose step
-    # graphs carry CUDA event nodes around the attention and FFN launches of
-    # every layer (kept out of the timed run: event nodes serialise neighbours).
+    K = args.steps
+    tokens_all = all_reduce(world, float(tokens_per_step * K), "sum")
+    audio_all = all_reduce(world, audio_s * K, "sum")
+    dev_a_max = all_reduce(world, dev_a, "max")
+    wall_a_max = all_reduce(world, wall_a, "max")
+    dev_b_max = all_reduce(world, dev_b, "max")
+    wall_b_max = all_reduce(world, wall_b, "max")
+    value = tokens_all / (dev_a_max / 1000.0) if dev_a_max > 0 else None
+    e2e = tokens_all / wall_a_max if wall_a_max > 0 else None
+
+    # Per-kernel-class device times: one more step of each leg on an engine that
+    # records CUDA events between launch groups (kept out of the timed run: the
+    # event nodes serialise their neighbours).
+    breakdown, rooflines = {}, {}
     if not args.no_profile:
-        prof = abi.Engine(lib, dev, wb, ws, max_slots=256, max_rows=1024, precision=args.precision,
-                          kv_pages=args.kv_pages, profile=1)
-        one_step(prof, [])
+        prof = make_engine(profile=1)
+        if "A" in legs:
+            leg_a(prof, [])
+        if "B" in legs:
+            leg_b(prof)
         p0 = prof.stats()
         r0 = prof.profile_report()
-        one_step(prof, [])
+        if "A" in legs:
+            leg_a(prof, [])
+        if "B" in legs:
+            leg_b(prof)
         p1 = prof.stats()
         r1 = prof.profile_report()
         prof.close()
-        breakdown = {k: {"ms_per_step": (v[0] - r0.get(k, [0, 0])[0]) / max(1, p1["steps"] - p0["steps"]),
-                         "launch_groups_per_step": (v[1] - r0.get(k, [0, 0])[1]) / max(1, p1["steps"] - p0["steps"])}
-                     for k, v in r1.items()}
         d = {k: p1[k] - p0[k] for k in p1}
-    else:
-        d = {k: 0.0 for k in dt}
-        breakdown = {}
-    classes = {
-        "paged cross-attention": (d["cross_attn_ms"], d["cross_kv_bytes"]),
-        "paged self-attention": (d["self_attn_ms"], d["self_kv_bytes"]),
-        "FFN GEMMs (tcgen05)": (d["ffn_ms"], d["ffn_bytes"]),
-    }
-    dom = max(classes, key=lambda k: classes[k][0])
-    ms, byts = classes[dom]
-    launches = d["steps"] * 8 * (2 if "GEMM" in dom else 1)
-    achieved = (byts / (ms / 1000.0)) / 1e9 if ms > 0 else 0.0
-    traffic = None
-    tpath = os.path.join(REPO, "profiles", "ncu_traffic.json")
-    if os.path.exists(tpath):
-        with open(tpath) as fh:
-            traffic = json.load(fh).get(dom)
-    roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": achieved / pk["hbm_gbs"], "peak_kind": pk_kind, "traffic": traffic,
-            "algorithmic_bytes_per_launch": byts / max(1, launches), "avg_launch_ms": ms / max(1, launches),
-            "measured": "CUDA event nodes around every launch of the class in one profiled bench step"}
-    shares = {k: v[0] / max(1e-9, d["step_ms"]) for k, v in classes.items()}
+        breakdown = {k: {"ms": v[0] - r0.get(k, [0, 0])[0], "launch_groups": v[1] - r0.get(k, [0, 0])[1]}
+                     for k, v in r1.items()}
+        # decode kernels (HBM-bound): algorithmic bytes / device time
+        for name, ms_, byts, n_l in (("paged cross-attention", d["cross_attn_ms"], d["cross_kv_bytes"], d["steps"] * 8),
+                                     ("paged self-attention", d["self_attn_ms"], d["self_kv_bytes"], d["steps"] * 8),
+                                     ("decode FFN GEMMs (tcgen05)", d["ffn_ms"], d["ffn_bytes"], d["steps"] * 16)):
+            if ms_ > 0:
+                ach = byts / (ms_ / 1000.0) / 1e9
+                rooflines[name] = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                   "frac": ach / pk["hbm_gbs"], "ms_per_step": ms_, "launches": n_l,
+                                   "algorithmic_bytes_per_launch": byts / max(1, n_l),
+                                   "avg_launch_ms": ms_ / max(1, n_l)}
+        # encoder FFN1 GEMM (tensor-bound): 2*T*N*K algorithmic flops per launch
+        if "enc_gemm_ffn1" in breakdown and breakdown["enc_gemm_ffn1"]["launch_groups"] > 0:
+            R3 = int(sum(int(x) for x in case["T_enc"]))
+            n_l = breakdown["enc_gemm_ffn1"]["launch_groups"]
+            ms_ = breakdown["enc_gemm_ffn1"]["ms"]
+            fl = 2.0 * R3 * 5120 * 1280
+            ach = fl / (ms_ / n_l / 1000.0) / 1e12
+            rooflines["encoder FFN1 GEMM (tcgen05, persistent)"] = {
+                "bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": ach / pk["bf16_tflops"], "ms_per_step": ms_, "launches": n_l,
+                "algorithmic_flops_per_launch": fl, "avg_launch_ms": ms_ / n_l,
+                "note": "activations as bf16 hi+lo planes: the tensor cores execute 2x the algorithmic flops"}
+    # the dominant kernel of the whole bench step by device time
+    roof = None
+    if rooflines:
+        dom = max(rooflines, key=lambda k: rooflines[k]["ms_per_step"])
+        r = rooflines[dom]
+        traffic = None
+        tpath = os.path.join(REPO, "profiles", "ncu_traffic.json")
+        if os.path.exists(tpath):
+            with open(tpath) as fh:
+                traffic = json.load(fh).get(dom)
+        roof = {"kernel": dom, "bound": r["bound"], "achieved": r["achieved"], "peak": r["peak"], "unit": r["unit"],
+                "frac": r["frac"], "peak_kind": pk_kind, "traffic": traffic,
+                "avg_launch_ms": r["avg_launch_ms"],
+                "measured": "CUDA events between launch groups in one profiled bench step"}
 
-    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": (dev_a_max + dev_b_max) / K, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
-            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d_a + h2d_b, "d2h_bytes_per_step": 2 * d2h},
+            "rtfx": {"value": audio_all / (dev_b_max / 1000.0) if dev_b_max > 0 else None,
+                     "e2e": audio_all / wall_b_max if wall_b_max > 0 else None, "unit": "audio s / s",
+                     "audio_s_per_step": audio_s * world, "encoder_ms_per_step": enc_ms / K,
+                     "h2d_bytes_per_step": h2d_b, "d2h_bytes_per_step": d2h},
             "p50_step_ms": statistics.median(step_times) if step_times else None,
-            "decode_steps_per_bench_step": dt["steps"] / args.steps,
-            "admit_ms_per_step": dt["admit_ms"] / args.steps,
-            "gpu_launches": int(dt["kernel_launches"]),
-            "roofline": roof, "time_shares": shares, "profiled_step_breakdown": breakdown, "clocks": clk.summary(), "device_status": status,
+            "gpu_launches": launches, "roofline": roof, "rooflines": rooflines,
+            "profiled_step_breakdown": breakdown, "clocks": clk.summary(), "device_status": status,
             "precision": "bf16 weights, activations as bf16 hi+lo planes, fp32 accumulate" if args.precision else
             "bf16 weights and activations, fp32 accumulate"}
     if rank == 0 and world == 1 and not args.no_cpu:
-        ref = ReferenceCPU(case, enc, ncores, args.cpu_tokens)
-        t, s = ref.run()
-        line["cpu_baseline"] = {"value": t / s, "unit": "tokens/s", "cores": ncores, "kind": "reference",
-                                "sample": ref.sample}
+        ref = ReferenceCPU(case, enc, mels, ncores, args.cpu_tokens)
+        t, s_ = ref.decode()
+        a_, s2 = ref.transcribe()
+        line["cpu_baseline"] = {"value": t / s_, "unit": "tokens/s", "cores": ncores, "kind": "reference",
+                                "sample": ref.sample, "rtfx": a_ / s2, "rtfx_sample": ref.sample_rtfx}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

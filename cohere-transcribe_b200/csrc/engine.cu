@@ -461,7 +461,8 @@ __global__ void update_kernel(DevState s, const int *next) {
 // ------------------------------------------------------------ host --------
 struct Pending {
     long long id;
-    std::vector<float> enc;
+    std::vector<float> enc;          // host encoder rows (submit_encoded) ...
+    const float *dev_rows = nullptr; // ... or device rows (encoded in-engine from log-mel)
     int T_enc, forced;
 };
 
@@ -517,7 +518,9 @@ struct ct_engine {
     int enc_rows_cap = 0;
     float *enc_stage = nullptr;      // pinned
     long long *off_stage = nullptr;  // pinned
-    int *slot_stage = nullptr;       // pinned slot records
+    int *slot_stage = nullptr;       // pinned admission records [max_slots][REC_INTS]
+    int *rec_dev = nullptr;          // their device copy
+    float *mel_rows = nullptr;       // encoder rows of the last in-engine encoder batch, awaiting admission
     // host slot bookkeeping
     std::vector<int> slot_live;      // 0 free, 1 live
     std::vector<int> slot_first;     // 1 until its first (prefill) step has been launched
@@ -740,15 +743,29 @@ static Bucket *bucket_for(ct_engine *e, int rows_needed) {
 }
 
 // Host mirror of the device slot record written at admission.
-enum { REC_STATE, REC_TOK, REC_POS, REC_GEN, REC_FORCED, REC_TENC, REC_N };
+enum { REC_SLOT, REC_STATE, REC_TOK, REC_POS, REC_GEN, REC_FORCED, REC_TENC, REC_N };
+constexpr int REC_INTS = REC_N + SELF_PAGES + CROSS_PAGES;   // one admission record
+
+// Writes the slot records of k admissions (built on the host, one H2D copy):
+// block r takes record r.
+__global__ void admit_records_kernel(DevState s, const int *rec) {
+    const int *r = rec + (size_t)blockIdx.x * REC_INTS;
+    const int slot = r[REC_SLOT];
+    if (slot < 0 || slot >= s.max_slots) { if (threadIdx.x == 0) set_status(CT_STATUS_BAD_ARG); return; }
+    if (threadIdx.x == 0) {
+        s.state[slot] = r[REC_STATE]; s.tok[slot] = r[REC_TOK]; s.pos[slot] = r[REC_POS];
+        s.gen[slot] = r[REC_GEN]; s.forced[slot] = r[REC_FORCED]; s.tenc[slot] = r[REC_TENC];
+    }
+    for (int j = threadIdx.x; j < SELF_PAGES; j += blockDim.x) s.self_pt[(size_t)slot * SELF_PAGES + j] = r[REC_N + j];
+    for (int j = threadIdx.x; j < CROSS_PAGES; j += blockDim.x)
+        s.cross_pt[(size_t)slot * CROSS_PAGES + j] = r[REC_N + SELF_PAGES + j];
+}
 
 static int admit(ct_engine *e) {
     // pick admissions: free slot, pages, rows budget, encoder-row staging budget
     int live_rows = 0;
     for (int i = 0; i < e->cfg.max_slots; ++i) live_rows += e->slot_live[i] ? 1 : 0;
-    std::vector<int> slots;
-    std::vector<Pending> adm;
-    int enc_rows = 0;
+    int enc_rows = 0, n_rec = 0;
     while (!e->pending.empty()) {
         Pending &p = e->pending.front();
         if (enc_rows + p.T_enc > e->enc_rows_cap) break;
@@ -770,24 +787,24 @@ static int admit(ct_engine *e) {
         e->slot_steps[slot] = 0;
         e->slot_tenc[slot] = p.T_enc;
         ++e->st_acc.admitted;
-        // slot record + page tables
-        int *rec = e->slot_stage;
+        // slot record + page tables (copied for all admissions at once below)
+        int *rec = e->slot_stage + (size_t)n_rec * REC_INTS;
+        ++n_rec;
+        rec[REC_SLOT] = slot;
         rec[REC_STATE] = S_PREFILL; rec[REC_TOK] = 0; rec[REC_POS] = 0; rec[REC_GEN] = 0;
         rec[REC_FORCED] = p.forced; rec[REC_TENC] = p.T_enc;
         int *spt = rec + REC_N, *cpt = spt + SELF_PAGES;
         for (int j = 0; j < SELF_PAGES; ++j) spt[j] = j < self_need ? pages[j] : -1;
         for (int j = 0; j < CROSS_PAGES; ++j) cpt[j] = j < cross_need ? pages[self_need + j] : -1;
-        int *const fields[REC_N] = {e->ds.state, e->ds.tok, e->ds.pos, e->ds.gen, e->ds.forced, e->ds.tenc};
-        for (int f = 0; f < REC_N; ++f)
-            EK(cudaMemcpyAsync(fields[f] + slot, rec + f, sizeof(int), cudaMemcpyHostToDevice, e->st));
-        EK(cudaMemcpyAsync(e->ds.self_pt + (size_t)slot * SELF_PAGES, spt, sizeof(int) * SELF_PAGES,
-                           cudaMemcpyHostToDevice, e->st));
-        EK(cudaMemcpyAsync(e->ds.cross_pt + (size_t)slot * CROSS_PAGES, cpt, sizeof(int) * CROSS_PAGES,
-                           cudaMemcpyHostToDevice, e->st));
-        // these staging copies must land before the staging area is rewritten
-        EK(cudaStreamSynchronize(e->st));
-        // encoder rows of this utterance -> staging, with their cross page offsets
-        memcpy(e->enc_stage + (size_t)enc_rows * D, p.enc.data(), sizeof(float) * (size_t)p.T_enc * D);
+        // encoder rows of this utterance -> contiguous device rows, with their cross page offsets
+        float *dst = e->enc_dev + (size_t)enc_rows * D;
+        const size_t bytes = sizeof(float) * (size_t)p.T_enc * D;
+        if (p.dev_rows) {
+            EK(cudaMemcpyAsync(dst, p.dev_rows, bytes, cudaMemcpyDeviceToDevice, e->st));
+        } else {
+            memcpy(e->enc_stage + (size_t)enc_rows * D, p.enc.data(), bytes);
+            EK(cudaMemcpyAsync(dst, e->enc_stage + (size_t)enc_rows * D, bytes, cudaMemcpyHostToDevice, e->st));
+        }
         for (int t = 0; t < p.T_enc; ++t)
             e->off_stage[enc_rows + t] = (long long)pages[self_need + t / PR] * PAGE_ELEMS + (long long)(t % PR) * D;
         enc_rows += p.T_enc;
@@ -796,8 +813,11 @@ static int admit(ct_engine *e) {
         e->pending.pop_front();
     }
     if (enc_rows == 0) return 0;
+    EK(cudaMemcpyAsync(e->rec_dev, e->slot_stage, sizeof(int) * (size_t)n_rec * REC_INTS, cudaMemcpyHostToDevice,
+                       e->st));
+    admit_records_kernel<<<n_rec, 64, 0, e->st>>>(e->ds, e->rec_dev);
+    EK(cudaGetLastError());
     // cross-attention K/V of all admitted utterances: one GEMM into their pages
-    EK(cudaMemcpyAsync(e->enc_dev, e->enc_stage, sizeof(float) * (size_t)enc_rows * D, cudaMemcpyHostToDevice, e->st));
     EK(cudaMemcpyAsync(e->enc_off, e->off_stage, sizeof(long long) * enc_rows, cudaMemcpyHostToDevice, e->st));
     EK(cudaEventRecord(e->aev0, e->st));
     const bool two = two_planes(e);
@@ -811,7 +831,7 @@ static int admit(ct_engine *e) {
     float ams = 0.0f;
     EK(cudaEventElapsedTime(&ams, e->aev0, e->aev1));
     e->st_acc.admit_ms += ams;
-    e->st_acc.kernel_launches += 2;   // plane split + cross K/V GEMM
+    e->st_acc.kernel_launches += 3;   // records + plane split + cross K/V GEMM
     return 0;
 }
 
@@ -876,8 +896,10 @@ static int encode_pending(ct_engine *e) {
     EK(cudaEventRecord(e->eev0, e->st));
     if (!enc::encode(e->st, *e->enc, n, mels.data(), T_mel.data(), off.data())) return CT_EINVAL;
     EK(cudaEventRecord(e->eev1, e->st));
-    std::vector<float> host((size_t)off[n] * D);
-    EK(cudaMemcpyAsync(host.data(), e->enc->enc_h, sizeof(float) * host.size(), cudaMemcpyDeviceToHost, e->st));
+    // the rows wait in mel_rows until admitted (the next encoder batch runs
+    // only once every pending utterance has been admitted)
+    EK(cudaMemcpyAsync(e->mel_rows, e->enc->enc_h, sizeof(float) * (size_t)off[n] * D, cudaMemcpyDeviceToDevice,
+                       e->st));
     EK(cudaStreamSynchronize(e->st));
     float ms = 0.f;
     EK(cudaEventElapsedTime(&ms, e->eev0, e->eev1));
@@ -891,7 +913,7 @@ static int encode_pending(ct_engine *e) {
         Pending p;
         p.id = j.id;
         p.T_enc = off[b + 1] - off[b];
-        p.enc.assign(host.begin() + (size_t)off[b] * D, host.begin() + (size_t)off[b + 1] * D);
+        p.dev_rows = e->mel_rows + (size_t)off[b] * D;
         p.forced = j.forced;
         e->pending.push_back(std::move(p));
         e->mel_pending.pop_front();
@@ -1089,7 +1111,8 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
                     e->enc_pl[1], e->enc_off, e->ds.state, e->ds.tok, e->ds.pos, e->ds.gen, e->ds.forced,
                     e->ds.tenc, e->ds.self_pt, e->ds.cross_pt, e->ds.out_tok, e->ds.prompt, e->ds.r_slot,
                     e->ds.r_pos, e->ds.r_tok, e->ds.r_off, e->ds.q_row, e->ds.q_slot, e->ds.n_rows, e->ds.n_seqs,
-                    e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.n_wself, e->ds.n_wcross};
+                    e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.n_wself, e->ds.n_wcross, e->rec_dev,
+                    e->mel_rows};
     for (void *p : ptrs) cudaFree(p);
     for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
     cudaFreeHost(e->h_done);
@@ -1223,7 +1246,8 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         dalloc(&e->enc_pl[1], (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_off, e->enc_rows_cap)) { ct_engine_destroy(e); return CT_ENOMEM; }
     EK(cudaHostAlloc(&e->enc_stage, sizeof(float) * (size_t)e->enc_rows_cap * D, cudaHostAllocDefault));
     EK(cudaHostAlloc(&e->off_stage, sizeof(long long) * e->enc_rows_cap, cudaHostAllocDefault));
-    EK(cudaHostAlloc(&e->slot_stage, sizeof(int) * (REC_N + SELF_PAGES + CROSS_PAGES), cudaHostAllocDefault));
+    EK(cudaHostAlloc(&e->slot_stage, sizeof(int) * (size_t)cfg.max_slots * REC_INTS, cudaHostAllocDefault));
+    if (dalloc(&e->rec_dev, (size_t)cfg.max_slots * REC_INTS)) { ct_engine_destroy(e); return CT_ENOMEM; }
     e->slot_live.assign(S, 0);
     e->slot_first.assign(S, 0);
     e->slot_id.assign(S, -1);
@@ -1279,7 +1303,10 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         }
         const int mu = cfg.enc_max_utts > 0 ? cfg.enc_max_utts : 64;
         const int mf = cfg.enc_max_frames > 0 ? cfg.enc_max_frames : 64 * 3001;
-        if (!ok || !enc::state_alloc(*st, mu, mf, cfg.precision != 0)) { ct_engine_destroy(e); return CT_ENOMEM; }
+        if (!ok || !enc::state_alloc(*st, mu, mf, cfg.precision != 0) || dalloc(&e->mel_rows, (size_t)st->R3_max * D)) {
+            ct_engine_destroy(e);
+            return CT_ENOMEM;
+        }
         st->prof = cfg.profile != 0;
     }
     EK(cudaDeviceSynchronize());

@@ -123,6 +123,10 @@ def bind_ref_decode(L: ctypes.CDLL) -> ctypes.CDLL:
     L.refh_parallel_decode.argtypes = [ctypes.c_int, ctypes.c_int, _f, _i, ctypes.c_int, _i,
                                        ctypes.c_int, _i, _i, _i]
     L.refh_parallel_decode.restype = ctypes.c_double
+    if hasattr(L, "refh_parallel_transcribe"):
+        L.refh_parallel_transcribe.argtypes = [ctypes.c_int, ctypes.c_int, _f, ctypes.c_int, _i, _i, ctypes.c_int,
+                                               _i, _i, _i]
+        L.refh_parallel_transcribe.restype = ctypes.c_double
     for fn in ("backend_weights_upload_blob",):
         getattr(L, fn).argtypes = [_vp, ctypes.c_size_t]
         getattr(L, fn).restype = None

@@ -262,3 +262,46 @@ double refh_parallel_decode(int n_threads, int count, const float *enc_h, const 
     free(th); free(jobs);
     return (t1.tv_sec - t0.tv_sec) + 1e-9 * (t1.tv_nsec - t0.tv_nsec);
 }
+
+/* ---- multi-threaded CPU transcription (encoder + decode): one host thread
+ * per group of utterances, as refh_parallel_decode, each thread running
+ * refh_transcribe_batch on its slice of the log-mel batch
+ * ([count][N_MELS][T_mel_max], zero padded). */
+typedef struct {
+    int dev, count, T_mel_max, n_prompt;
+    const float *mel; const int *T_mel, *prompt, *forced_len;
+    int *tokens, *n_tok;
+} TJob;
+
+static void *tjob_main(void *p) {
+    TJob *j = (TJob *)p;
+    backend_init(j->dev);
+    refh_transcribe_batch(j->count, j->mel, j->T_mel_max, j->T_mel, j->prompt, j->n_prompt, j->forced_len, NULL,
+                          j->tokens, j->n_tok, NULL, NULL, NULL);
+    backend_thread_cleanup();
+    return NULL;
+}
+
+double refh_parallel_transcribe(int n_threads, int count, const float *mel, int T_mel_max, const int *T_mel,
+                                const int *prompt, int n_prompt, const int *forced_len, int *tokens, int *n_tok) {
+    struct timespec t0, t1;
+    if (n_threads > count) n_threads = count;
+    pthread_t *th = malloc(sizeof(pthread_t) * n_threads);
+    TJob *jobs = malloc(sizeof(TJob) * n_threads);
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    int start = 0;
+    for (int i = 0; i < n_threads; i++) {
+        int n = count / n_threads + (i < count % n_threads);
+        TJob *j = &jobs[i];
+        j->dev = i; j->count = n; j->T_mel_max = T_mel_max; j->n_prompt = n_prompt;
+        j->mel = mel + (size_t)start * N_MELS * T_mel_max;
+        j->T_mel = T_mel + start; j->prompt = prompt; j->forced_len = forced_len + start;
+        j->tokens = tokens + (size_t)start * MAX_SEQ; j->n_tok = n_tok + start;
+        pthread_create(&th[i], NULL, tjob_main, j);
+        start += n;
+    }
+    for (int i = 0; i < n_threads; i++) pthread_join(th[i], NULL);
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    free(th); free(jobs);
+    return (t1.tv_sec - t0.tv_sec) + 1e-9 * (t1.tv_nsec - t0.tv_nsec);
+}
