@@ -236,6 +236,7 @@ def main():
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel-class profiling pass")
     ap.add_argument("--no-pdl", action="store_true", help="launch step kernels without programmatic dependent launch")
     ap.add_argument("--legs", default="AB", help="A = decode leg, B = transcription leg (profiling cases)")
+    ap.add_argument("--max-slots", type=int, default=256, help="engine slots (profiling cases)")
     args = ap.parse_args()
 
     world, rank, local = dist_setup()
@@ -286,15 +287,17 @@ def main():
     abi = importlib.import_module("cohere-transcribe_b200.abi")
     W = importlib.import_module("cohere-transcribe_b200.weights")
     lib = abi.load()
-    wb = W.make_blob(W.FULL_DIMS, seed=0)
+    legs = args.legs.upper()
+    # the decode leg alone needs no encoder (a decoder-only blob keeps profiling cases small)
+    wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("enc", "dec") if "B" in legs else ("dec",))
     ws = W.weights_struct(wb)
     dev = local if world > 1 else 0
     enc_frames = int(case["T_mel"].sum())
 
     def make_engine(profile=0):
-        return abi.Engine(lib, dev, wb, ws, max_slots=256, max_rows=1024, precision=args.precision,
+        return abi.Engine(lib, dev, wb, ws, max_slots=args.max_slots, max_rows=1024, precision=args.precision,
                           kv_pages=args.kv_pages, no_pdl=int(args.no_pdl), profile=profile,
-                          enc_max_utts=nb, enc_max_frames=enc_frames)
+                          enc_max_utts=nb if "B" in legs else -1, enc_max_frames=enc_frames)
 
     eng = make_engine()
     # host inputs: encoder rows (leg A) and log-mel (leg B), fp32 host memory
@@ -324,7 +327,6 @@ def main():
         assert len(out) == nb
         return out
 
-    legs = args.legs.upper()
     for _ in range(args.warmup):
         if "A" in legs:
             leg_a(eng, [])

@@ -106,6 +106,57 @@ __device__ __forceinline__ void epilogue16(const GemmEpilogue &ep, int t0, int t
             if (off[j] >= 0) ep.kv_pool[off[j] + col] = __float2bfloat16_rn(v[j]);
         break;
     }
+    case EPI_STORE:
+    case EPI_SILU:
+    case EPI_RELU: {
+        // one branch per chunk, not per element
+        float *y = ep.Y + (size_t)t0 * ep.ldy + n;
+        const size_t ld = (size_t)ep.ldy;
+        if (ep.epi == EPI_STORE) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (keep[j]) y[j * ld] = v[j];
+        } else if (ep.epi == EPI_SILU) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (keep[j]) y[j * ld] = v[j] / (1.0f + expf(-v[j]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (keep[j]) y[j * ld] = fmaxf(v[j], 0.0f);
+        }
+        break;
+    }
+    case EPI_BF16: {
+        float a[16];
+        if (ep.act == 1) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) a[j] = v[j] / (1.0f + expf(-v[j]));
+        } else if (ep.act == 2) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) a[j] = fmaxf(v[j], 0.0f);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) a[j] = v[j];
+        }
+        const size_t ld = (size_t)ep.ldy;
+        bf16 *yh = ep.Ybf + (size_t)t0 * ld + n;
+        if (ep.Ybf_lo) {
+            bf16 *yl = ep.Ybf_lo + (size_t)t0 * ld + n;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                if (!keep[j]) continue;
+                const bf16 hb = __float2bfloat16_rn(a[j]);
+                yh[j * ld] = hb;
+                yl[j * ld] = __float2bfloat16_rn(a[j] - __bfloat162float(hb));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (keep[j]) yh[j * ld] = __float2bfloat16_rn(a[j]);
+        }
+        break;
+    }
     default:
 #pragma unroll
         for (int j = 0; j < 16; ++j)
@@ -348,8 +399,10 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
 // epilogue) and acc_empty (4 epilogue warps -> MMA).  Per output element the
 // MMA sequence over K is the one of gemm_tc_kernel, so both forms give
 // bit-identical results.
+static constexpr int kThreadsP = 320;   // persistent kernel: TMA warp, MMA warp, 8 epilogue warps
+
 template <int BN, bool TWO>
-__global__ void __launch_bounds__(kThreads, 1) gemm_pers_kernel(const __grid_constant__ CUtensorMap tmW,
+__global__ void __launch_bounds__(kThreadsP, 1) gemm_pers_kernel(const __grid_constant__ CUtensorMap tmW,
                                                                 const __grid_constant__ CUtensorMap tmXh,
                                                                 const __grid_constant__ CUtensorMap tmXl,
                                                                 const KernelParams p) {
@@ -374,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pers_kernel(const __grid_con
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 4); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 8); }
         fence_mbar_init();
         prefetch_tmap(&tmW);
         prefetch_tmap(&tmXh);
@@ -439,7 +492,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pers_kernel(const __grid_con
             }
         }
     } else {
+        // epilogue warps 2..9: warp w reads TMEM lanes 32*(w%4).. (its lane
+        // quarter) and half (w-2)/4 of the accumulator's BN columns
         const int q = warp & 3;
+        const int c_lo = ((warp - 2) >> 2) * (BN / 2), c_hi = c_lo + BN / 2;
         uint32_t lt = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++lt) {
             const uint32_t buf = lt & 1u, use = lt >> 1;
@@ -452,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pers_kernel(const __grid_con
             const float bias = (n < p.N && p.ep.bias) ? bf2f(p.ep.bias[n]) : 0.0f;
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = c_lo; c < c_hi; c += 32) {
                 if (t0 + c >= p.T) break;   // warp-uniform
                 float v[32];
                 tmem_ld32(tbase + (uint32_t)c, v);
@@ -673,7 +729,7 @@ static void launch_pers(cudaStream_t st, const CUtensorMap &mw, const CUtensorMa
     const int n_tiles = ((p.N + BM - 1) / BM) * ((p.T + BN - 1) / BN);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(std::min(n_tiles, n_sm));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(kThreadsP);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
