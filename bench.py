@@ -235,7 +235,8 @@ def main():
     ap.add_argument("--max-len", type=int, default=0, help="cap the forced lengths (profiling cases)")
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel-class profiling pass")
     ap.add_argument("--no-pdl", action="store_true", help="launch step kernels without programmatic dependent launch")
-    ap.add_argument("--legs", default="AB", help="A = decode leg, B = transcription leg (profiling cases)")
+    ap.add_argument("--legs", default="AB", help="A = decode leg, B = transcription leg, E = encoder only "
+                    "(profiling cases)")
     ap.add_argument("--max-slots", type=int, default=256, help="engine slots (profiling cases)")
     args = ap.parse_args()
 
@@ -289,7 +290,8 @@ def main():
     lib = abi.load()
     legs = args.legs.upper()
     # the decode leg alone needs no encoder (a decoder-only blob keeps profiling cases small)
-    wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("enc", "dec") if "B" in legs else ("dec",))
+    with_enc = "B" in legs or "E" in legs
+    wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("enc", "dec") if with_enc else ("dec",))
     ws = W.weights_struct(wb)
     dev = local if world > 1 else 0
     enc_frames = int(case["T_mel"].sum())
@@ -297,7 +299,7 @@ def main():
     def make_engine(profile=0):
         return abi.Engine(lib, dev, wb, ws, max_slots=args.max_slots, max_rows=1024, precision=args.precision,
                           kv_pages=args.kv_pages, no_pdl=int(args.no_pdl), profile=profile,
-                          enc_max_utts=nb if "B" in legs else -1, enc_max_frames=enc_frames)
+                          enc_max_utts=nb if with_enc else -1, enc_max_frames=enc_frames)
 
     eng = make_engine()
     # host inputs: encoder rows (leg A) and log-mel (leg B), fp32 host memory
@@ -320,6 +322,8 @@ def main():
         return out
 
     def leg_b(e):
+        if "E" in legs:   # encoder only (profiling cases): one packed encoder batch
+            return e.encode(mels)
         for b in range(nb):
             e.submit_mel(b, mels[b], int(case["forced_len"][b]))
         e.run()
@@ -330,7 +334,7 @@ def main():
     for _ in range(args.warmup):
         if "A" in legs:
             leg_a(eng, [])
-        if "B" in legs:
+        if with_enc:
             leg_b(eng)
     if eng.status() != 0:
         raise RuntimeError("device status set during warm-up")
@@ -348,7 +352,7 @@ def main():
                 wall_a += time.perf_counter() - t0
                 s1 = eng.stats()
                 dev_a += (s1["step_ms"] - s0["step_ms"]) + (s1["admit_ms"] - s0["admit_ms"])
-            if "B" in legs:
+            if with_enc:
                 s0 = eng.stats()
                 t0 = time.perf_counter()
                 leg_b(eng)
@@ -381,13 +385,13 @@ def main():
         prof = make_engine(profile=1)
         if "A" in legs:
             leg_a(prof, [])
-        if "B" in legs:
+        if with_enc:
             leg_b(prof)
         p0 = prof.stats()
         r0 = prof.profile_report()
         if "A" in legs:
             leg_a(prof, [])
-        if "B" in legs:
+        if with_enc:
             leg_b(prof)
         p1 = prof.stats()
         r1 = prof.profile_report()

@@ -106,42 +106,48 @@ __global__ void dw_packed(const float *in, int Fi, const int *in_off, const int 
     }
 }
 
-// LayerNorm (eps 1e-5) of packed rows of width D: optional fp32 output (may
-// alias x) and bf16 hi/lo planes.
+// LayerNorm (eps 1e-5, biased variance; backends/cpu/backend.c:109-122) of
+// packed rows of width D, one warp per row (40 values per lane in registers):
+// optional fp32 output y (may alias x) and bf16 hi/lo planes.
 __global__ void __launch_bounds__(256) ln_enc(const float *x, int R, const bf16 *w, const bf16 *b, float *y,
                                               bf16 *hi, bf16 *lo) {
-    __shared__ float red[8];
-    const int r = blockIdx.x;
+    constexpr int NV = D / 128;   // float4 per lane
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
     if (r >= R) return;
-    const float *xr = x + (size_t)r * D;
-    float v[D / 256];
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)r * D);
+    float4 v[NV];
     float s = 0.0f;
 #pragma unroll
-    for (int j = 0; j < D / 256; ++j) { v[j] = xr[threadIdx.x + 256 * j]; s += v[j]; }
-    auto bsum = [&](float a) {
-        a = warp_sum(a);
-        __syncthreads();
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
-        __syncthreads();
-        float t = 0.0f;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) t += red[k];
-        return t;
-    };
-    const float mean = bsum(s) / D;
+    for (int j = 0; j < NV; ++j) {
+        v[j] = xr[lane + 32 * j];
+        s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    }
+    const float mean = warp_sum(s) / D;
     float var = 0.0f;
 #pragma unroll
-    for (int j = 0; j < D / 256; ++j) { const float c = v[j] - mean; var += c * c; }
-    const float inv = 1.0f / sqrtf(bsum(var) / D + 1e-5f);
+    for (int j = 0; j < NV; ++j) {
+        const float a = v[j].x - mean, b2 = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
+        var += (a * a + b2 * b2) + (c * c + d * d);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(var) / D + 1e-5f);
 #pragma unroll
-    for (int j = 0; j < D / 256; ++j) {
-        const int k = threadIdx.x + 256 * j;
-        const float o = (v[j] - mean) * inv * bf2f(w[k]) + bf2f(b[k]);
-        if (y) y[(size_t)r * D + k] = o;
+    for (int j = 0; j < NV; ++j) {
+        const int k = 4 * (lane + 32 * j);
+        const float o[4] = {(v[j].x - mean) * inv * bf2f(w[k]) + bf2f(b[k]),
+                            (v[j].y - mean) * inv * bf2f(w[k + 1]) + bf2f(b[k + 1]),
+                            (v[j].z - mean) * inv * bf2f(w[k + 2]) + bf2f(b[k + 2]),
+                            (v[j].w - mean) * inv * bf2f(w[k + 3]) + bf2f(b[k + 3])};
+        if (y) *reinterpret_cast<float4 *>(y + (size_t)r * D + k) = make_float4(o[0], o[1], o[2], o[3]);
         if (hi) {
-            const bf16 h = __float2bfloat16_rn(o);
-            hi[(size_t)r * D + k] = h;
-            if (lo) lo[(size_t)r * D + k] = __float2bfloat16_rn(o - __bfloat162float(h));
+            bf16 h4[4], l4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                h4[e] = __float2bfloat16_rn(o[e]);
+                l4[e] = __float2bfloat16_rn(o[e] - __bfloat162float(h4[e]));
+            }
+            *reinterpret_cast<uint2 *>(hi + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(h4);
+            if (lo) *reinterpret_cast<uint2 *>(lo + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(l4);
         }
     }
 }
@@ -327,26 +333,49 @@ __global__ void __launch_bounds__(256) relpos_flash(const float *QKV, const floa
 
 // GLU(pw1) -> depthwise conv (kernel CK, same padding inside the utterance) ->
 // eval BatchNorm -> SiLU (backends/cpu/backend.c:304-334); output bf16 planes.
-__global__ void glu_dw_packed(const float *pw1, Batch b, const bf16 *dww, const bf16 *dwb, const bf16 *bnw,
-                              const bf16 *bnb, const bf16 *bnm, const bf16 *bnv, bf16 *hi, bf16 *lo) {
-    const size_t n = (size_t)b.R3 * D;
-    const int pad = (CK - 1) / 2;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int row = (int)(i / D), c = (int)(i % D);
-        const int u = b.row_utt3[row];
-        const int base = b.r3_off[u];
-        const int T = b.r3_off[u + 1] - base;
-        const int t = row - base;
-        float s = bf2f(dwb[c]);
-        for (int k = 0; k < CK; ++k) {
-            const int ti = t - pad + k;
-            if (ti < 0 || ti >= T) continue;
-            const float a = pw1[(size_t)(base + ti) * 2 * D + c];
-            const float g = pw1[(size_t)(base + ti) * 2 * D + D + c];
-            s += bf2f(dww[c * CK + k]) * (a / (1.0f + expf(-g)));
+// Block = GR packed rows x GC channels: the GLU of rows [r0 - pad, r0 + GR +
+// pad) is computed once into shared memory (coalesced along channels), then
+// each output sums its CK taps from there, skipping taps outside its own
+// utterance.
+constexpr int GR = 32, GC = 128;
+__global__ void __launch_bounds__(256) glu_dw_packed(const float *pw1, Batch b, const bf16 *dww, const bf16 *dwb,
+                                                     const bf16 *bnw, const bf16 *bnb, const bf16 *bnm,
+                                                     const bf16 *bnv, bf16 *hi, bf16 *lo) {
+    constexpr int pad = (CK - 1) / 2, HR = GR + CK - 1;
+    __shared__ float g_s[HR][GC];
+    const int r0 = blockIdx.x * GR, c0 = blockIdx.y * GC;
+    const int tc = threadIdx.x & (GC - 1), tr = threadIdx.x / GC;   // 2 row lanes x 128 channels
+    const int c = c0 + tc;
+    for (int hr = tr; hr < HR; hr += 256 / GC) {
+        const int row = r0 - pad + hr;
+        float gv = 0.0f;
+        if (row >= 0 && row < b.R3) {
+            const float a = pw1[(size_t)row * 2 * D + c];
+            const float g = pw1[(size_t)row * 2 * D + D + c];
+            gv = a / (1.0f + expf(-g));
         }
-        float v = (s - bf2f(bnm[c])) / sqrtf(bf2f(bnv[c]) + 1e-5f) * bf2f(bnw[c]) + bf2f(bnb[c]);
+        g_s[hr][tc] = gv;
+    }
+    float wk[CK];
+#pragma unroll
+    for (int k = 0; k < CK; ++k) wk[k] = bf2f(dww[c * CK + k]);
+    const float bias = bf2f(dwb[c]);
+    const float bn_scale = bf2f(bnw[c]) / sqrtf(bf2f(bnv[c]) + 1e-5f), bn_mean = bf2f(bnm[c]), bn_b = bf2f(bnb[c]);
+    __syncthreads();
+    for (int rr = tr; rr < GR; rr += 256 / GC) {
+        const int row = r0 + rr;
+        if (row >= b.R3) break;
+        const int u = b.row_utt3[row];
+        const int lo_row = b.r3_off[u], hi_row = b.r3_off[u + 1];
+        float sum = bias;
+#pragma unroll
+        for (int k = 0; k < CK; ++k) {
+            const int ti = row - pad + k;
+            if (ti >= lo_row && ti < hi_row) sum += wk[k] * g_s[rr + k][tc];
+        }
+        float v = (sum - bn_mean) * bn_scale + bn_b;
         v = v / (1.0f + expf(-v));
+        const size_t i = (size_t)row * D + c;
         const bf16 hb = __float2bfloat16_rn(v);
         hi[i] = hb;
         if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(hb));
@@ -550,7 +579,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     for (int l = 0; l < NL; ++l) {
         const Layer &L = w.L[l];
         // FFN1: x += 0.5 * W2 silu(W1 LN(x) + b1) + b2
-        ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.ff1_lnw, L.ff1_lnb, nullptr, st.xa[0], lo_a);
+        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.ff1_lnw, L.ff1_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
         GemmEpilogue f1;
         f1.epi = EPI_BF16; f1.act = 1; f1.bias = L.ff1_b1; f1.Ybf = st.hid[0]; f1.Ybf_lo = lo_h; f1.ldy = FF;
@@ -561,7 +590,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         egemm_enc(s, st, L.ff1_w2, D, FF, hidp, R3, RT, f2);
         mark(s, st, "enc_gemm_ffn2");
         // relative-position self-attention: x += Wo attn(LN(x)) + bo
-        ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.sa_lnw, L.sa_lnb, nullptr, st.xa[0], lo_a);
+        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.sa_lnw, L.sa_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
         GemmEpilogue eq;
         eq.bias = L.qkv_b; eq.Y = st.qkv; eq.ldy = 3 * D;
@@ -578,13 +607,13 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         egemm_enc(s, st, L.sa_ow, D, D, app, R3, RT, eo2);
         mark(s, st, "enc_gemm_o");
         // conv module: x += pw2(silu(bn(dw(glu(pw1(LN(x)))))))
-        ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.cv_lnw, L.cv_lnb, nullptr, st.xa[0], lo_a);
+        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.cv_lnw, L.cv_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
         GemmEpilogue e1;
         e1.bias = L.cv_pw1b; e1.Y = st.qkv; e1.ldy = 2 * D;
         egemm_enc(s, st, L.cv_pw1w, 2 * D, D, xap, R3, RT, e1);
         mark(s, st, "enc_gemm_pw1");
-        glu_dw_packed<<<grid_of((size_t)R3 * D), 256, 0, s>>>(st.qkv, bt, L.cv_dww, L.cv_dwb, L.cv_bnw, L.cv_bnb,
+        glu_dw_packed<<<dim3((R3 + GR - 1) / GR, D / GC), 256, 0, s>>>(st.qkv, bt, L.cv_dww, L.cv_dwb, L.cv_bnw, L.cv_bnb,
                                                               L.cv_bnm, L.cv_bnv, st.ap[0], lo_p);
         mark(s, st, "enc_glu_dwconv");
         GemmEpilogue e2;
@@ -592,7 +621,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         egemm_enc(s, st, L.cv_pw2w, D, D, app, R3, RT, e2);
         mark(s, st, "enc_gemm_pw2");
         // FFN2
-        ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.ff2_lnw, L.ff2_lnb, nullptr, st.xa[0], lo_a);
+        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.ff2_lnw, L.ff2_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
         GemmEpilogue g1 = f1;
         g1.bias = L.ff2_b1;
@@ -603,7 +632,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         egemm_enc(s, st, L.ff2_w2, D, FF, hidp, R3, RT, g2);
         mark(s, st, "enc_gemm_ffn2");
         // x = LN_out(x); its planes feed the next layer's nothing / the projection
-        ln_enc<<<R3, 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a);
+        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
     }
     // ---- encoder -> decoder projection (model.h:607) ----
