@@ -4,8 +4,11 @@
 Workload (full-size model, one B200 per rank): 64
 utterances per GPU of U(5, 30) s of seeded N(0, 1) log-mel (128 bins, 10 ms
 hop), EOS forced at U{20..220} generated tokens, seeded random-init bf16
-weights (there is no network for checkpoints or audio).  Rank r draws its own
-64 utterances (seed r): the job is sharded by utterance, with no collective.
+weights (there is no network for checkpoints or audio).  With N GPUs the job
+is 64 * N utterances, dispatched to the ranks by queued audio seconds
+(cohere-transcribe_b200/dispatch.py); each rank runs its own engine on its
+shard, with no collective on the data path (NCCL carries only the barrier and
+the max / sum of the timings).
 
 One bench step runs two legs over that batch:
 
@@ -53,16 +56,27 @@ CPU_CUT_S = 1.0        # seconds of log-mel per utterance in the CPU transcripti
 CPU_CUT_TOKENS = 8     # generated-token cap per utterance in the CPU transcription sample
 
 
-def workload(seed: int = 0, batch: int = BATCH):
+def workload(seed: int = 0, batch: int = BATCH, rank: int = 0, world: int = 1):
     """Configuration 3: seconds ~ U(5, 30), forced lengths ~ U{20..220}; log-mel
-    N(0, 1) [128, 100 s + 1] per utterance; encoder rows N(0, 1) [T_enc, 1024]."""
+    N(0, 1) [128, 100 s + 1] per utterance; encoder rows N(0, 1) [T_enc, 1024].
+    With world > 1 the job is batch * world utterances, dispatched by queued
+    audio seconds; this rank's shard is returned (inputs seeded per utterance,
+    so a shard is generated alone)."""
     import inputs
-    case = inputs.ragged_decode_case(batch, seed=seed, t_lo=5.0, t_hi=30.0, l_lo=20, l_hi=220)
-    enc = inputs.enc_outputs(case["T_enc"], case["enc_seed"])
+    disp = importlib.import_module("cohere-transcribe_b200.dispatch")
+    full = inputs.ragged_decode_case(batch * world, seed=seed, t_lo=5.0, t_hi=30.0, l_lo=20, l_hi=220)
+    idx = np.array([i for i, _ in disp.shard(list(range(batch * world)), full["seconds"], rank, world)], np.int64)
+    case = {k: (v[idx] if isinstance(v, np.ndarray) else v) for k, v in full.items()}
+    case["index"] = idx
+    T_enc = case["T_enc"]
+    enc = np.zeros((len(idx), int(T_enc.max()), 1024), np.float32)
+    for j, (i, t) in enumerate(zip(idx, T_enc)):
+        rng = np.random.default_rng([full["enc_seed"], int(i)])
+        enc[j, :t] = rng.standard_normal((int(t), 1024), dtype=np.float32)
     T_mel = np.array([inputs.ctb.t_mel_of_seconds(x) for x in case["seconds"]], np.int32)
     mels = []
-    for b, t in enumerate(T_mel):
-        rng = np.random.default_rng([seed, 7, b])
+    for i, t in zip(idx, T_mel):
+        rng = np.random.default_rng([seed, 7, int(i)])
         mels.append(rng.standard_normal((128, int(t)), dtype=np.float32))
     case["T_mel"] = T_mel
     return case, enc, mels
@@ -242,16 +256,18 @@ def main():
 
     world, rank, local = dist_setup()
     pk, pk_kind = peaks()
-    case, enc, mels = workload(rank, args.batch)
+    case, enc, mels = workload(0, args.batch, rank, world)
     if args.max_len > 0:
         case["forced_len"] = np.minimum(case["forced_len"], args.max_len).astype(np.int32)
-    nb = args.batch
+    nb = len(case["T_enc"])
     tokens_per_step = int(case["forced_len"].sum())
     audio_s = float(case["seconds"].sum())
     ncores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
-    cfg = {"workload": f"config 3: {nb} ragged utterances/GPU of U(5,30) s log-mel, EOS forced at U{{20..220}}",
-           "global_batch": nb * world, "model": "encoder 48 x 1280 (8 heads, FFN 5120, dw-K 9), decoder 8 x 1024 "
+    cfg = {"workload": f"config 3: {args.batch} ragged utterances/GPU of U(5,30) s log-mel, EOS forced at U{{20..220}}"
+                       + (f"; {args.batch * world} utterances dispatched to {world} GPUs by queued audio seconds"
+                          if world > 1 else ""),
+           "global_batch": args.batch * world, "model": "encoder 48 x 1280 (8 heads, FFN 5120, dw-K 9), decoder 8 x 1024 "
            "(8 heads, FFN 4096, vocab 16384): model.h dims, random-init bf16",
            "prompt_tokens": 10, "kv": "bf16 pages of 16 rows",
            "l2": "not flushed: per-step working sets (3.8 GB encoder weights, 268 MB decoder weights + KV) > 126 MB L2",
