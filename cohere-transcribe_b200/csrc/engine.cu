@@ -33,10 +33,12 @@ constexpr int SELF_PAGES = MAX_SEQ / PR;     // 64
 constexpr int CROSS_PAGES = 64;              // T_enc <= 1024
 constexpr long long PAGE_ELEMS = (long long)NL * 2 * PR * D;
 enum { S_FREE = 0, S_PREFILL = 1, S_DECODE = 2, S_DONE = 3 };
-constexpr int KCH = 64;                        // attention keys per work item (4 pages)
 constexpr int AW = 8;                          // consumer warps per attention CTA (one per head)
-constexpr int KCH_MAX = (MAX_SEQ + KCH - 1) / KCH;   // chunks per row (self and cross)
 constexpr int ANST = 3;                        // page stages in the attention pipeline
+constexpr int PMIN = 5;                        // minimum pages per attention CTA
+constexpr int SEG_MAX = 16;                    // segments a row can be split into across CTAs
+static_assert((SELF_PAGES + PMIN - 1) / PMIN + 1 <= SEG_MAX && (CROSS_PAGES + PMIN - 1) / PMIN + 1 <= SEG_MAX,
+              "a row of 64 pages over CTAs of >= PMIN pages must fit SEG_MAX segments");
 
 struct DevState {
     int *state, *tok, *pos, *gen, *forced, *tenc;
@@ -49,8 +51,12 @@ struct DevState {
     long long *r_off;            // self page offset of each row
     int *q_row, *q_slot;         // per sequence: last row, slot
     int *n_rows, *n_seqs;        // device counts
-    int *w_self, *w_cross;       // attention work items: row << 8 | chunk
-    int *n_wself, *n_wcross;     // item counts
+    // attention page lists of the step (self, cross): one entry per (row, page):
+    // meta = row | page-in-row << 10 | (valid keys - 1) << 16 | last-page << 20
+    int *w_self, *w_cross;       // meta, [rows * 64]
+    int *pid_self, *pid_cross;   // pool page id, [rows * 64]
+    int *rp_self, *rp_cross;     // per row: first entry (prefix sum over rows), [rows + 1]
+    int *n_wself, *n_wcross;     // entry counts
     int max_slots, max_rows, n_prompt;
 };
 
@@ -88,18 +94,18 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     const int st = i < s.max_slots ? s.state[i] : S_FREE;
     int nr = st == S_PREFILL ? s.n_prompt : st == S_DECODE ? 1 : 0;
     const int te = nr > 0 ? s.tenc[i] : 0;
-    const int cross_ck = (te + KCH - 1) / KCH;
-    int self_items = 0;
-    if (st == S_PREFILL) for (int j = 0; j < nr; ++j) self_items += (j + 1 + KCH - 1) / KCH;
-    else if (st == S_DECODE) self_items = (s.pos[i] + 1 + KCH - 1) / KCH;
-    int total = 0, nseq = 0, n_ws = 0, n_wc = 0;
+    const int cross_np = (te + PR - 1) / PR;
+    int self_np = 0;   // self-attention pages over the slot's rows
+    if (st == S_PREFILL) for (int j = 0; j < nr; ++j) self_np += (j + 1 + PR - 1) / PR;
+    else if (st == S_DECODE) self_np = (s.pos[i] + 1 + PR - 1) / PR;
+    int total = 0, nseq = 0, n_ps = 0, n_pc = 0;
     const int base = block_excl_scan(nr, tmp, &total);
     __syncthreads();
     const int sidx = block_excl_scan(nr > 0 ? 1 : 0, tmp2, &nseq);
     __syncthreads();
-    const int wsb = block_excl_scan(self_items, tmp, &n_ws);
+    const int psb = block_excl_scan(self_np, tmp, &n_ps);
     __syncthreads();
-    const int wcb = block_excl_scan(nr * cross_ck, tmp2, &n_wc);
+    const int pcb = block_excl_scan(nr * cross_np, tmp2, &n_pc);
     if (total > row_cap || nseq > seq_cap) {   // the host bounds admissions; never expected
         if (i == 0) { set_status(CT_STATUS_BAD_ARG); *s.n_rows = 0; *s.n_seqs = 0; }
         return;
@@ -114,16 +120,34 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
         s.r_off[r] = page >= 0 ? (long long)page * PAGE_ELEMS + (long long)(p % PR) * D : -1;
     }
     if (nr > 0) { s.q_row[sidx] = base + nr - 1; s.q_slot[sidx] = i; }
-    // attention work lists: (row, 32-key chunk) pairs, rows in order
-    int ws_i = wsb, wc_i = wcb;
+    // attention page lists, rows in order: row r's entries are [rp[r], rp[r+1])
+    int gs = psb, gc = pcb;
     for (int j = 0; j < nr; ++j) {
         const int r = base + j;
-        const int p = st == S_PREFILL ? j : s.pos[i];
-        const int nck = (p + 1 + KCH - 1) / KCH;
-        for (int c = 0; c < nck && ws_i < row_cap * KCH_MAX; ++c) s.w_self[ws_i++] = (r << 8) | c;
-        for (int c = 0; c < cross_ck && wc_i < row_cap * KCH_MAX; ++c) s.w_cross[wc_i++] = (r << 8) | c;
+        const int L = (st == S_PREFILL ? j : s.pos[i]) + 1;      // causal: keys 0 .. position
+        const int np = min((L + PR - 1) / PR, SELF_PAGES);
+        s.rp_self[r] = gs;
+        for (int q = 0; q < np; ++q, ++gs) {
+            int pid = s.self_pt[i * SELF_PAGES + q];
+            if (pid < 0) { set_status(CT_STATUS_BAD_ARG); pid = 0; }
+            const int nv = min(PR, L - q * PR);
+            s.pid_self[gs] = pid;
+            s.w_self[gs] = r | q << 10 | (nv - 1) << 16 | (q == np - 1) << 20;
+        }
+        s.rp_cross[r] = gc;
+        for (int q = 0; q < cross_np; ++q, ++gc) {
+            int pid = s.cross_pt[i * CROSS_PAGES + q];
+            if (pid < 0) { set_status(CT_STATUS_BAD_ARG); pid = 0; }
+            const int nv = min(PR, te - q * PR);
+            s.pid_cross[gc] = pid;
+            s.w_cross[gc] = r | q << 10 | (nv - 1) << 16 | (q == cross_np - 1) << 20;
+        }
     }
-    if (i == 0) { *s.n_rows = total; *s.n_seqs = nseq; *s.n_wself = n_ws; *s.n_wcross = n_wc; }
+    if (i == 0) {
+        *s.n_rows = total; *s.n_seqs = nseq; *s.n_wself = n_ps; *s.n_wcross = n_pc;
+        s.rp_self[total] = n_ps;
+        s.rp_cross[total] = n_pc;
+    }
 }
 
 __device__ __forceinline__ void store_planes(float v, bf16 *hi, bf16 *lo, size_t idx) {
@@ -221,20 +245,15 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const int *n, const int *r
 // merges them in chunk order.
 struct AttnSmem {
     bf16 kv[ANST][2][PR * D];                  // [stage][K,V][16 rows x 1024]
+    float pbuf[AW][PR];                        // per consumer warp: the page's probabilities
     uint64_t full[ANST], empty[ANST];
-    int last_flag;
 };
 
-__device__ __forceinline__ void item_span(const DevState &s, int cross, int w, int &r, int &c, int &L, int &p0,
-                                          int &p1, const int *&pt) {
-    r = w >> 8;
-    c = w & 255;
-    const int slot = s.r_slot[r];
-    L = cross ? s.tenc[slot] : s.r_pos[r] + 1;
-    pt = (cross ? s.cross_pt : s.self_pt) + slot * (cross ? CROSS_PAGES : SELF_PAGES);
-    const int k0 = c * KCH, k1 = min(L, k0 + KCH);
-    p0 = k0 / PR;
-    p1 = k1 > k0 ? (k1 - 1) / PR + 1 : p0;     // pages [p0, p1)
+// Attention CTA count actually used for `pages` entries (>= PMIN pages each).
+__device__ __forceinline__ int attn_ctas_used(int pages, int grid) { return max(1, min(grid, pages / PMIN)); }
+// The CTA whose entry range [g*P/G ...) holds entry g.
+__device__ __forceinline__ int attn_cta_of(int g, int P, int G) {
+    return (int)(((long long)(g + 1) * G - 1) / P);
 }
 
 __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s, const float *Q, const bf16 *pool,
@@ -248,118 +267,159 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
         fence_mbar_init();
     }
     __syncthreads();
-    pdl_wait();
-    pdl_trigger();
-    const int n_items = cross ? *s.n_wcross : *s.n_wself;
-    const int *items = cross ? s.w_cross : s.w_self;
+    // The page lists (row builder) and the K/V pages of earlier positions are
+    // written at least two kernels upstream, so they may be read before the
+    // dependency wait (this kernel's predecessor completes only after every
+    // kernel before it has).  Only Q and, for self-attention, a row's last
+    // page (which holds the row just projected) need the wait.
+    const int P = cross ? *s.n_wcross : *s.n_wself;
+    const int G = attn_ctas_used(P, gridDim.x);
+    const int b = blockIdx.x;
+    if (b >= G || P == 0) {
+        pdl_wait();
+        pdl_trigger();
+        return;
+    }
+    const int g0 = (int)((long long)b * P / G), g1 = (int)((long long)(b + 1) * P / G);
+    const int n = g1 - g0;
+    const int *meta_l = (cross ? s.w_cross : s.w_self) + g0;
+    const int *pid_l = (cross ? s.pid_cross : s.pid_self) + g0;
+    const int *rp = cross ? s.rp_cross : s.rp_self;
     const long long kvoff = (long long)layer * 2 * PR * D;
 
     if (warp == AW) {
-        // ---------------------------------------------------------- producer
-        if (lane == 0) {
-            int g = 0;   // pages issued so far (ring position)
-            for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-                int r, c, L, p0, p1;
-                const int *pt;
-                item_span(s, cross, items[it], r, c, L, p0, p1, pt);
-                for (int p = p0; p < p1; ++p, ++g) {
-                    const int st = g % ANST;
-                    if (g >= ANST && !mbar_wait(&sm.empty[st], ((g / ANST) & 1) ^ 1, CT_STATUS_TIMEOUT_FREE)) return;
-                    const int page = max(pt[p], 0);
-                    const bf16 *src = pool + (long long)page * PAGE_ELEMS + kvoff;
-                    mbar_expect_tx(&sm.full[st], 2 * PR * D * sizeof(bf16));
-                    bulk_load(sm.kv[st][0], src, PR * D * sizeof(bf16), &sm.full[st]);
-                    bulk_load(sm.kv[st][1], src + PR * D, PR * D * sizeof(bf16), &sm.full[st]);
+        // ------------------------------------------------------ producer warp
+        // page ids fetched 32 at a time (one round trip), bulk loads by lane 0;
+        // the first stages are issued before the dependency wait when allowed
+        bool waited = false;
+        for (int i0 = 0; i0 < n; i0 += 32) {
+            const int pid_v = i0 + lane < n ? pid_l[i0 + lane] : 0;
+            const int last_v = (!cross && i0 + lane < n) ? (meta_l[i0 + lane] >> 20) & 1 : 0;
+            const int cnt = min(32, n - i0);
+            for (int j = 0; j < cnt; ++j) {
+                const int pid = __shfl_sync(0xffffffffu, pid_v, j);
+                const int lastp = __shfl_sync(0xffffffffu, last_v, j);
+                const int g = i0 + j, st = g % ANST;
+                if (!waited && (g >= ANST || lastp)) {
+                    pdl_wait();
+                    pdl_trigger();
+                    waited = true;
                 }
+                bool ok = true;
+                if (lane == 0) {
+                    if (g >= ANST) ok = mbar_wait(&sm.empty[st], ((g / ANST) & 1) ^ 1, CT_STATUS_TIMEOUT_FREE);
+                    if (ok) {
+                        const bf16 *src = pool + (long long)pid * PAGE_ELEMS + kvoff;
+                        mbar_expect_tx(&sm.full[st], 2 * PR * D * sizeof(bf16));
+                        bulk_load(sm.kv[st][0], src, PR * D * sizeof(bf16), &sm.full[st]);
+                        bulk_load(sm.kv[st][1], src + PR * D, PR * D * sizeof(bf16), &sm.full[st]);
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, (int)ok, 0)) return;
             }
         }
+        if (!waited) { pdl_wait(); pdl_trigger(); }
         return;
     }
-    // -------------------------------------------------------------- consumers
+    pdl_wait();
+    pdl_trigger();
+    // ---------------------------------------------------------- consumer warps
     const int hh = warp;
     const float scale = 1.0f / sqrtf((float)DK);
-    int g = 0;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-        int r, c, L, p0, p1;
-        const int *pt;
-        item_span(s, cross, items[it], r, c, L, p0, p1, pt);
-        const int nck = (L + KCH - 1) / KCH;
-        for (int p = p0; p < p1; ++p)
-            if (pt[p] < 0) { if (lane == 0) set_status(CT_STATUS_BAD_ARG); }
-        const float4 qv = *reinterpret_cast<const float4 *>(Q + (size_t)r * D + hh * DK + 4 * lane);
-        float m = -INFINITY, l = 0.0f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-        for (int p = p0; p < p1; ++p, ++g) {
-            const int st = g % ANST;
-            if (!mbar_wait(&sm.full[st], (g / ANST) & 1, CT_STATUS_TIMEOUT_TMA)) return;
-            const bf16 *Ks = sm.kv[st][0] + hh * DK + 4 * lane;
-            const bf16 *Vs = sm.kv[st][1] + hh * DK + 4 * lane;
-            // partial dot products of the page's 16 keys over this lane's 4 dims
-            float sc[PR];
-#pragma unroll
-            for (int k = 0; k < PR; ++k) {
-                const uint2 u = *reinterpret_cast<const uint2 *>(Ks + k * D);
-                const bf16 *e = reinterpret_cast<const bf16 *>(&u);
-                sc[k] = qv.x * __bfloat162float(e[0]) + qv.y * __bfloat162float(e[1]) +
-                        qv.z * __bfloat162float(e[2]) + qv.w * __bfloat162float(e[3]);
-            }
-            // butterfly reduce-scatter: after it lane l holds key (l >> 1)'s full score
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const bool up = lane & 16;
-                const float send = up ? sc[k] : sc[k + 8];
-                const float keep = up ? sc[k + 8] : sc[k];
-                sc[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const bool up = lane & 8;
-                const float send = up ? sc[k] : sc[k + 4];
-                const float keep = up ? sc[k + 4] : sc[k];
-                sc[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-            }
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                const bool up = lane & 4;
-                const float send = up ? sc[k] : sc[k + 2];
-                const float keep = up ? sc[k + 2] : sc[k];
-                sc[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-            }
-            {
-                const bool up = lane & 2;
-                const float send = up ? sc[0] : sc[1];
-                const float keep = up ? sc[1] : sc[0];
-                sc[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-            }
-            sc[0] += __shfl_xor_sync(0xffffffffu, sc[0], 1);
-            // lane l now holds the score of key j = bit-reversed index built above
-            const int j = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
-            const int key = p * PR + j;
-            const bool valid = key >= c * KCH && key < min(L, (c + 1) * KCH);
-            const float sj = valid ? sc[0] * scale : -INFINITY;
-            const float mn = fmaxf(m, warp_max(sj));
-            const float corr = expf(m - mn);   // m = -inf before the first valid key -> 0
-            const float pj = valid ? expf(sj - mn) : 0.0f;
-            l = l * corr + warp_sum(pj) * 0.5f;   // every key is held by two lanes
-            o0 *= corr; o1 *= corr; o2 *= corr; o3 *= corr;
-#pragma unroll
-            for (int k = 0; k < PR; ++k) {
-                // key k sits on lanes whose bits 4..1 spell k
-                const int src = ((k >> 3) & 1) << 4 | ((k >> 2) & 1) << 3 | ((k >> 1) & 1) << 2 | (k & 1) << 1;
-                const float pk = __shfl_sync(0xffffffffu, pj, src);
-                if (pk == 0.0f) continue;   // masked (or underflowed) key: its V row may be stale or unset
-                const uint2 u = *reinterpret_cast<const uint2 *>(Vs + k * D);
-                const bf16 *e = reinterpret_cast<const bf16 *>(&u);
-                o0 += pk * __bfloat162float(e[0]);
-                o1 += pk * __bfloat162float(e[1]);
-                o2 += pk * __bfloat162float(e[2]);
-                o3 += pk * __bfloat162float(e[3]);
-            }
-            m = mn;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.empty[st]);
+    float *pb = sm.pbuf[warp];
+    float m = -INFINITY, l = 0.0f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+    float4 qv = make_float4(0.f, 0.f, 0.f, 0.f);
+    int rpa = 0, rpb = 0;        // the current row's entry range
+    int meta_v = 0;
+    for (int g = 0; g < n; ++g) {
+        if ((g & 31) == 0) meta_v = g + lane < n ? meta_l[g + lane] : 0;
+        const int meta = __shfl_sync(0xffffffffu, meta_v, g & 31);
+        const int r = meta & 1023, pg = (meta >> 10) & 63, nv = ((meta >> 16) & 15) + 1, last = (meta >> 20) & 1;
+        if (g == 0 || pg == 0) {   // a row segment starts
+            qv = *reinterpret_cast<const float4 *>(Q + (size_t)r * D + hh * DK + 4 * lane);
+            rpa = rp[r];
+            rpb = rp[r + 1];
+            m = -INFINITY; l = 0.0f; o0 = o1 = o2 = o3 = 0.0f;
         }
+        const int st = g % ANST;
+        if (!mbar_wait(&sm.full[st], (g / ANST) & 1, CT_STATUS_TIMEOUT_TMA)) return;
+        const bf16 *Ks = sm.kv[st][0] + hh * DK + 4 * lane;
+        const bf16 *Vs = sm.kv[st][1] + hh * DK + 4 * lane;
+        // partial dot products of the page's 16 keys over this lane's 4 dims
+        float sc[PR];
+#pragma unroll
+        for (int k = 0; k < PR; ++k) {
+            const uint2 u = *reinterpret_cast<const uint2 *>(Ks + k * D);
+            const bf16 *e = reinterpret_cast<const bf16 *>(&u);
+            sc[k] = qv.x * __bfloat162float(e[0]) + qv.y * __bfloat162float(e[1]) +
+                    qv.z * __bfloat162float(e[2]) + qv.w * __bfloat162float(e[3]);
+        }
+        // butterfly reduce-scatter: afterwards lanes 2j', 2j'+1 hold one key's score
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const bool up = lane & 16;
+            const float send = up ? sc[k] : sc[k + 8];
+            const float keep = up ? sc[k + 8] : sc[k];
+            sc[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const bool up = lane & 8;
+            const float send = up ? sc[k] : sc[k + 4];
+            const float keep = up ? sc[k + 4] : sc[k];
+            sc[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const bool up = lane & 4;
+            const float send = up ? sc[k] : sc[k + 2];
+            const float keep = up ? sc[k + 2] : sc[k];
+            sc[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+        {
+            const bool up = lane & 2;
+            const float send = up ? sc[0] : sc[1];
+            const float keep = up ? sc[1] : sc[0];
+            sc[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+        }
+        sc[0] += __shfl_xor_sync(0xffffffffu, sc[0], 1);
+        // lane l holds the score of key j: bits 4..1 of l, reversed
+        const int j = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+        const bool valid = j < nv;
+        const float sj = valid ? sc[0] * scale : -INFINITY;
+        const float mn = fmaxf(m, warp_max(sj));       // key 0 of the page is always valid
+        const float corr = expf(m - mn);               // m = -inf at a segment start -> 0
+        const float pj = valid ? expf(sj - mn) : 0.0f;
+        l = l * corr + warp_sum(pj) * 0.5f;            // every key is held by two lanes
+        o0 *= corr; o1 *= corr; o2 *= corr; o3 *= corr;
+        m = mn;
+        if ((lane & 1) == 0) pb[j] = pj;
+        __syncwarp();
+        // P.V: probabilities broadcast from shared memory; masked keys have p = 0
+        // (their V rows are finite: the pool starts zeroed and holds only
+        // projected values)
+        const float4 *p4 = reinterpret_cast<const float4 *>(pb);
+#pragma unroll
+        for (int k4 = 0; k4 < PR / 4; ++k4) {
+            const float4 pk = p4[k4];
+            const float pv[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const uint2 u = *reinterpret_cast<const uint2 *>(Vs + (4 * k4 + t) * D);
+                const bf16 *e = reinterpret_cast<const bf16 *>(&u);
+                o0 += pv[t] * __bfloat162float(e[0]);
+                o1 += pv[t] * __bfloat162float(e[1]);
+                o2 += pv[t] * __bfloat162float(e[2]);
+                o3 += pv[t] * __bfloat162float(e[3]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[st]);
+        if (!(last || g == n - 1)) continue;
+        // ---- the row segment ends here
         const size_t idx = (size_t)r * D + hh * DK + 4 * lane;
-        if (nck == 1) {
+        const int c0 = attn_cta_of(rpa, P, G), nseg = attn_cta_of(rpb - 1, P, G) - c0 + 1;
+        if (nseg == 1) {
             const float inv = 1.0f / l;
             store_planes(o0 * inv, hi, lo, idx);
             store_planes(o1 * inv, hi, lo, idx + 1);
@@ -367,21 +427,24 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
             store_planes(o3 * inv, hi, lo, idx + 3);
             continue;
         }
-        float *wp = ws + ((size_t)r * KCH_MAX + c) * (2 * H + D);
+        const int seg = b - c0;
+        float *wp = ws + ((size_t)r * SEG_MAX + seg) * (2 * H + D);
         if (lane == 0) { wp[hh] = m; wp[H + hh] = l; }
         *reinterpret_cast<float4 *>(wp + 2 * H + hh * DK + 4 * lane) = make_float4(o0, o1, o2, o3);
+        // per-(row, head) ticket: the warp that completes the head's last
+        // segment combines it (no barrier between the consumer warps)
         __threadfence();
-        asm volatile("bar.sync 1, %0;" ::"n"(AW * 32));   // consumer warps only
-        if (threadIdx.x == 0) sm.last_flag = atomicAdd(&tickets[r], 1) == nck - 1;
-        asm volatile("bar.sync 1, %0;" ::"n"(AW * 32));
-        if (!sm.last_flag) continue;
+        __syncwarp();
+        int tk = 0;
+        if (lane == 0) tk = atomicAdd(&tickets[r * H + hh], 1);
+        if (__shfl_sync(0xffffffffu, tk, 0) != nseg - 1) continue;
         __threadfence();
-        const float *wr = ws + (size_t)r * KCH_MAX * (2 * H + D);
+        const float *wr = ws + (size_t)r * SEG_MAX * (2 * H + D);
         float Mg = -INFINITY;
-        for (int cc = 0; cc < nck; ++cc) Mg = fmaxf(Mg, wr[(size_t)cc * (2 * H + D) + hh]);
+        for (int cc = 0; cc < nseg; ++cc) Mg = fmaxf(Mg, wr[(size_t)cc * (2 * H + D) + hh]);
         float Lg = 0.0f;
         float4 og = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int cc = 0; cc < nck; ++cc) {
+        for (int cc = 0; cc < nseg; ++cc) {
             const float *pc = wr + (size_t)cc * (2 * H + D);
             const float f = expf(pc[hh] - Mg);
             Lg += pc[H + hh] * f;
@@ -393,8 +456,7 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
         store_planes(og.y * inv, hi, lo, idx + 1);
         store_planes(og.z * inv, hi, lo, idx + 2);
         store_planes(og.w * inv, hi, lo, idx + 3);
-        asm volatile("bar.sync 1, %0;" ::"n"(AW * 32));   // everyone has read last_flag
-        if (threadIdx.x == 0) tickets[r] = 0;                // ready for the next launch
+        if (lane == 0) tickets[r * H + hh] = 0;              // ready for the next launch
     }
 }
 
@@ -506,7 +568,7 @@ struct ct_engine {
     int *h_done = nullptr;   // host view of done_map
     // step buffers
     float *h = nullptr, *q = nullptr, *attn_ws = nullptr, *logits = nullptr;
-    int *tickets = nullptr;          // per-row chunk counters of the attention kernel
+    int *tickets = nullptr;          // per (row, head) segment counters of the attention kernel
     int attn_ctas = 296;             // persistent attention grid (2 per SM)
     bf16 *xa[2], *xb[2], *xm[2], *lm[2];
     int *next = nullptr;
@@ -1111,7 +1173,8 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
                     e->enc_pl[1], e->enc_off, e->ds.state, e->ds.tok, e->ds.pos, e->ds.gen, e->ds.forced,
                     e->ds.tenc, e->ds.self_pt, e->ds.cross_pt, e->ds.out_tok, e->ds.prompt, e->ds.r_slot,
                     e->ds.r_pos, e->ds.r_tok, e->ds.r_off, e->ds.q_row, e->ds.q_slot, e->ds.n_rows, e->ds.n_seqs,
-                    e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.n_wself, e->ds.n_wcross, e->rec_dev,
+                    e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.pid_self, e->ds.pid_cross, e->ds.rp_self,
+                    e->ds.rp_cross, e->ds.n_wself, e->ds.n_wcross, e->rec_dev,
                     e->mel_rows};
     for (void *p : ptrs) cudaFree(p);
     for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
@@ -1152,7 +1215,9 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     if (cfg.max_slots <= 0) cfg.max_slots = 256;
     if (cfg.max_rows <= 0) cfg.max_rows = 1024;
     if (cfg.n_prompt <= 0) cfg.n_prompt = 10;
-    if (cfg.max_slots > 1024 || cfg.n_prompt > 64 || cfg.max_rows < cfg.n_prompt) return CT_EINVAL;
+    // attention page entries pack the row index in 10 bits
+    if (cfg.max_slots > 1024 || cfg.n_prompt > 64 || cfg.max_rows < cfg.n_prompt || cfg.max_rows > 1024)
+        return CT_EINVAL;
     static const int kPrompt[10] = {13764, 7, 4, 16, 62, 62, 5, 9, 11, 13};
     ct_engine *e = new ct_engine();
     e->cfg = cfg;
@@ -1215,7 +1280,9 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         dalloc(&s.out_tok, (size_t)S * MAX_SEQ) || dalloc(&s.prompt, cfg.n_prompt) || dalloc(&s.r_slot, R) ||
         dalloc(&s.r_pos, R) || dalloc(&s.r_tok, R) || dalloc(&s.r_off, R) || dalloc(&s.q_row, S) ||
         dalloc(&s.q_slot, S) || dalloc(&s.n_rows, 1) || dalloc(&s.n_seqs, 1) ||
-        dalloc(&s.w_self, (size_t)R * KCH_MAX) || dalloc(&s.w_cross, (size_t)R * KCH_MAX) || dalloc(&s.n_wself, 1) ||
+        dalloc(&s.w_self, (size_t)R * SELF_PAGES) || dalloc(&s.w_cross, (size_t)R * CROSS_PAGES) ||
+        dalloc(&s.pid_self, (size_t)R * SELF_PAGES) || dalloc(&s.pid_cross, (size_t)R * CROSS_PAGES) ||
+        dalloc(&s.rp_self, (size_t)R + 1) || dalloc(&s.rp_cross, (size_t)R + 1) || dalloc(&s.n_wself, 1) ||
         dalloc(&s.n_wcross, 1)) { ct_engine_destroy(e); return CT_ENOMEM; }
     {
         int sms = 148;
@@ -1234,12 +1301,12 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         dalloc(&e->xa[1], (size_t)R * D) || dalloc(&e->xb[0], (size_t)R * D) || dalloc(&e->xb[1], (size_t)R * D) ||
         dalloc(&e->xm[0], (size_t)R * FF) || dalloc(&e->xm[1], (size_t)R * FF) || dalloc(&e->lm[0], (size_t)S * D) ||
         dalloc(&e->lm[1], (size_t)S * D) || dalloc(&e->logits, (size_t)S * V) || dalloc(&e->next, S)) { ct_engine_destroy(e); return CT_ENOMEM; }
-    e->attn_ws_floats = (size_t)R * KCH_MAX * (2 * H + D);
-    if (dalloc(&e->attn_ws, e->attn_ws_floats) || dalloc(&e->tickets, R)) {
+    e->attn_ws_floats = (size_t)R * SEG_MAX * (2 * H + D);
+    if (dalloc(&e->attn_ws, e->attn_ws_floats) || dalloc(&e->tickets, (size_t)R * H)) {
         ct_engine_destroy(e);
         return CT_ENOMEM;
     }
-    EK(cudaMemset(e->tickets, 0, sizeof(int) * R));
+    EK(cudaMemset(e->tickets, 0, sizeof(int) * (size_t)R * H));
     // admission staging: up to 64 utterances of 30 s worth of encoder rows
     e->enc_rows_cap = 64 * 400;
     if (dalloc(&e->enc_dev, (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_pl[0], (size_t)e->enc_rows_cap * D) ||

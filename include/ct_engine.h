@@ -43,7 +43,7 @@ typedef struct ct_engine ct_engine;
 
 typedef struct {
     int max_slots;       /* concurrent sequences (default 256, max 1024) */
-    int max_rows;        /* packed query rows per step (default 1024) */
+    int max_rows;        /* packed query rows per step (default and maximum 1024) */
     int kv_pages;        /* pages in the pool; 0 = size for max_slots full-length sequences */
     int precision;       /* 1 = activations as bf16 hi+lo planes (near fp32, default), 0 = bf16 */
     int n_prompt;        /* prompt length (default 10) */
