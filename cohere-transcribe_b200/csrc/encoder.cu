@@ -152,36 +152,99 @@ __global__ void __launch_bounds__(256) ln_enc(const float *x, int R, const bf16 
     }
 }
 
-// Relative-position attention over packed rows (backends/cpu/backend.c:262-295),
-// fp32 throughout.  One CTA per (query tile of RQ rows of one utterance, head);
-// key tiles of RQ keys; the DK = 160 dimensions are staged through shared
-// memory in chunks of RC.  Thread (ty, tx) of 16 x 16 owns a 4 x 4 block of
-// the score tile: queries ty*4 + i, keys tx*4 + j.  Both score terms
-//   AC[q][k] = (Q[q] + u) . K[k]          BD[q][k] = (Q[q] + v) . P[k - q + T_max - 1]
-// are accumulated together; the P rows a tile needs form a band of 2*RQ - 1
-// consecutive rows (relative offset k - q from -(RQ-1) to RQ-1), of which a
-// thread's block reads 7 consecutive ones.  Online softmax per query row (the
-// 16 threads of a row are 16 consecutive lanes), probabilities to shared
-// memory, then O[q][c] += p[q][k] V[k][c] with thread (ty, tx) owning rows
-// ty*4 + i and columns tx + 16*jj.  QKV rows hold [Q | K | V] (stride 3D); P
-// is the projected table of 2*T_max - 1 rows.  Output: bf16 hi/lo planes.
-constexpr int RQ = 64, RC = 32, RPAD = 4;
-constexpr int RP_ROWS = 2 * RQ;   // band of 2*RQ - 1 rows, padded to a multiple of 4
+// Relative-position attention over packed rows (backends/cpu/backend.c:262-295)
+// on the tensor cores.  One CTA per (query tile of 64 rows of one utterance,
+// head); warp w owns queries 16w .. 16w+15 of the tile; key tiles of 64.
+//   score[q][k] = ((Q+u).K[k] + (Q+v).P[k - q + T_max - 1]) / sqrt(DK)
+// is computed as Q.K^T + u.K[k] + Q.Pb^T + v.Pb[m], the bias terms u.K and v.P
+// as fp32 dot products over the staged rows.  Q, K, V and P arrive as bf16
+// hi/lo planes (written so by the projection GEMMs' epilogues) and are copied
+// to shared memory with asynchronous 16-byte copies.  The products run as
+// warp-level bf16 MMAs (m16n8k16, fp32 accumulate) on both planes, three
+// passes (hi.hi + hi.lo + lo.hi): about 16 mantissa bits per product, like the
+// fp32 reference to ~1e-5 relative.  The BD term: each warp
+// multiplies its 16 queries by the 80 consecutive P rows its (query, key)
+// pairs can reach (a band GEMM), parks that 16 x 80 tile in shared memory and
+// reads it back along the diagonals k - q.  Online softmax per query row over
+// the quad of threads that holds it; the probabilities feed the P.V MMA
+// directly from the score accumulators.  qkv_h / qkv_l rows hold [Q | K | V]
+// (stride 3D); P_h / P_l the projected table of 2*T_max - 1 rows.  Output:
+// bf16 hi/lo planes.
+constexpr int RQ = 64, RB = 128, RS = DK + 8;   // query/key tile, CTA band rows, smem row stride (bf16)
 struct RelposSmem {
-    union {
-        struct {
-            float qu[RC][RQ + RPAD], qv[RC][RQ + RPAD], k[RC][RQ + RPAD], p[RC][RP_ROWS + RPAD];
-        } c;                       // score phase: one chunk of dimensions, transposed (d-major)
-        float v[RQ][DK];           // value phase
-    } u;
-    float pr[RQ][RQ + RPAD];       // probabilities of the key tile
+    bf16 qh[RQ][RS], ql[RQ][RS];
+    bf16 kh[RQ][RS], kl[RQ][RS];   // K tile, then the V tile of the same keys
+    bf16 ph[RB][RS], pl[RB][RS];   // P band
+    float uk[RQ], vp[RB];          // u.K[k], v.P[m]
+    float bd[4][16][84];           // per warp: its 16 x 80 band tile
 };
 
-__global__ void __launch_bounds__(256) relpos_flash(const float *QKV, const float *P, Batch b, const bf16 *pbu,
-                                                    const bf16 *pbv, bf16 *hi, bf16 *lo) {
+__device__ __forceinline__ void ldsm_x4(const void *p, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(const void *p, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo_col, float hi_col) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo_col, hi_col);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+__device__ __forceinline__ float bf_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+// Asynchronously copy N rows of DK bf16 values from the hi and lo planes
+// (row i at plane + src_row(i) * ld + col0, or zeros where src_row(i) < 0) into
+// padded shared rows; 16-byte pieces spread over the 128 threads.
+template <int N, class RowOf>
+__device__ __forceinline__ void stage_planes(RowOf src_row, const bf16 *ph_g, const bf16 *pl_g, size_t ld, int col0,
+                                             bf16 (*hi)[RS], bf16 (*lo)[RS]) {
+    constexpr int CH = DK / 8;   // 16-byte pieces per row and plane
+    for (int id = threadIdx.x; id < N * 2 * CH; id += 128) {
+        const int row = id / (2 * CH), rem = id % (2 * CH), plane = rem / CH, c = (rem % CH) * 8;
+        const int sr = src_row(row);
+        const bf16 *g = plane ? pl_g : ph_g;
+        const bf16 *src = sr >= 0 ? g + (size_t)sr * ld + col0 + c : g;
+        cp_async16(plane ? &lo[row][c] : &hi[row][c], src, sr >= 0);
+    }
+}
+// dot[i] = bias . (hi[i] + lo[i]) for N rows, 128 / N threads per row.
+template <int N>
+__device__ __forceinline__ void row_dots(const bf16 (*hi)[RS], const bf16 (*lo)[RS], const bf16 *bias, float *dot) {
+    constexpr int TPR = 128 / N, PER = DK / TPR;
+    const int row = threadIdx.x / TPR, part = threadIdx.x % TPR;
+    float acc = 0.0f;
+    for (int c = part * PER; c < part * PER + PER; ++c)
+        acc += bf2f(bias[c]) * (__bfloat162float(hi[row][c]) + __bfloat162float(lo[row][c]));
+#pragma unroll
+    for (int o = 1; o < TPR; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (part == 0) dot[row] = acc;
+}
+
+__global__ void __launch_bounds__(128, 1) relpos_tc(const bf16 *qkv_h, const bf16 *qkv_l, const bf16 *P_h,
+                                                    const bf16 *P_l, Batch b, const bf16 *pbu, const bf16 *pbv,
+                                                    bf16 *hi, bf16 *lo) {
     extern __shared__ __align__(16) uint8_t relpos_raw[];
     RelposSmem &sm = *reinterpret_cast<RelposSmem *>(relpos_raw);
-    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, tig = lane & 3;
     const int h = blockIdx.y;
     const int wq = b.qtile[blockIdx.x];
     const int u = wq >> 16, q0 = wq & 0xFFFF;
@@ -190,140 +253,159 @@ __global__ void __launch_bounds__(256) relpos_flash(const float *QKV, const floa
     const int Tm = b.T_max, PL = 2 * Tm - 1;
     const float scale = 1.0f / sqrtf((float)DK);
     const size_t ld = (size_t)3 * D;
+    const bf16 *ub = pbu + h * DK, *vb = pbv + h * DK;
 
-    float o[4][DK / 16];
-    float m[4], l[4];
+    stage_planes<RQ>([&](int r) { return q0 + r < T ? base + q0 + r : -1; }, qkv_h, qkv_l, ld, h * DK, sm.qh, sm.ql);
+
+    float o[DK / 8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        m[i] = -INFINITY;
-        l[i] = 0.0f;
-#pragma unroll
-        for (int jj = 0; jj < DK / 16; ++jj) o[i][jj] = 0.0f;
-    }
+    for (int i = 0; i < DK / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;   // rows g and g + 8
+    const int mbw = 48 - 16 * warp;                                // this warp's band start (CTA band rows)
+    cp_async_wait_all();   // Q tile (made visible by the loop's first barrier)
 
     for (int k0 = 0; k0 < T; k0 += RQ) {
-        float sc[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
-        // band row m <-> relative offset (k - q) = (k0 - q0) - (RQ - 1) + m
-        const int rb = (k0 - q0) - (RQ - 1) + Tm - 1;
-        for (int d0 = 0; d0 < DK; d0 += RC) {
-            // ---- stage the chunk [d0, d0 + RC) of Q+u, Q+v, K (RQ rows) and the P band
-            {
-                const int r = tid >> 2, dd = (tid & 3) * 8;   // 64 rows x 4 groups of 8 dims
-                const int q = q0 + r, k = k0 + r;
-                float4 qa = make_float4(0.f, 0.f, 0.f, 0.f), qb = qa, ka = qa, kb2 = qa;
-                if (q < T) {
-                    const float4 *src = reinterpret_cast<const float4 *>(QKV + (size_t)(base + q) * ld + h * DK + d0 + dd);
-                    qa = src[0]; qb = src[1];
-                }
-                if (k < T) {
-                    const float4 *src = reinterpret_cast<const float4 *>(QKV + (size_t)(base + k) * ld + D + h * DK + d0 + dd);
-                    ka = src[0]; kb2 = src[1];
-                }
-                const float qv8[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                const float kv8[8] = {ka.x, ka.y, ka.z, ka.w, kb2.x, kb2.y, kb2.z, kb2.w};
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int d = dd + e;
-                    sm.u.c.qu[d][r] = qv8[e] + bf2f(pbu[h * DK + d0 + d]);
-                    sm.u.c.qv[d][r] = qv8[e] + bf2f(pbv[h * DK + d0 + d]);
-                    sm.u.c.k[d][r] = kv8[e];
-                }
-                // P band: 2*RQ - 1 rows; rows outside the table (only reached by
-                // padded queries or keys, whose scores are discarded) read as 0
-                for (int idx = tid; idx < RP_ROWS * (RC / 4); idx += 256) {
-                    const int mrow = idx / (RC / 4), d4 = (idx % (RC / 4)) * 4;
-                    const int pr = rb + mrow;
-                    float4 pv = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (mrow < 2 * RQ - 1 && pr >= 0 && pr < PL)
-                        pv = *reinterpret_cast<const float4 *>(P + (size_t)pr * D + h * DK + d0 + d4);
-                    sm.u.c.p[d4 + 0][mrow] = pv.x;
-                    sm.u.c.p[d4 + 1][mrow] = pv.y;
-                    sm.u.c.p[d4 + 2][mrow] = pv.z;
-                    sm.u.c.p[d4 + 3][mrow] = pv.w;
-                }
-            }
-            __syncthreads();
-            // ---- scores: block rows ty*4+i, keys tx*4+j; band index
-            // (tx*4 + j) - (ty*4 + i) + RQ - 1 = mb + (j - i) + 3
-            const int mb = (tx - ty) * 4 + RQ - 4;
-#pragma unroll 4
-            for (int d = 0; d < RC; ++d) {
-                const float4 a = *reinterpret_cast<const float4 *>(&sm.u.c.qu[d][ty * 4]);
-                const float4 c = *reinterpret_cast<const float4 *>(&sm.u.c.qv[d][ty * 4]);
-                const float4 kk = *reinterpret_cast<const float4 *>(&sm.u.c.k[d][tx * 4]);
-                const float4 p0 = *reinterpret_cast<const float4 *>(&sm.u.c.p[d][mb]);
-                const float4 p1 = *reinterpret_cast<const float4 *>(&sm.u.c.p[d][mb + 4]);
-                const float av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
-                const float kv[4] = {kk.x, kk.y, kk.z, kk.w};
-                const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) sc[i][j] += av[i] * kv[j] + cv[i] * pv[j - i + 3];
-            }
-            __syncthreads();
-        }
-        // ---- online softmax over this key tile
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float rmax = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const bool valid = k0 + tx * 4 + j < T;
-                sc[i][j] = valid ? sc[i][j] * scale : -INFINITY;
-                rmax = fmaxf(rmax, sc[i][j]);
-            }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
-            const float mn = fmaxf(m[i], rmax);   // finite: key k0 is valid
-            const float corr = expf(m[i] - mn);
-            float rs = 0.0f;
-            float pj[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) { pj[j] = expf(sc[i][j] - mn); rs += pj[j]; }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
-            l[i] = l[i] * corr + rs;
-            m[i] = mn;
-#pragma unroll
-            for (int jj = 0; jj < DK / 16; ++jj) o[i][jj] *= corr;
-            *reinterpret_cast<float4 *>(&sm.pr[ty * 4 + i][tx * 4]) = make_float4(pj[0], pj[1], pj[2], pj[3]);
-        }
-        // ---- value tile (aliases the chunk buffers, free after the last sync)
-        for (int idx = tid; idx < RQ * (DK / 4); idx += 256) {
-            const int r = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
-            float4 vv = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (k0 + r < T) vv = *reinterpret_cast<const float4 *>(QKV + (size_t)(base + k0 + r) * ld + 2 * D + h * DK + c4);
-            *reinterpret_cast<float4 *>(&sm.u.v[r][c4]) = vv;
-        }
+        __syncthreads();   // the previous tile's V and band reads are done
+        stage_planes<RQ>([&](int r) { return k0 + r < T ? base + k0 + r : -1; }, qkv_h, qkv_l, ld, D + h * DK, sm.kh,
+                         sm.kl);
+        // CTA band row m <-> relative offset (k - q) = (k0 - q0 - 63) + m
+        const int prow0 = (k0 - q0) - (RQ - 1) + Tm - 1;
+        stage_planes<RB>([&](int m) {
+            const int pr = prow0 + m;
+            return (m < 2 * RQ - 1 && pr >= 0 && pr < PL) ? pr : -1;
+        }, P_h, P_l, (size_t)D, h * DK, sm.ph, sm.pl);
+        cp_async_wait_all();
         __syncthreads();
-        const int kn = min(RQ, T - k0);
-        for (int kk = 0; kk < kn; ++kk) {
-            float pq[4];
+        row_dots<RQ>(sm.kh, sm.kl, ub, sm.uk);
+        row_dots<RB>(sm.ph, sm.pl, vb, sm.vp);
+        __syncthreads();
+
+        float sc[RQ / 8][4], bnd[10][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) pq[i] = sm.pr[ty * 4 + i][kk];
+        for (int i = 0; i < RQ / 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.0f;
 #pragma unroll
-            for (int jj = 0; jj < DK / 16; ++jj) {
-                const float vv = sm.u.v[kk][tx + 16 * jj];
+        for (int i = 0; i < 10; ++i) bnd[i][0] = bnd[i][1] = bnd[i][2] = bnd[i][3] = 0.0f;
+        const int arow = 16 * warp + (lane & 15), acol = (lane >> 4) * 8;
+        const int brow = (lane & 7) + ((lane >> 4) << 3), bcol = ((lane >> 3) & 1) * 8;
+#pragma unroll 2
+        for (int ks = 0; ks < DK / 16; ++ks) {
+            uint32_t ah0, ah1, ah2, ah3, al0, al1, al2, al3;
+            ldsm_x4(&sm.qh[arow][ks * 16 + acol], ah0, ah1, ah2, ah3);
+            ldsm_x4(&sm.ql[arow][ks * 16 + acol], al0, al1, al2, al3);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) o[i][jj] += pq[i] * vv;
+            for (int np = 0; np < RQ / 16; ++np) {   // key n8-tile pairs
+                uint32_t bh0, bh1, bh2, bh3, bl0, bl1, bl2, bl3;
+                ldsm_x4(&sm.kh[np * 16 + brow][ks * 16 + bcol], bh0, bh1, bh2, bh3);
+                ldsm_x4(&sm.kl[np * 16 + brow][ks * 16 + bcol], bl0, bl1, bl2, bl3);
+                mma16816(sc[2 * np], ah0, ah1, ah2, ah3, bh0, bh1);
+                mma16816(sc[2 * np], ah0, ah1, ah2, ah3, bl0, bl1);
+                mma16816(sc[2 * np], al0, al1, al2, al3, bh0, bh1);
+                mma16816(sc[2 * np + 1], ah0, ah1, ah2, ah3, bh2, bh3);
+                mma16816(sc[2 * np + 1], ah0, ah1, ah2, ah3, bl2, bl3);
+                mma16816(sc[2 * np + 1], al0, al1, al2, al3, bh2, bh3);
+            }
+#pragma unroll
+            for (int np = 0; np < 5; ++np) {         // band n8-tile pairs
+                uint32_t bh0, bh1, bh2, bh3, bl0, bl1, bl2, bl3;
+                ldsm_x4(&sm.ph[mbw + np * 16 + brow][ks * 16 + bcol], bh0, bh1, bh2, bh3);
+                ldsm_x4(&sm.pl[mbw + np * 16 + brow][ks * 16 + bcol], bl0, bl1, bl2, bl3);
+                mma16816(bnd[2 * np], ah0, ah1, ah2, ah3, bh0, bh1);
+                mma16816(bnd[2 * np], ah0, ah1, ah2, ah3, bl0, bl1);
+                mma16816(bnd[2 * np], al0, al1, al2, al3, bh0, bh1);
+                mma16816(bnd[2 * np + 1], ah0, ah1, ah2, ah3, bh2, bh3);
+                mma16816(bnd[2 * np + 1], ah0, ah1, ah2, ah3, bl2, bl3);
+                mma16816(bnd[2 * np + 1], al0, al1, al2, al3, bh2, bh3);
             }
         }
+        // band tile -> shared memory, read back along the diagonals
+        float (*bd)[84] = sm.bd[warp];
+#pragma unroll
+        for (int bt = 0; bt < 10; ++bt) {
+            bd[g][bt * 8 + 2 * tig] = bnd[bt][0];
+            bd[g][bt * 8 + 2 * tig + 1] = bnd[bt][1];
+            bd[g + 8][bt * 8 + 2 * tig] = bnd[bt][2];
+            bd[g + 8][bt * 8 + 2 * tig + 1] = bnd[bt][3];
+        }
+        __syncwarp();
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int kt = 0; kt < RQ / 8; ++kt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i = g + (e >> 1) * 8, j = kt * 8 + 2 * tig + (e & 1);
+                const int mm = j - i + 15;   // diagonal index in this warp's band
+                float v = (sc[kt][e] + sm.uk[j] + bd[i][mm] + sm.vp[mbw + mm]) * scale;
+                if (k0 + j >= T) v = -INFINITY;
+                sc[kt][e] = v;
+                if (e < 2) mx0 = fmaxf(mx0, v); else mx1 = fmaxf(mx1, v);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);   // finite: key k0 is valid
+        const float c0 = expf(m0 - n0), c1 = expf(m1 - n1);
+        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+        for (int kt = 0; kt < RQ / 8; ++kt) {
+            sc[kt][0] = expf(sc[kt][0] - n0); s0 += sc[kt][0];
+            sc[kt][1] = expf(sc[kt][1] - n0); s0 += sc[kt][1];
+            sc[kt][2] = expf(sc[kt][2] - n1); s1 += sc[kt][2];
+            sc[kt][3] = expf(sc[kt][3] - n1); s1 += sc[kt][3];
+        }
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+        l0 = l0 * c0 + s0;
+        l1 = l1 * c1 + s1;
+        m0 = n0;
+        m1 = n1;
+#pragma unroll
+        for (int i = 0; i < DK / 8; ++i) { o[i][0] *= c0; o[i][1] *= c0; o[i][2] *= c1; o[i][3] *= c1; }
+
+        __syncthreads();   // every warp is done with the K tile: stage V over it
+        stage_planes<RQ>([&](int r) { return k0 + r < T ? base + k0 + r : -1; }, qkv_h, qkv_l, ld, 2 * D + h * DK,
+                         sm.kh, sm.kl);
+        cp_async_wait_all();
         __syncthreads();
+        // O += P.V, P from the score accumulators (16-key blocks)
+#pragma unroll
+        for (int kk = 0; kk < RQ / 16; ++kk) {
+            const float *pa = sc[2 * kk], *pb2 = sc[2 * kk + 1];
+            const float hv[8] = {bf_round(pa[0]), bf_round(pa[1]), bf_round(pa[2]), bf_round(pa[3]),
+                                 bf_round(pb2[0]), bf_round(pb2[1]), bf_round(pb2[2]), bf_round(pb2[3])};
+            const uint32_t ph0 = pack_bf16(hv[0], hv[1]), ph1 = pack_bf16(hv[2], hv[3]);
+            const uint32_t ph2 = pack_bf16(hv[4], hv[5]), ph3 = pack_bf16(hv[6], hv[7]);
+            const uint32_t pl0 = pack_bf16(pa[0] - hv[0], pa[1] - hv[1]), pl1 = pack_bf16(pa[2] - hv[2], pa[3] - hv[3]);
+            const uint32_t pl2 = pack_bf16(pb2[0] - hv[4], pb2[1] - hv[5]),
+                           pl3 = pack_bf16(pb2[2] - hv[6], pb2[3] - hv[7]);
+#pragma unroll
+            for (int dp = 0; dp < DK / 16; ++dp) {   // dim n8-tile pairs
+                uint32_t vh0, vh1, vh2, vh3, vl0, vl1, vl2, vl3;
+                ldsm_x4_t(&sm.kh[kk * 16 + (lane & 15)][dp * 16 + (lane >> 4) * 8], vh0, vh1, vh2, vh3);
+                ldsm_x4_t(&sm.kl[kk * 16 + (lane & 15)][dp * 16 + (lane >> 4) * 8], vl0, vl1, vl2, vl3);
+                mma16816(o[2 * dp], ph0, ph1, ph2, ph3, vh0, vh1);
+                mma16816(o[2 * dp], ph0, ph1, ph2, ph3, vl0, vl1);
+                mma16816(o[2 * dp], pl0, pl1, pl2, pl3, vh0, vh1);
+                mma16816(o[2 * dp + 1], ph0, ph1, ph2, ph3, vh2, vh3);
+                mma16816(o[2 * dp + 1], ph0, ph1, ph2, ph3, vl2, vl3);
+                mma16816(o[2 * dp + 1], pl0, pl1, pl2, pl3, vh2, vh3);
+            }
+        }
     }
+    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+    const int qa = q0 + 16 * warp + g, qb = qa + 8;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int q = q0 + ty * 4 + i;
-        if (q >= T) continue;
-        const float inv = 1.0f / l[i];
+    for (int nt = 0; nt < DK / 8; ++nt) {
+        const int c = h * DK + nt * 8 + 2 * tig;
 #pragma unroll
-        for (int jj = 0; jj < DK / 16; ++jj) {
-            const float v = o[i][jj] * inv;
-            const size_t idx = (size_t)(base + q) * D + h * DK + tx + 16 * jj;
+        for (int e = 0; e < 4; ++e) {
+            const int q = e < 2 ? qa : qb;
+            if (q >= T) continue;
+            const float v = o[nt][e] * (e < 2 ? i0 : i1);
+            const size_t idx = (size_t)(base + q) * D + c + (e & 1);
             const bf16 hb = __float2bfloat16_rn(v);
             hi[idx] = hb;
             if (lo) lo[idx] = __float2bfloat16_rn(v - __bfloat162float(hb));
@@ -388,10 +470,11 @@ struct State {
     int max_utts = 0, max_frames = 0;     // capacity: utterances and log-mel frames per batch
     int R1_max = 0, R2_max = 0, R3_max = 0, T_cap = 0;
     bool two = true;                       // activations as hi+lo bf16 planes
-    float *mel = nullptr, *s1 = nullptr, *s2 = nullptr, *x = nullptr, *qkv = nullptr, *pos = nullptr, *P = nullptr;
+    float *mel = nullptr, *s1 = nullptr, *s2 = nullptr, *x = nullptr, *qkv = nullptr, *pos = nullptr;
     float *enc_h = nullptr;
     bf16 *xa[2] = {nullptr, nullptr}, *hid[2] = {nullptr, nullptr}, *ap[2] = {nullptr, nullptr};
     bf16 *posp[2] = {nullptr, nullptr};
+    bf16 *qkvp[2] = {nullptr, nullptr}, *Pp[2] = {nullptr, nullptr};   // Q|K|V and P as bf16 hi/lo planes
     int *tab = nullptr;                    // device tables
     std::vector<int> htab;
     std::vector<void *> owned;
@@ -442,7 +525,9 @@ static bool state_alloc(State &st, int max_utts, int max_frames, bool two) {
     const size_t R = st.R3_max;
     bool ok = ealloc(st, &st.mel, (size_t)max_frames * F0) && ealloc(st, &st.s1, s1) && ealloc(st, &st.s2, s2) &&
               ealloc(st, &st.x, R * D) && ealloc(st, &st.qkv, R * 3 * D) && ealloc(st, &st.enc_h, R * DEC_D) &&
-              ealloc(st, &st.pos, (size_t)(2 * st.T_cap) * D) && ealloc(st, &st.P, (size_t)(2 * st.T_cap) * D) &&
+              ealloc(st, &st.pos, (size_t)(2 * st.T_cap) * D) && ealloc(st, &st.qkvp[0], R * 3 * D) &&
+              ealloc(st, &st.qkvp[1], R * 3 * D) && ealloc(st, &st.Pp[0], (size_t)(2 * st.T_cap) * D) &&
+              ealloc(st, &st.Pp[1], (size_t)(2 * st.T_cap) * D) &&
               ealloc(st, &st.tab, (size_t)9 * max_utts + 8 + st.R1_max + st.R2_max + st.R3_max + st.R3_max / RQ + 1);
     const size_t hidn = std::max((size_t)R * FF, (size_t)st.R2_max * F2 * C);
     for (int k = 0; k < (two ? 2 : 1); ++k)
@@ -541,7 +626,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     int dev = 0;
     CT_CHECK(cudaGetDevice(&dev));
     if (relpos_dev != dev) {
-        CT_CHECK(cudaFuncSetAttribute(relpos_flash, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(RelposSmem)));
+        CT_CHECK(cudaFuncSetAttribute(relpos_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(RelposSmem)));
         relpos_dev = dev;
     }
     const Weights_ &w = st.w;
@@ -593,14 +678,15 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.sa_lnw, L.sa_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
         GemmEpilogue eq;
-        eq.bias = L.qkv_b; eq.Y = st.qkv; eq.ldy = 3 * D;
+        eq.epi = EPI_BF16; eq.bias = L.qkv_b; eq.Ybf = st.qkvp[0]; eq.Ybf_lo = st.qkvp[1]; eq.ldy = 3 * D;
         egemm_enc(s, st, L.qkv_w, 3 * D, D, xap, R3, RT, eq);
         mark(s, st, "enc_gemm_qkv");
         GemmEpilogue ep;
-        ep.Y = st.P; ep.ldy = D;
+        ep.epi = EPI_BF16; ep.Ybf = st.Pp[0]; ep.Ybf_lo = st.Pp[1]; ep.ldy = D;
         egemm_enc(s, st, L.sa_pw, D, D, st.posp, PL, 2 * st.T_cap, ep);
         mark(s, st, "enc_gemm_pos");
-        relpos_flash<<<dim3(NQ, H), 256, sizeof(RelposSmem), s>>>(st.qkv, st.P, bt, L.sa_pbu, L.sa_pbv, st.ap[0], lo_p);
+        relpos_tc<<<dim3(NQ, H), 128, sizeof(RelposSmem), s>>>(st.qkvp[0], st.qkvp[1], st.Pp[0], st.Pp[1], bt,
+                                                               L.sa_pbu, L.sa_pbv, st.ap[0], lo_p);
         mark(s, st, "enc_relpos_attn");
         GemmEpilogue eo2;
         eo2.epi = EPI_FMADD; eo2.scale = 1.0f; eo2.bias = L.sa_ob; eo2.Y = st.x; eo2.ldy = D;
