@@ -597,3 +597,114 @@ int orc_decode_batch(const ct_dims *d, const Weights *W, int B, const int *T_enc
     free(active); free(cur); free(next); free(gen); free(cak_b); free(cav_b); free(sak_b); free(sav_b);
     return 0;
 }
+
+/* ------------------------------------------------------------------ */
+/* log-mel front-end                                                   */
+/* ------------------------------------------------------------------ */
+
+/* transcribe.c:45-50: symmetric Hann window of ORC_WIN points. */
+void orc_hann(float *w) {
+    for (int i = 0; i < ORC_WIN; i++)
+        w[i] = 0.5f * (1.0f - cosf(2.0f * (float)M_PI * i / (ORC_WIN - 1)));
+}
+
+/* transcribe.c:56-70: Slaney mel scale (linear below 1 kHz, log above). */
+static double slaney_hz_to_mel(double f) {
+    const double f_sp = 200.0 / 3.0, brk = 1000.0, brk_mel = brk / f_sp, step = log(6.4) / 27.0;
+    return f < brk ? f / f_sp : brk_mel + log(f / brk) / step;
+}
+static double slaney_mel_to_hz(double m) {
+    const double f_sp = 200.0 / 3.0, brk = 1000.0, brk_mel = brk / f_sp, step = log(6.4) / 27.0;
+    return m < brk_mel ? f_sp * m : brk * exp(step * (m - brk_mel));
+}
+
+/* transcribe.c:72-97: triangular filters between ORC_N_MELS + 2 points equally
+ * spaced in mel from 0 to SR/2, area-normalised (librosa norm='slaney'). */
+void orc_mel_filterbank(float *fb) {
+    double pts[ORC_N_MELS + 2], gap[ORC_N_MELS + 1];
+    const double lo = slaney_hz_to_mel(0.0), hi = slaney_hz_to_mel(ORC_SR / 2.0);
+    for (int i = 0; i < ORC_N_MELS + 2; i++)
+        pts[i] = slaney_mel_to_hz(lo + (hi - lo) * i / (ORC_N_MELS + 1));
+    for (int i = 0; i < ORC_N_MELS + 1; i++) gap[i] = pts[i + 1] - pts[i];
+    for (int m = 0; m < ORC_N_MELS; m++) {
+        const double norm = 2.0 / (pts[m + 2] - pts[m]);
+        for (int k = 0; k < ORC_N_BINS; k++) {
+            const double f = (ORC_SR / 2.0) * k / (ORC_N_BINS - 1);
+            const double up = (f - pts[m]) / gap[m], down = (pts[m + 2] - f) / gap[m + 1];
+            const double w = up < down ? up : down;
+            fb[m * ORC_N_BINS + k] = (float)(w > 0.0 ? w * norm : 0.0);
+        }
+    }
+}
+
+/* transcribe.c:99-123: iterative radix-2 decimation-in-time FFT, bit-reversal
+ * permutation first, twiddles advanced by complex multiplication per stage. */
+static void orc_fft(float *re, float *im, int n) {
+    for (int i = 1, j = 0; i < n; i++) {
+        int bit = n >> 1;
+        for (; j & bit; bit >>= 1) j ^= bit;
+        j ^= bit;
+        if (i < j) {
+            float t = re[i]; re[i] = re[j]; re[j] = t;
+            t = im[i]; im[i] = im[j]; im[j] = t;
+        }
+    }
+    for (int len = 2; len <= n; len <<= 1) {
+        const float ang = -2.0f * (float)M_PI / len;
+        const float wr = cosf(ang), wi = sinf(ang);
+        for (int i = 0; i < n; i += len) {
+            float cr = 1, ci = 0;
+            for (int k = 0; k < len / 2; k++) {
+                const int a = i + k, b = i + k + len / 2;
+                const float ur = re[a], ui = im[a];
+                const float vr = re[b] * cr - im[b] * ci;
+                const float vi = re[b] * ci + im[b] * cr;
+                re[a] = ur + vr; im[a] = ui + vi;
+                re[b] = ur - vr; im[b] = ui - vi;
+                const float nc = cr * wr - ci * wi;
+                ci = cr * wi + ci * wr;
+                cr = nc;
+            }
+        }
+    }
+}
+
+/* transcribe.c:177-214: zero-pad WIN/2 on both sides, pre-emphasis 0.97,
+ * Hann-windowed 512-point power spectra every HOP samples, mel projection,
+ * log(x + 2^-24), then per-mel-bin normalisation over time (mean, unbiased
+ * variance, eps 1e-5). */
+void orc_compute_mel(const float *samples, int N, float *mel) {
+    static float hann[ORC_WIN], fb[ORC_N_MELS * ORC_N_BINS];
+    static int ready = 0;
+    if (!ready) { orc_hann(hann); orc_mel_filterbank(fb); ready = 1; }
+    const int T = 1 + N / ORC_HOP, pad = ORC_WIN / 2, Np = N + 2 * pad;
+    float *s = XMALLOC(sizeof(float) * (size_t)Np);
+    memset(s, 0, sizeof(float) * (size_t)Np);
+    memcpy(s + pad, samples, sizeof(float) * (size_t)N);
+    for (int i = Np - 1; i > 0; i--) s[i] -= 0.97f * s[i - 1];
+    float re[ORC_N_FFT], im[ORC_N_FFT], ps[ORC_N_BINS];
+    for (int t = 0; t < T; t++) {
+        const int off = t * ORC_HOP;
+        for (int i = 0; i < ORC_N_FFT; i++) re[i] = im[i] = 0.0f;
+        for (int i = 0; i < ORC_WIN && off + i < Np; i++) re[i] = s[off + i] * hann[i];
+        orc_fft(re, im, ORC_N_FFT);
+        for (int k = 0; k < ORC_N_BINS; k++) ps[k] = re[k] * re[k] + im[k] * im[k];
+        for (int m = 0; m < ORC_N_MELS; m++) {
+            float v = 0;
+            for (int k = 0; k < ORC_N_BINS; k++) v += fb[m * ORC_N_BINS + k] * ps[k];
+            mel[(size_t)m * T + t] = v;
+        }
+    }
+    const float guard = powf(2.0f, -24.0f);
+    for (int m = 0; m < ORC_N_MELS; m++) {
+        float *row = mel + (size_t)m * T;
+        float mean = 0, var = 0;
+        for (int t = 0; t < T; t++) { row[t] = logf(row[t] + guard); mean += row[t]; }
+        mean /= T;
+        for (int t = 0; t < T; t++) { const float d = row[t] - mean; var += d * d; }
+        var /= (T - 1);
+        const float inv = 1.0f / sqrtf(var + 1e-5f);
+        for (int t = 0; t < T; t++) row[t] = (row[t] - mean) * inv;
+    }
+    free(s);
+}

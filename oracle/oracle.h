@@ -102,6 +102,18 @@ int orc_decode_batch(const ct_dims *d, const Weights *W, int B, const int *T_enc
 /* top-1 index and (top1 - top2) over n logits */
 void orc_top2(const float *lg, int n, int *idx, float *margin);
 
+/* ---- log-mel front-end (transcribe.c:45-123, :177-214) -------------------
+ * 16 kHz mono samples -> normalised log-mel [ORC_N_MELS][T_mel], T_mel = 1 + N / 160. */
+#define ORC_SR 16000
+#define ORC_N_FFT 512
+#define ORC_WIN 400
+#define ORC_HOP 160
+#define ORC_N_MELS 128
+#define ORC_N_BINS (ORC_N_FFT / 2 + 1)
+void orc_mel_filterbank(float *fb /* [ORC_N_MELS * ORC_N_BINS] */);
+void orc_hann(float *w /* [ORC_WIN] */);
+void orc_compute_mel(const float *samples, int N, float *mel /* [ORC_N_MELS][1 + N / ORC_HOP] */);
+
 #ifdef __cplusplus
 }
 #endif

@@ -93,6 +93,7 @@ def lib() -> ctypes.CDLL:
             "orc_encoder_forward_batch": [D, _vp, _f, ctypes.c_int, ctypes.c_int, _i, _i, ctypes.c_int, _f],
             "orc_decode_batch": [D, _vp, ctypes.c_int, _i, ctypes.c_int, _f, _i, ctypes.c_int, _i, _i,
                                  _i, _i, _i, _f],
+            "orc_compute_mel": [_f, ctypes.c_int, _f],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)
@@ -166,3 +167,11 @@ def decode_batch(dims: dict, wstruct, enc_h: np.ndarray, T_enc: np.ndarray, prom
                        ip(forced), ip(ft) if ft is not None else null_i(), ip(tokens), ip(n_tok),
                        ip(am), fp(mg) if want_margin else null_f())
     return tokens, n_tok, am, mg
+
+
+def compute_mel(samples: np.ndarray) -> np.ndarray:
+    """Oracle log-mel of 16 kHz samples: [128, 1 + N // 160] (transcribe.c:177-214)."""
+    x = np.ascontiguousarray(samples, dtype=np.float32)
+    out = np.zeros((128, 1 + len(x) // 160), np.float32)
+    lib().orc_compute_mel(fp(x), len(x), fp(out))
+    return out

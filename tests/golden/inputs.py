@@ -89,3 +89,20 @@ def enc_outputs(T_enc, seed: int, d: int = 1024, std: float = 1.0) -> np.ndarray
         rng = np.random.default_rng([seed, b])
         enc[b, :t] = rng.standard_normal((int(t), d), dtype=np.float32) * np.float32(std)
     return enc
+
+
+def audio(seconds: float, seed: int) -> np.ndarray:
+    """Seeded 16 kHz test signal: a few tones plus white noise, float32."""
+    n = int(round(seconds * 16000))
+    rng = np.random.default_rng(seed)
+    t = np.arange(n, dtype=np.float64) / 16000.0
+    x = np.zeros(n)
+    for f, a in zip(rng.uniform(80.0, 4000.0, 4), rng.uniform(0.05, 0.3, 4)):
+        x += a * np.sin(2 * np.pi * f * t + rng.uniform(0, 2 * np.pi))
+    x += 0.02 * rng.standard_normal(n)
+    return x.astype(np.float32)
+
+
+def mel_case():
+    """Front-end fixture inputs: lengths with and without a partial last hop."""
+    return [(seconds, 900 + i) for i, seconds in enumerate((1.0, 2.3456, 0.37))]

@@ -12,6 +12,8 @@ oracle/Makefile into oracle/_ref/) and records their outputs:
                              reference model.h + CPU backend at the tiny dims
   full_decode_ref.npz        full-size decoder: prefill + batched greedy decode of
                              two sequences from seeded encoder outputs
+  mel_ref.npz                the log-mel front-end (transcribe.c compute_mel) on
+                             seeded 16 kHz signals
 
 Inputs are regenerated from seeds by tests/golden/inputs.py; a checksum of
 each input is stored with the outputs so drift is detected.
@@ -92,7 +94,22 @@ def main(ref: str) -> None:
                            pyoracle.fp(mg))
     np.savez_compressed(os.path.join(HERE, "full_decode_ref.npz"), tokens=tokens, n_tok=n_tok, argmax=am,
                         margin=mg, enc_checksum=np.float64(enc.astype(np.float64).sum()))
+    make_mel_fixture()
     print("golden fixtures written to", HERE)
+
+
+def make_mel_fixture() -> None:
+    """5. the reference front-end (transcribe.c compute_mel) on seeded signals."""
+    R = ctypes.CDLL(os.path.join(pyoracle.REF_DIR, "libref_mel.so"))
+    R.refmel_compute.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    out = {}
+    for k, (seconds, seed) in enumerate(inputs.mel_case()):
+        x = inputs.audio(seconds, seed)
+        mel = np.zeros((128, 1 + len(x) // 160), np.float32)
+        R.refmel_compute(x.ctypes.data, len(x), mel.ctypes.data)
+        out[f"mel{k}"] = mel
+        out[f"checksum{k}"] = np.float64(x.astype(np.float64).sum())
+    np.savez_compressed(os.path.join(HERE, "mel_ref.npz"), **out)
 
 
 if __name__ == "__main__":

@@ -6,8 +6,10 @@
    function on seeded inputs -- bit-exact (same arithmetic order, same flags).
 3. End to end: configuration 1 (tiny model, log-mel -> tokens) and a full-size
    decoder slice, against fixtures produced by the reference's model.h.
+4. The log-mel front-end against the reference's compute_mel.
 """
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -264,3 +266,25 @@ def test_full_decoder_slice(wmod):
     assert np.array_equal(tokens, gold["tokens"])
     sel = ~np.isnan(gold["margin"])
     np.testing.assert_allclose(mg[sel], gold["margin"][sel], rtol=0, atol=1e-5)
+
+
+def test_mel_front_end_matches_reference():
+    """The oracle's log-mel front-end equals the reference's compute_mel
+    (transcribe.c:177-214), recorded in tests/golden/mel_ref.npz from the
+    reference built here; and, when that build is present, on fresh lengths."""
+    gold = np.load(os.path.join(os.path.dirname(inputs.__file__), "mel_ref.npz"))
+    for k, (seconds, seed) in enumerate(inputs.mel_case()):
+        x = inputs.audio(seconds, seed)
+        assert np.float64(x.astype(np.float64).sum()) == gold[f"checksum{k}"]
+        assert np.array_equal(po.compute_mel(x), gold[f"mel{k}"]), k
+    path = os.path.join(po.REF_DIR, "libref_mel.so")
+    if os.path.exists(path):
+        R = ctypes.CDLL(path)
+        R.refmel_compute.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        for n in (160, 159, 31999, 80000):
+            x = inputs.audio(n / 16000.0, n)
+            ref = np.zeros((128, 1 + n // 160), np.float32)
+            R.refmel_compute(x.ctypes.data, len(x), ref.ctypes.data)
+            # one frame (n < 160): the unbiased variance divides by T - 1 = 0 and
+            # the reference yields NaN; the oracle reproduces it
+            assert np.array_equal(po.compute_mel(x), ref, equal_nan=True), n
