@@ -2,8 +2,8 @@
 """Benchmark: decode tokens/s, RTFx and p50 step latency of the engine.
 
 Workload (full-size model, one B200 per rank): 64
-utterances per GPU of U(5, 30) s of seeded N(0, 1) log-mel (128 bins, 10 ms
-hop), EOS forced at U{20..220} generated tokens, seeded random-init bf16
+utterances per GPU of U(5, 30) s of seeded 16 kHz test signals (a few tones
+plus noise), EOS forced at U{20..220} generated tokens, seeded random-init bf16
 weights (there is no network for checkpoints or audio).  With N GPUs the job
 is 64 * N utterances, dispatched to the ranks by queued audio seconds
 (cohere-transcribe_b200/dispatch.py); each rank runs its own engine on its
@@ -20,17 +20,18 @@ One bench step runs two legs over that batch:
        e2e    the same count / wall time of the C-ABI calls from host buffers
               (H2D of the encoder rows, D2H of the tokens), every step.
        p50_step_ms  median device time of one packed decode step.
-  B  transcribe: submit the 64 log-mel inputs (ct_engine_submit_mel), which
-     the engine encodes as one packed ragged batch (48 Conformer layers),
-     admits and decodes; poll the tokens.
-       rtfx.value  audio seconds / device time (encoder + admission + decode)
-       rtfx.e2e    audio seconds / wall time of the C-ABI calls from host log-mel
+  B  transcribe: submit the 64 utterances as 16 kHz samples
+     (ct_engine_submit_audio); the engine computes their log-mel on the GPU,
+     encodes them as one packed ragged batch (48 Conformer layers), admits and
+     decodes them; poll the tokens.
+       rtfx.value  audio seconds / device time (front-end + encoder + admission + decode)
+       rtfx.e2e    audio seconds / wall time of the C-ABI calls from host samples
 
 `--impl reference` times the reference's own CPU implementation (its
 backends/cpu/backend.c driven by its model.h, prebuilt under oracle/_ref/) on
 bounded samples of the same workload, one utterance per host thread: greedy
 decode from the same encoder rows (tokens/s), and full transcription
-(encoder + decode) of 1 s cuts of the log-mel inputs (RTFx).
+(log-mel front-end + encoder + decode) of 1 s cuts of the audio (RTFx).
 """
 from __future__ import annotations
 
@@ -74,12 +75,10 @@ def workload(seed: int = 0, batch: int = BATCH, rank: int = 0, world: int = 1):
         rng = np.random.default_rng([full["enc_seed"], int(i)])
         enc[j, :t] = rng.standard_normal((int(t), 1024), dtype=np.float32)
     T_mel = np.array([inputs.ctb.t_mel_of_seconds(x) for x in case["seconds"]], np.int32)
-    mels = []
-    for i, t in zip(idx, T_mel):
-        rng = np.random.default_rng([seed, 7, int(i)])
-        mels.append(rng.standard_normal((128, int(t)), dtype=np.float32))
+    # 16 kHz signals (a few tones plus noise) of the drawn durations
+    audio = [inputs.audio(float(x), 10_000 * (seed + 1) + int(i)) for i, x in zip(idx, case["seconds"])]
     case["T_mel"] = T_mel
-    return case, enc, mels
+    return case, enc, audio
 
 
 def peaks():
@@ -184,7 +183,7 @@ class ReferenceCPU:
                   utterance's log-mel, to min(forced, CPU_CUT_TOKENS) tokens
                   -> RTFx (audio seconds / wall seconds)."""
 
-    def __init__(self, case, enc, mels, n_threads: int, cap: int):
+    def __init__(self, case, enc, audio, n_threads: int, cap: int):
         sys.path.insert(0, os.path.join(REPO, "oracle"))
         import inputs as _in
         import pyoracle as po
@@ -207,14 +206,16 @@ class ReferenceCPU:
         self.prompt = np.array(_in.ctb.PROMPT_FULL, np.int32)
         cut = _in.ctb.t_mel_of_seconds(CPU_CUT_S)
         self.T_mel_cut = np.full(n, cut, np.int32)
-        self.mel_cut = np.ascontiguousarray(np.stack([mels[i][:, :cut] for i in idx]), dtype=np.float32)
+        self.audio_cut = [np.ascontiguousarray(audio[i][:int(CPU_CUT_S * 16000)]) for i in idx]
+        self.M = ctypes.CDLL(os.path.join(po.REF_DIR, "libref_mel.so"))
+        self.M.refmel_compute.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
         self.forced_cut = np.ascontiguousarray(np.minimum(case["forced_len"][idx], CPU_CUT_TOKENS), dtype=np.int32)
         self.sample = (f"first {n} utterances of the workload (T_enc {int(self.T_enc.min())}-{int(self.T_enc.max())}),"
                        f" each cross-K/V + 10-token prefill + greedy decode to min(forced length, {cap}) tokens"
                        f" ({int(self.forced.sum())} tokens), one utterance per host thread")
-        self.sample_rtfx = (f"first {n} utterances of the workload cut to their first {CPU_CUT_S:g} s of log-mel,"
-                            f" each encoder (48 layers) + prefill + greedy decode to {CPU_CUT_TOKENS} tokens,"
-                            f" one utterance per host thread")
+        self.sample_rtfx = (f"first {n} utterances of the workload cut to their first {CPU_CUT_S:g} s of audio,"
+                            f" each log-mel front-end + encoder (48 layers) + prefill + greedy decode to"
+                            f" {CPU_CUT_TOKENS} tokens, one utterance per host thread")
 
     def decode(self):
         po = self.po
@@ -229,9 +230,14 @@ class ReferenceCPU:
         po = self.po
         tokens = np.zeros((self.n, 1024), np.int32)
         n_tok = np.zeros(self.n, np.int32)
-        secs = self.L.refh_parallel_transcribe(self.n, self.n, po.fp(self.mel_cut), int(self.T_mel_cut[0]),
-                                               po.ip(self.T_mel_cut), po.ip(self.prompt), len(self.prompt),
-                                               po.ip(self.forced_cut), po.ip(tokens), po.ip(n_tok))
+        t0 = time.perf_counter()
+        mel = np.zeros((self.n, 128, int(self.T_mel_cut[0])), np.float32)
+        for b, x in enumerate(self.audio_cut):   # the reference front-end (one host thread)
+            self.M.refmel_compute(x.ctypes.data, len(x), mel[b].ctypes.data)
+        secs = time.perf_counter() - t0
+        secs += self.L.refh_parallel_transcribe(self.n, self.n, po.fp(mel), int(self.T_mel_cut[0]),
+                                                po.ip(self.T_mel_cut), po.ip(self.prompt), len(self.prompt),
+                                                po.ip(self.forced_cut), po.ip(tokens), po.ip(n_tok))
         return self.n * CPU_CUT_S, secs
 
 
@@ -256,7 +262,7 @@ def main():
 
     world, rank, local = dist_setup()
     pk, pk_kind = peaks()
-    case, enc, mels = workload(0, args.batch, rank, world)
+    case, enc, audio = workload(0, args.batch, rank, world)
     if args.max_len > 0:
         case["forced_len"] = np.minimum(case["forced_len"], args.max_len).astype(np.int32)
     nb = len(case["T_enc"])
@@ -276,7 +282,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        ref = ReferenceCPU(case, enc, mels, ncores, args.cpu_tokens)
+        ref = ReferenceCPU(case, enc, audio, ncores, args.cpu_tokens)
         for _ in range(args.warmup):
             ref.decode()
             ref.transcribe()
@@ -321,7 +327,7 @@ def main():
     # host inputs: encoder rows (leg A) and log-mel (leg B), fp32 host memory
     enc_rows = [np.ascontiguousarray(enc[b, :case["T_enc"][b]]) for b in range(nb)]
     h2d_a = int(sum(x.nbytes for x in enc_rows))
-    h2d_b = int(sum(m.nbytes for m in mels))
+    h2d_b = int(sum(x.nbytes for x in audio))
     d2h = int(4 * tokens_per_step)
 
     def leg_a(e, step_times):
@@ -338,10 +344,10 @@ def main():
         return out
 
     def leg_b(e):
-        if "E" in legs:   # encoder only (profiling cases): one packed encoder batch
-            return e.encode(mels)
+        if "E" in legs:   # encoder only (profiling cases): front-end + one packed encoder batch
+            return e.encode(e.log_mel(audio))
         for b in range(nb):
-            e.submit_mel(b, mels[b], int(case["forced_len"][b]))
+            e.submit_audio(b, audio[b], int(case["forced_len"][b]))
         e.run()
         out = e.poll()
         assert len(out) == nb
@@ -466,7 +472,7 @@ def main():
             "precision": "bf16 weights, activations as bf16 hi+lo planes, fp32 accumulate" if args.precision else
             "bf16 weights and activations, fp32 accumulate"}
     if rank == 0 and world == 1 and not args.no_cpu:
-        ref = ReferenceCPU(case, enc, mels, ncores, args.cpu_tokens)
+        ref = ReferenceCPU(case, enc, audio, ncores, args.cpu_tokens)
         t, s_ = ref.decode()
         a_, s2 = ref.transcribe()
         line["cpu_baseline"] = {"value": t / s_, "unit": "tokens/s", "cores": ncores, "kind": "reference",

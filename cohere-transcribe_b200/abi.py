@@ -76,6 +76,8 @@ SIGNATURES = {
     "ct_engine_encode": (_int, [_vp, _int, _vp, _vp, _vp, _vp]),
     "ct_linear_bf16": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _vp]),
     "ct_engine_submit_mel": (_int, [_vp, ctypes.c_longlong, _vp, _int, _int]),
+    "ct_engine_submit_audio": (_int, [_vp, ctypes.c_longlong, _vp, _int, _int]),
+    "ct_engine_log_mel": (_int, [_vp, _int, _vp, _vp, _vp]),
 }
 
 
@@ -127,6 +129,26 @@ class Engine:
         rc = self.lib.ct_engine_submit_mel(self.h, utt_id, a.ctypes.data, a.shape[1], int(forced_len))
         if rc != 0:
             raise RuntimeError(f"submit_mel failed: {rc}")
+
+    def submit_audio(self, utt_id, samples, forced_len):
+        a = np.ascontiguousarray(samples, dtype=np.float32)      # 16 kHz mono
+        rc = self.lib.ct_engine_submit_audio(self.h, utt_id, a.ctypes.data, len(a), int(forced_len))
+        if rc != 0:
+            raise RuntimeError(f"submit_audio failed: {rc}")
+
+    def log_mel(self, signals):
+        """signals: list of 16 kHz float arrays -> list of [128, 1 + len // 160] log-mel."""
+        arrs = [np.ascontiguousarray(x, dtype=np.float32) for x in signals]
+        n = len(arrs)
+        ptrs = (ctypes.c_void_p * n)(*[x.ctypes.data for x in arrs])
+        ns = np.array([len(x) for x in arrs], np.int32)
+        T = 1 + ns // 160
+        out = np.zeros(int(T.sum()) * 128, np.float32)
+        rc = self.lib.ct_engine_log_mel(self.h, n, ptrs, ns.ctypes.data, out.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"log_mel failed: {rc}")
+        offs = np.concatenate([[0], np.cumsum(T)]) * 128
+        return [out[offs[b]:offs[b + 1]].reshape(128, T[b]) for b in range(n)]
 
     def encode(self, mels):
         """mels: list of [N_MELS, T_mel] arrays -> list of [T_enc, DEC_D] encoder outputs."""

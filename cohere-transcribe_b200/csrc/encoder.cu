@@ -18,6 +18,7 @@
 #include <string.h>
 #include <vector>
 
+#include "frontend.cu"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
@@ -480,6 +481,7 @@ struct State {
     std::vector<void *> owned;
     // profile mode: events recorded between kernel groups, with the label of
     // the group each closes (labels[0] is unused)
+    fe::Front fe;                          // log-mel front-end (audio input)
     bool prof = false;
     std::vector<cudaEvent_t> ev;
     std::vector<const char *> labels;
@@ -533,12 +535,13 @@ static bool state_alloc(State &st, int max_utts, int max_frames, bool two) {
     for (int k = 0; k < (two ? 2 : 1); ++k)
         ok = ok && ealloc(st, &st.xa[k], R * D) && ealloc(st, &st.hid[k], hidn) && ealloc(st, &st.ap[k], R * D) &&
              ealloc(st, &st.posp[k], (size_t)(2 * st.T_cap) * D);
-    return ok;
+    return ok && fe::front_alloc(st.fe, max_utts, max_frames);
 }
 
 static void state_free(State &st) {
     for (void *p : st.owned) cudaFree(p);
     st.owned.clear();
+    fe::front_free(st.fe);
     for (cudaEvent_t e : st.ev) cudaEventDestroy(e);
     st.ev.clear();
 }
@@ -554,10 +557,10 @@ static void egemm_enc(cudaStream_t s, const State &st, const bf16 *W, int N, int
     gemm_bf16(s, W, N, K, xp[0], st.two ? xp[1] : nullptr, T, ep, false);
 }
 
-// Encode n utterances (host log-mel, mel[b] = [N_MELS][T_mel[b]]) into
-// st.enc_h: packed rows [R3, DEC_D], utterance b at rows r3_off[b] ..
-// r3_off[b+1] - 1 (returned in r3_off_out, n+1 entries).  Returns false when
-// the batch exceeds the capacity.
+// Encode n utterances (host log-mel, mel[b] = [N_MELS][T_mel[b]]; mel == null:
+// the log-mel is already in st.mel, packed) into st.enc_h: packed rows
+// [R3, DEC_D], utterance b at rows r3_off[b] .. r3_off[b+1] - 1 (returned in
+// r3_off_out, n+1 entries).  Returns false when the batch exceeds the capacity.
 static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, const int *T_mel, int *r3_off_out) {
     if (n <= 0 || n > st.max_utts) return false;
     // ---- tables (host) ----
@@ -606,8 +609,10 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     }
     memcpy(u3 + R3, qt.data(), sizeof(int) * NQ);
     CT_CHECK(cudaMemcpyAsync(st.tab, hp, sizeof(int) * h.size(), cudaMemcpyHostToDevice, s));
-    for (int b = 0; b < n; ++b)
-        CT_CHECK(cudaMemcpyAsync(st.mel + mel_off[b], mel[b], sizeof(float) * F0 * T_mel[b], cudaMemcpyHostToDevice, s));
+    if (mel)
+        for (int b = 0; b < n; ++b)
+            CT_CHECK(cudaMemcpyAsync(st.mel + mel_off[b], mel[b], sizeof(float) * F0 * T_mel[b],
+                                     cudaMemcpyHostToDevice, s));
     Batch bt;
     bt.n = n;
     bt.T_mel = st.tab;
@@ -631,8 +636,10 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     }
     const Weights_ &w = st.w;
     bf16 *hidp[2] = {st.hid[0], st.hid[1]};
-    st.n_marks = 0;
-    mark(s, st, "");
+    if (mel) {
+        st.n_marks = 0;
+        mark(s, st, "");
+    }
     // ---- subsampling (backends/cpu/backend.c:188-229), channels last ----
     conv0_packed<<<grid_of((size_t)R1 * F1 * C), 256, 0, s>>>(st.mel, bt, w.s0w, w.s0b, st.s1);
     dw_packed<<<grid_of((size_t)R2 * F2 * C), 256, 0, s>>>(st.s1, F1, bt.r1_off, bt.r2_off, bt.row_utt2, R2, w.s2w,
@@ -729,6 +736,17 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     CT_CHECK(cudaGetLastError());
     memcpy(r3_off_out, r3.data(), sizeof(int) * (n + 1));
     return true;
+}
+
+// Encode n utterances from host 16 kHz samples: the log-mel front-end writes
+// st.mel, then encode() runs on it.  T_mel[b] = 1 + n_samples[b] / 160.
+static bool encode_audio(cudaStream_t s, State &st, int n, const float *const *samples, const int *n_samples,
+                         int *T_mel, int *r3_off_out) {
+    st.n_marks = 0;
+    mark(s, st, "");
+    if (!fe::log_mel(s, st.fe, n, samples, n_samples, st.mel, T_mel)) return false;
+    mark(s, st, "enc_log_mel");
+    return encode(s, st, n, nullptr, T_mel, r3_off_out);
 }
 
 }  // namespace enc

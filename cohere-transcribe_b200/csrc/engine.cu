@@ -602,7 +602,8 @@ struct ct_engine {
     cudaEvent_t aev0 = nullptr, aev1 = nullptr;
     std::vector<int> slot_steps;     // steps run since admission (host mirror of the KV length)
     enc::State *enc = nullptr;       // packed encoder (null when the blob has no encoder weights)
-    struct MelJob { long long id; std::vector<float> mel; int T_mel, forced; };
+    // queued utterance: log-mel [N_MELS][T_mel] or 16 kHz samples (n_samples > 0)
+    struct MelJob { long long id; std::vector<float> mel; int T_mel, n_samples, forced; };
     std::deque<MelJob> mel_pending;
     cudaEvent_t eev0 = nullptr, eev1 = nullptr;
     std::vector<int> slot_tenc;
@@ -944,19 +945,25 @@ static bool admissible(const ct_engine *e, int T_enc, int forced_len);
 static int encode_pending(ct_engine *e) {
     if (e->mel_pending.empty()) return 0;
     if (!e->enc) return CT_EINVAL;
+    // one batch: a prefix of the queue of one input kind, within capacity
     std::vector<const float *> mels;
-    std::vector<int> T_mel;
+    std::vector<int> T_mel, n_samp;
     int frames = 0;
+    const bool audio = e->mel_pending.front().n_samples > 0;
     for (auto &j : e->mel_pending) {
+        if ((j.n_samples > 0) != audio) break;
         if ((int)mels.size() >= e->enc->max_utts || frames + j.T_mel > e->enc->max_frames) break;
         mels.push_back(j.mel.data());
         T_mel.push_back(j.T_mel);
+        n_samp.push_back(j.n_samples);
         frames += j.T_mel;
     }
     const int n = (int)mels.size();
     std::vector<int> off(n + 1);
     EK(cudaEventRecord(e->eev0, e->st));
-    if (!enc::encode(e->st, *e->enc, n, mels.data(), T_mel.data(), off.data())) return CT_EINVAL;
+    const bool ok = audio ? enc::encode_audio(e->st, *e->enc, n, mels.data(), n_samp.data(), T_mel.data(), off.data())
+                          : enc::encode(e->st, *e->enc, n, mels.data(), T_mel.data(), off.data());
+    if (!ok) return CT_EINVAL;
     EK(cudaEventRecord(e->eev1, e->st));
     // the rows wait in mel_rows until admitted (the next encoder batch runs
     // only once every pending utterance has been admitted)
@@ -1061,8 +1068,40 @@ extern "C" int ct_engine_submit_mel(ct_engine *e, long long utt_id, const float 
     j.id = utt_id;
     j.mel.assign(mel, mel + (size_t)N_MELS * T_mel);
     j.T_mel = T_mel;
+    j.n_samples = 0;
     j.forced = forced_len;
     e->mel_pending.push_back(std::move(j));
+    return CT_OK;
+}
+
+extern "C" int ct_engine_submit_audio(ct_engine *e, long long utt_id, const float *samples, int n_samples,
+                                      int forced_len) {
+    if (!e || !samples || n_samples < fe::HOP || forced_len < 0) return CT_EINVAL;
+    const int T_mel = 1 + n_samples / fe::HOP;
+    if (!e->enc || T_mel > e->enc->max_frames) return CT_EINVAL;
+    const int t1 = (T_mel + 1) / 2, t2 = (t1 + 1) / 2, T_enc = (t2 + 1) / 2;
+    if (!admissible(e, T_enc, forced_len)) return CT_EINVAL;
+    ct_engine::MelJob j;
+    j.id = utt_id;
+    j.mel.assign(samples, samples + n_samples);
+    j.T_mel = T_mel;
+    j.n_samples = n_samples;
+    j.forced = forced_len;
+    e->mel_pending.push_back(std::move(j));
+    return CT_OK;
+}
+
+extern "C" int ct_engine_log_mel(ct_engine *e, int n, const float *const *samples, const int *n_samples,
+                                 float *mel_out) {
+    if (!e || n <= 0 || !samples || !n_samples || !mel_out) return CT_EINVAL;
+    if (!e->enc) return CT_EINVAL;
+    EK(cudaSetDevice(e->device));
+    std::vector<int> T_mel(n);
+    if (!fe::log_mel(e->st, e->enc->fe, n, samples, n_samples, e->enc->mel, T_mel.data())) return CT_EINVAL;
+    size_t frames = 0;
+    for (int b = 0; b < n; ++b) frames += (size_t)T_mel[b];
+    EK(cudaMemcpyAsync(mel_out, e->enc->mel, sizeof(float) * N_MELS * frames, cudaMemcpyDeviceToHost, e->st));
+    EK(cudaStreamSynchronize(e->st));
     return CT_OK;
 }
 

@@ -85,6 +85,16 @@ int ct_engine_encode(ct_engine *e, int n, const float *const *mel, const int *T_
  * and then decoded like ct_engine_submit_encoded ones. */
 int ct_engine_submit_mel(ct_engine *e, long long utt_id, const float *mel, int T_mel, int forced_len);
 
+/* Queue one utterance from 16 kHz mono samples (host, n_samples >= 160): the
+ * engine computes its log-mel on the GPU (the front-end of transcribe.c:177-214)
+ * and then encodes and decodes it like ct_engine_submit_mel input. */
+int ct_engine_submit_audio(ct_engine *e, long long utt_id, const float *samples, int n_samples, int forced_len);
+
+/* The GPU log-mel front-end alone: n utterances of 16 kHz samples (host) ->
+ * mel_out (host), utterance b's [N_MELS][T_mel[b]] block after those of
+ * utterances 0 .. b-1, T_mel = 1 + n_samples / 160 (transcribe.c:268). */
+int ct_engine_log_mel(ct_engine *e, int n, const float *const *samples, const int *n_samples, float *mel_out);
+
 /* Run up to n_steps packed steps (admitting queued utterances when slots and
  * pages allow).  Returns the number of sequences still queued or live, or a
  * negative error. */

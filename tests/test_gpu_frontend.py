@@ -1,0 +1,101 @@
+"""GPU tests of the log-mel front-end (ct_engine_log_mel, ct_engine_submit_audio)
+against the CPU oracle's orc_compute_mel, which equals the reference's
+compute_mel bit for bit (tests/test_oracle_golden.py).
+
+Tolerance: the GPU FFT uses exact twiddles (the reference advances them by
+complex multiplication) and fused multiply-adds, so power spectra differ in the
+last bits; after log and the per-bin normalisation the log-mel agrees to
+MEL_TOL absolute (values are O(1)).
+"""
+import ctypes
+import importlib
+
+import numpy as np
+import pytest
+
+import inputs
+import pyoracle as po
+
+pytestmark = pytest.mark.gpu
+MEL_TOL = 1e-3
+E2E_MARGIN_TOL = 0.05
+
+
+@pytest.fixture(scope="module")
+def full_model(wmod):
+    wb = wmod.make_blob(wmod.FULL_DIMS, seed=23)
+    return wb, wmod.weights_struct(wb)
+
+
+@pytest.fixture(scope="module")
+def engine(full_model):
+    abi = importlib.import_module("cohere-transcribe_b200.abi")
+    wb, ws = full_model
+    eng = abi.Engine(abi.load(), 0, wb, ws, enc_max_utts=8, enc_max_frames=8192)
+    yield eng
+    eng.close()
+
+
+def test_log_mel_matches_oracle(engine):
+    sigs = [inputs.audio(s, seed) for s, seed in inputs.mel_case()] + [inputs.audio(30.0, 77),
+                                                                       inputs.audio(0.01, 78)]
+    got = engine.log_mel(sigs)
+    assert engine.status() == 0
+    for k, x in enumerate(sigs):
+        ref = po.compute_mel(x)
+        assert got[k].shape == ref.shape
+        err = float(np.max(np.abs(got[k] - ref)))
+        assert err <= MEL_TOL, (k, err)
+
+
+def test_log_mel_batch_invariance(engine):
+    sigs = [inputs.audio(1.7, 80), inputs.audio(0.9, 81), inputs.audio(3.1, 82)]
+    together = engine.log_mel(sigs)
+    for k, x in enumerate(sigs):
+        assert np.array_equal(engine.log_mel([x])[0], together[k]), k
+
+
+def test_submit_audio_end_to_end(engine, full_model, wmod):
+    """16 kHz samples in, tokens out: equals submitting the engine's own log-mel,
+    and agrees with the oracle's front-end + encoder + decoder (teacher forced,
+    at steps whose oracle top-2 margin is at least E2E_MARGIN_TOL)."""
+    sigs = [inputs.audio(1.4, 90), inputs.audio(0.66, 91), inputs.audio(2.05, 92)]
+    forced = np.array([9, 6, 12], np.int32)
+    for b in range(3):
+        engine.submit_audio(b, sigs[b], forced[b])
+    engine.run()
+    via_audio = engine.poll()
+    mels = engine.log_mel(sigs)
+    for b in range(3):
+        engine.submit_mel(10 + b, mels[b], forced[b])
+    engine.run()
+    via_mel = engine.poll()
+    assert engine.status() == 0
+    for b in range(3):
+        assert np.array_equal(via_audio[b], via_mel[10 + b]), b
+    # oracle: front-end, encoder, decoder
+    ws = full_model[1]
+    ref_mels = [po.compute_mel(x) for x in sigs]
+    T_mel = np.array([m.shape[1] for m in ref_mels], np.int32)
+    mel = np.zeros((3, 128, int(T_mel.max())), np.float32)
+    for b in range(3):
+        mel[b, :, :T_mel[b]] = ref_mels[b]
+    T_enc = np.array([(((t + 1) // 2 + 1) // 2 + 1) // 2 for t in T_mel], np.int32)
+    enc = np.zeros((3, int(T_enc.max()), 1024), np.float32)
+    d = po.dims_struct(wmod.FULL_DIMS)
+    po.lib().orc_encoder_forward_batch(ctypes.byref(d), ctypes.addressof(ws), po.fp(mel), 3, mel.shape[2],
+                                       po.ip(T_mel), po.ip(T_enc), int(T_enc.max()), po.fp(enc))
+    prompt = np.array(inputs.ctb.PROMPT_FULL, np.int32)
+    n_p = len(prompt)
+    force = np.zeros((3, 1024), np.int32)
+    for b in range(3):
+        force[b, n_p:n_p + len(via_audio[b])] = via_audio[b]
+    _t, _n, am, mg = po.decode_batch(wmod.FULL_DIMS, ws, enc, T_enc, prompt, forced, force_tokens=force)
+    checked = 0
+    for b in range(3):
+        assert len(via_audio[b]) == forced[b] and via_audio[b][-1] == 3
+        for g in range(forced[b] - 1):
+            if mg[b, n_p + g] >= E2E_MARGIN_TOL:
+                assert via_audio[b][g] == am[b, n_p + g], (b, g)
+                checked += 1
+    assert checked >= 0.5 * (forced.sum() - 3)
