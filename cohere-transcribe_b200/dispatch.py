@@ -65,3 +65,22 @@ def long_form_windows(T_mel: int, window_s: float = 30.0, hop_s: float = 29.0) -
         if end >= T_mel:
             return out
         start += hop
+
+
+def long_form_sample_windows(n_samples: int, window_s: float = 30.0, hop_s: float = 29.0,
+                             sr: int = 16000) -> list[tuple[int, int]]:
+    """The same windows on the 16 kHz samples: [start, end) sample ranges, each
+    window's audio decoded as an independent utterance (its log-mel is computed
+    from its own samples, as the reference does for each chunk it cuts,
+    transcribe.c:397-535)."""
+    if n_samples <= 0:
+        return []
+    win, hop = int(round(window_s * sr)), int(round(hop_s * sr))
+    out = []
+    start = 0
+    while True:
+        end = min(start + win, n_samples)
+        out.append((start, end))
+        if end >= n_samples:
+            return out
+        start += hop

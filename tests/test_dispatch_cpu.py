@@ -50,6 +50,16 @@ def test_long_form_windows_300s():
     assert disp.long_form_windows(0) == []
 
 
+def test_long_form_sample_windows():
+    w = disp.long_form_sample_windows(300 * 16000)
+    assert len(w) == 11 and w[-1] == (290 * 16000, 300 * 16000)
+    assert all(a[1] - b[0] == 16000 for a, b in zip(w, w[1:]))   # 1 s overlap
+    # the frames of each window's own log-mel are the frame windows'
+    fw = disp.long_form_windows(disp.t_mel_of_seconds(300.0))
+    assert [1 + (e - s) // 160 for s, e in w] == [e - s for s, e in fw]
+    assert disp.long_form_sample_windows(65 * 16000) == [(0, 480000), (464000, 944000), (928000, 1040000)]
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
