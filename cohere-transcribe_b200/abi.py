@@ -78,6 +78,7 @@ SIGNATURES = {
     "ct_engine_submit_mel": (_int, [_vp, ctypes.c_longlong, _vp, _int, _int]),
     "ct_engine_submit_audio": (_int, [_vp, ctypes.c_longlong, _vp, _int, _int]),
     "ct_engine_log_mel": (_int, [_vp, _int, _vp, _vp, _vp]),
+    "ct_engine_step_times": (_int, [_vp, _vp, _int]),
 }
 
 
@@ -164,6 +165,14 @@ class Engine:
             raise RuntimeError(f"encode failed: {rc}")
         offs = np.concatenate([[0], np.cumsum(T_enc)])
         return [out[offs[b]:offs[b + 1]] for b in range(n)]
+
+    def step_times(self):
+        """Device ms of each step since the previous call (the log is cleared)."""
+        out = np.zeros(1 << 16, np.float32)
+        n = self.lib.ct_engine_step_times(self.h, out.ctypes.data, len(out))
+        if n < 0:
+            raise RuntimeError(f"step_times failed: {n}")
+        return out[:n].copy()
 
     def step(self, n=1):
         rc = self.lib.ct_engine_step(self.h, n)

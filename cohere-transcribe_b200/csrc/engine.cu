@@ -523,7 +523,8 @@ __global__ void update_kernel(DevState s, const int *next) {
 // ------------------------------------------------------------ host --------
 struct Pending {
     long long id;
-    std::vector<float> enc;          // host encoder rows (submit_encoded) ...
+    long long ring_off = -1;         // host encoder rows in the pinned submission ring (row offset) ...
+    std::vector<float> enc;          // ... or in pageable memory when the ring was full ...
     const float *dev_rows = nullptr; // ... or device rows (encoded in-engine from log-mel)
     int T_enc, forced;
 };
@@ -546,6 +547,10 @@ struct ct_engine {
     int device = -1;
     cudaStream_t st = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    // step graphs in flight between host synchronisations: their start / end events
+    static constexpr int kStepRing = 8;
+    cudaEvent_t sev0[kStepRing] = {}, sev1[kStepRing] = {};
+    std::vector<float> step_log;      // device time of each step since the last ct_engine_step_times
     ct_engine_config cfg;
     std::vector<int> prompt;
     // weights
@@ -578,7 +583,9 @@ struct ct_engine {
     bf16 *enc_pl[2];
     long long *enc_off = nullptr;
     int enc_rows_cap = 0;
-    float *enc_stage = nullptr;      // pinned
+    float *enc_stage = nullptr;      // pinned submission ring for host encoder rows (enc_rows_cap rows)
+    long long ring_head = 0, ring_tail = 0, ring_used = 0;   // FIFO ring state, in rows
+    int *tok_stage = nullptr;        // pinned [max_slots][MAX_SEQ]: harvested tokens
     long long *off_stage = nullptr;  // pinned
     int *slot_stage = nullptr;       // pinned admission records [max_slots][REC_INTS]
     int *rec_dev = nullptr;          // their device copy
@@ -824,11 +831,38 @@ __global__ void admit_records_kernel(DevState s, const int *rec) {
         s.cross_pt[(size_t)slot * CROSS_PAGES + j] = r[REC_N + SELF_PAGES + j];
 }
 
+// Submission ring (pinned): contiguous blocks of encoder rows, allocated at
+// submit and released in submission (= admission) order.  Returns the block's
+// row offset, or -1 when no contiguous space is free.
+static long long ring_alloc(ct_engine *e, int n) {
+    const long long C = e->enc_rows_cap;
+    if (n <= 0 || n > C) return -1;
+    if (e->ring_used == 0) e->ring_head = e->ring_tail = 0;
+    long long off = -1;
+    if (e->ring_used > 0 && e->ring_head == e->ring_tail) return -1;   // full
+    if (e->ring_head >= e->ring_tail) {            // free: [head, C) and [0, tail)
+        if (e->ring_head + n <= C) off = e->ring_head;
+        else if (n <= e->ring_tail) off = 0;
+    } else if (e->ring_head + n <= e->ring_tail) { // free: [head, tail)
+        off = e->ring_head;
+    }
+    if (off < 0) return -1;
+    e->ring_head = off + n;
+    e->ring_used += n;
+    return off;
+}
+static void ring_free(ct_engine *e, long long off, int n) {
+    e->ring_tail = off + n;
+    e->ring_used -= n;
+    if (e->ring_used == 0) e->ring_head = e->ring_tail = 0;
+}
+
 static int admit(ct_engine *e) {
     // pick admissions: free slot, pages, rows budget, encoder-row staging budget
     int live_rows = 0;
     for (int i = 0; i < e->cfg.max_slots; ++i) live_rows += e->slot_live[i] ? 1 : 0;
     int enc_rows = 0, n_rec = 0;
+    std::vector<std::pair<long long, int>> ring_release;   // ring blocks of the admitted utterances
     while (!e->pending.empty()) {
         Pending &p = e->pending.front();
         if (enc_rows + p.T_enc > e->enc_rows_cap) break;
@@ -864,9 +898,11 @@ static int admit(ct_engine *e) {
         const size_t bytes = sizeof(float) * (size_t)p.T_enc * D;
         if (p.dev_rows) {
             EK(cudaMemcpyAsync(dst, p.dev_rows, bytes, cudaMemcpyDeviceToDevice, e->st));
-        } else {
-            memcpy(e->enc_stage + (size_t)enc_rows * D, p.enc.data(), bytes);
-            EK(cudaMemcpyAsync(dst, e->enc_stage + (size_t)enc_rows * D, bytes, cudaMemcpyHostToDevice, e->st));
+        } else if (p.ring_off >= 0) {   // pinned: asynchronous; the ring space is released after the sync below
+            EK(cudaMemcpyAsync(dst, e->enc_stage + (size_t)p.ring_off * D, bytes, cudaMemcpyHostToDevice, e->st));
+            ring_release.push_back({p.ring_off, p.T_enc});
+        } else {                        // pageable: the call returns once the source has been staged
+            EK(cudaMemcpyAsync(dst, p.enc.data(), bytes, cudaMemcpyHostToDevice, e->st));
         }
         for (int t = 0; t < p.T_enc; ++t)
             e->off_stage[enc_rows + t] = (long long)pages[self_need + t / PR] * PAGE_ELEMS + (long long)(t % PR) * D;
@@ -891,6 +927,7 @@ static int admit(ct_engine *e) {
           false);
     EK(cudaEventRecord(e->aev1, e->st));
     EK(cudaStreamSynchronize(e->st));   // staging reuse
+    for (auto &rb : ring_release) ring_free(e, rb.first, rb.second);
     float ams = 0.0f;
     EK(cudaEventElapsedTime(&ams, e->aev0, e->aev1));
     e->st_acc.admit_ms += ams;
@@ -899,23 +936,28 @@ static int admit(ct_engine *e) {
 }
 
 static int harvest(ct_engine *e) {
+    // finished sequences: copy all their tokens out, free their slots, then one sync
+    std::vector<std::pair<int, int>> done;   // (slot, generated tokens)
     for (int i = 0; i < e->cfg.max_slots; ++i) {
         if (!e->slot_live[i]) continue;
         const int ng = ((volatile int *)e->h_done)[i];
         if (ng <= 0) continue;
-        std::vector<int> toks(ng);
-        EK(cudaMemcpyAsync(toks.data(), e->ds.out_tok + (size_t)i * MAX_SEQ, sizeof(int) * ng,
+        EK(cudaMemcpyAsync(e->tok_stage + (size_t)i * MAX_SEQ, e->ds.out_tok + (size_t)i * MAX_SEQ, sizeof(int) * ng,
                            cudaMemcpyDeviceToHost, e->st));
-        const int zero = S_FREE;
-        EK(cudaMemcpyAsync(e->ds.state + i, &zero, sizeof(int), cudaMemcpyHostToDevice, e->st));
-        EK(cudaStreamSynchronize(e->st));
+        EK(cudaMemsetAsync(e->ds.state + i, 0, sizeof(int), e->st));   // S_FREE
+        done.push_back({i, ng});
+    }
+    if (done.empty()) return 0;
+    EK(cudaStreamSynchronize(e->st));
+    for (auto &d : done) {
+        const int i = d.first, ng = d.second;
         ((volatile int *)e->h_done)[i] = 0;
         ct_result r;
         r.utt_id = e->slot_id[i];
         r.n_tokens = ng;
         r.status = 0;
         e->results.push_back(r);
-        e->result_tokens.push_back(std::move(toks));
+        e->result_tokens.emplace_back(e->tok_stage + (size_t)i * MAX_SEQ, e->tok_stage + (size_t)i * MAX_SEQ + ng);
         for (int pg : e->slot_pages[i]) e->free_pages.push_back(pg);
         e->slot_pages[i].clear();
         e->slot_live[i] = 0;
@@ -993,15 +1035,18 @@ static int encode_pending(ct_engine *e) {
 extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
     if (!e) return CT_EINVAL;
     EK(cudaSetDevice(e->device));
+    int inflight = 0;   // steps launched since the last synchronisation
     for (int it = 0; it < n_steps; ++it) {
-        if (e->pending.empty() && !e->mel_pending.empty()) {
-            const int rc = encode_pending(e);
+        if (inflight == 0) {   // harvest and admit only at synchronisation points
+            if (e->pending.empty() && !e->mel_pending.empty()) {
+                const int rc = encode_pending(e);
+                if (rc) return rc;
+            }
+            int rc = harvest(e);
+            if (rc) return rc;
+            rc = admit(e);
             if (rc) return rc;
         }
-        int rc = harvest(e);
-        if (rc) return rc;
-        rc = admit(e);
-        if (rc) return rc;
         if (e->n_live == 0) {
             if (!e->pending.empty()) return CT_EBUSY;   // nothing live and nothing admissible
             break;
@@ -1022,13 +1067,25 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
             }
         }
         Bucket *b = bucket_for(e, std::max(rows, 1));
-        EK(cudaEventRecord(e->ev0, e->st));
+        const int k = inflight;
+        EK(cudaEventRecord(e->sev0[k], e->st));
         EK(cudaGraphLaunch(b->exec, e->st));
-        EK(cudaEventRecord(e->ev1, e->st));
-        EK(cudaEventSynchronize(e->ev1));
-        float ms = 0.0f;
-        EK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
-        e->step_ms += ms;
+        EK(cudaEventRecord(e->sev1[k], e->st));
+        ++inflight;
+        // The next step's rows come from the device state (finished sequences
+        // drop out there), so further graphs can be queued before this one
+        // ends; the host synchronises every kStepRing steps, at the last step,
+        // and for every step in profile mode.
+        if (inflight == ct_engine::kStepRing || it == n_steps - 1 || e->cfg.profile) {
+            EK(cudaEventSynchronize(e->sev1[inflight - 1]));
+            for (int j = 0; j < inflight; ++j) {
+                float ms = 0.0f;
+                EK(cudaEventElapsedTime(&ms, e->sev0[j], e->sev1[j]));
+                e->step_ms += ms;
+                e->step_log.push_back(ms);
+            }
+            inflight = 0;
+        }
         e->st_acc.kernel_launches += b->kernels;
         ++e->n_steps;
         e->n_rows += rows;
@@ -1143,7 +1200,9 @@ extern "C" int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const fl
     if (!e || !enc_h || !admissible(e, T_enc, forced_len)) return CT_EINVAL;
     Pending p;
     p.id = utt_id;
-    p.enc.assign(enc_h, enc_h + (size_t)T_enc * D);
+    p.ring_off = ring_alloc(e, T_enc);
+    if (p.ring_off >= 0) memcpy(e->enc_stage + (size_t)p.ring_off * D, enc_h, sizeof(float) * (size_t)T_enc * D);
+    else p.enc.assign(enc_h, enc_h + (size_t)T_enc * D);
     p.T_enc = T_enc;
     p.forced = forced_len;
     e->pending.push_back(std::move(p));
@@ -1192,6 +1251,14 @@ extern "C" int ct_engine_profile_report(ct_engine *e, char *buf, int cap) {
     return (int)s.size();
 }
 
+extern "C" int ct_engine_step_times(ct_engine *e, float *out, int max) {
+    if (!e || (!out && max > 0)) return CT_EINVAL;
+    const int n = std::min<int>(max, (int)e->step_log.size());
+    for (int i = 0; i < n; ++i) out[i] = e->step_log[i];
+    e->step_log.clear();
+    return n;
+}
+
 extern "C" int ct_engine_status(ct_engine *e) {
     if (!e) return CT_EINVAL;
     EK(cudaSetDevice(e->device));
@@ -1219,9 +1286,14 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
     for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
     cudaFreeHost(e->h_done);
     cudaFreeHost(e->enc_stage);
+    cudaFreeHost(e->tok_stage);
     cudaFreeHost(e->off_stage);
     cudaFreeHost(e->slot_stage);
     cudaEventDestroy(e->ev0);
+    for (int j = 0; j < ct_engine::kStepRing; ++j) {
+        if (e->sev0[j]) cudaEventDestroy(e->sev0[j]);
+        if (e->sev1[j]) cudaEventDestroy(e->sev1[j]);
+    }
     cudaEventDestroy(e->ev1);
     cudaEventDestroy(e->aev0);
     cudaEventDestroy(e->aev1);
@@ -1266,6 +1338,10 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     if (cudaSetDevice(device) != cudaSuccess) { delete e; return CT_EDEVICE; }
     EK(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
     EK(cudaEventCreate(&e->ev0));
+    for (int j = 0; j < ct_engine::kStepRing; ++j) {
+        EK(cudaEventCreate(&e->sev0[j]));
+        EK(cudaEventCreate(&e->sev1[j]));
+    }
     EK(cudaEventCreate(&e->ev1));
     EK(cudaEventCreate(&e->aev0));
     EK(cudaEventCreate(&e->aev1));
@@ -1351,6 +1427,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     if (dalloc(&e->enc_dev, (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_pl[0], (size_t)e->enc_rows_cap * D) ||
         dalloc(&e->enc_pl[1], (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_off, e->enc_rows_cap)) { ct_engine_destroy(e); return CT_ENOMEM; }
     EK(cudaHostAlloc(&e->enc_stage, sizeof(float) * (size_t)e->enc_rows_cap * D, cudaHostAllocDefault));
+    EK(cudaHostAlloc(&e->tok_stage, sizeof(int) * (size_t)cfg.max_slots * MAX_SEQ, cudaHostAllocDefault));
     EK(cudaHostAlloc(&e->off_stage, sizeof(long long) * e->enc_rows_cap, cudaHostAllocDefault));
     EK(cudaHostAlloc(&e->slot_stage, sizeof(int) * (size_t)cfg.max_slots * REC_INTS, cudaHostAllocDefault));
     if (dalloc(&e->rec_dev, (size_t)cfg.max_slots * REC_INTS)) { ct_engine_destroy(e); return CT_ENOMEM; }

@@ -96,8 +96,10 @@ int ct_engine_submit_audio(ct_engine *e, long long utt_id, const float *samples,
 int ct_engine_log_mel(ct_engine *e, int n, const float *const *samples, const int *n_samples, float *mel_out);
 
 /* Run up to n_steps packed steps (admitting queued utterances when slots and
- * pages allow).  Returns the number of sequences still queued or live, or a
- * negative error. */
+ * pages allow).  Step graphs are queued back to back and the host synchronises
+ * every 8 steps (and after the last), harvesting finished sequences and
+ * admitting new ones at those points.  Returns the number of sequences still
+ * queued or live, or a negative error. */
 int ct_engine_step(ct_engine *e, int n_steps);
 
 /* Run until every submitted utterance has finished. */
@@ -127,6 +129,11 @@ typedef struct {
     long long enc_utts, enc_frames;
 } ct_engine_stats_t;
 int ct_engine_stats(ct_engine *e, ct_engine_stats_t *out);
+
+/* Device time (ms) of each packed step run since the previous call, oldest
+ * first: up to max values are copied to out, the log is cleared, and the number
+ * copied is returned. */
+int ct_engine_step_times(ct_engine *e, float *out, int max);
 
 /* Profile mode: JSON object {label: [total device ms, launches]} of every
  * launch group of the step graph, from the event nodes between them.
