@@ -22,6 +22,14 @@ PROMPT_TINY = [13764 % 1024, 7, 4, 16, LANG_ID, LANG_ID, 5, 9, 11, 13]
 TOK_EOS = 3
 
 
+def prompt_tokens(lang_id: int = LANG_ID, pnc: bool = True, itn: bool = False, timestamps: bool = False,
+                  diarize: bool = False, leading_space: int = 13764) -> list:
+    """The ten prompt tokens of transcribe.c:1320-1330 for one utterance's
+    options (token ids of model.h:24-36)."""
+    return [leading_space, 7, 4, 16, lang_id, lang_id, 5 if pnc else 6, 8 if itn else 9,
+            10 if timestamps else 11, 12 if diarize else 13]
+
+
 def t_enc_of(t_mel: int) -> int:
     """Encoder frames after 8x subsampling (transcribe.c:268-271)."""
     t1 = (t_mel + 1) // 2

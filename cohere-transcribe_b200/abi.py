@@ -79,6 +79,7 @@ SIGNATURES = {
     "ct_engine_submit_audio": (_int, [_vp, ctypes.c_longlong, _vp, _int, _int]),
     "ct_engine_log_mel": (_int, [_vp, _int, _vp, _vp, _vp]),
     "ct_engine_step_times": (_int, [_vp, _vp, _int]),
+    "ct_engine_set_prompt": (_int, [_vp, _vp, _int]),
 }
 
 
@@ -165,6 +166,16 @@ class Engine:
             raise RuntimeError(f"encode failed: {rc}")
         offs = np.concatenate([[0], np.cumsum(T_enc)])
         return [out[offs[b]:offs[b + 1]] for b in range(n)]
+
+    def set_prompt(self, prompt=None):
+        """Prompt for the utterances submitted next (None: the engine default)."""
+        if prompt is None:
+            rc = self.lib.ct_engine_set_prompt(self.h, None, 0)
+        else:
+            p = np.ascontiguousarray(prompt, dtype=np.int32)
+            rc = self.lib.ct_engine_set_prompt(self.h, p.ctypes.data, len(p))
+        if rc != 0:
+            raise RuntimeError(f"set_prompt failed: {rc}")
 
     def step_times(self):
         """Device ms of each step since the previous call (the log is cleared)."""

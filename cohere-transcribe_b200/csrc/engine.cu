@@ -44,7 +44,7 @@ struct DevState {
     int *state, *tok, *pos, *gen, *forced, *tenc;
     int *self_pt, *cross_pt;     // [slots][64]
     int *out_tok;                // [slots][MAX_SEQ]
-    int *prompt;                 // [n_prompt]
+    int *prompt;                 // [slots][n_prompt]: each slot's prompt (written at admission)
     int *done_map;               // host-mapped [slots]: n_gen when finished (device pointer)
     // per-step rows
     int *r_slot, *r_pos, *r_tok;
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
         const int p = st == S_PREFILL ? j : s.pos[i];
         s.r_slot[r] = i;
         s.r_pos[r] = p;
-        s.r_tok[r] = st == S_PREFILL ? s.prompt[j] : s.tok[i];
+        s.r_tok[r] = st == S_PREFILL ? s.prompt[i * s.n_prompt + j] : s.tok[i];
         const int page = (p >= 0 && p < MAX_SEQ) ? s.self_pt[i * SELF_PAGES + p / PR] : -1;
         s.r_off[r] = page >= 0 ? (long long)page * PAGE_ELEMS + (long long)(p % PR) * D : -1;
     }
@@ -521,8 +521,38 @@ __global__ void update_kernel(DevState s, const int *next) {
 }
 
 // ------------------------------------------------------------ host --------
+// Pinned host ring: contiguous blocks allocated at submission and released
+// in submission order, so inputs are copied once from the caller and uploaded
+// asynchronously.  alloc returns the block offset or -1 when no contiguous
+// space is free (the caller then keeps a pageable copy).
+struct PinnedRing {
+    long long cap = 0, head = 0, tail = 0, used = 0;
+    long long alloc(long long n) {
+        if (n <= 0 || n > cap) return -1;
+        if (used == 0) head = tail = 0;
+        if (used > 0 && head == tail) return -1;   // full
+        long long off = -1;
+        if (head >= tail) {                        // free: [head, cap) and [0, tail)
+            if (head + n <= cap) off = head;
+            else if (n <= tail) off = 0;
+        } else if (head + n <= tail) {             // free: [head, tail)
+            off = head;
+        }
+        if (off < 0) return -1;
+        head = off + n;
+        used += n;
+        return off;
+    }
+    void release(long long off, long long n) {
+        tail = off + n;
+        used -= n;
+        if (used == 0) head = tail = 0;
+    }
+};
+
 struct Pending {
     long long id;
+    std::vector<int> prompt;         // this utterance's prompt (empty: the engine's)
     long long ring_off = -1;         // host encoder rows in the pinned submission ring (row offset) ...
     std::vector<float> enc;          // ... or in pageable memory when the ring was full ...
     const float *dev_rows = nullptr; // ... or device rows (encoded in-engine from log-mel)
@@ -584,7 +614,9 @@ struct ct_engine {
     long long *enc_off = nullptr;
     int enc_rows_cap = 0;
     float *enc_stage = nullptr;      // pinned submission ring for host encoder rows (enc_rows_cap rows)
-    long long ring_head = 0, ring_tail = 0, ring_used = 0;   // FIFO ring state, in rows
+    PinnedRing ring;                 // over enc_stage, in rows
+    PinnedRing job_ring;             // over job_stage: queued audio / log-mel inputs, in floats
+    float *job_stage = nullptr;
     int *tok_stage = nullptr;        // pinned [max_slots][MAX_SEQ]: harvested tokens
     long long *off_stage = nullptr;  // pinned
     int *slot_stage = nullptr;       // pinned admission records [max_slots][REC_INTS]
@@ -610,7 +642,15 @@ struct ct_engine {
     std::vector<int> slot_steps;     // steps run since admission (host mirror of the KV length)
     enc::State *enc = nullptr;       // packed encoder (null when the blob has no encoder weights)
     // queued utterance: log-mel [N_MELS][T_mel] or 16 kHz samples (n_samples > 0)
-    struct MelJob { long long id; std::vector<float> mel; int T_mel, n_samples, forced; };
+    // input in job_ring (ring_off >= 0, float offset) or in the vector (ring full)
+    struct MelJob {
+        long long id, ring_off;
+        std::vector<float> mel;
+        int T_mel, n_samples, forced;
+        std::vector<int> prompt;
+        size_t count;                // floats of input
+    };
+    std::vector<int> next_prompt;    // prompt of the utterances submitted next (empty: the engine's)
     std::deque<MelJob> mel_pending;
     cudaEvent_t eev0 = nullptr, eev1 = nullptr;
     std::vector<int> slot_tenc;
@@ -814,7 +854,8 @@ static Bucket *bucket_for(ct_engine *e, int rows_needed) {
 
 // Host mirror of the device slot record written at admission.
 enum { REC_SLOT, REC_STATE, REC_TOK, REC_POS, REC_GEN, REC_FORCED, REC_TENC, REC_N };
-constexpr int REC_INTS = REC_N + SELF_PAGES + CROSS_PAGES;   // one admission record
+constexpr int REC_PROMPT_MAX = 64;
+constexpr int REC_INTS = REC_N + SELF_PAGES + CROSS_PAGES + REC_PROMPT_MAX;   // one admission record
 
 // Writes the slot records of k admissions (built on the host, one H2D copy):
 // block r takes record r.
@@ -829,33 +870,12 @@ __global__ void admit_records_kernel(DevState s, const int *rec) {
     for (int j = threadIdx.x; j < SELF_PAGES; j += blockDim.x) s.self_pt[(size_t)slot * SELF_PAGES + j] = r[REC_N + j];
     for (int j = threadIdx.x; j < CROSS_PAGES; j += blockDim.x)
         s.cross_pt[(size_t)slot * CROSS_PAGES + j] = r[REC_N + SELF_PAGES + j];
+    for (int j = threadIdx.x; j < s.n_prompt; j += blockDim.x)
+        s.prompt[(size_t)slot * s.n_prompt + j] = r[REC_N + SELF_PAGES + CROSS_PAGES + j];
 }
 
-// Submission ring (pinned): contiguous blocks of encoder rows, allocated at
-// submit and released in submission (= admission) order.  Returns the block's
-// row offset, or -1 when no contiguous space is free.
-static long long ring_alloc(ct_engine *e, int n) {
-    const long long C = e->enc_rows_cap;
-    if (n <= 0 || n > C) return -1;
-    if (e->ring_used == 0) e->ring_head = e->ring_tail = 0;
-    long long off = -1;
-    if (e->ring_used > 0 && e->ring_head == e->ring_tail) return -1;   // full
-    if (e->ring_head >= e->ring_tail) {            // free: [head, C) and [0, tail)
-        if (e->ring_head + n <= C) off = e->ring_head;
-        else if (n <= e->ring_tail) off = 0;
-    } else if (e->ring_head + n <= e->ring_tail) { // free: [head, tail)
-        off = e->ring_head;
-    }
-    if (off < 0) return -1;
-    e->ring_head = off + n;
-    e->ring_used += n;
-    return off;
-}
-static void ring_free(ct_engine *e, long long off, int n) {
-    e->ring_tail = off + n;
-    e->ring_used -= n;
-    if (e->ring_used == 0) e->ring_head = e->ring_tail = 0;
-}
+static long long ring_alloc(ct_engine *e, int n) { return e->ring.alloc(n); }
+static void ring_free(ct_engine *e, long long off, int n) { e->ring.release(off, n); }
 
 static int admit(ct_engine *e) {
     // pick admissions: free slot, pages, rows budget, encoder-row staging budget
@@ -893,6 +913,8 @@ static int admit(ct_engine *e) {
         int *spt = rec + REC_N, *cpt = spt + SELF_PAGES;
         for (int j = 0; j < SELF_PAGES; ++j) spt[j] = j < self_need ? pages[j] : -1;
         for (int j = 0; j < CROSS_PAGES; ++j) cpt[j] = j < cross_need ? pages[self_need + j] : -1;
+        const std::vector<int> &pr = p.prompt.empty() ? e->prompt : p.prompt;
+        std::copy(pr.begin(), pr.end(), cpt + CROSS_PAGES);
         // encoder rows of this utterance -> contiguous device rows, with their cross page offsets
         float *dst = e->enc_dev + (size_t)enc_rows * D;
         const size_t bytes = sizeof(float) * (size_t)p.T_enc * D;
@@ -995,7 +1017,7 @@ static int encode_pending(ct_engine *e) {
     for (auto &j : e->mel_pending) {
         if ((j.n_samples > 0) != audio) break;
         if ((int)mels.size() >= e->enc->max_utts || frames + j.T_mel > e->enc->max_frames) break;
-        mels.push_back(j.mel.data());
+        mels.push_back(j.ring_off >= 0 ? e->job_stage + j.ring_off : j.mel.data());
         T_mel.push_back(j.T_mel);
         n_samp.push_back(j.n_samples);
         frames += j.T_mel;
@@ -1021,11 +1043,13 @@ static int encode_pending(ct_engine *e) {
     e->st_acc.kernel_launches += 5 + 3 + 1 + 2 + NL * (5 + 2 + 2 + 2 + 1 + 2 + 2 + 1 + 3) + 1;
     for (int b = 0; b < n; ++b) {
         const auto &j = e->mel_pending.front();
+        if (j.ring_off >= 0) e->job_ring.release(j.ring_off, (long long)j.count);   // uploaded (synchronised above)
         Pending p;
         p.id = j.id;
         p.T_enc = off[b + 1] - off[b];
         p.dev_rows = e->mel_rows + (size_t)off[b] * D;
         p.forced = j.forced;
+        p.prompt = j.prompt;
         e->pending.push_back(std::move(p));
         e->mel_pending.pop_front();
     }
@@ -1116,6 +1140,15 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
     return (int)e->pending.size() + (int)e->mel_pending.size() + e->n_live;
 }
 
+// Copy a queued utterance's input once: into the pinned job ring when it has
+// room, else into the job's own (pageable) vector.
+static void stage_job(ct_engine *e, ct_engine::MelJob &j, const float *src, size_t count) {
+    j.count = count;
+    j.ring_off = e->job_ring.alloc((long long)count);
+    if (j.ring_off >= 0) memcpy(e->job_stage + j.ring_off, src, sizeof(float) * count);
+    else j.mel.assign(src, src + count);
+}
+
 extern "C" int ct_engine_submit_mel(ct_engine *e, long long utt_id, const float *mel, int T_mel, int forced_len) {
     if (!e || !mel || T_mel <= 0 || forced_len < 0) return CT_EINVAL;
     if (!e->enc || T_mel > e->enc->max_frames) return CT_EINVAL;
@@ -1123,10 +1156,11 @@ extern "C" int ct_engine_submit_mel(ct_engine *e, long long utt_id, const float 
     if (!admissible(e, T_enc, forced_len)) return CT_EINVAL;
     ct_engine::MelJob j;
     j.id = utt_id;
-    j.mel.assign(mel, mel + (size_t)N_MELS * T_mel);
+    stage_job(e, j, mel, (size_t)N_MELS * T_mel);
     j.T_mel = T_mel;
     j.n_samples = 0;
     j.forced = forced_len;
+    j.prompt = e->next_prompt;
     e->mel_pending.push_back(std::move(j));
     return CT_OK;
 }
@@ -1140,10 +1174,11 @@ extern "C" int ct_engine_submit_audio(ct_engine *e, long long utt_id, const floa
     if (!admissible(e, T_enc, forced_len)) return CT_EINVAL;
     ct_engine::MelJob j;
     j.id = utt_id;
-    j.mel.assign(samples, samples + n_samples);
+    stage_job(e, j, samples, (size_t)n_samples);
     j.T_mel = T_mel;
     j.n_samples = n_samples;
     j.forced = forced_len;
+    j.prompt = e->next_prompt;
     e->mel_pending.push_back(std::move(j));
     return CT_OK;
 }
@@ -1200,6 +1235,7 @@ extern "C" int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const fl
     if (!e || !enc_h || !admissible(e, T_enc, forced_len)) return CT_EINVAL;
     Pending p;
     p.id = utt_id;
+    p.prompt = e->next_prompt;
     p.ring_off = ring_alloc(e, T_enc);
     if (p.ring_off >= 0) memcpy(e->enc_stage + (size_t)p.ring_off * D, enc_h, sizeof(float) * (size_t)T_enc * D);
     else p.enc.assign(enc_h, enc_h + (size_t)T_enc * D);
@@ -1251,6 +1287,16 @@ extern "C" int ct_engine_profile_report(ct_engine *e, char *buf, int cap) {
     return (int)s.size();
 }
 
+extern "C" int ct_engine_set_prompt(ct_engine *e, const int *prompt, int n_prompt) {
+    if (!e) return CT_EINVAL;
+    if (!prompt) { e->next_prompt.clear(); return CT_OK; }
+    if (n_prompt != e->cfg.n_prompt) return CT_EINVAL;
+    for (int j = 0; j < n_prompt; ++j)
+        if (prompt[j] < 0 || prompt[j] >= V) return CT_EINVAL;
+    e->next_prompt.assign(prompt, prompt + n_prompt);
+    return CT_OK;
+}
+
 extern "C" int ct_engine_step_times(ct_engine *e, float *out, int max) {
     if (!e || (!out && max > 0)) return CT_EINVAL;
     const int n = std::min<int>(max, (int)e->step_log.size());
@@ -1287,6 +1333,7 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
     cudaFreeHost(e->h_done);
     cudaFreeHost(e->enc_stage);
     cudaFreeHost(e->tok_stage);
+    if (e->job_stage) cudaFreeHost(e->job_stage);
     cudaFreeHost(e->off_stage);
     cudaFreeHost(e->slot_stage);
     cudaEventDestroy(e->ev0);
@@ -1392,7 +1439,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     s.max_slots = S; s.max_rows = R; s.n_prompt = cfg.n_prompt;
     if (dalloc(&s.state, S) || dalloc(&s.tok, S) || dalloc(&s.pos, S) || dalloc(&s.gen, S) || dalloc(&s.forced, S) ||
         dalloc(&s.tenc, S) || dalloc(&s.self_pt, (size_t)S * SELF_PAGES) || dalloc(&s.cross_pt, (size_t)S * CROSS_PAGES) ||
-        dalloc(&s.out_tok, (size_t)S * MAX_SEQ) || dalloc(&s.prompt, cfg.n_prompt) || dalloc(&s.r_slot, R) ||
+        dalloc(&s.out_tok, (size_t)S * MAX_SEQ) || dalloc(&s.prompt, (size_t)S * cfg.n_prompt) || dalloc(&s.r_slot, R) ||
         dalloc(&s.r_pos, R) || dalloc(&s.r_tok, R) || dalloc(&s.r_off, R) || dalloc(&s.q_row, S) ||
         dalloc(&s.q_slot, S) || dalloc(&s.n_rows, 1) || dalloc(&s.n_seqs, 1) ||
         dalloc(&s.w_self, (size_t)R * SELF_PAGES) || dalloc(&s.w_cross, (size_t)R * CROSS_PAGES) ||
@@ -1407,7 +1454,9 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     EK(cudaMemset(s.state, 0, sizeof(int) * S));
     EK(cudaMemset(s.n_rows, 0, sizeof(int)));
     EK(cudaMemset(s.n_seqs, 0, sizeof(int)));
-    EK(cudaMemcpy(s.prompt, e->prompt.data(), sizeof(int) * cfg.n_prompt, cudaMemcpyHostToDevice));
+    for (int i = 0; i < S; ++i)
+        EK(cudaMemcpy(s.prompt + (size_t)i * cfg.n_prompt, e->prompt.data(), sizeof(int) * cfg.n_prompt,
+                      cudaMemcpyHostToDevice));
     EK(cudaHostAlloc(&e->h_done, sizeof(int) * S, cudaHostAllocMapped));
     memset(e->h_done, 0, sizeof(int) * S);
     EK(cudaHostGetDevicePointer(&s.done_map, e->h_done, 0));
@@ -1428,6 +1477,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         dalloc(&e->enc_pl[1], (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_off, e->enc_rows_cap)) { ct_engine_destroy(e); return CT_ENOMEM; }
     EK(cudaHostAlloc(&e->enc_stage, sizeof(float) * (size_t)e->enc_rows_cap * D, cudaHostAllocDefault));
     EK(cudaHostAlloc(&e->tok_stage, sizeof(int) * (size_t)cfg.max_slots * MAX_SEQ, cudaHostAllocDefault));
+    e->ring.cap = e->enc_rows_cap;
     EK(cudaHostAlloc(&e->off_stage, sizeof(long long) * e->enc_rows_cap, cudaHostAllocDefault));
     EK(cudaHostAlloc(&e->slot_stage, sizeof(int) * (size_t)cfg.max_slots * REC_INTS, cudaHostAllocDefault));
     if (dalloc(&e->rec_dev, (size_t)cfg.max_slots * REC_INTS)) { ct_engine_destroy(e); return CT_ENOMEM; }
@@ -1491,6 +1541,9 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
             return CT_ENOMEM;
         }
         st->prof = cfg.profile != 0;
+        // one encoder batch of audio input (the larger of samples and log-mel)
+        e->job_ring.cap = (long long)mf * fe::HOP;
+        EK(cudaHostAlloc(&e->job_stage, sizeof(float) * (size_t)e->job_ring.cap, cudaHostAllocDefault));
     }
     EK(cudaDeviceSynchronize());
     *out = e;

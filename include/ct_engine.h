@@ -67,6 +67,14 @@ int ct_engine_create(ct_engine **out, int device, const void *host_blob, size_t 
                      const ct_engine_config *cfg);
 void ct_engine_destroy(ct_engine *e);
 
+/* Prompt of the utterances submitted from now on (any of the submit calls):
+ * n_prompt tokens, which must equal the engine's prompt length (10 for the
+ * reference's prompt, transcribe.c:1320-1330, whose variants -- language,
+ * punctuation, ITN, timestamps, diarisation -- change token values only).
+ * prompt == NULL restores the engine's default.  Utterances with different
+ * prompts decode together in one packed batch. */
+int ct_engine_set_prompt(ct_engine *e, const int *prompt, int n_prompt);
+
 /* Queue one utterance from its encoder output enc_h (host, fp32 [T_enc, DEC_D],
  * the rows model.h's encoder_forward_batch produces).  forced_len > 0 forces EOS
  * as the forced_len-th generated token (natural EOS before it is ignored);

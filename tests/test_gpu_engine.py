@@ -126,3 +126,46 @@ def test_engine_long_sequences_and_long_cross(abi, dec_model, wmod):
     out, _ = run_engine(abi, dec_model, enc, T_enc, forced)
     checked = check_against_oracle(wmod, dec_model, enc, T_enc, forced, out, MARGIN_TOL)
     assert checked > 100
+
+
+def test_engine_per_sequence_prompts(abi, dec_model, wmod):
+    """Utterances with different prompts (the variants of transcribe.c:1320-1330)
+    decode together in one packed batch: each equals its run alone under its
+    prompt, and a no-punctuation/ITN prompt agrees with the oracle decoding
+    with that prompt (teacher forced, margin rule)."""
+    ctb = inputs.ctb
+    case = inputs.ragged_decode_case(5, seed=600, l_lo=8, l_hi=30)
+    enc = inputs.enc_outputs(case["T_enc"], case["enc_seed"])
+    prompts = [ctb.prompt_tokens(), ctb.prompt_tokens(pnc=False, itn=True), ctb.prompt_tokens(timestamps=True),
+               ctb.prompt_tokens(diarize=True), ctb.prompt_tokens(lang_id=63)]
+    wb, ws = dec_model
+
+    def run(ids):
+        eng = abi.Engine(abi.load(), 0, wb, ws)
+        try:
+            for b in ids:
+                eng.set_prompt(prompts[b])
+                eng.submit(b, enc[b, :case["T_enc"][b]], case["forced_len"][b])
+            eng.run()
+            out = eng.poll()
+            assert eng.status() == 0
+        finally:
+            eng.close()
+        return out
+
+    together = run(range(5))
+    for b in range(5):
+        assert np.array_equal(run([b])[b], together[b]), b
+    b = 1
+    prompt = np.array(prompts[b], np.int32)
+    n_p = len(prompt)
+    force = np.zeros((1, 1024), np.int32)
+    force[0, n_p:n_p + len(together[b])] = together[b]
+    _t, _n, am, mg = po.decode_batch(wmod.FULL_DIMS, ws, enc[b:b + 1], case["T_enc"][b:b + 1], prompt,
+                                     case["forced_len"][b:b + 1], force_tokens=force)
+    checked = 0
+    for g in range(case["forced_len"][b] - 1):
+        if mg[0, n_p + g] >= MARGIN_TOL:
+            assert together[b][g] == am[0, n_p + g], g
+            checked += 1
+    assert checked > 0.8 * (case["forced_len"][b] - 1)
