@@ -33,6 +33,7 @@ constexpr int SELF_PAGES = MAX_SEQ / PR;     // 64
 constexpr int CROSS_PAGES = 64;              // T_enc <= 1024
 constexpr long long PAGE_ELEMS = (long long)NL * 2 * PR * D;
 enum { S_FREE = 0, S_PREFILL = 1, S_DECODE = 2, S_DONE = 3 };
+constexpr int PROMPT_MAX = 96;                 // longest prompt (the reference's long-form prompts reach 2 + 64 + 16)
 constexpr int AW = 8;                          // consumer warps per attention CTA (one per head)
 constexpr int ANST = 3;                        // page stages in the attention pipeline
 constexpr int PMIN = 5;                        // minimum pages per attention CTA
@@ -44,7 +45,8 @@ struct DevState {
     int *state, *tok, *pos, *gen, *forced, *tenc;
     int *self_pt, *cross_pt;     // [slots][64]
     int *out_tok;                // [slots][MAX_SEQ]
-    int *prompt;                 // [slots][n_prompt]: each slot's prompt (written at admission)
+    int *prompt;                 // [slots][PROMPT_MAX]: each slot's prompt (written at admission)
+    int *plen;                   // [slots]: its length
     int *done_map;               // host-mapped [slots]: n_gen when finished (device pointer)
     // per-step rows
     int *r_slot, *r_pos, *r_tok;
@@ -92,7 +94,7 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     __shared__ int tmp2[64];
     const int i = threadIdx.x;
     const int st = i < s.max_slots ? s.state[i] : S_FREE;
-    int nr = st == S_PREFILL ? s.n_prompt : st == S_DECODE ? 1 : 0;
+    int nr = st == S_PREFILL ? s.plen[i] : st == S_DECODE ? 1 : 0;
     const int te = nr > 0 ? s.tenc[i] : 0;
     const int cross_np = (te + PR - 1) / PR;
     int self_np = 0;   // self-attention pages over the slot's rows
@@ -115,7 +117,7 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
         const int p = st == S_PREFILL ? j : s.pos[i];
         s.r_slot[r] = i;
         s.r_pos[r] = p;
-        s.r_tok[r] = st == S_PREFILL ? s.prompt[i * s.n_prompt + j] : s.tok[i];
+        s.r_tok[r] = st == S_PREFILL ? s.prompt[i * PROMPT_MAX + j] : s.tok[i];
         const int page = (p >= 0 && p < MAX_SEQ) ? s.self_pt[i * SELF_PAGES + p / PR] : -1;
         s.r_off[r] = page >= 0 ? (long long)page * PAGE_ELEMS + (long long)(p % PR) * D : -1;
     }
@@ -507,9 +509,9 @@ __global__ void update_kernel(DevState s, const int *next) {
     if (forced > 0 && gen >= forced) tok = CT_TOK_EOS;
     if (gen - 1 < MAX_SEQ) s.out_tok[(size_t)slot * MAX_SEQ + gen - 1] = tok;
     s.gen[slot] = gen;
-    s.pos[slot] += st == S_PREFILL ? s.n_prompt : 1;
+    s.pos[slot] += st == S_PREFILL ? s.plen[slot] : 1;
     s.tok[slot] = tok;
-    const bool done = (forced > 0 ? gen >= forced : tok == CT_TOK_EOS) || s.n_prompt + gen >= MAX_SEQ;
+    const bool done = (forced > 0 ? gen >= forced : tok == CT_TOK_EOS) || s.plen[slot] + gen >= MAX_SEQ;
     if (done) {
         s.state[slot] = S_DONE;
         volatile int *dm = s.done_map;
@@ -654,6 +656,7 @@ struct ct_engine {
     std::deque<MelJob> mel_pending;
     cudaEvent_t eev0 = nullptr, eev1 = nullptr;
     std::vector<int> slot_tenc;
+    std::vector<int> slot_plen;      // prompt length of each slot's sequence
     std::vector<void *> owned;       // aligned copies of misaligned weights
 };
 
@@ -854,7 +857,7 @@ static Bucket *bucket_for(ct_engine *e, int rows_needed) {
 
 // Host mirror of the device slot record written at admission.
 enum { REC_SLOT, REC_STATE, REC_TOK, REC_POS, REC_GEN, REC_FORCED, REC_TENC, REC_N };
-constexpr int REC_PROMPT_MAX = 64;
+constexpr int REC_PROMPT_MAX = 1 + PROMPT_MAX;   // prompt length, then its tokens
 constexpr int REC_INTS = REC_N + SELF_PAGES + CROSS_PAGES + REC_PROMPT_MAX;   // one admission record
 
 // Writes the slot records of k admissions (built on the host, one H2D copy):
@@ -870,8 +873,9 @@ __global__ void admit_records_kernel(DevState s, const int *rec) {
     for (int j = threadIdx.x; j < SELF_PAGES; j += blockDim.x) s.self_pt[(size_t)slot * SELF_PAGES + j] = r[REC_N + j];
     for (int j = threadIdx.x; j < CROSS_PAGES; j += blockDim.x)
         s.cross_pt[(size_t)slot * CROSS_PAGES + j] = r[REC_N + SELF_PAGES + j];
-    for (int j = threadIdx.x; j < s.n_prompt; j += blockDim.x)
-        s.prompt[(size_t)slot * s.n_prompt + j] = r[REC_N + SELF_PAGES + CROSS_PAGES + j];
+    const int *pr = r + REC_N + SELF_PAGES + CROSS_PAGES;   // length, then tokens
+    if (threadIdx.x == 0) s.plen[slot] = pr[0];
+    for (int j = threadIdx.x; j < pr[0]; j += blockDim.x) s.prompt[(size_t)slot * PROMPT_MAX + j] = pr[1 + j];
 }
 
 static long long ring_alloc(ct_engine *e, int n) { return e->ring.alloc(n); }
@@ -886,9 +890,11 @@ static int admit(ct_engine *e) {
     while (!e->pending.empty()) {
         Pending &p = e->pending.front();
         if (enc_rows + p.T_enc > e->enc_rows_cap) break;
-        if (live_rows + e->cfg.n_prompt > e->cfg.max_rows) break;
-        const int gen_max = p.forced > 0 ? p.forced : MAX_SEQ - e->cfg.n_prompt;
-        const int self_need = (std::min(MAX_SEQ, e->cfg.n_prompt + gen_max) + PR - 1) / PR;
+        const std::vector<int> &pr = p.prompt.empty() ? e->prompt : p.prompt;
+        const int plen = (int)pr.size();
+        if (live_rows + plen > e->cfg.max_rows) break;
+        const int gen_max = p.forced > 0 ? p.forced : MAX_SEQ - plen;
+        const int self_need = (std::min(MAX_SEQ, plen + gen_max) + PR - 1) / PR;
         const int cross_need = (p.T_enc + PR - 1) / PR;
         if ((int)e->free_pages.size() < self_need + cross_need) break;
         int slot = -1;
@@ -913,8 +919,9 @@ static int admit(ct_engine *e) {
         int *spt = rec + REC_N, *cpt = spt + SELF_PAGES;
         for (int j = 0; j < SELF_PAGES; ++j) spt[j] = j < self_need ? pages[j] : -1;
         for (int j = 0; j < CROSS_PAGES; ++j) cpt[j] = j < cross_need ? pages[self_need + j] : -1;
-        const std::vector<int> &pr = p.prompt.empty() ? e->prompt : p.prompt;
-        std::copy(pr.begin(), pr.end(), cpt + CROSS_PAGES);
+        cpt[CROSS_PAGES] = plen;
+        std::copy(pr.begin(), pr.end(), cpt + CROSS_PAGES + 1);
+        e->slot_plen[slot] = plen;
         // encoder rows of this utterance -> contiguous device rows, with their cross page offsets
         float *dst = e->enc_dev + (size_t)enc_rows * D;
         const size_t bytes = sizeof(float) * (size_t)p.T_enc * D;
@@ -929,7 +936,7 @@ static int admit(ct_engine *e) {
         for (int t = 0; t < p.T_enc; ++t)
             e->off_stage[enc_rows + t] = (long long)pages[self_need + t / PR] * PAGE_ELEMS + (long long)(t % PR) * D;
         enc_rows += p.T_enc;
-        live_rows += e->cfg.n_prompt;
+        live_rows += plen;
         ++e->n_live;
         e->pending.pop_front();
     }
@@ -1081,12 +1088,12 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
         for (int i = 0; i < e->cfg.max_slots; ++i) {
             if (!e->slot_live[i]) continue;
             if (e->slot_first[i]) {
-                rows += e->cfg.n_prompt;
-                for (int p = 0; p < e->cfg.n_prompt; ++p) self_b += (p + 1) * kv_row;
-                cross_b += (double)e->cfg.n_prompt * e->slot_tenc[i] * kv_row;
+                rows += e->slot_plen[i];
+                for (int p = 0; p < e->slot_plen[i]; ++p) self_b += (p + 1) * kv_row;
+                cross_b += (double)e->slot_plen[i] * e->slot_tenc[i] * kv_row;
             } else {
                 rows += 1;
-                self_b += (double)(e->cfg.n_prompt + e->slot_steps[i]) * kv_row;
+                self_b += (double)(e->slot_plen[i] + e->slot_steps[i]) * kv_row;
                 cross_b += (double)e->slot_tenc[i] * kv_row;
             }
         }
@@ -1226,8 +1233,11 @@ extern "C" int ct_engine_run(ct_engine *e) {
 // An utterance of T_enc encoder rows that could ever be admitted.
 static bool admissible(const ct_engine *e, int T_enc, int forced_len) {
     if (T_enc <= 0 || T_enc > CROSS_PAGES * PR || forced_len < 0 || T_enc > e->enc_rows_cap) return false;
-    const int gen_max = forced_len > 0 ? forced_len : MAX_SEQ - e->cfg.n_prompt;
-    const int need = (std::min(MAX_SEQ, e->cfg.n_prompt + gen_max) + PR - 1) / PR + (T_enc + PR - 1) / PR;
+    // with the prompt the utterance is submitted with
+    const int plen = e->next_prompt.empty() ? e->cfg.n_prompt : (int)e->next_prompt.size();
+    const int gen_max = forced_len > 0 ? forced_len : MAX_SEQ - plen;
+    if (plen + 1 > MAX_SEQ) return false;
+    const int need = (std::min(MAX_SEQ, plen + gen_max) + PR - 1) / PR + (T_enc + PR - 1) / PR;
     return need <= e->n_pages;
 }
 
@@ -1290,7 +1300,7 @@ extern "C" int ct_engine_profile_report(ct_engine *e, char *buf, int cap) {
 extern "C" int ct_engine_set_prompt(ct_engine *e, const int *prompt, int n_prompt) {
     if (!e) return CT_EINVAL;
     if (!prompt) { e->next_prompt.clear(); return CT_OK; }
-    if (n_prompt != e->cfg.n_prompt) return CT_EINVAL;
+    if (n_prompt <= 0 || n_prompt > PROMPT_MAX || n_prompt > e->cfg.max_rows) return CT_EINVAL;
     for (int j = 0; j < n_prompt; ++j)
         if (prompt[j] < 0 || prompt[j] >= V) return CT_EINVAL;
     e->next_prompt.assign(prompt, prompt + n_prompt);
@@ -1323,7 +1333,7 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
     void *ptrs[] = {e->blob, e->pool, e->cakv_w, e->cakv_b, e->h, e->q, e->attn_ws, e->logits, e->xa[0], e->xa[1],
                     e->xb[0], e->xb[1], e->xm[0], e->xm[1], e->lm[0], e->lm[1], e->next, e->enc_dev, e->enc_pl[0],
                     e->enc_pl[1], e->enc_off, e->ds.state, e->ds.tok, e->ds.pos, e->ds.gen, e->ds.forced,
-                    e->ds.tenc, e->ds.self_pt, e->ds.cross_pt, e->ds.out_tok, e->ds.prompt, e->ds.r_slot,
+                    e->ds.tenc, e->ds.self_pt, e->ds.cross_pt, e->ds.out_tok, e->ds.prompt, e->ds.plen, e->ds.r_slot,
                     e->ds.r_pos, e->ds.r_tok, e->ds.r_off, e->ds.q_row, e->ds.q_slot, e->ds.n_rows, e->ds.n_seqs,
                     e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.pid_self, e->ds.pid_cross, e->ds.rp_self,
                     e->ds.rp_cross, e->ds.n_wself, e->ds.n_wcross, e->rec_dev,
@@ -1374,7 +1384,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     if (cfg.max_rows <= 0) cfg.max_rows = 1024;
     if (cfg.n_prompt <= 0) cfg.n_prompt = 10;
     // attention page entries pack the row index in 10 bits
-    if (cfg.max_slots > 1024 || cfg.n_prompt > 64 || cfg.max_rows < cfg.n_prompt || cfg.max_rows > 1024)
+    if (cfg.max_slots > 1024 || cfg.n_prompt > PROMPT_MAX || cfg.max_rows < cfg.n_prompt || cfg.max_rows > 1024)
         return CT_EINVAL;
     static const int kPrompt[10] = {13764, 7, 4, 16, 62, 62, 5, 9, 11, 13};
     ct_engine *e = new ct_engine();
@@ -1439,7 +1449,8 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     s.max_slots = S; s.max_rows = R; s.n_prompt = cfg.n_prompt;
     if (dalloc(&s.state, S) || dalloc(&s.tok, S) || dalloc(&s.pos, S) || dalloc(&s.gen, S) || dalloc(&s.forced, S) ||
         dalloc(&s.tenc, S) || dalloc(&s.self_pt, (size_t)S * SELF_PAGES) || dalloc(&s.cross_pt, (size_t)S * CROSS_PAGES) ||
-        dalloc(&s.out_tok, (size_t)S * MAX_SEQ) || dalloc(&s.prompt, (size_t)S * cfg.n_prompt) || dalloc(&s.r_slot, R) ||
+        dalloc(&s.out_tok, (size_t)S * MAX_SEQ) || dalloc(&s.prompt, (size_t)S * PROMPT_MAX) ||
+        dalloc(&s.plen, S) || dalloc(&s.r_slot, R) ||
         dalloc(&s.r_pos, R) || dalloc(&s.r_tok, R) || dalloc(&s.r_off, R) || dalloc(&s.q_row, S) ||
         dalloc(&s.q_slot, S) || dalloc(&s.n_rows, 1) || dalloc(&s.n_seqs, 1) ||
         dalloc(&s.w_self, (size_t)R * SELF_PAGES) || dalloc(&s.w_cross, (size_t)R * CROSS_PAGES) ||
@@ -1454,9 +1465,11 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     EK(cudaMemset(s.state, 0, sizeof(int) * S));
     EK(cudaMemset(s.n_rows, 0, sizeof(int)));
     EK(cudaMemset(s.n_seqs, 0, sizeof(int)));
-    for (int i = 0; i < S; ++i)
-        EK(cudaMemcpy(s.prompt + (size_t)i * cfg.n_prompt, e->prompt.data(), sizeof(int) * cfg.n_prompt,
+    for (int i = 0; i < S; ++i) {
+        EK(cudaMemcpy(s.prompt + (size_t)i * PROMPT_MAX, e->prompt.data(), sizeof(int) * cfg.n_prompt,
                       cudaMemcpyHostToDevice));
+        EK(cudaMemcpy(s.plen + i, &cfg.n_prompt, sizeof(int), cudaMemcpyHostToDevice));
+    }
     EK(cudaHostAlloc(&e->h_done, sizeof(int) * S, cudaHostAllocMapped));
     memset(e->h_done, 0, sizeof(int) * S);
     EK(cudaHostGetDevicePointer(&s.done_map, e->h_done, 0));
@@ -1487,6 +1500,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     e->slot_pages.assign(S, {});
     e->slot_steps.assign(S, 0);
     e->slot_tenc.assign(S, 0);
+    e->slot_plen.assign(S, cfg.n_prompt);
     EK(cudaEventCreate(&e->eev0));
     EK(cudaEventCreate(&e->eev1));
     // packed encoder, when the blob carries the encoder weights

@@ -46,7 +46,7 @@ typedef struct {
     int max_rows;        /* packed query rows per step (default and maximum 1024) */
     int kv_pages;        /* pages in the pool; 0 = size for max_slots full-length sequences */
     int precision;       /* 1 = activations as bf16 hi+lo planes (near fp32, default), 0 = bf16 */
-    int n_prompt;        /* prompt length (default 10) */
+    int n_prompt;        /* default prompt length (default 10, at most 96) */
     const int *prompt;   /* prompt tokens (default: transcribe.c:1320-1330 with a synthetic language id) */
     int profile;         /* 1 = capture CUDA event nodes around the attention and FFN launches of
                             every layer (per-kernel-class device times in ct_engine_stats); the
@@ -68,11 +68,12 @@ int ct_engine_create(ct_engine **out, int device, const void *host_blob, size_t 
 void ct_engine_destroy(ct_engine *e);
 
 /* Prompt of the utterances submitted from now on (any of the submit calls):
- * n_prompt tokens, which must equal the engine's prompt length (10 for the
- * reference's prompt, transcribe.c:1320-1330, whose variants -- language,
- * punctuation, ITN, timestamps, diarisation -- change token values only).
- * prompt == NULL restores the engine's default.  Utterances with different
- * prompts decode together in one packed batch. */
+ * 1 to 96 tokens -- the reference's 10 (transcribe.c:1320-1330: language,
+ * punctuation, ITN, timestamp and diarisation variants), or its long-form
+ * prompts with up to 64 tokens carried over from the previous chunk inserted
+ * after the first two (transcribe.c:484-532).  prompt == NULL restores the
+ * engine's default.  Utterances with different prompts, of any lengths,
+ * decode together in one packed batch. */
 int ct_engine_set_prompt(ct_engine *e, const int *prompt, int n_prompt);
 
 /* Queue one utterance from its encoder output enc_h (host, fp32 [T_enc, DEC_D],

@@ -106,3 +106,27 @@ def audio(seconds: float, seed: int) -> np.ndarray:
 def mel_case():
     """Front-end fixture inputs: lengths with and without a partial last hop."""
     return [(seconds, 900 + i) for i, seconds in enumerate((1.0, 2.3456, 0.37))]
+
+
+def speech_like(seconds: float, seed: int) -> np.ndarray:
+    """Seeded 16 kHz signal of tone bursts (0.6-6 s) separated by near-silent
+    gaps (0.05-0.8 s, noise floor 1e-3): long-form chunking test input."""
+    rng = np.random.default_rng(seed)
+    n = int(round(seconds * 16000))
+    x = (rng.standard_normal(n) * 1e-3).astype(np.float64)
+    t = 0
+    while t < n:
+        burst = int(rng.uniform(0.6, 6.0) * 16000)
+        e = min(n, t + burst)
+        tt = np.arange(e - t) / 16000.0
+        f = rng.uniform(100.0, 3000.0)
+        x[t:e] += rng.uniform(0.05, 0.3) * np.sin(2 * np.pi * f * tt) + 0.02 * rng.standard_normal(e - t)
+        t = e + int(rng.uniform(0.05, 0.8) * 16000)
+    return x.astype(np.float32)
+
+
+def longform_case():
+    """(seconds, seed, silence_db, silence_dur, target_sec) of the long-form split fixtures."""
+    nan = float("nan")
+    return [(45.0, 1201, nan, 0.2, 20.0), (130.0, 1202, nan, 0.2, 20.0), (75.5, 1203, -40.0, 0.3, 12.0),
+            (61.0, 1204, nan, 0.5, 30.0)]

@@ -14,6 +14,8 @@ oracle/Makefile into oracle/_ref/) and records their outputs:
                              two sequences from seeded encoder outputs
   mel_ref.npz                the log-mel front-end (transcribe.c compute_mel) on
                              seeded 16 kHz signals
+  longform_ref.npz           the long-form split points (transcribe.c:484-507) of
+                             seeded signals with silences
 
 Inputs are regenerated from seeds by tests/golden/inputs.py; a checksum of
 each input is stored with the outputs so drift is detected.
@@ -95,6 +97,7 @@ def main(ref: str) -> None:
     np.savez_compressed(os.path.join(HERE, "full_decode_ref.npz"), tokens=tokens, n_tok=n_tok, argmax=am,
                         margin=mg, enc_checksum=np.float64(enc.astype(np.float64).sum()))
     make_mel_fixture()
+    make_longform_fixture()
     print("golden fixtures written to", HERE)
 
 
@@ -110,6 +113,21 @@ def make_mel_fixture() -> None:
         out[f"mel{k}"] = mel
         out[f"checksum{k}"] = np.float64(x.astype(np.float64).sum())
     np.savez_compressed(os.path.join(HERE, "mel_ref.npz"), **out)
+
+
+def make_longform_fixture() -> None:
+    """6. the reference's long-form split points (transcribe.c:484-507)."""
+    R = ctypes.CDLL(os.path.join(pyoracle.REF_DIR, "libref_mel.so"))
+    R.refsplit.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                           ctypes.c_void_p, ctypes.c_int]
+    out = {}
+    for k, (seconds, seed, db, dur, target) in enumerate(inputs.longform_case()):
+        x = inputs.speech_like(seconds, seed)
+        buf = np.zeros(4096, np.int32)
+        n = R.refsplit(x.ctypes.data, len(x), db, dur, target, buf.ctypes.data, len(buf))
+        out[f"splits{k}"] = buf[:n].copy()
+        out[f"checksum{k}"] = np.float64(x.astype(np.float64).sum())
+    np.savez_compressed(os.path.join(HERE, "longform_ref.npz"), **out)
 
 
 if __name__ == "__main__":
