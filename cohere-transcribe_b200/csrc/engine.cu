@@ -36,10 +36,9 @@ enum { S_FREE = 0, S_PREFILL = 1, S_DECODE = 2, S_DONE = 3 };
 constexpr int PROMPT_MAX = 96;                 // longest prompt (the reference's long-form prompts reach 2 + 64 + 16)
 constexpr int AW = 8;                          // consumer warps per attention CTA (one per head)
 constexpr int ANST = 3;                        // page stages in the attention pipeline
-constexpr int PMIN = 5;                        // minimum pages per attention CTA
-constexpr int SEG_MAX = 16;                    // segments a row can be split into across CTAs
-static_assert((SELF_PAGES + PMIN - 1) / PMIN + 1 <= SEG_MAX && (CROSS_PAGES + PMIN - 1) / PMIN + 1 <= SEG_MAX,
-              "a row of 64 pages over CTAs of >= PMIN pages must fit SEG_MAX segments");
+constexpr int GP = 2;                          // pages per attention group: a row's keys are cut into
+                                               // fixed groups of GP pages, whatever else is in the batch
+constexpr int SEG_MAX = (SELF_PAGES > CROSS_PAGES ? SELF_PAGES : CROSS_PAGES) / GP;   // groups per row
 
 struct DevState {
     int *state, *tok, *pos, *gen, *forced, *tenc;
@@ -55,10 +54,13 @@ struct DevState {
     int *n_rows, *n_seqs;        // device counts
     // attention page lists of the step (self, cross): one entry per (row, page):
     // meta = row | page-in-row << 10 | (valid keys - 1) << 16 | last-page << 20
+    //        | written-this-step << 21
     int *w_self, *w_cross;       // meta, [rows * 64]
     int *pid_self, *pid_cross;   // pool page id, [rows * 64]
     int *rp_self, *rp_cross;     // per row: first entry (prefix sum over rows), [rows + 1]
     int *n_wself, *n_wcross;     // entry counts
+    int *grp_self, *grp_cross;   // first entry of each group (rows in order, GP entries per group), [rows * 32 + 1]
+    int *n_grp;                  // [2]: group counts (self, cross)
     int max_slots, max_rows, n_prompt;
 };
 
@@ -97,10 +99,19 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     int nr = st == S_PREFILL ? s.plen[i] : st == S_DECODE ? 1 : 0;
     const int te = nr > 0 ? s.tenc[i] : 0;
     const int cross_np = (te + PR - 1) / PR;
-    int self_np = 0;   // self-attention pages over the slot's rows
-    if (st == S_PREFILL) for (int j = 0; j < nr; ++j) self_np += (j + 1 + PR - 1) / PR;
-    else if (st == S_DECODE) self_np = (s.pos[i] + 1 + PR - 1) / PR;
-    int total = 0, nseq = 0, n_ps = 0, n_pc = 0;
+    int self_np = 0, self_ng = 0;   // self-attention pages and groups over the slot's rows
+    if (st == S_PREFILL) {
+        for (int j = 0; j < nr; ++j) {
+            const int np = (j + 1 + PR - 1) / PR;
+            self_np += np;
+            self_ng += (np + GP - 1) / GP;
+        }
+    } else if (st == S_DECODE) {
+        self_np = (s.pos[i] + 1 + PR - 1) / PR;
+        self_ng = (self_np + GP - 1) / GP;
+    }
+    const int cross_ng = (cross_np + GP - 1) / GP;
+    int total = 0, nseq = 0, n_ps = 0, n_pc = 0, n_gs = 0, n_gc = 0;
     const int base = block_excl_scan(nr, tmp, &total);
     __syncthreads();
     const int sidx = block_excl_scan(nr > 0 ? 1 : 0, tmp2, &nseq);
@@ -108,6 +119,10 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     const int psb = block_excl_scan(self_np, tmp, &n_ps);
     __syncthreads();
     const int pcb = block_excl_scan(nr * cross_np, tmp2, &n_pc);
+    __syncthreads();
+    const int gsb = block_excl_scan(self_ng, tmp, &n_gs);
+    __syncthreads();
+    const int gcb = block_excl_scan(nr * cross_ng, tmp2, &n_gc);
     if (total > row_cap || nseq > seq_cap) {   // the host bounds admissions; never expected
         if (i == 0) { set_status(CT_STATUS_BAD_ARG); *s.n_rows = 0; *s.n_seqs = 0; }
         return;
@@ -123,18 +138,23 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     }
     if (nr > 0) { s.q_row[sidx] = base + nr - 1; s.q_slot[sidx] = i; }
     // attention page lists, rows in order: row r's entries are [rp[r], rp[r+1])
-    int gs = psb, gc = pcb;
+    int gs = psb, gc = pcb, qs = gsb, qc = gcb;
     for (int j = 0; j < nr; ++j) {
         const int r = base + j;
         const int L = (st == S_PREFILL ? j : s.pos[i]) + 1;      // causal: keys 0 .. position
         const int np = min((L + PR - 1) / PR, SELF_PAGES);
+        for (int k = 0; k < np; k += GP) s.grp_self[qs++] = gs + k;
+        for (int k = 0; k < cross_np; k += GP) s.grp_cross[qc++] = gc + k;
         s.rp_self[r] = gs;
         for (int q = 0; q < np; ++q, ++gs) {
             int pid = s.self_pt[i * SELF_PAGES + q];
             if (pid < 0) { set_status(CT_STATUS_BAD_ARG); pid = 0; }
             const int nv = min(PR, L - q * PR);
             s.pid_self[gs] = pid;
-            s.w_self[gs] = r | q << 10 | (nv - 1) << 16 | (q == np - 1) << 20;
+            // bit 21: written by this step's QKV projection (every page of a
+            // prefill row, the last page of a decode row)
+            const int fresh = st == S_PREFILL || q == np - 1;
+            s.w_self[gs] = r | q << 10 | (nv - 1) << 16 | (q == np - 1) << 20 | fresh << 21;
         }
         s.rp_cross[r] = gc;
         for (int q = 0; q < cross_np; ++q, ++gc) {
@@ -147,8 +167,12 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     }
     if (i == 0) {
         *s.n_rows = total; *s.n_seqs = nseq; *s.n_wself = n_ps; *s.n_wcross = n_pc;
+        s.n_grp[0] = n_gs;
+        s.n_grp[1] = n_gc;
         s.rp_self[total] = n_ps;
         s.rp_cross[total] = n_pc;
+        s.grp_self[n_gs] = n_ps;
+        s.grp_cross[n_gc] = n_pc;
     }
 }
 
@@ -251,12 +275,6 @@ struct AttnSmem {
     uint64_t full[ANST], empty[ANST];
 };
 
-// Attention CTA count actually used for `pages` entries (>= PMIN pages each).
-__device__ __forceinline__ int attn_ctas_used(int pages, int grid) { return max(1, min(grid, pages / PMIN)); }
-// The CTA whose entry range [g*P/G ...) holds entry g.
-__device__ __forceinline__ int attn_cta_of(int g, int P, int G) {
-    return (int)(((long long)(g + 1) * G - 1) / P);
-}
 
 __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s, const float *Q, const bf16 *pool,
                                                                       int layer, int cross, bf16 *hi, bf16 *lo,
@@ -269,20 +287,23 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
         fence_mbar_init();
     }
     __syncthreads();
-    // The page lists (row builder) and the K/V pages of earlier positions are
-    // written at least two kernels upstream, so they may be read before the
-    // dependency wait (this kernel's predecessor completes only after every
-    // kernel before it has).  Only Q and, for self-attention, a row's last
-    // page (which holds the row just projected) need the wait.
-    const int P = cross ? *s.n_wcross : *s.n_wself;
-    const int G = attn_ctas_used(P, gridDim.x);
+    // The page lists (row builder), the cross pages and the self pages of
+    // earlier steps are written at least two kernels upstream, so they may be
+    // read before the dependency wait (this kernel's predecessor completes only
+    // after every kernel before it has).  Q and the self pages written by this
+    // step's QKV projection (flagged by the row builder) need the wait.
+    // CTAs take equal shares of the groups (each GP pages of one row); a
+    // group's partial result depends only on the row, never on the split
+    const int NG = s.n_grp[cross ? 1 : 0];
+    const int G = max(1, min((int)gridDim.x, NG));
     const int b = blockIdx.x;
-    if (b >= G || P == 0) {
+    if (b >= G || NG == 0) {
         pdl_wait();
         pdl_trigger();
         return;
     }
-    const int g0 = (int)((long long)b * P / G), g1 = (int)((long long)(b + 1) * P / G);
+    const int *grp = cross ? s.grp_cross : s.grp_self;
+    const int g0 = grp[(int)((long long)b * NG / G)], g1 = grp[(int)((long long)(b + 1) * NG / G)];
     const int n = g1 - g0;
     const int *meta_l = (cross ? s.w_cross : s.w_self) + g0;
     const int *pid_l = (cross ? s.pid_cross : s.pid_self) + g0;
@@ -296,13 +317,13 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
         bool waited = false;
         for (int i0 = 0; i0 < n; i0 += 32) {
             const int pid_v = i0 + lane < n ? pid_l[i0 + lane] : 0;
-            const int last_v = (!cross && i0 + lane < n) ? (meta_l[i0 + lane] >> 20) & 1 : 0;
+            const int fresh_v = (!cross && i0 + lane < n) ? (meta_l[i0 + lane] >> 21) & 1 : 0;
             const int cnt = min(32, n - i0);
             for (int j = 0; j < cnt; ++j) {
                 const int pid = __shfl_sync(0xffffffffu, pid_v, j);
-                const int lastp = __shfl_sync(0xffffffffu, last_v, j);
+                const int fresh = __shfl_sync(0xffffffffu, fresh_v, j);
                 const int g = i0 + j, st = g % ANST;
-                if (!waited && (g >= ANST || lastp)) {
+                if (!waited && (g >= ANST || fresh)) {
                     pdl_wait();
                     pdl_trigger();
                     waited = true;
@@ -337,7 +358,7 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
         if ((g & 31) == 0) meta_v = g + lane < n ? meta_l[g + lane] : 0;
         const int meta = __shfl_sync(0xffffffffu, meta_v, g & 31);
         const int r = meta & 1023, pg = (meta >> 10) & 63, nv = ((meta >> 16) & 15) + 1, last = (meta >> 20) & 1;
-        if (g == 0 || pg == 0) {   // a row segment starts
+        if (pg % GP == 0) {   // a group starts (CTA ranges start at group starts)
             qv = *reinterpret_cast<const float4 *>(Q + (size_t)r * D + hh * DK + 4 * lane);
             rpa = rp[r];
             rpb = rp[r + 1];
@@ -417,10 +438,10 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[st]);
-        if (!(last || g == n - 1)) continue;
-        // ---- the row segment ends here
+        if (!(last || pg % GP == GP - 1)) continue;
+        // ---- the group ends here
         const size_t idx = (size_t)r * D + hh * DK + 4 * lane;
-        const int c0 = attn_cta_of(rpa, P, G), nseg = attn_cta_of(rpb - 1, P, G) - c0 + 1;
+        const int nseg = (rpb - rpa + GP - 1) / GP;   // the row's groups
         if (nseg == 1) {
             const float inv = 1.0f / l;
             store_planes(o0 * inv, hi, lo, idx);
@@ -429,7 +450,7 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
             store_planes(o3 * inv, hi, lo, idx + 3);
             continue;
         }
-        const int seg = b - c0;
+        const int seg = pg / GP;
         float *wp = ws + ((size_t)r * SEG_MAX + seg) * (2 * H + D);
         if (lane == 0) { wp[hh] = m; wp[H + hh] = l; }
         *reinterpret_cast<float4 *>(wp + 2 * H + hh * DK + 4 * lane) = make_float4(o0, o1, o2, o3);
@@ -1336,7 +1357,8 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
                     e->ds.tenc, e->ds.self_pt, e->ds.cross_pt, e->ds.out_tok, e->ds.prompt, e->ds.plen, e->ds.r_slot,
                     e->ds.r_pos, e->ds.r_tok, e->ds.r_off, e->ds.q_row, e->ds.q_slot, e->ds.n_rows, e->ds.n_seqs,
                     e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.pid_self, e->ds.pid_cross, e->ds.rp_self,
-                    e->ds.rp_cross, e->ds.n_wself, e->ds.n_wcross, e->rec_dev,
+                    e->ds.rp_cross, e->ds.n_grp, e->ds.grp_self, e->ds.grp_cross, e->ds.n_wself, e->ds.n_wcross,
+                    e->rec_dev,
                     e->mel_rows};
     for (void *p : ptrs) cudaFree(p);
     for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
@@ -1455,7 +1477,9 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         dalloc(&s.q_slot, S) || dalloc(&s.n_rows, 1) || dalloc(&s.n_seqs, 1) ||
         dalloc(&s.w_self, (size_t)R * SELF_PAGES) || dalloc(&s.w_cross, (size_t)R * CROSS_PAGES) ||
         dalloc(&s.pid_self, (size_t)R * SELF_PAGES) || dalloc(&s.pid_cross, (size_t)R * CROSS_PAGES) ||
-        dalloc(&s.rp_self, (size_t)R + 1) || dalloc(&s.rp_cross, (size_t)R + 1) || dalloc(&s.n_wself, 1) ||
+        dalloc(&s.rp_self, (size_t)R + 1) || dalloc(&s.rp_cross, (size_t)R + 1) || dalloc(&s.n_grp, 2) ||
+        dalloc(&s.grp_self, (size_t)R * SEG_MAX + 1) || dalloc(&s.grp_cross, (size_t)R * SEG_MAX + 1) ||
+        dalloc(&s.n_wself, 1) ||
         dalloc(&s.n_wcross, 1)) { ct_engine_destroy(e); return CT_ENOMEM; }
     {
         int sms = 148;
