@@ -61,7 +61,9 @@ struct DevState {
     int *n_wself, *n_wcross;     // entry counts
     int *grp_self, *grp_cross;   // first entry of each group (rows in order, GP entries per group), [rows * 32 + 1]
     int *n_grp;                  // [2]: group counts (self, cross)
+    int *crange;                 // [2][n_cta + 1]: first entry of each attention CTA's range (self, cross)
     int max_slots, max_rows, n_prompt;
+    int n_cta;                   // attention grid (one CTA per SM)
 };
 
 // ------------------------------------------------------------ kernels -----
@@ -125,6 +127,7 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     const int gcb = block_excl_scan(nr * cross_ng, tmp2, &n_gc);
     if (total > row_cap || nseq > seq_cap) {   // the host bounds admissions; never expected
         if (i == 0) { set_status(CT_STATUS_BAD_ARG); *s.n_rows = 0; *s.n_seqs = 0; }
+        if (i <= s.n_cta) { s.crange[i] = 0; s.crange[s.n_cta + 1 + i] = 0; }
         return;
     }
     for (int j = 0; j < nr; ++j) {
@@ -173,6 +176,18 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
         s.rp_cross[total] = n_pc;
         s.grp_self[n_gs] = n_ps;
         s.grp_cross[n_gc] = n_pc;
+    }
+    // attention CTA b takes groups [b*NG/G, (b+1)*NG/G) of G = min(n_cta, NG)
+    // equal shares; CTAs b >= G get an empty range
+    __syncthreads();
+    if (i <= s.n_cta) {
+        for (int c = 0; c < 2; ++c) {
+            const int NG = c ? n_gc : n_gs;
+            const int *grp = c ? s.grp_cross : s.grp_self;
+            const int G = max(1, min(s.n_cta, NG));
+            const int b = min(i, G);
+            s.crange[c * (s.n_cta + 1) + i] = grp[(int)((long long)b * NG / G)];
+        }
     }
 }
 
@@ -257,23 +272,26 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const int *n, const int *r
     }
 }
 
-// Paged attention over bf16 K/V with TMA-staged pages.  Work items are
-// (row, 64-key chunk) pairs listed by build_rows.  Row r of slot s attends, in
-// self mode, to positions [0, r_pos[r]] of the slot's self pages (the causal
-// prefix; a decode row is its last position), in cross mode to rows
-// [0, T_enc[s]) of its cross pages.  A persistent CTA walks its items; warp 8
-// streams every page the items touch -- the layer's 16 K rows (32 KB) and 16 V
-// rows (32 KB), contiguous in the pool -- into a ring of ANST shared-memory
-// stages with cp.async.bulk; warps 0..7 (head = warp) read their head's 256-byte
-// slices from shared memory, reduce the 16 scores of a page with a butterfly
-// over the lanes and keep an online softmax per head.  A row split over several
-// items leaves (m, l, o) per head in ws; the row's last item (atomic ticket)
-// merges them in chunk order.
+// Paged attention over bf16 K/V with bulk-copied pages.  The row builder lists
+// every (row, 16-key page) entry of the step, rows in order, and cuts each row
+// into fixed groups of GP pages; CTA b takes the entry range the builder wrote
+// for it (equal shares of the groups).  Row r of slot s attends, in self mode,
+// to positions [0, r_pos[r]] of the slot's self pages (the causal prefix; a
+// decode row is its last position), in cross mode to rows [0, T_enc[s]) of its
+// cross pages.  Warp AW streams each entry's K page (32 KB) and V page (32 KB),
+// contiguous in the pool, into a ring of ANST shared-memory stages with
+// cp.async.bulk; warps 0..AW-1 (head = warp) read their head's 256-byte slices,
+// reduce the 16 scores of a page with a butterfly over the lanes and keep an
+// online softmax per group.  A one-group row is written directly; otherwise
+// each group leaves (m, l, o) per head in ws and takes a per-(row, head)
+// ticket, and the warp holding the last ticket merges the row's groups in
+// order (lane c loads group c's (m, l); the o loads go four groups at a time).
 struct AttnSmem {
     bf16 kv[ANST][2][PR * D];                  // [stage][K,V][16 rows x 1024]
     float pbuf[AW][PR];                        // per consumer warp: the page's probabilities
     uint64_t full[ANST], empty[ANST];
 };
+static_assert(SEG_MAX <= 32, "a row's groups are merged one per lane");
 
 
 __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s, const float *Q, const bf16 *pool,
@@ -292,19 +310,18 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
     // read before the dependency wait (this kernel's predecessor completes only
     // after every kernel before it has).  Q and the self pages written by this
     // step's QKV projection (flagged by the row builder) need the wait.
-    // CTAs take equal shares of the groups (each GP pages of one row); a
-    // group's partial result depends only on the row, never on the split
-    const int NG = s.n_grp[cross ? 1 : 0];
-    const int G = max(1, min((int)gridDim.x, NG));
+    // CTAs take equal shares of the groups (ranges listed by the row builder
+    // for a grid of s.n_cta); a group's partial result depends only on the
+    // row, never on the split
+    const int *cr = s.crange + (cross ? s.n_cta + 1 : 0);
     const int b = blockIdx.x;
-    if (b >= G || NG == 0) {
+    const int g0 = b < s.n_cta ? cr[b] : 0, g1 = b < s.n_cta ? cr[b + 1] : 0;
+    const int n = g1 - g0;
+    if (n <= 0) {
         pdl_wait();
         pdl_trigger();
         return;
     }
-    const int *grp = cross ? s.grp_cross : s.grp_self;
-    const int g0 = grp[(int)((long long)b * NG / G)], g1 = grp[(int)((long long)(b + 1) * NG / G)];
-    const int n = g1 - g0;
     const int *meta_l = (cross ? s.w_cross : s.w_self) + g0;
     const int *pid_l = (cross ? s.pid_cross : s.pid_self) + g0;
     const int *rp = cross ? s.rp_cross : s.rp_self;
@@ -344,18 +361,19 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
         if (!waited) { pdl_wait(); pdl_trigger(); }
         return;
     }
+    // ---------------------------------------------------------- consumer warps
+    // the first 32 entries' metadata (row builder output) before the wait
+    int meta_v = lane < n ? meta_l[lane] : 0;
     pdl_wait();
     pdl_trigger();
-    // ---------------------------------------------------------- consumer warps
     const int hh = warp;
     const float scale = 1.0f / sqrtf((float)DK);
     float *pb = sm.pbuf[warp];
     float m = -INFINITY, l = 0.0f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
     float4 qv = make_float4(0.f, 0.f, 0.f, 0.f);
     int rpa = 0, rpb = 0;        // the current row's entry range
-    int meta_v = 0;
     for (int g = 0; g < n; ++g) {
-        if ((g & 31) == 0) meta_v = g + lane < n ? meta_l[g + lane] : 0;
+        if ((g & 31) == 0 && g > 0) meta_v = g + lane < n ? meta_l[g + lane] : 0;
         const int meta = __shfl_sync(0xffffffffu, meta_v, g & 31);
         const int r = meta & 1023, pg = (meta >> 10) & 63, nv = ((meta >> 16) & 15) + 1, last = (meta >> 20) & 1;
         if (pg % GP == 0) {   // a group starts (CTA ranges start at group starts)
@@ -463,16 +481,31 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
         if (__shfl_sync(0xffffffffu, tk, 0) != nseg - 1) continue;
         __threadfence();
         const float *wr = ws + (size_t)r * SEG_MAX * (2 * H + D);
-        float Mg = -INFINITY;
-        for (int cc = 0; cc < nseg; ++cc) Mg = fmaxf(Mg, wr[(size_t)cc * (2 * H + D) + hh]);
+        // merge in group order: lane c loads group c's (m, l); the o loads are
+        // issued four groups at a time, so the merge costs a few L2 round trips
+        const int cl = min(lane, nseg - 1);
+        const float mc = __ldcg(wr + (size_t)cl * (2 * H + D) + hh);
+        const float lc = __ldcg(wr + (size_t)cl * (2 * H + D) + H + hh);
+        const float Mg = warp_max(mc);                 // lanes >= nseg repeat group nseg - 1
+        const float fc = expf(mc - Mg);
         float Lg = 0.0f;
         float4 og = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int cc = 0; cc < nseg; ++cc) {
-            const float *pc = wr + (size_t)cc * (2 * H + D);
-            const float f = expf(pc[hh] - Mg);
-            Lg += pc[H + hh] * f;
-            const float4 v = *reinterpret_cast<const float4 *>(pc + 2 * H + hh * DK + 4 * lane);
-            og.x += v.x * f; og.y += v.y * f; og.z += v.z * f; og.w += v.w * f;
+        for (int c0 = 0; c0 < nseg; c0 += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int cc = min(c0 + t, nseg - 1);
+                v[t] = __ldcg(reinterpret_cast<const float4 *>(wr + (size_t)cc * (2 * H + D) + 2 * H + hh * DK) + lane);
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float f = __shfl_sync(0xffffffffu, fc, min(c0 + t, nseg - 1));
+                const float lt = __shfl_sync(0xffffffffu, lc, min(c0 + t, nseg - 1));
+                if (c0 + t < nseg) {
+                    Lg += lt * f;
+                    og.x += v[t].x * f; og.y += v[t].y * f; og.z += v[t].z * f; og.w += v[t].w * f;
+                }
+            }
         }
         const float inv = 1.0f / Lg;
         store_planes(og.x * inv, hi, lo, idx);
@@ -627,7 +660,7 @@ struct ct_engine {
     // step buffers
     float *h = nullptr, *q = nullptr, *attn_ws = nullptr, *logits = nullptr;
     int *tickets = nullptr;          // per (row, head) segment counters of the attention kernel
-    int attn_ctas = 296;             // persistent attention grid (2 per SM)
+    int attn_ctas = 148;             // attention grid (one CTA per SM; set from the device)
     bf16 *xa[2], *xb[2], *xm[2], *lm[2];
     int *next = nullptr;
     size_t attn_ws_floats = 0;
@@ -1358,7 +1391,7 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
                     e->ds.r_pos, e->ds.r_tok, e->ds.r_off, e->ds.q_row, e->ds.q_slot, e->ds.n_rows, e->ds.n_seqs,
                     e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.pid_self, e->ds.pid_cross, e->ds.rp_self,
                     e->ds.rp_cross, e->ds.n_grp, e->ds.grp_self, e->ds.grp_cross, e->ds.n_wself, e->ds.n_wcross,
-                    e->rec_dev,
+                    e->ds.crange, e->rec_dev,
                     e->mel_rows};
     for (void *p : ptrs) cudaFree(p);
     for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
@@ -1469,7 +1502,13 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     // device slot table
     DevState &s = e->ds;
     s.max_slots = S; s.max_rows = R; s.n_prompt = cfg.n_prompt;
-    if (dalloc(&s.state, S) || dalloc(&s.tok, S) || dalloc(&s.pos, S) || dalloc(&s.gen, S) || dalloc(&s.forced, S) ||
+    {
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        e->attn_ctas = std::min(sms, 1023);   // the row builder (1024 threads) fills the range table
+        s.n_cta = e->attn_ctas;
+    }
+    if (dalloc(&s.crange, 2 * ((size_t)s.n_cta + 1)) || dalloc(&s.state, S) || dalloc(&s.tok, S) || dalloc(&s.pos, S) || dalloc(&s.gen, S) || dalloc(&s.forced, S) ||
         dalloc(&s.tenc, S) || dalloc(&s.self_pt, (size_t)S * SELF_PAGES) || dalloc(&s.cross_pt, (size_t)S * CROSS_PAGES) ||
         dalloc(&s.out_tok, (size_t)S * MAX_SEQ) || dalloc(&s.prompt, (size_t)S * PROMPT_MAX) ||
         dalloc(&s.plen, S) || dalloc(&s.r_slot, R) ||
@@ -1481,11 +1520,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         dalloc(&s.grp_self, (size_t)R * SEG_MAX + 1) || dalloc(&s.grp_cross, (size_t)R * SEG_MAX + 1) ||
         dalloc(&s.n_wself, 1) ||
         dalloc(&s.n_wcross, 1)) { ct_engine_destroy(e); return CT_ENOMEM; }
-    {
-        int sms = 148;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-        e->attn_ctas = sms;
-    }
+    EK(cudaMemset(s.crange, 0, sizeof(int) * 2 * ((size_t)s.n_cta + 1)));
     EK(cudaMemset(s.state, 0, sizeof(int) * S));
     EK(cudaMemset(s.n_rows, 0, sizeof(int)));
     EK(cudaMemset(s.n_seqs, 0, sizeof(int)));
