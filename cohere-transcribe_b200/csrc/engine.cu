@@ -873,7 +873,7 @@ static void encode_step(ct_engine *e, int rows) {
     mark(e, "layernorm_final");
     GemmEpilogue lh;
     lh.bias = e->hdb; lh.Y = e->logits; lh.ldy = V; lh.T_dev = s.n_seqs;
-    lh.split = 4;   // 128 vocabulary tiles x 4 K-splits: enough CTAs to stream the 32 MB table
+    lh.split = 1;   // 128 vocabulary tiles, one wave: each CTA streams its 128 x 1024 slice of the table
     egemm(e, e->etw, V, D, e->lm[0], lm_lo, seqs, e->cfg.max_slots, lh, true);
     mark(e, "gemm_lm_head");
     launch_pdl(st, dim3(seqs), dim3(256), argmax_seq_kernel, s, (const float *)e->logits, e->next);

@@ -165,44 +165,133 @@ __device__ __forceinline__ void epilogue16(const GemmEpilogue &ep, int t0, int t
     }
 }
 
-// Epilogue of token t for the four features nf .. nf + 3 (split-K path), the
-// same load-before-store order as epilogue16.
-__device__ __forceinline__ void epilogue_f4(const GemmEpilogue &ep, int t, int nf, int N, const float (&v)[4]) {
-    if (ep.row_mask && !ep.row_mask[t]) return;
+// Epilogue of token t for the four features nf .. nf + 3 (split-K path), in
+// two halves: epilogue_f4_pre issues every load the stores need (row mask, KV
+// slot, page offset, the old values of an FMADD) and epilogue_f4_post stores,
+// so that a caller can issue the loads of several tokens, and its own partial
+// sums, before the first store.  Four consecutive outputs go out as one
+// vector store where they are contiguous and aligned.
+struct EpiPre {
+    float4 old;        // EPI_FMADD: the previous values
+    long long off;     // paged modes: row offset; EPI_KVCACHE: slot
+    bool keep;
+};
+
+__device__ __forceinline__ EpiPre epilogue_f4_pre(const GemmEpilogue &ep, int t, int nf, int N) {
+    EpiPre e;
+    e.old = make_float4(0.f, 0.f, 0.f, 0.f);
+    e.off = -1;
+    e.keep = !ep.row_mask || ep.row_mask[t];
     switch (ep.epi) {
     case EPI_FMADD: {
-        float old[4];
+        const float *y = ep.Y + (size_t)t * ep.ldy + nf;
+        if (nf + 3 < N && ((reinterpret_cast<uintptr_t>(y) & 15) == 0)) {
+            e.old = *reinterpret_cast<const float4 *>(y);
+        } else {
+            e.old.x = nf < N ? y[0] : 0.0f;
+            e.old.y = nf + 1 < N ? y[1] : 0.0f;
+            e.old.z = nf + 2 < N ? y[2] : 0.0f;
+            e.old.w = nf + 3 < N ? y[3] : 0.0f;
+        }
+        break;
+    }
+    case EPI_KVCACHE: e.off = ep.pos[t] - 1; break;
+    case EPI_QKV_PAGED:
+    case EPI_CAKV_PAGED: {
+        bool any_kv = false;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) old[i] = nf + i < N ? ep.Y[(size_t)t * ep.ldy + nf + i] : 0.0f;
+        for (int i = 0; i < 4; ++i) any_kv |= !(ep.epi == EPI_QKV_PAGED && nf + i < ep.qdim);
+        if (any_kv) e.off = ep.row_off[t];
+        break;
+    }
+    default: break;
+    }
+    return e;
+}
+
+__device__ __forceinline__ void store_bf16x4(bf16 *dst, const float (&a)[4]) {
+    __nv_bfloat162 h01 = __floats2bfloat162_rn(a[0], a[1]), h23 = __floats2bfloat162_rn(a[2], a[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t *>(&h01);
+    u.y = *reinterpret_cast<const uint32_t *>(&h23);
+    *reinterpret_cast<uint2 *>(dst) = u;
+}
+
+__device__ __forceinline__ void epilogue_f4_post(const GemmEpilogue &ep, int t, int nf, int N, const float (&v)[4],
+                                                 const EpiPre &e) {
+    if (!e.keep) return;
+    switch (ep.epi) {
+    case EPI_FMADD: {
+        float *y = ep.Y + (size_t)t * ep.ldy + nf;
+        const float o[4] = {e.old.x + ep.scale * v[0], e.old.y + ep.scale * v[1], e.old.z + ep.scale * v[2],
+                            e.old.w + ep.scale * v[3]};
+        if (nf + 3 < N && ((reinterpret_cast<uintptr_t>(y) & 15) == 0)) {
+            *reinterpret_cast<float4 *>(y) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            if (nf + i < N) ep.Y[(size_t)t * ep.ldy + nf + i] = old[i] + ep.scale * v[i];
+            for (int i = 0; i < 4; ++i)
+                if (nf + i < N) y[i] = o[i];
+        }
         break;
     }
     case EPI_KVCACHE: {
-        const int slot = ep.pos[t] - 1;
+        const long long slot = e.off;
         if (slot < 0 || slot >= ep.kv_stride) { set_status(CT_STATUS_BAD_ARG); break; }
 #pragma unroll
         for (int i = 0; i < 4; ++i)
             if (nf + i < N) ep.Y[((size_t)t * ep.kv_stride + slot) * ep.ldy + nf + i] = v[i];
         break;
     }
+    case EPI_BF16: {
+        float a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            a[i] = v[i];
+            if (ep.act == 1) a[i] = v[i] / (1.0f + expf(-v[i]));
+            else if (ep.act == 2) a[i] = v[i] > 0.0f ? v[i] : 0.0f;
+        }
+        const size_t idx = (size_t)t * ep.ldy + nf;
+        if (nf + 3 < N && (idx & 3) == 0 && ((reinterpret_cast<uintptr_t>(ep.Ybf) & 7) == 0) &&
+            (!ep.Ybf_lo || (reinterpret_cast<uintptr_t>(ep.Ybf_lo) & 7) == 0)) {
+            float hf[4], lf[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                hf[i] = __bfloat162float(__float2bfloat16_rn(a[i]));
+                lf[i] = a[i] - hf[i];
+            }
+            store_bf16x4(ep.Ybf + idx, hf);
+            if (ep.Ybf_lo) store_bf16x4(ep.Ybf_lo + idx, lf);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (nf + i < N) store_epilogue(ep, t, nf + i, v[i]);
+        }
+        break;
+    }
     case EPI_QKV_PAGED:
     case EPI_CAKV_PAGED: {
-        long long off = -1;
-        bool any_kv = false;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) any_kv |= !(ep.epi == EPI_QKV_PAGED && nf + i < ep.qdim);
-        if (any_kv) off = ep.row_off[t];
+        const long long off = e.off;
+        const bool qpart = ep.epi == EPI_QKV_PAGED && nf < ep.qdim;
+        const int n2 = ep.epi == EPI_QKV_PAGED ? nf - ep.qdim : nf;
+        if (!qpart && off >= 0 && nf + 3 < N && (nf + 3 >= ep.qdim || ep.epi != EPI_QKV_PAGED) &&
+            n2 % ep.kv_width + 3 < ep.kv_width) {
+            // four K/V values of one pool row
+            const int lk = ep.epi == EPI_QKV_PAGED ? ep.layer * 2 + n2 / ep.kv_width : n2 / ep.kv_width;
+            bf16 *dst = ep.kv_pool + off + (long long)lk * kPageRows * ep.kv_width + n2 % ep.kv_width;
+            if ((reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+                store_bf16x4(dst, v);
+                break;
+            }
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int n = nf + i;
             if (n >= N) continue;
             if (ep.epi == EPI_QKV_PAGED && n < ep.qdim) { ep.Y[(size_t)t * ep.ldy + n] = v[i]; continue; }
             if (off < 0) continue;
-            const int n2 = ep.epi == EPI_QKV_PAGED ? n - ep.qdim : n;
-            const int lk = ep.epi == EPI_QKV_PAGED ? ep.layer * 2 + n2 / ep.kv_width : n2 / ep.kv_width;
-            ep.kv_pool[off + (long long)lk * kPageRows * ep.kv_width + n2 % ep.kv_width] = __float2bfloat16_rn(v[i]);
+            const int m2 = ep.epi == EPI_QKV_PAGED ? n - ep.qdim : n;
+            const int lk = ep.epi == EPI_QKV_PAGED ? ep.layer * 2 + m2 / ep.kv_width : m2 / ep.kv_width;
+            ep.kv_pool[off + (long long)lk * kPageRows * ep.kv_width + m2 % ep.kv_width] = __float2bfloat16_rn(v[i]);
         }
         break;
     }
@@ -211,6 +300,48 @@ __device__ __forceinline__ void epilogue_f4(const GemmEpilogue &ep, int t, int n
         for (int i = 0; i < 4; ++i)
             if (nf + i < N) store_epilogue(ep, t, nf + i, v[i]);
         break;
+    }
+}
+
+// Split-K reduction of one CTA's token slice (CS = cluster size): epilogue
+// warp w2 handles tokens tb + w2, tb + w2 + 4, ... of the tile, P = min(2, 16 / CS)
+// of them per pass; lane owns features 4*lane .. 4*lane + 3.  Per pass every
+// load -- the epilogue's, then one 16-byte remote load per (token, CTA) -- is
+// issued before the first sum, and the sums run in CTA rank order.
+template <int CS>
+__device__ __forceinline__ void splitk_reduce(const KernelParams &p, int t0, int T_eff, int n0, int tb, int slice,
+                                              int w2, int lane, uint32_t base, const float (&b4)[4]) {
+    constexpr int P = CS >= 16 ? 1 : 2;
+    const int f0 = 4 * lane;
+    for (int j0 = w2; j0 < slice; j0 += 4 * P) {
+        if (t0 + tb + j0 >= T_eff) break;
+        bool on[P];
+        EpiPre pre[P];
+#pragma unroll
+        for (int pp = 0; pp < P; ++pp) {
+            const int j = j0 + 4 * pp;
+            on[pp] = j < slice && t0 + tb + j < T_eff;
+            if (on[pp]) pre[pp] = epilogue_f4_pre(p.ep, t0 + tb + j, n0 + f0, p.N);
+        }
+        float4 part[P][CS];
+#pragma unroll
+        for (int pp = 0; pp < P; ++pp) {
+            const uint32_t off = base + (uint32_t)(((tb + j0 + 4 * pp) * BM + f0) * 4);
+#pragma unroll
+            for (int r = 0; r < CS; ++r)
+                if (on[pp]) part[pp][r] = dsmem_ld4(dsmem_addr(off, (uint32_t)r));
+        }
+#pragma unroll
+        for (int pp = 0; pp < P; ++pp) {
+            if (!on[pp]) continue;
+            float4 sum = part[pp][0];
+#pragma unroll
+            for (int r = 1; r < CS; ++r) {
+                sum.x += part[pp][r].x; sum.y += part[pp][r].y; sum.z += part[pp][r].z; sum.w += part[pp][r].w;
+            }
+            const float vals[4] = {sum.x + b4[0], sum.y + b4[1], sum.z + b4[2], sum.w + b4[3]};
+            epilogue_f4_post(p.ep, t0 + tb + j0 + 4 * pp, n0 + f0, p.N, vals, pre[pp]);
+        }
     }
 }
 
@@ -356,32 +487,21 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
         }
         cluster_sync();
         if (epi_warp) {
-            // warp w2 = warp - 2 handles tokens tb + w2, tb + w2 + 4, ...; lane
-            // owns features 4*lane .. 4*lane+3 (one 16-byte remote load per CTA)
             const int cs = p.nsplit;
             const int slice = BN / cs;
             const int tb = (int)cluster_ctarank() * slice;
-            const int w2 = warp - 2;
             const uint32_t base = smem_u32(acc_s);
             const int f0 = 4 * lane;
             float b4[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
                 b4[i] = (n0 + f0 + i < p.N && p.ep.bias) ? bf2f(p.ep.bias[n0 + f0 + i]) : 0.0f;
-            for (int j = w2; j < slice; j += 4) {
-                const int t = t0 + tb + j;
-                if (t >= T_eff) break;
-                const uint32_t off = base + (uint32_t)(((tb + j) * BM + f0) * 4);
-                float4 part[16];
-#pragma unroll
-                for (int r = 0; r < 16; ++r)
-                    if (r < cs) part[r] = dsmem_ld4(dsmem_addr(off, (uint32_t)r));
-                float4 sum = part[0];
-#pragma unroll
-                for (int r = 1; r < 16; ++r)
-                    if (r < cs) { sum.x += part[r].x; sum.y += part[r].y; sum.z += part[r].z; sum.w += part[r].w; }
-                const float vals[4] = {sum.x + b4[0], sum.y + b4[1], sum.z + b4[2], sum.w + b4[3]};
-                epilogue_f4(p.ep, t, n0 + f0, p.N, vals);
+            switch (cs) {
+            case 2: splitk_reduce<2>(p, t0, T_eff, n0, tb, slice, warp - 2, lane, base, b4); break;
+            case 4: splitk_reduce<4>(p, t0, T_eff, n0, tb, slice, warp - 2, lane, base, b4); break;
+            case 8: splitk_reduce<8>(p, t0, T_eff, n0, tb, slice, warp - 2, lane, base, b4); break;
+            case 16: splitk_reduce<16>(p, t0, T_eff, n0, tb, slice, warp - 2, lane, base, b4); break;
+            default: if (lane == 0) set_status(CT_STATUS_BAD_ARG); break;   // the host picks powers of two
             }
         }
         cluster_sync();   // no CTA leaves while another still reads its shared memory
