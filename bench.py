@@ -10,7 +10,7 @@ is 64 * N utterances, dispatched to the ranks by queued audio seconds
 shard, with no collective on the data path (NCCL carries only the barrier and
 the max / sum of the timings).
 
-One bench step runs two legs over that batch:
+One bench step runs three legs (A and B over that batch, C alone):
 
   A  decode: submit the 64 utterances' encoder rows (host fp32, seeded
      N(0, 1)), decode all to their forced EOS, poll the tokens.
@@ -26,6 +26,10 @@ One bench step runs two legs over that batch:
      decodes them; poll the tokens.
        rtfx.value  audio seconds / device time (front-end + encoder + admission + decode)
        rtfx.e2e    audio seconds / wall time of the C-ABI calls from host samples
+  C  configuration 2 (batch 1): one 30 s utterance of seeded N(0, 1) log-mel
+     (ct_engine_submit_mel), encoded, admitted and decoded alone to EOS forced
+     at the 200th token; reported under "config2" (p50 step latency at batch 1,
+     decode tokens/s, RTFx), beside the configuration-3 headline.
 
 `--impl reference` times the reference's own CPU implementation (its
 backends/cpu/backend.c driven by its model.h, prebuilt under oracle/_ref/) on
@@ -55,6 +59,26 @@ METRIC = "decode tokens/s and RTFx per B200 (ragged continuous batch); p50 step 
 BATCH = 64
 CPU_CUT_S = 1.0        # seconds of log-mel per utterance in the CPU transcription sample
 CPU_CUT_TOKENS = 8     # generated-token cap per utterance in the CPU transcription sample
+CFG2_SECONDS, CFG2_TOKENS = 30.0, 200   # configuration 2: one 30 s utterance, EOS forced at the 200th token
+
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one ncu capture
+# per kernel class, on a smaller case than the bench's, with the units that
+# capture processed.  The bench scales it to its own launches by units, for the
+# classes whose traffic grows in proportion to them.
+NCU_TRAFFIC = {
+    # profiles/attn_paged_decode.md: one cross launch, 64 rows over 14,080
+    # encoder keys (57,671,680 algorithmic bytes): 59.354368 MB read + 0.41216 MB
+    # written.  Unit: algorithmic byte (the K/V rows the launch must read).
+    "paged cross-attention": {"bytes": 59.354368e6 + 0.41216e6, "units": 14080 * 4096.0,
+                              "unit": "algorithmic byte", "source": "profiles/attn_paged_decode.md"},
+    # profiles/gemm_persistent_encoder_ffn1.md: layer 0's FFN1 over 3,545 packed
+    # rows: 31.509504 MB read + 24.338688 MB written.  Unit: packed row.  The
+    # 13.1 MB of weights do not grow with the rows, so the scaled figure is an
+    # upper bound at larger batches.
+    "encoder FFN1 GEMM (tcgen05, persistent)": {"bytes": 31.509504e6 + 24.338688e6, "units": 3545.0,
+                                                "unit": "packed row",
+                                                "source": "profiles/gemm_persistent_encoder_ffn1.md"},
+}
 
 
 def workload(seed: int = 0, batch: int = BATCH, rank: int = 0, world: int = 1):
@@ -241,6 +265,22 @@ class ReferenceCPU:
         return self.n * CPU_CUT_S, secs
 
 
+def config2_summary(dev, wall_s, step_times, K):
+    """Configuration 2 (batch 1, one 30 s utterance, 200 tokens) from K timed runs:
+    device times from the engine's CUDA events (encoder, admission, steps),
+    wall time of the C-ABI calls from the host log-mel to the polled tokens."""
+    dec_ms = dev["admit_ms"] + dev["step_ms"]
+    all_ms = dec_ms + dev["enc_ms"]
+    return {"workload": f"config 2: one {CFG2_SECONDS:g} s utterance of seeded N(0, 1) log-mel, batch 1, "
+                        f"EOS forced at token {CFG2_TOKENS}",
+            "p50_step_ms": statistics.median(step_times) if step_times else None,
+            "steps_per_run": len(step_times) // K if K else None,
+            "decode_tokens_per_s": CFG2_TOKENS * K / (dec_ms / 1000.0) if dec_ms > 0 else None,
+            "rtfx": CFG2_SECONDS * K / (all_ms / 1000.0) if all_ms > 0 else None,
+            "e2e_rtfx": CFG2_SECONDS * K / wall_s if wall_s > 0 else None,
+            "encoder_ms": dev["enc_ms"] / K, "decode_ms": dec_ms / K, "wall_ms": 1000.0 * wall_s / K}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -255,8 +295,8 @@ def main():
     ap.add_argument("--max-len", type=int, default=0, help="cap the forced lengths (profiling cases)")
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel-class profiling pass")
     ap.add_argument("--no-pdl", action="store_true", help="launch step kernels without programmatic dependent launch")
-    ap.add_argument("--legs", default="AB", help="A = decode leg, B = transcription leg, E = encoder only "
-                    "(profiling cases)")
+    ap.add_argument("--legs", default="ABC", help="A = decode leg, B = transcription leg, C = configuration 2 "
+                    "(batch 1), E = encoder only (profiling cases)")
     ap.add_argument("--max-slots", type=int, default=256, help="engine slots (profiling cases)")
     args = ap.parse_args()
 
@@ -313,15 +353,21 @@ def main():
     legs = args.legs.upper()
     # the decode leg alone needs no encoder (a decoder-only blob keeps profiling cases small)
     with_enc = "B" in legs or "E" in legs
-    wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("enc", "dec") if with_enc else ("dec",))
+    with_c = "C" in legs
+    wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("enc", "dec") if (with_enc or with_c) else ("dec",))
     ws = W.weights_struct(wb)
     dev = local if world > 1 else 0
     enc_frames = int(case["T_mel"].sum())
+    # configuration 2: one 30 s utterance of seeded N(0, 1) log-mel [128, 3001]
+    mel2 = np.random.default_rng([0, 2]).standard_normal(
+        (128, importlib.import_module("cohere-transcribe_b200").t_mel_of_seconds(CFG2_SECONDS)), dtype=np.float32)
+    if with_c:
+        enc_frames = max(enc_frames, int(mel2.shape[1]))
 
     def make_engine(profile=0):
         return abi.Engine(lib, dev, wb, ws, max_slots=args.max_slots, max_rows=1024, precision=args.precision,
                           kv_pages=args.kv_pages, no_pdl=int(args.no_pdl), profile=profile,
-                          enc_max_utts=nb if with_enc else -1, enc_max_frames=enc_frames)
+                          enc_max_utts=nb if (with_enc or with_c) else -1, enc_max_frames=enc_frames)
 
     eng = make_engine()
     # host inputs: encoder rows (leg A) and log-mel (leg B), fp32 host memory
@@ -350,16 +396,28 @@ def main():
         assert len(out) == nb
         return out
 
+    def leg_c(e, step_times):
+        e.step_times()                       # drop earlier steps' times
+        e.submit_mel(0, mel2, CFG2_TOKENS)
+        e.run()
+        step_times.extend(e.step_times().tolist())
+        out = e.poll()
+        assert len(out) == 1
+        return out
+
     for _ in range(args.warmup):
         if "A" in legs:
             leg_a(eng, [])
         if with_enc:
             leg_b(eng)
+        if with_c:
+            leg_c(eng, [])
     if eng.status() != 0:
         raise RuntimeError("device status set during warm-up")
-    step_times = []
-    wall_a = wall_b = 0.0
+    step_times, step_times_c = [], []
+    wall_a = wall_b = wall_c = 0.0
     dev_a = dev_b = enc_ms = 0.0
+    dev_c = {"enc_ms": 0.0, "admit_ms": 0.0, "step_ms": 0.0}
     barrier(world)
     s_start = eng.stats()
     with ClockSampler(local) as clk:
@@ -380,6 +438,14 @@ def main():
                 dev_b += (s1["step_ms"] - s0["step_ms"]) + (s1["admit_ms"] - s0["admit_ms"]) + \
                     (s1["enc_ms"] - s0["enc_ms"])
                 enc_ms += s1["enc_ms"] - s0["enc_ms"]
+            if with_c:
+                s0 = eng.stats()
+                t0 = time.perf_counter()
+                leg_c(eng, step_times_c)
+                wall_c += time.perf_counter() - t0
+                s1 = eng.stats()
+                for k in dev_c:
+                    dev_c[k] += s1[k] - s0[k]
     barrier(world)
     s_end = eng.stats()
     status = eng.status()
@@ -445,13 +511,19 @@ def main():
     if rooflines:
         dom = max(rooflines, key=lambda k: rooflines[k]["ms_per_step"])
         r = rooflines[dom]
-        traffic = None
-        tpath = os.path.join(REPO, "profiles", "ncu_traffic.json")
-        if os.path.exists(tpath):
-            with open(tpath) as fh:
-                traffic = json.load(fh).get(dom)
+        traffic, traffic_note = None, None
+        if dom in NCU_TRAFFIC:
+            t = NCU_TRAFFIC[dom]
+            if t["unit"] == "packed row":
+                units = float(sum(int(x) for x in case["T_enc"]))
+            else:
+                units = r["algorithmic_bytes_per_launch"]
+            traffic = t["bytes"] / t["units"] * units
+            traffic_note = (f"DRAM read + write bytes per launch: the ncu capture in {t['source']} "
+                            f"({t['bytes'] / 1e6:.2f} MB over {t['units']:.0f} {t['unit']}s), scaled to this "
+                            f"launch's {units:.0f} {t['unit']}s")
         roof = {"kernel": dom, "bound": r["bound"], "achieved": r["achieved"], "peak": r["peak"], "unit": r["unit"],
-                "frac": r["frac"], "peak_kind": pk_kind, "traffic": traffic,
+                "frac": r["frac"], "peak_kind": pk_kind, "traffic": traffic, "traffic_note": traffic_note,
                 "avg_launch_ms": r["avg_launch_ms"],
                 "measured": "CUDA events between launch groups in one profiled bench step"}
 
@@ -464,6 +536,7 @@ def main():
                      "audio_s_per_step": audio_s * world, "encoder_ms_per_step": enc_ms / K,
                      "h2d_bytes_per_step": h2d_b, "d2h_bytes_per_step": d2h},
             "p50_step_ms": statistics.median(step_times) if step_times else None,
+            "config2": config2_summary(dev_c, wall_c, step_times_c, K) if with_c else None,
             "gpu_launches": launches, "roofline": roof, "rooflines": rooflines,
             "profiled_step_breakdown": breakdown, "clocks": clk.summary(), "device_status": status,
             "precision": "bf16 weights, activations as bf16 hi+lo planes, fp32 accumulate" if args.precision else
