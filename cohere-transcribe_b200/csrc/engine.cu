@@ -1310,7 +1310,7 @@ extern "C" int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const fl
 }
 
 extern "C" int ct_engine_poll(ct_engine *e, ct_result *out, int max, int *tokens, int tok_stride) {
-    if (!e || (max > 0 && !out)) return CT_EINVAL;
+    if (!e || max < 0 || (max > 0 && !out) || (tokens && tok_stride <= 0)) return CT_EINVAL;
     int n = 0;
     while (n < max && !e->results.empty()) {
         out[n] = e->results.front();
@@ -1362,7 +1362,7 @@ extern "C" int ct_engine_set_prompt(ct_engine *e, const int *prompt, int n_promp
 }
 
 extern "C" int ct_engine_step_times(ct_engine *e, float *out, int max) {
-    if (!e || (!out && max > 0)) return CT_EINVAL;
+    if (!e || max < 0 || (!out && max > 0)) return CT_EINVAL;
     const int n = std::min<int>(max, (int)e->step_log.size());
     for (int i = 0; i < n; ++i) out[i] = e->step_log[i];
     e->step_log.clear();
@@ -1442,10 +1442,13 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     if (cfg.max_slots > 1024 || cfg.n_prompt > PROMPT_MAX || cfg.max_rows < cfg.n_prompt || cfg.max_rows > 1024)
         return CT_EINVAL;
     static const int kPrompt[10] = {13764, 7, 4, 16, 62, 62, 5, 9, 11, 13};
+    if (!cfg.prompt && cfg.n_prompt != 10) return CT_EINVAL;   // the default prompt has 10 tokens
+    if (cfg.prompt)
+        for (int j = 0; j < cfg.n_prompt; ++j)
+            if (cfg.prompt[j] < 0 || cfg.prompt[j] >= V) return CT_EINVAL;
     ct_engine *e = new ct_engine();
     e->cfg = cfg;
     e->prompt.assign(cfg.prompt ? cfg.prompt : kPrompt, (cfg.prompt ? cfg.prompt : kPrompt) + cfg.n_prompt);
-    if (!cfg.prompt && cfg.n_prompt != 10) { delete e; return CT_EINVAL; }
     e->device = device;
     if (cudaSetDevice(device) != cudaSuccess) { delete e; return CT_EDEVICE; }
     EK(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
