@@ -88,6 +88,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads of them (tcgen05.mma operands, bulk copies out).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 // Bounded wait; returns false (and records `code`) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code) {
     if (mbar_try_wait(bar, parity)) return true;

@@ -659,6 +659,7 @@ struct ct_engine {
     int *h_done = nullptr;   // host view of done_map
     // step buffers
     float *h = nullptr, *q = nullptr, *attn_ws = nullptr, *logits = nullptr;
+    float2 *ln_stats = nullptr;   // per row and 128-feature tile of h: (mean, M2), written by the residual GEMMs
     int *tickets = nullptr;          // per (row, head) segment counters of the attention kernel
     int attn_ctas = 148;             // attention grid (one CTA per SM; set from the device)
     bf16 *xa[2], *xb[2], *xm[2], *lm[2];
@@ -824,24 +825,32 @@ static void encode_step(ct_engine *e, int rows) {
     launch_pdl(st, dim3(rows), dim3(256), embed_rows_kernel, s, e->etw, e->epw, e->elnw, e->elnb, e->L[0].sa_lnw,
                e->L[0].sa_lnb, e->h, e->xa[0], xa_lo);
     mark(e, "embed_ln");
+    // The pre-LayerNorms of the QKV (layers 1..7), cross-query and FFN1
+    // projections run inside those GEMMs: each residual GEMM (EPI_FMADD) leaves
+    // per-row (mean, M2) partials of its 128-feature tiles in ln_stats, and the
+    // next GEMM normalises its own K slice of h into shared memory.  Layer 0's
+    // self-attention LayerNorm is fused into the embedding, which writes planes.
+    auto ln_input = [&](GemmEpilogue &g, const bf16 *w, const bf16 *b) {
+        g.ln_x = e->h; g.ln_stats = e->ln_stats; g.ln_g = w; g.ln_b = b;
+    };
     for (int l = 0; l < NL; ++l) {
         const auto &Ly = e->L[l];
         GemmEpilogue qkv;
         qkv.epi = EPI_QKV_PAGED; qkv.bias = Ly.qkv_b; qkv.Y = e->q; qkv.ldy = D; qkv.qdim = D;
         qkv.kv_pool = e->pool; qkv.row_off = s.r_off; qkv.layer = l; qkv.T_dev = s.n_rows;
+        if (l > 0) ln_input(qkv, Ly.sa_lnw, Ly.sa_lnb);
         egemm(e, Ly.qkv_w, 3 * D, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, qkv, true);
         mark(e, "gemm_qkv");
         launch_attn(st, e->attn_ctas, s, e->q, e->pool, l, 0, e->xb[0], xb_lo, e->attn_ws, e->tickets);
         mark(e, "attn_self");
         GemmEpilogue o;
         o.epi = EPI_FMADD; o.scale = 1.0f; o.bias = Ly.sa_ob; o.Y = e->h; o.ldy = D; o.T_dev = s.n_rows;
+        o.stats_out = e->ln_stats;
         egemm(e, Ly.sa_ow, D, D, e->xb[0], xb_lo, rows, e->cfg.max_rows, o, true);
         mark(e, "gemm_o");
-        launch_pdl(st, dim3(rows), dim3(256), ln_rows_kernel, (const int *)s.n_rows, (const int *)nullptr, (const float *)e->h,
-                   Ly.ca_lnw, Ly.ca_lnb, e->xa[0], xa_lo);
-        mark(e, "layernorm");
         GemmEpilogue qc;
         qc.bias = Ly.ca_qb; qc.Y = e->q; qc.ldy = D; qc.T_dev = s.n_rows;
+        ln_input(qc, Ly.ca_lnw, Ly.ca_lnb);
         egemm(e, Ly.ca_qw, D, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, qc, true);
         mark(e, "gemm_q_cross");
         launch_attn(st, e->attn_ctas, s, e->q, e->pool, l, 1, e->xb[0], xb_lo, e->attn_ws, e->tickets);
@@ -850,23 +859,16 @@ static void encode_step(ct_engine *e, int rows) {
         oc.bias = Ly.ca_ob;
         egemm(e, Ly.ca_ow, D, D, e->xb[0], xb_lo, rows, e->cfg.max_rows, oc, true);
         mark(e, "gemm_o");
-        launch_pdl(st, dim3(rows), dim3(256), ln_rows_kernel, (const int *)s.n_rows, (const int *)nullptr, (const float *)e->h,
-                   Ly.ffn_lnw, Ly.ffn_lnb, e->xa[0], xa_lo);
-        mark(e, "layernorm");
         GemmEpilogue f1;
         f1.epi = EPI_BF16; f1.act = 2; f1.bias = Ly.ffn_b1; f1.Ybf = e->xm[0]; f1.Ybf_lo = xm_lo; f1.ldy = FF;
         f1.T_dev = s.n_rows;
+        ln_input(f1, Ly.ffn_lnw, Ly.ffn_lnb);
         egemm(e, Ly.ffn_w1, FF, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, f1, true);
         mark(e, "gemm_ffn1");
         GemmEpilogue f2 = o;
         f2.bias = Ly.ffn_b2;
         egemm(e, Ly.ffn_w2, D, FF, e->xm[0], xm_lo, rows, e->cfg.max_rows, f2, true);
         mark(e, "gemm_ffn2");
-        if (l + 1 < NL) {   // the next layer's self-attention LayerNorm (layer 0's is fused into the embedding)
-            launch_pdl(st, dim3(rows), dim3(256), ln_rows_kernel, (const int *)s.n_rows, (const int *)nullptr,
-                       (const float *)e->h, e->L[l + 1].sa_lnw, e->L[l + 1].sa_lnb, e->xa[0], xa_lo);
-            mark(e, "layernorm");
-        }
     }
     launch_pdl(st, dim3(seqs), dim3(256), ln_rows_kernel, (const int *)s.n_seqs, (const int *)s.q_row, (const float *)e->h,
                e->dlnw, e->dlnb, e->lm[0], lm_lo);
@@ -1392,7 +1394,7 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
                     e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.pid_self, e->ds.pid_cross, e->ds.rp_self,
                     e->ds.rp_cross, e->ds.n_grp, e->ds.grp_self, e->ds.grp_cross, e->ds.n_wself, e->ds.n_wcross,
                     e->ds.crange, e->rec_dev,
-                    e->mel_rows};
+                    e->mel_rows, e->ln_stats};
     for (void *p : ptrs) cudaFree(p);
     for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
     cudaFreeHost(e->h_done);
@@ -1473,12 +1475,13 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     for (int l = 0; l < NL; ++l) {
         const DLayer &d = w->dec[l];
         auto &Ly = e->L[l];
-        Ly.sa_lnw = ew(e, d.sa_lnw); Ly.sa_lnb = ew(e, d.sa_lnb); Ly.sa_ob = ew(e, d.sa_ob);
+        // LayerNorm vectors are read 16 bytes at a time by the LayerNorm-input GEMMs
+        Ly.sa_lnw = ew_matrix(e, d.sa_lnw, D); Ly.sa_lnb = ew_matrix(e, d.sa_lnb, D); Ly.sa_ob = ew(e, d.sa_ob);
         Ly.sa_ow = ew_matrix(e, d.sa_ow, (size_t)D * D);
-        Ly.ca_lnw = ew(e, d.ca_lnw); Ly.ca_lnb = ew(e, d.ca_lnb); Ly.ca_qb = ew(e, d.ca_qb);
+        Ly.ca_lnw = ew_matrix(e, d.ca_lnw, D); Ly.ca_lnb = ew_matrix(e, d.ca_lnb, D); Ly.ca_qb = ew(e, d.ca_qb);
         Ly.ca_qw = ew_matrix(e, d.ca_qw, (size_t)D * D);
         Ly.ca_ow = ew_matrix(e, d.ca_ow, (size_t)D * D); Ly.ca_ob = ew(e, d.ca_ob);
-        Ly.ffn_lnw = ew(e, d.ffn_lnw); Ly.ffn_lnb = ew(e, d.ffn_lnb);
+        Ly.ffn_lnw = ew_matrix(e, d.ffn_lnw, D); Ly.ffn_lnb = ew_matrix(e, d.ffn_lnb, D);
         Ly.ffn_w1 = ew_matrix(e, d.ffn_w1, (size_t)FF * D);
         Ly.ffn_b1 = ew(e, d.ffn_b1); Ly.ffn_w2 = ew_matrix(e, d.ffn_w2, (size_t)D * FF); Ly.ffn_b2 = ew(e, d.ffn_b2);
         const bf16 *parts[3] = {ew(e, d.sa_qw), ew(e, d.sa_kw), ew(e, d.sa_vw)};
@@ -1539,7 +1542,9 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     if (dalloc(&e->h, (size_t)R * D) || dalloc(&e->q, (size_t)R * D) || dalloc(&e->xa[0], (size_t)R * D) ||
         dalloc(&e->xa[1], (size_t)R * D) || dalloc(&e->xb[0], (size_t)R * D) || dalloc(&e->xb[1], (size_t)R * D) ||
         dalloc(&e->xm[0], (size_t)R * FF) || dalloc(&e->xm[1], (size_t)R * FF) || dalloc(&e->lm[0], (size_t)S * D) ||
-        dalloc(&e->lm[1], (size_t)S * D) || dalloc(&e->logits, (size_t)S * V) || dalloc(&e->next, S)) { ct_engine_destroy(e); return CT_ENOMEM; }
+        dalloc(&e->lm[1], (size_t)S * D) || dalloc(&e->logits, (size_t)S * V) || dalloc(&e->next, S) ||
+        dalloc(&e->ln_stats, (size_t)R * (D / 128))) { ct_engine_destroy(e); return CT_ENOMEM; }
+    EK(cudaMemset(e->ln_stats, 0, sizeof(float2) * (size_t)R * (D / 128)));
     e->attn_ws_floats = (size_t)R * SEG_MAX * (2 * H + D);
     if (dalloc(&e->attn_ws, e->attn_ws_floats) || dalloc(&e->tickets, (size_t)R * H)) {
         ct_engine_destroy(e);

@@ -217,14 +217,17 @@ __device__ __forceinline__ void store_bf16x4(bf16 *dst, const float (&a)[4]) {
     *reinterpret_cast<uint2 *>(dst) = u;
 }
 
+// EPI_FMADD leaves the four stored values in `stored` (for the row statistics).
 __device__ __forceinline__ void epilogue_f4_post(const GemmEpilogue &ep, int t, int nf, int N, const float (&v)[4],
-                                                 const EpiPre &e) {
+                                                 const EpiPre &e, float (&stored)[4]) {
     if (!e.keep) return;
     switch (ep.epi) {
     case EPI_FMADD: {
         float *y = ep.Y + (size_t)t * ep.ldy + nf;
         const float o[4] = {e.old.x + ep.scale * v[0], e.old.y + ep.scale * v[1], e.old.z + ep.scale * v[2],
                             e.old.w + ep.scale * v[3]};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) stored[i] = o[i];
         if (nf + 3 < N && ((reinterpret_cast<uintptr_t>(y) & 15) == 0)) {
             *reinterpret_cast<float4 *>(y) = make_float4(o[0], o[1], o[2], o[3]);
         } else {
@@ -340,7 +343,96 @@ __device__ __forceinline__ void splitk_reduce(const KernelParams &p, int t0, int
                 sum.x += part[pp][r].x; sum.y += part[pp][r].y; sum.z += part[pp][r].z; sum.w += part[pp][r].w;
             }
             const float vals[4] = {sum.x + b4[0], sum.y + b4[1], sum.z + b4[2], sum.w + b4[3]};
-            epilogue_f4_post(p.ep, t0 + tb + j0 + 4 * pp, n0 + f0, p.N, vals, pre[pp]);
+            float o[4] = {0.f, 0.f, 0.f, 0.f};
+            const int t = t0 + tb + j0 + 4 * pp;
+            epilogue_f4_post(p.ep, t, n0 + f0, p.N, vals, pre[pp], o);
+            if (p.ep.stats_out) {
+                // (mean, M2) of the tile's 128 new values of row t: the warp holds
+                // all of them (four per lane); the host allows this only for
+                // EPI_FMADD without a row mask and N a multiple of 128
+                const float m = warp_sum((o[0] + o[1]) + (o[2] + o[3])) * (1.0f / 128.0f);
+                const float d0 = o[0] - m, d1 = o[1] - m, d2 = o[2] - m, d3 = o[3] - m;
+                const float q = warp_sum((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3));
+                if (lane == 0) p.ep.stats_out[(size_t)t * (p.N / BM) + blockIdx.x] = make_float2(m, q);
+            }
+        }
+    }
+}
+
+// LayerNorm-input mode: the four epilogue warps (et = 0..127) form the CTA's
+// activation tiles, LN(x[t]) for t in [t0, t0 + BN) over k-blocks kb0 ..
+// kb0 + nkb - 1, as bf16 hi (and lo) planes in the layout a 128-byte-swizzled
+// TMA load writes: row r of a [BN x 64] tile at r * 128 bytes, its 16-byte
+// chunk c at position c ^ (r & 7).  Tiles sit at xs + (kb * planes + plane) *
+// BN * 128.  The row's mean and variance merge the eight (mean, M2) partials
+// of its 128-feature tiles in tile order (equal counts of 128); rows past the
+// device row count are zero.
+template <int BN, bool TWO>
+__device__ __forceinline__ void ln_fill(const GemmEpilogue &ep, uint8_t *xs, int t0, int T_eff, int kb0, int nkb,
+                                        int et) {
+    constexpr int K = 1024;
+    constexpr int TPR = BN >= 128 ? 1 : 128 / BN;   // threads per row
+    constexpr int CPT = 8 / TPR;                    // 16-byte chunks per thread and k-block
+    constexpr int RSTEP = 128 / TPR;                // rows per pass of the 128 threads
+    constexpr uint32_t TILE = BN * 128;
+    for (int r = et / TPR; r < BN; r += RSTEP) {
+        const int t = t0 + r;
+        const int c0 = (et % TPR) * CPT;
+        const bool valid = t < T_eff;
+        float mu = 0.0f, rs = 0.0f;
+        if (valid) {
+            const float4 *sp = reinterpret_cast<const float4 *>(ep.ln_stats + (size_t)t * (K / 128));
+            const float4 a0 = sp[0], a1 = sp[1], a2 = sp[2], a3 = sp[3];
+            const float m[8] = {a0.x, a0.z, a1.x, a1.z, a2.x, a2.z, a3.x, a3.z};
+            const float q[8] = {a0.y, a0.w, a1.y, a1.w, a2.y, a2.w, a3.y, a3.w};
+            float ms = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ms += m[j];
+            mu = ms * 0.125f;
+            float m2 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float d = m[j] - mu;
+                m2 += q[j] + 128.0f * d * d;
+            }
+            rs = 1.0f / sqrtf(m2 * (1.0f / K) + 1e-5f);
+        }
+        for (int kb = 0; kb < nkb; ++kb) {
+            uint8_t *tile = xs + (size_t)kb * (TWO ? 2 : 1) * TILE;
+#pragma unroll
+            for (int cc = 0; cc < CPT; ++cc) {
+                const int c = c0 + cc;
+                uint4 hv = make_uint4(0u, 0u, 0u, 0u), lv = make_uint4(0u, 0u, 0u, 0u);
+                if (valid) {
+                    const int k = (kb0 + kb) * BK + c * 8;
+                    const float4 x0 = *reinterpret_cast<const float4 *>(ep.ln_x + (size_t)t * K + k);
+                    const float4 x1 = *reinterpret_cast<const float4 *>(ep.ln_x + (size_t)t * K + k + 4);
+                    const uint4 g = *reinterpret_cast<const uint4 *>(ep.ln_g + k);
+                    const uint4 b = *reinterpret_cast<const uint4 *>(ep.ln_b + k);
+                    const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, bw[4] = {b.x, b.y, b.z, b.w};
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        float v[2];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const float gg = __uint_as_float(((gw[i] >> (16 * h)) & 0xFFFFu) << 16);
+                            const float bb = __uint_as_float(((bw[i] >> (16 * h)) & 0xFFFFu) << 16);
+                            v[h] = (x[2 * i + h] - mu) * rs * gg + bb;
+                        }
+                        const __nv_bfloat162 hh = __floats2bfloat162_rn(v[0], v[1]);
+                        const __nv_bfloat162 ll = __floats2bfloat162_rn(v[0] - __low2float(hh), v[1] - __high2float(hh));
+                        hw[i] = *reinterpret_cast<const uint32_t *>(&hh);
+                        lw[i] = *reinterpret_cast<const uint32_t *>(&ll);
+                    }
+                    hv = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    lv = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                }
+                const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
+                *reinterpret_cast<uint4 *>(tile + off) = hv;
+                if (TWO) *reinterpret_cast<uint4 *>(tile + TILE + off) = lv;
+            }
         }
     }
 }
@@ -358,10 +450,16 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int stages = p.stages;
+    // LayerNorm-input mode: stages hold only weight tiles; the activation
+    // tiles of all this CTA's k-blocks follow them (see ln_fill)
+    const bool lnx = p.ep.ln_x != nullptr;
+    const uint32_t stage_bytes = lnx ? A_BYTES : STAGE_BYTES;
+    uint8_t *xs = smem + (size_t)stages * stage_bytes;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.bar_off);
     uint64_t *empty = full + stages;
     uint64_t *accb = empty + stages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accb + 1);
+    uint64_t *xfull = accb + 1;   // LayerNorm-input mode: the 128 epilogue threads filled xs
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accb + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BM, t0 = blockIdx.y * BN, z = blockIdx.z;
@@ -377,10 +475,13 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_init(accb, 1);
+        mbar_init(xfull, 128);
         fence_mbar_init();
         prefetch_tmap(&tmW);
-        prefetch_tmap(&tmXh);
-        if (TWO) prefetch_tmap(&tmXl);
+        if (!lnx) {
+            prefetch_tmap(&tmXh);
+            if (TWO) prefetch_tmap(&tmXl);
+        }
     }
     if (warp == 1) { tmem_alloc(tmem_slot, NCOLS); tmem_relinquish(); }
     tc_fence_before();
@@ -393,8 +494,8 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
     const int pre = min(stages, nkb);
     if (warp == 0 && lane == 0) {
         for (int i = 0; i < pre; ++i) {
-            mbar_expect_tx(&full[i], STAGE_BYTES);
-            tma_load_2d(smem + (size_t)i * STAGE_BYTES, &tmW, &full[i], (kb0 + i) * BK, n0);
+            mbar_expect_tx(&full[i], stage_bytes);
+            tma_load_2d(smem + (size_t)i * stage_bytes, &tmW, &full[i], (kb0 + i) * BK, n0);
         }
     }
     pdl_wait();
@@ -405,33 +506,37 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % stages;
                 const uint32_t ph = (uint32_t)(i / stages) & 1u;
-                uint8_t *a = smem + (size_t)s * STAGE_BYTES;
+                uint8_t *a = smem + (size_t)s * stage_bytes;
                 const int kc = (kb0 + i) * BK;
                 if (i >= pre) {
                     if (!mbar_wait(&empty[s], ph ^ 1u, CT_STATUS_TIMEOUT_FREE)) break;
-                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    mbar_expect_tx(&full[s], stage_bytes);
                     tma_load_2d(a, &tmW, &full[s], kc, n0);
                 }
-                tma_load_2d(a + A_BYTES, &tmXh, &full[s], kc, t0);
-                if (TWO) tma_load_2d(a + A_BYTES + B_BYTES, &tmXl, &full[s], kc, t0);
+                if (!lnx) {
+                    tma_load_2d(a + A_BYTES, &tmXh, &full[s], kc, t0);
+                    if (TWO) tma_load_2d(a + A_BYTES + B_BYTES, &tmXl, &full[s], kc, t0);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16(BM, BN);
-            for (int i = 0; i < nkb; ++i) {
+            const bool xok = !lnx || mbar_wait(xfull, 0, CT_STATUS_TIMEOUT_TMA);
+            for (int i = 0; i < nkb && xok; ++i) {
                 const int s = i % stages;
                 const uint32_t ph = (uint32_t)(i / stages) & 1u;
                 if (!mbar_wait(&full[s], ph, CT_STATUS_TIMEOUT_TMA)) break;
                 tc_fence_after();
-                const uint32_t a = smem_u32(smem + (size_t)s * STAGE_BYTES);
+                const uint32_t a = smem_u32(smem + (size_t)s * stage_bytes);
+                const uint32_t b = lnx ? smem_u32(xs) + (uint32_t)i * (TWO ? 2u : 1u) * B_BYTES : a + A_BYTES;
                 const uint64_t ad = sw128_desc(a);
-                const uint64_t bd = sw128_desc(a + A_BYTES);
+                const uint64_t bd = sw128_desc(b);
 #pragma unroll
                 for (int k = 0; k < BK / 16; ++k)
                     mma_bf16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
                 if (TWO) {
-                    const uint64_t ld = sw128_desc(a + A_BYTES + B_BYTES);
+                    const uint64_t ld = sw128_desc(b + B_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) mma_bf16(tmem, ad + 2 * k, ld + 2 * k, idesc, 1u);
                 }
@@ -445,6 +550,11 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
     const int q = warp & 3;
     const int n = n0 + q * 32 + lane;
     const bool epi_warp = warp >= 2;
+    if (epi_warp && lnx) {
+        ln_fill<BN, TWO>(p.ep, xs, t0, T_eff, kb0, nkb, threadIdx.x - 64);
+        fence_proxy_async_smem();   // the MMA reads these tiles through the async proxy
+        mbar_arrive(xfull);
+    }
     bool ok = true;
     if (epi_warp) {
         ok = mbar_wait(accb, 0, CT_STATUS_TIMEOUT_MMA);
@@ -769,12 +879,17 @@ int split_factor(int N, int K) {
 template <int BN, bool TWO>
 static void launch_tc(cudaStream_t st, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml,
                       KernelParams p, bool pdl) {
-    constexpr int STAGE = BM * BK * 2 + BN * BK * 2 * (TWO ? 2 : 1);
+    // LayerNorm-input mode: weight-only stages, then the activation tiles of
+    // all of a CTA's k-blocks
+    const bool lnx = p.ep.ln_x != nullptr;
+    const int STAGE = lnx ? BM * BK * 2 : BM * BK * 2 + BN * BK * 2 * (TWO ? 2 : 1);
+    const int xbytes = lnx ? p.kbps * BN * BK * 2 * (TWO ? 2 : 1) : 0;
     // large clusters: keep two CTAs per SM so a 16-CTA cluster fits in a GPC
     const int budget = p.nsplit > 8 ? 100 * 1024 : kSmemBudget;
-    const int max_stages = std::max(1, (budget - 2048) / STAGE);
+    if (xbytes + STAGE + 2048 > budget) CT_FATAL("LayerNorm-input GEMM tile does not fit: %d B of activations", xbytes);
+    const int max_stages = std::max(1, (budget - 2048 - xbytes) / STAGE);
     p.stages = std::min(std::min(p.kbps, max_stages), 8);
-    size_t body = (size_t)p.stages * STAGE;
+    size_t body = (size_t)p.stages * STAGE + xbytes;
     if (p.nsplit > 1) body = std::max(body, (size_t)BM * BN * sizeof(float));   // parked accumulator
     p.bar_off = (int)((body + 15) & ~(size_t)15);
     const size_t smem = 1024 + p.bar_off + 16 * (2 * p.stages + 2);
@@ -877,8 +992,12 @@ void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, c
     // X maps use the scratch capacity (or the caller's buffer rows) as the row count
     const long xrows = (X_hi == c->xhi || X_hi == c->xlo) ? (long)(c->x_elems / K) : (ep.x_rows > 0 ? ep.x_rows : (long)T);
     // large problems without K split or device row count: persistent kernel
-    const bool pers = nsplit == 1 && !ep.T_dev && T > (two ? 64 : 128);
+    const bool pers = nsplit == 1 && !ep.T_dev && !ep.ln_x && T > (two ? 64 : 128);
     if (pers) BN = two ? 128 : 256;
+    if (ep.ln_x && (K != 1024 || !ep.ln_stats || !ep.ln_g || !ep.ln_b || (((uintptr_t)ep.ln_g | (uintptr_t)ep.ln_b) & 15)))
+        CT_FATAL("LayerNorm-input GEMM needs K = 1024, row statistics and 16-byte aligned LN weights");
+    if (ep.stats_out && (ep.epi != EPI_FMADD || ep.row_mask || N % BM || nsplit < 2))
+        CT_FATAL("row statistics need EPI_FMADD with a K split, no row mask and N a multiple of %d", BM);
     const CUtensorMap &mw = tmap_bf16(c, W, N, K, BM);
     const CUtensorMap &mh = tmap_bf16(c, X_hi, xrows, K, BN);
     const CUtensorMap &ml = two ? tmap_bf16(c, X_lo, xrows, K, BN) : mh;

@@ -51,6 +51,21 @@ struct GemmEpilogue {
     bool pdl = false;             // launch with programmatic stream serialization
     int split = 0;                // K-split factor override (0 = split_factor(N, K)); a fixed
                                   // per-call-site value keeps results independent of T
+    // Row statistics of the stored values (EPI_FMADD with a K split): for token t
+    // and 128-feature tile j, stats_out[t * (N / 128) + j] = (mean, sum of squared
+    // deviations) of the tile's 128 new values -- the partials a following
+    // LayerNorm-input GEMM merges into the row's mean and variance.
+    float2 *stats_out = nullptr;
+    // LayerNorm-input mode: instead of TMA-loading bf16 planes, the kernel forms
+    // its activation tiles as LN(ln_x[t]) = (x - mean) * rstd * ln_g + ln_b
+    // (eps 1e-5, biased variance), split into hi/lo planes in shared memory.
+    // ln_stats holds the (mean, M2) partials of the K / 128 feature tiles of
+    // each row, as stats_out writes them; ln_x rows have stride K.  K must be a
+    // multiple of 128 and at most 1024; ln_g / ln_b 16-byte aligned.
+    const float *ln_x = nullptr;
+    const float2 *ln_stats = nullptr;
+    const bf16 *ln_g = nullptr;
+    const bf16 *ln_b = nullptr;
 };
 
 // Per-thread GEMM context: stream, workspaces, tensor-map cache.
