@@ -67,39 +67,58 @@ struct DevState {
 };
 
 // ------------------------------------------------------------ kernels -----
-// Block-wide exclusive scan (blockDim = 1024).
-__device__ int block_excl_scan(int v, int *tmp, int *total) {
+// Block-wide exclusive scan of NV values per thread at once (blockDim = 1024):
+// out[v] = sum of v-th values of threads < this one, total[v] = block sum.
+template <int NV>
+__device__ void block_excl_scan_n(const int (&v)[NV], int (&out)[NV], int (&total)[NV], int (*tmp)[64]) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    int x = v;
+    int x[NV];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) tmp[w] = x;
-    __syncthreads();
-    if (w == 0) {
-        int s = lane < (int)(blockDim.x >> 5) ? tmp[lane] : 0;
+    for (int k = 0; k < NV; ++k) {
+        x[k] = v[k];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, s, o);
-            if (lane >= o) s += y;
+            const int y = __shfl_up_sync(0xffffffffu, x[k], o);
+            if (lane >= o) x[k] += y;
         }
-        tmp[32 + lane] = s;   // inclusive per-warp prefix
+        if (lane == 31) tmp[k][w] = x[k];
     }
     __syncthreads();
-    const int warp_base = w > 0 ? tmp[32 + w - 1] : 0;
-    *total = tmp[32 + (blockDim.x >> 5) - 1];
-    return warp_base + x - v;
+    if (w < NV) {   // warp k scans the 32 warp totals of value k
+        int t = tmp[w][lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        tmp[w][32 + lane] = t;   // inclusive per-warp prefix
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        out[k] = (w > 0 ? tmp[k][32 + w - 1] : 0) + x[k] - v[k];
+        total[k] = tmp[k][63];
+    }
 }
 
+// Packs the step: thread i (slot i) counts its rows, pages and page groups; one
+// block scan gives every slot its offsets; the thread writes its rows'
+// (slot, position, token, self-page offset).  Then warp w lists the attention
+// pages of sequences w, w + 32, ... with the lanes over pages: the slot's page
+// ids are loaded once (read-only path), then each row's self entries (causal
+// prefix of the slot's pages) and cross entries (all its encoder pages) are
+// stored, rows in order, with the group starts and per-row first entries.
+// Finally the per-CTA entry ranges of the attention grid.
 __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_cap, int seq_cap) {
-    __shared__ int tmp[64];
-    __shared__ int tmp2[64];
+    __shared__ int tmp[6][64];
+    __shared__ int4 seq_a[1024];   // per sequence: slot, first row, rows, position (-1: prefill)
+    __shared__ int4 seq_b[1024];   // per sequence: first self entry, first cross entry, first self / cross group
+    __shared__ int seq_te[1024];   // per sequence: encoder rows
     const int i = threadIdx.x;
     const int st = i < s.max_slots ? s.state[i] : S_FREE;
-    int nr = st == S_PREFILL ? s.plen[i] : st == S_DECODE ? 1 : 0;
+    const int nr = st == S_PREFILL ? s.plen[i] : st == S_DECODE ? 1 : 0;
     const int te = nr > 0 ? s.tenc[i] : 0;
+    const int pos = st == S_DECODE ? s.pos[i] : -1;
     const int cross_np = (te + PR - 1) / PR;
     int self_np = 0, self_ng = 0;   // self-attention pages and groups over the slot's rows
     if (st == S_PREFILL) {
@@ -109,22 +128,15 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
             self_ng += (np + GP - 1) / GP;
         }
     } else if (st == S_DECODE) {
-        self_np = (s.pos[i] + 1 + PR - 1) / PR;
+        self_np = (pos + 1 + PR - 1) / PR;
         self_ng = (self_np + GP - 1) / GP;
     }
     const int cross_ng = (cross_np + GP - 1) / GP;
-    int total = 0, nseq = 0, n_ps = 0, n_pc = 0, n_gs = 0, n_gc = 0;
-    const int base = block_excl_scan(nr, tmp, &total);
-    __syncthreads();
-    const int sidx = block_excl_scan(nr > 0 ? 1 : 0, tmp2, &nseq);
-    __syncthreads();
-    const int psb = block_excl_scan(self_np, tmp, &n_ps);
-    __syncthreads();
-    const int pcb = block_excl_scan(nr * cross_np, tmp2, &n_pc);
-    __syncthreads();
-    const int gsb = block_excl_scan(self_ng, tmp, &n_gs);
-    __syncthreads();
-    const int gcb = block_excl_scan(nr * cross_ng, tmp2, &n_gc);
+    const int cnt[6] = {nr, nr > 0 ? 1 : 0, self_np, nr * cross_np, self_ng, nr * cross_ng};
+    int off[6], tot[6];
+    block_excl_scan_n<6>(cnt, off, tot, tmp);
+    const int base = off[0], sidx = off[1];
+    const int total = tot[0], nseq = tot[1], n_ps = tot[2], n_pc = tot[3], n_gs = tot[4], n_gc = tot[5];
     if (total > row_cap || nseq > seq_cap) {   // the host bounds admissions; never expected
         if (i == 0) { set_status(CT_STATUS_BAD_ARG); *s.n_rows = 0; *s.n_seqs = 0; }
         if (i <= s.n_cta) { s.crange[i] = 0; s.crange[s.n_cta + 1 + i] = 0; }
@@ -132,41 +144,19 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     }
     for (int j = 0; j < nr; ++j) {
         const int r = base + j;
-        const int p = st == S_PREFILL ? j : s.pos[i];
+        const int p = st == S_PREFILL ? j : pos;
         s.r_slot[r] = i;
         s.r_pos[r] = p;
         s.r_tok[r] = st == S_PREFILL ? s.prompt[i * PROMPT_MAX + j] : s.tok[i];
         const int page = (p >= 0 && p < MAX_SEQ) ? s.self_pt[i * SELF_PAGES + p / PR] : -1;
         s.r_off[r] = page >= 0 ? (long long)page * PAGE_ELEMS + (long long)(p % PR) * D : -1;
     }
-    if (nr > 0) { s.q_row[sidx] = base + nr - 1; s.q_slot[sidx] = i; }
-    // attention page lists, rows in order: row r's entries are [rp[r], rp[r+1])
-    int gs = psb, gc = pcb, qs = gsb, qc = gcb;
-    for (int j = 0; j < nr; ++j) {
-        const int r = base + j;
-        const int L = (st == S_PREFILL ? j : s.pos[i]) + 1;      // causal: keys 0 .. position
-        const int np = min((L + PR - 1) / PR, SELF_PAGES);
-        for (int k = 0; k < np; k += GP) s.grp_self[qs++] = gs + k;
-        for (int k = 0; k < cross_np; k += GP) s.grp_cross[qc++] = gc + k;
-        s.rp_self[r] = gs;
-        for (int q = 0; q < np; ++q, ++gs) {
-            int pid = s.self_pt[i * SELF_PAGES + q];
-            if (pid < 0) { set_status(CT_STATUS_BAD_ARG); pid = 0; }
-            const int nv = min(PR, L - q * PR);
-            s.pid_self[gs] = pid;
-            // bit 21: written by this step's QKV projection (every page of a
-            // prefill row, the last page of a decode row)
-            const int fresh = st == S_PREFILL || q == np - 1;
-            s.w_self[gs] = r | q << 10 | (nv - 1) << 16 | (q == np - 1) << 20 | fresh << 21;
-        }
-        s.rp_cross[r] = gc;
-        for (int q = 0; q < cross_np; ++q, ++gc) {
-            int pid = s.cross_pt[i * CROSS_PAGES + q];
-            if (pid < 0) { set_status(CT_STATUS_BAD_ARG); pid = 0; }
-            const int nv = min(PR, te - q * PR);
-            s.pid_cross[gc] = pid;
-            s.w_cross[gc] = r | q << 10 | (nv - 1) << 16 | (q == cross_np - 1) << 20;
-        }
+    if (nr > 0) {
+        s.q_row[sidx] = base + nr - 1;
+        s.q_slot[sidx] = i;
+        seq_a[sidx] = make_int4(i, base, nr, pos);
+        seq_b[sidx] = make_int4(off[2], off[3], off[4], off[5]);
+        seq_te[sidx] = te;
     }
     if (i == 0) {
         *s.n_rows = total; *s.n_seqs = nseq; *s.n_wself = n_ps; *s.n_wcross = n_pc;
@@ -176,6 +166,51 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
         s.rp_cross[total] = n_pc;
         s.grp_self[n_gs] = n_ps;
         s.grp_cross[n_gc] = n_pc;
+    }
+    __syncthreads();
+    // attention page lists, rows in order: row r's entries are [rp[r], rp[r+1])
+    const int lane = i & 31;
+    for (int q = i >> 5; q < nseq; q += 32) {
+        const int4 a = seq_a[q], b = seq_b[q];
+        const int slot = a.x, r0 = a.y, rows = a.z, dpos = a.w;
+        const int tq = seq_te[q];
+        const int cnp = (tq + PR - 1) / PR, cng = (cnp + GP - 1) / GP;
+        // lane k holds page ids k and k + 32 of both tables (64 each)
+        const int sp0 = __ldg(s.self_pt + slot * SELF_PAGES + lane), sp1 = __ldg(s.self_pt + slot * SELF_PAGES + 32 + lane);
+        const int cp0 = __ldg(s.cross_pt + slot * CROSS_PAGES + lane), cp1 = __ldg(s.cross_pt + slot * CROSS_PAGES + 32 + lane);
+        int gs = b.x, gc = b.y, qs = b.z, qc = b.w;
+        for (int j = 0; j < rows; ++j) {
+            const int r = r0 + j;
+            const bool prefill = dpos < 0;
+            const int L = (prefill ? j : dpos) + 1;      // causal: keys 0 .. position
+            const int np = min((L + PR - 1) / PR, SELF_PAGES);
+            const int ng = (np + GP - 1) / GP;
+            for (int g = lane; g < ng; g += 32) s.grp_self[qs + g] = gs + g * GP;
+            for (int g = lane; g < cng; g += 32) s.grp_cross[qc + g] = gc + g * GP;
+            if (lane == 0) { s.rp_self[r] = gs; s.rp_cross[r] = gc; }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int k = lane + 32 * h;
+                if (k < np) {
+                    int pid = h ? sp1 : sp0;
+                    if (pid < 0) { set_status(CT_STATUS_BAD_ARG); pid = 0; }
+                    const int nv = min(PR, L - k * PR);
+                    // bit 21: written by this step's QKV projection (every page of a
+                    // prefill row, the last page of a decode row)
+                    const int fresh = prefill || k == np - 1;
+                    s.pid_self[gs + k] = pid;
+                    s.w_self[gs + k] = r | k << 10 | (nv - 1) << 16 | (k == np - 1) << 20 | fresh << 21;
+                }
+                if (k < cnp) {
+                    int pid = h ? cp1 : cp0;
+                    if (pid < 0) { set_status(CT_STATUS_BAD_ARG); pid = 0; }
+                    const int nv = min(PR, tq - k * PR);
+                    s.pid_cross[gc + k] = pid;
+                    s.w_cross[gc + k] = r | k << 10 | (nv - 1) << 16 | (k == cnp - 1) << 20;
+                }
+            }
+            gs += np; gc += cnp; qs += ng; qc += cng;
+        }
     }
     // attention CTA b takes groups [b*NG/G, (b+1)*NG/G) of G = min(n_cta, NG)
     // equal shares; CTAs b >= G get an empty range
