@@ -6,11 +6,13 @@
 //   page pool (bf16): [page][DEC_N][K,V][16 rows][DEC_D]
 //   step buffers sized for max_rows packed query rows
 // One step = build rows (block prefix sum over slots) -> embed+LN ->
-// DEC_N x [LN, QKV GEMM (K/V scattered into pages), paged self-attention,
-// O GEMM + residual, LN, Q GEMM, paged cross-attention, O GEMM + residual,
-// LN, FFN1 (ReLU), FFN2 + residual] -> final LN of each sequence's last row ->
-// LM head GEMM -> argmax -> retire / append on the GPU.  Kernels read the row
-// and sequence counts from device memory, so one captured graph per capacity
+// DEC_N x [QKV GEMM (K/V scattered into pages), paged self-attention,
+// O GEMM + residual, Q GEMM, paged cross-attention, O GEMM + residual,
+// FFN1 (ReLU), FFN2 + residual] -> final LN of each sequence's last row ->
+// LM head GEMM -> argmax + retire / append on the GPU.  The pre-LayerNorms of
+// the Q, FFN1 and (from layer 1) QKV GEMMs run inside those GEMMs, from row
+// statistics the residual GEMMs leave behind.  Kernels read the row and
+// sequence counts from device memory, so one captured graph per capacity
 // bucket serves every step.
 #include <algorithm>
 #include <deque>
@@ -552,7 +554,11 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
 }
 
 // next[q] = argmax over the vocabulary of sequence q's logits (first max).
-__global__ void __launch_bounds__(256) argmax_seq_kernel(DevState s, const float *logits, int *next) {
+// Greedy argmax of each sequence's logits (first index of the maximum), then
+// that sequence's bookkeeping: append the token (EOS when the forced length is
+// reached), advance its position, retire it on EOS / forced length / MAX_SEQ
+// (done_map tells the host).  One CTA per sequence; sequences are independent.
+__global__ void __launch_bounds__(256) argmax_update_kernel(DevState s, const float *logits, int *next) {
     pdl_wait();
     pdl_trigger();
     __shared__ float bv[256];
@@ -580,19 +586,11 @@ __global__ void __launch_bounds__(256) argmax_seq_kernel(DevState s, const float
         }
         __syncthreads();
     }
-    if (threadIdx.x == 0) next[q] = bi[0] == 0x7fffffff ? 0 : bi[0];
-}
-
-// Append the step's token to every live sequence, advance its KV length and
-// retire it on forced length / EOS / MAX_SEQ (transcribe.c:771-794).
-__global__ void update_kernel(DevState s, const int *next) {
-    pdl_wait();
-    pdl_trigger();
-    const int q = blockIdx.x * blockDim.x + threadIdx.x;
-    if (q >= *s.n_seqs) return;
+    if (threadIdx.x != 0) return;
+    int tok = bi[0] == 0x7fffffff ? 0 : bi[0];
+    next[q] = tok;
     const int slot = s.q_slot[q];
     const int st = s.state[slot];
-    int tok = next[q];
     const int gen = s.gen[slot] + 1;
     const int forced = s.forced[slot];
     if (forced > 0 && gen >= forced) tok = CT_TOK_EOS;
@@ -913,8 +911,7 @@ static void encode_step(ct_engine *e, int rows) {
     lh.split = 1;   // 128 vocabulary tiles, one wave: each CTA streams its 128 x 1024 slice of the table
     egemm(e, e->etw, V, D, e->lm[0], lm_lo, seqs, e->cfg.max_slots, lh, true);
     mark(e, "gemm_lm_head");
-    launch_pdl(st, dim3(seqs), dim3(256), argmax_seq_kernel, s, (const float *)e->logits, e->next);
-    launch_pdl(st, dim3((seqs + 255) / 256), dim3(256), update_kernel, s, (const int *)e->next);
+    launch_pdl(st, dim3(seqs), dim3(256), argmax_update_kernel, s, (const float *)e->logits, e->next);
     mark(e, "argmax_update");
 }
 
