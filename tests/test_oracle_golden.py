@@ -288,3 +288,51 @@ def test_mel_front_end_matches_reference():
             # one frame (n < 160): the unbiased variance divides by T - 1 = 0 and
             # the reference yields NaN; the oracle reproduces it
             assert np.array_equal(po.compute_mel(x), ref, equal_nan=True), n
+
+
+def test_full_size_encoder_matches_live_reference(wmod):
+    """Full-size encoder (48 Conformer layers at width 1280, model.h dims) plus a
+    short greedy decode: the oracle's orc_encoder_forward_batch and decoder give
+    the same encoder rows and tokens, bit for bit, as the reference's own
+    model.h encoder_forward_batch + decode loop on its CPU backend
+    (oracle/_ref/libref_decode_cpu.so, built from the reference sources).  Two
+    short ragged utterances keep the reference's single-threaded run to
+    seconds; the arithmetic per row is the one every length uses."""
+    L = po.ref_lib("libref_decode_cpu.so")
+    if L is None:
+        pytest.skip("reference decode harness not built (oracle/_ref/ needs the reference tree)")
+    L = po.bind_ref_decode(L)
+    dims = wmod.FULL_DIMS
+    wb = wmod.make_blob(dims, seed=11)
+    ws = wmod.weights_struct(wb)
+    secs = [0.6, 0.35]
+    mel, T_mel = inputs.mel_batch(secs, seed=907)
+    B, T_mel_max = mel.shape[0], mel.shape[2]
+    T_enc = np.array([inputs.ctb.t_enc_of(int(t)) for t in T_mel], np.int32)
+    Tm = inputs.ctb.t_enc_of(T_mel_max)
+    prompt = np.array(inputs.ctb.PROMPT_FULL, np.int32)
+    forced = np.array([5, 4], np.int32)
+
+    L.refh_bind_weights(ctypes.addressof(ws))
+    L.backend_init(0)
+    r_tok = np.zeros((B, 1024), np.int32)
+    r_n = np.zeros(B, np.int32)
+    r_am = np.full((B, 1024), -1, np.int32)
+    r_mg = np.full((B, 1024), np.nan, np.float32)
+    r_enc = np.zeros((B, Tm, dims["dec_d"]), np.float32)
+    L.refh_transcribe_batch(B, po.fp(mel), T_mel_max, po.ip(T_mel), po.ip(prompt), len(prompt), po.ip(forced),
+                            po.null_i(), po.ip(r_tok), po.ip(r_n), po.ip(r_am), po.fp(r_mg), po.fp(r_enc))
+    L.backend_thread_cleanup()
+
+    O = po.lib()
+    d = po.dims_struct(dims)
+    o_enc = np.zeros((B, Tm, dims["dec_d"]), np.float32)
+    O.orc_encoder_forward_batch(ctypes.byref(d), ctypes.addressof(ws), po.fp(mel), B, T_mel_max, po.ip(T_mel),
+                                po.ip(T_enc), Tm, po.fp(o_enc))
+    for b in range(B):
+        assert np.array_equal(o_enc[b, :T_enc[b]], r_enc[b, :T_enc[b]]), f"encoder rows of utterance {b}"
+    tokens, n_tok, am, mg = po.decode_batch(dims, ws, o_enc, T_enc, prompt, forced)
+    assert np.array_equal(n_tok, r_n)
+    assert np.array_equal(tokens, r_tok)
+    sel = ~np.isnan(r_mg)
+    assert np.array_equal(mg[sel], r_mg[sel])
