@@ -179,7 +179,7 @@ class Engine:
 
     def step_times(self):
         """Device ms of each step since the previous call (the log is cleared)."""
-        out = np.zeros(1 << 16, np.float32)
+        out = np.empty(1 << 16, np.float32)
         n = self.lib.ct_engine_step_times(self.h, out.ctypes.data, len(out))
         if n < 0:
             raise RuntimeError(f"step_times failed: {n}")
@@ -198,7 +198,8 @@ class Engine:
 
     def poll(self, max_results=4096, tok_stride=1024):
         res = (Result * max_results)()
-        toks = np.zeros((max_results, tok_stride), np.int32)
+        # uninitialised: only the rows of returned results are written and read
+        toks = np.empty((max_results, tok_stride), np.int32)
         n = self.lib.ct_engine_poll(self.h, res, max_results, toks.ctypes.data, tok_stride)
         if n < 0:
             raise RuntimeError(f"poll failed: {n}")
