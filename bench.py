@@ -30,6 +30,12 @@ One bench step runs three legs (A and B over that batch, C alone):
      (ct_engine_submit_mel), encoded, admitted and decoded alone to EOS forced
      at the 200th token; reported under "config2" (p50 step latency at batch 1,
      decode tokens/s, RTFx), beside the configuration-3 headline.
+  S  (optional, not in the default legs) configuration 4: a stream of
+     --stream-n utterances of seeded log-mel with Poisson arrivals at 200/s
+     (or all at t = 0 with --stream-saturated), log-normal lengths, 3 tokens
+     per audio second, replayed in real time by cohere-transcribe_b200/stream.py
+     after the timed legs; reported under "config4" (latency p50 / p95, tokens/s,
+     RTFx over the stream's wall time).
 
 `--impl reference` times the reference's own CPU implementation (its
 backends/cpu/backend.c driven by its model.h, prebuilt under oracle/_ref/) on
@@ -298,6 +304,8 @@ def main():
     ap.add_argument("--legs", default="ABC", help="A = decode leg, B = transcription leg, C = configuration 2 "
                     "(batch 1), E = encoder only (profiling cases)")
     ap.add_argument("--max-slots", type=int, default=256, help="engine slots (profiling cases)")
+    ap.add_argument("--stream-n", type=int, default=4096, help="leg S: utterances in the stream")
+    ap.add_argument("--stream-saturated", action="store_true", help="leg S: every utterance arrives at t = 0")
     args = ap.parse_args()
 
     world, rank, local = dist_setup()
@@ -354,7 +362,8 @@ def main():
     # the decode leg alone needs no encoder (a decoder-only blob keeps profiling cases small)
     with_enc = "B" in legs or "E" in legs
     with_c = "C" in legs
-    wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("enc", "dec") if (with_enc or with_c) else ("dec",))
+    with_s = "S" in legs
+    wb = W.make_blob(W.FULL_DIMS, seed=0, parts=("enc", "dec") if (with_enc or with_c or with_s) else ("dec",))
     ws = W.weights_struct(wb)
     dev = local if world > 1 else 0
     enc_frames = int(case["T_mel"].sum())
@@ -363,11 +372,15 @@ def main():
         (128, importlib.import_module("cohere-transcribe_b200").t_mel_of_seconds(CFG2_SECONDS)), dtype=np.float32)
     if with_c:
         enc_frames = max(enc_frames, int(mel2.shape[1]))
+    enc_utts = nb
+    if with_s:   # configuration 4 packs encoder batches of up to 64 utterances of up to 30 s
+        enc_utts, enc_frames = max(nb, 64), max(enc_frames, 64 * 3001)
 
     def make_engine(profile=0):
         return abi.Engine(lib, dev, wb, ws, max_slots=args.max_slots, max_rows=1024, precision=args.precision,
                           kv_pages=args.kv_pages, no_pdl=int(args.no_pdl), profile=profile,
-                          enc_max_utts=nb if (with_enc or with_c) else -1, enc_max_frames=enc_frames)
+                          enc_max_utts=enc_utts if (with_enc or with_c or with_s) else -1,
+                          enc_max_frames=enc_frames)
 
     eng = make_engine()
     # host inputs: encoder rows (leg A) and log-mel (leg B), fp32 host memory
@@ -450,6 +463,19 @@ def main():
     s_end = eng.stats()
     status = eng.status()
     launches = int(s_end["kernel_launches"] - s_start["kernel_launches"])
+    config4 = None
+    if with_s:   # configuration 4, after the timed legs (its own wall-clock measurement)
+        stream = importlib.import_module("cohere-transcribe_b200.stream")
+        warm = stream.stream_case(64, seed=1, saturated=True)
+        stream.run_stream(eng, warm, inputs=[warm.log_mel(i) for i in range(64)])
+        sc = stream.stream_case(args.stream_n, seed=0, saturated=args.stream_saturated)
+        mels = [sc.log_mel(i) for i in range(args.stream_n)]   # generated before the replay starts
+        config4 = stream.run_stream(eng, sc, inputs=mels).summary()
+        config4["workload"] = (f"config 4: {args.stream_n} utterances of seeded N(0, 1) log-mel, "
+                               + ("all arriving at t = 0" if args.stream_saturated else "Poisson arrivals 200/s")
+                               + ", log-normal lengths (median 8 s, sigma 0.5, 1-30 s), 3 tokens/s of audio "
+                                 "+-20% with EOS forced, <= 256 concurrent sequences, encoder batches <= 64")
+        status = status or eng.status()
     eng.close()
 
     K = args.steps
@@ -537,6 +563,7 @@ def main():
                      "h2d_bytes_per_step": h2d_b, "d2h_bytes_per_step": d2h},
             "p50_step_ms": statistics.median(step_times) if step_times else None,
             "config2": config2_summary(dev_c, wall_c, step_times_c, K) if with_c else None,
+            "config4": config4,
             "gpu_launches": launches, "roofline": roof, "rooflines": rooflines,
             "profiled_step_breakdown": breakdown, "clocks": clk.summary(), "device_status": status,
             "precision": "bf16 weights, activations as bf16 hi+lo planes, fp32 accumulate" if args.precision else

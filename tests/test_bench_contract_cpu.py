@@ -42,8 +42,11 @@ def bench_mod(monkeypatch):
         submit_audio = submit
 
         def submit_mel(self, i, x, f):
-            assert x.shape == (128, 3001)
+            assert x.shape[0] == 128
             self.q[i] = int(f)
+
+        def step(self, n):   # the stand-in finishes everything it holds at once
+            return 0
 
         def encode(self, m):
             return m
@@ -143,3 +146,12 @@ def test_reference_arm_line(bench_mod, capsys, monkeypatch):
     assert d["cpu_baseline"]["kind"] == "reference" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["rtfx"]["value"] == pytest.approx(2.0)
+
+
+def test_stream_leg_summary(bench_mod, capsys, monkeypatch):
+    d = _run(bench_mod, capsys, monkeypatch, ["--no-cpu", "--legs", "S", "--stream-n", "40", "--stream-saturated",
+                                              "--steps", "3", "--warmup", "3"])
+    c4 = d["config4"]
+    assert c4["utterances"] == 40 and c4["workload"].startswith("config 4: 40 utterances")
+    assert c4["latency_p50_s"] <= c4["latency_p95_s"] <= c4["latency_max_s"]
+    assert c4["generated_tokens"] > 0 and c4["rtfx"] > 0
