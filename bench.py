@@ -35,7 +35,11 @@ One bench step runs three legs (A and B over that batch, C alone):
      (or all at t = 0 with --stream-saturated), log-normal lengths, 3 tokens
      per audio second, replayed in real time by cohere-transcribe_b200/stream.py
      after the timed legs; reported under "config4" (latency p50 / p95, tokens/s,
-     RTFx over the stream's wall time).
+     RTFx over the stream's wall time).  --stream-config 5 replays configuration
+     5 instead (32768 utterances at 1600/s plus 64 five-minute inputs as 30 s /
+     29 s-hop windows), each rank its share by queued audio seconds; reported
+     under "config5" with tokens and audio summed over ranks and the worst
+     rank's wall time.
 
 `--impl reference` times the reference's own CPU implementation (its
 backends/cpu/backend.c driven by its model.h, prebuilt under oracle/_ref/) on
@@ -304,7 +308,11 @@ def main():
     ap.add_argument("--legs", default="ABC", help="A = decode leg, B = transcription leg, C = configuration 2 "
                     "(batch 1), E = encoder only (profiling cases)")
     ap.add_argument("--max-slots", type=int, default=256, help="engine slots (profiling cases)")
-    ap.add_argument("--stream-n", type=int, default=4096, help="leg S: utterances in the stream")
+    ap.add_argument("--stream-config", type=int, default=4, choices=[4, 5],
+                    help="leg S: configuration 4 (one GPU's stream) or 5 (8x the rate plus long-form windows, "
+                         "dispatched over the ranks)")
+    ap.add_argument("--stream-n", type=int, default=0,
+                    help="leg S: utterances in the stream (0 = the configuration's: 4096, or 32768 for 5)")
     ap.add_argument("--stream-saturated", action="store_true", help="leg S: every utterance arrives at t = 0")
     args = ap.parse_args()
 
@@ -466,15 +474,39 @@ def main():
     config4 = None
     if with_s:   # configuration 4, after the timed legs (its own wall-clock measurement)
         stream = importlib.import_module("cohere-transcribe_b200.stream")
+        disp = importlib.import_module("cohere-transcribe_b200.dispatch")
         warm = stream.stream_case(64, seed=1, saturated=True)
         stream.run_stream(eng, warm, inputs=[warm.log_mel(i) for i in range(64)])
-        sc = stream.stream_case(args.stream_n, seed=0, saturated=args.stream_saturated)
-        mels = [sc.log_mel(i) for i in range(args.stream_n)]   # generated before the replay starts
-        config4 = stream.run_stream(eng, sc, inputs=mels).summary()
-        config4["workload"] = (f"config 4: {args.stream_n} utterances of seeded N(0, 1) log-mel, "
-                               + ("all arriving at t = 0" if args.stream_saturated else "Poisson arrivals 200/s")
-                               + ", log-normal lengths (median 8 s, sigma 0.5, 1-30 s), 3 tokens/s of audio "
-                                 "+-20% with EOS forced, <= 256 concurrent sequences, encoder batches <= 64")
+        if args.stream_config == 5:
+            n_s = args.stream_n or 32768
+            full = stream.config5_case(n_s, seed=0)
+            if args.stream_saturated:
+                full.arrival_s[:] = 0.0
+        else:
+            n_s = args.stream_n or 4096
+            full = stream.stream_case(n_s, seed=0, saturated=args.stream_saturated)
+        mine = [i for i, _ in disp.shard(list(range(len(full.seconds))), full.seconds, rank, world)]
+        sc = stream.subset(full, mine)
+        mels = [sc.log_mel(i) for i in range(len(sc.seconds))]   # generated before the replay starts
+        barrier(world)
+        res = stream.run_stream(eng, sc, inputs=mels)
+        config4 = res.summary()
+        if world > 1:   # whole job: tokens and audio summed, wall time and latency tails the worst rank's
+            for k in ("utterances", "generated_tokens", "audio_s"):
+                config4[k] = all_reduce(world, float(config4[k]), "sum")
+            for k in ("wall_s", "latency_p95_s", "latency_max_s"):
+                config4[k] = all_reduce(world, float(config4[k]), "max")
+            config4["tokens_per_s"] = config4["generated_tokens"] / config4["wall_s"]
+            config4["rtfx"] = config4["audio_s"] / config4["wall_s"]
+            config4["latency_p50_s"] = f"rank 0: {config4['latency_p50_s']}"
+        arrivals = "all arriving at t = 0" if args.stream_saturated else (
+            "Poisson arrivals 1600/s" if args.stream_config == 5 else "Poisson arrivals 200/s")
+        config4["workload"] = (f"config {args.stream_config}: {n_s} utterances of seeded N(0, 1) log-mel, {arrivals}"
+                               ", log-normal lengths (median 8 s, sigma 0.5, 1-30 s), 3 tokens/s of audio "
+                               "+-20% with EOS forced, <= 256 concurrent sequences per GPU, encoder batches <= 64"
+                               + (", plus 64 x 300 s long-form inputs as 704 windows of 30 s every 29 s at t = 0"
+                                  if args.stream_config == 5 else "")
+                               + (f"; dispatched to {world} GPUs by queued audio seconds" if world > 1 else ""))
         status = status or eng.status()
     eng.close()
 
@@ -563,7 +595,7 @@ def main():
                      "h2d_bytes_per_step": h2d_b, "d2h_bytes_per_step": d2h},
             "p50_step_ms": statistics.median(step_times) if step_times else None,
             "config2": config2_summary(dev_c, wall_c, step_times_c, K) if with_c else None,
-            "config4": config4,
+            ("config5" if args.stream_config == 5 else "config4"): config4,
             "gpu_launches": launches, "roofline": roof, "rooflines": rooflines,
             "profiled_step_breakdown": breakdown, "clocks": clk.summary(), "device_status": status,
             "precision": "bf16 weights, activations as bf16 hi+lo planes, fp32 accumulate" if args.precision else

@@ -18,6 +18,13 @@ advances the engine a few steps, and harvests finished utterances. It returns
 per-utterance latency (finish time - arrival time) and whole-stream throughput.
 With `saturated=True` every utterance arrives at t = 0, which measures capacity
 instead of the arrival rate.
+
+`config5_case` is configuration 5's stream, for 1 to 8 GPUs: 32,768 utterances
+with configuration 4's lengths and arrivals at 8x the rate (1,600/s). It adds
+64 long-form 5-minute inputs, cut into 30 s windows every 29 s (1 s overlap)
+that decode as independent utterances, all arriving at t = 0. `subset` takes
+one replica's share (see dispatch.shard) and keeps every utterance's seed, so
+a shard's inputs equal the full stream's.
 """
 from __future__ import annotations
 
@@ -34,14 +41,36 @@ def t_mel_of_seconds(sec: float) -> int:
 
 @dataclass
 class StreamCase:
-    arrival_s: np.ndarray      # [n] arrival times, seconds from the stream start, non-decreasing
+    arrival_s: np.ndarray      # [n] arrival times, seconds from the stream start
     seconds: np.ndarray        # [n] utterance durations
     forced_len: np.ndarray     # [n] generated tokens, EOS forced at the last
     seed: int
+    ids: np.ndarray = None     # [n] utterance ids in the full stream (seeds); default 0..n-1
+    windows: dict = None       # id -> (long input, first frame, end frame) for long-form windows
+    long_frames: int = 0       # log-mel frames of each long-form input
+
+    def __post_init__(self):
+        if self.ids is None:
+            self.ids = np.arange(len(self.seconds))
+        if self.windows is None:
+            self.windows = {}
+        self._long = (None, None)
+
+    def long_mel(self, j: int) -> np.ndarray:
+        """Long-form input j's seeded N(0, 1) log-mel [128, long_frames]."""
+        if self._long[0] != j:
+            rng = np.random.default_rng([self.seed, 9, j])
+            self._long = (j, rng.standard_normal((128, self.long_frames), dtype=np.float32))
+        return self._long[1]
 
     def log_mel(self, i: int) -> np.ndarray:
-        """Utterance i's seeded N(0, 1) log-mel [128, T_mel] (generated on demand)."""
-        rng = np.random.default_rng([self.seed, 7, i])
+        """Utterance i's seeded N(0, 1) log-mel [128, T_mel] (generated on demand);
+        a long-form window is its frames of the long input."""
+        uid = int(self.ids[i])
+        if uid in self.windows:
+            j, a, b = self.windows[uid]
+            return np.ascontiguousarray(self.long_mel(j)[:, a:b])
+        rng = np.random.default_rng([self.seed, 7, uid])
         return rng.standard_normal((128, t_mel_of_seconds(float(self.seconds[i]))), dtype=np.float32)
 
 
@@ -57,6 +86,35 @@ def stream_case(n: int = 4096, seed: int = 0, rate: float = 200.0, median_s: flo
     secs = np.clip(np.exp(rng.normal(np.log(median_s), sigma, n)), lo_s, hi_s)
     forced = np.maximum(1, np.round(tokens_per_s * secs * rng.uniform(1.0 - jitter, 1.0 + jitter, n)))
     return StreamCase(arrival_s=arrival, seconds=secs, forced_len=forced.astype(np.int32), seed=seed)
+
+
+def config5_case(n: int = 32768, seed: int = 0, rate: float = 1600.0, longform_n: int = 64,
+                 longform_s: float = 300.0, tokens_per_s: float = 3.0, jitter: float = 0.2) -> StreamCase:
+    """Configuration 5: configuration 4's draw at 8x the rate, plus the 30 s /
+    29 s-hop windows of `longform_n` long inputs, arriving at t = 0."""
+    from .dispatch import long_form_windows
+    base = stream_case(n, seed=seed, rate=rate, tokens_per_s=tokens_per_s, jitter=jitter)
+    T_long = t_mel_of_seconds(longform_s)
+    spans = long_form_windows(T_long)
+    rng = np.random.default_rng([seed, 5])
+    windows, secs = {}, []
+    for j in range(longform_n):
+        for a, b in spans:
+            windows[n + len(secs)] = (j, a, b)
+            secs.append((b - a - 1) / 100.0)   # T_mel = 1 + 100 s
+    secs = np.array(secs)
+    forced = np.maximum(1, np.round(tokens_per_s * secs * rng.uniform(1.0 - jitter, 1.0 + jitter, len(secs))))
+    return StreamCase(arrival_s=np.concatenate([base.arrival_s, np.zeros(len(secs))]),
+                      seconds=np.concatenate([base.seconds, secs]),
+                      forced_len=np.concatenate([base.forced_len, forced.astype(np.int32)]), seed=seed,
+                      windows=windows, long_frames=T_long)
+
+
+def subset(case: StreamCase, idx) -> StreamCase:
+    """The utterances `idx` of `case` (one replica's share), same seeds and windows."""
+    idx = np.asarray(idx, np.int64)
+    return StreamCase(arrival_s=case.arrival_s[idx], seconds=case.seconds[idx], forced_len=case.forced_len[idx],
+                      seed=case.seed, ids=case.ids[idx], windows=case.windows, long_frames=case.long_frames)
 
 
 @dataclass

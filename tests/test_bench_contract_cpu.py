@@ -155,3 +155,10 @@ def test_stream_leg_summary(bench_mod, capsys, monkeypatch):
     assert c4["utterances"] == 40 and c4["workload"].startswith("config 4: 40 utterances")
     assert c4["latency_p50_s"] <= c4["latency_p95_s"] <= c4["latency_max_s"]
     assert c4["generated_tokens"] > 0 and c4["rtfx"] > 0
+
+
+def test_stream_leg_configuration_5(bench_mod, capsys, monkeypatch):
+    d = _run(bench_mod, capsys, monkeypatch, ["--no-cpu", "--legs", "S", "--stream-config", "5", "--stream-n", "30",
+                                              "--stream-saturated", "--steps", "3", "--warmup", "3"])
+    c5 = d["config5"]
+    assert c5["utterances"] == 30 + 704 and "704 windows" in c5["workload"]

@@ -110,3 +110,26 @@ def test_replay_reports_lost_utterances():
     with pytest.raises(RuntimeError, match="never finished"):
         stream.run_stream(Losing(clk, case), case, clock=clk, sleep=clk.sleep,
                           inputs=[np.zeros((128, 4), np.float32)] * 3)
+
+
+def test_config5_case_windows_and_shards():
+    c = stream.config5_case(200, seed=4, longform_n=3)
+    n_win = 3 * 11                                       # 300 s in 30 s windows every 29 s: 11 each
+    assert len(c.seconds) == 200 + n_win
+    assert np.all(c.arrival_s[200:] == 0)
+    assert abs(np.diff(c.arrival_s[:200]).mean() - 1 / 1600) < 0.0003   # 8x configuration 4's rate
+    w = [c.windows[200 + k] for k in range(11)]
+    assert w[0] == (0, 0, 3001) and w[-1] == (0, 29000, 30001)
+    assert np.allclose(c.seconds[200:211], [30.0] * 10 + [10.0])
+    a, b = c.log_mel(200), c.log_mel(201)
+    assert a.shape == (128, 3001)
+    assert np.array_equal(a[:, 2900:], b[:, :101])          # 1 s of overlap between neighbours
+    assert np.array_equal(c.log_mel(211), c.long_mel(1)[:, :3001])
+    # a replica's share keeps each utterance's input
+    disp = importlib.import_module("cohere-transcribe_b200.dispatch")
+    mine = [i for i, _ in disp.shard(list(range(len(c.seconds))), c.seconds, 1, 4)]
+    sub = stream.subset(c, mine)
+    for k in (0, len(mine) // 2, len(mine) - 1):
+        assert np.array_equal(sub.log_mel(k), c.log_mel(mine[k]))
+    shares = [len(disp.shard(list(range(len(c.seconds))), c.seconds, r, 4)) for r in range(4)]
+    assert sum(shares) == len(c.seconds)
