@@ -1525,7 +1525,8 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
             EK(cudaMemcpy(Ly.qkv_b + (size_t)j * D, bparts[j], sizeof(bf16) * D, cudaMemcpyDeviceToDevice));
         }
         const bf16 *ck = ew(e, d.ca_kw), *cv = ew(e, d.ca_vw), *ckb = ew(e, d.ca_kb), *cvb = ew(e, d.ca_vb);
-        if (!ck || !cv || !ckb || !cvb || !Ly.sa_ow || !Ly.ca_qw || !Ly.ffn_w1 || !Ly.ffn_w2) { ct_engine_destroy(e); return CT_EINVAL; }
+        if (!ck || !cv || !ckb || !cvb || !Ly.sa_ow || !Ly.ca_qw || !Ly.ffn_w1 || !Ly.ffn_w2 || !Ly.sa_lnw ||
+            !Ly.sa_lnb || !Ly.ca_lnw || !Ly.ca_lnb || !Ly.ffn_lnw || !Ly.ffn_lnb) { ct_engine_destroy(e); return CT_EINVAL; }
         EK(cudaMemcpy(e->cakv_w + (size_t)(2 * l) * D * D, ck, sizeof(bf16) * D * D, cudaMemcpyDeviceToDevice));
         EK(cudaMemcpy(e->cakv_w + (size_t)(2 * l + 1) * D * D, cv, sizeof(bf16) * D * D, cudaMemcpyDeviceToDevice));
         EK(cudaMemcpy(e->cakv_b + (size_t)(2 * l) * D, ckb, sizeof(bf16) * D, cudaMemcpyDeviceToDevice));
