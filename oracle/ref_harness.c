@@ -28,6 +28,22 @@ int verbose = 0;
 /* Copy a table of host weight pointers (same struct as model.h's W). */
 void refh_bind_weights(const Weights *w) { W = *w; }
 
+#ifndef EMBEDDED_MODEL
+#include <unistd.h>
+/* The reference's own model-file loader (model.h load_weights: sf_load of
+ * model_files/model.safetensors, then sf_get of every tensor by its Hugging
+ * Face name) run in directory `dir`; the resulting weight table is copied to
+ * *out.  A missing tensor makes the reference loader exit(1). */
+int refh_load_model_file(const char *dir, Weights *out) {
+    char cwd[4096];
+    if (!getcwd(cwd, sizeof cwd) || chdir(dir) != 0) return -1;
+    load_weights();
+    const int rc = chdir(cwd);
+    *out = W;
+    return rc;
+}
+#endif
+
 static int t_enc_of(int T_mel) {
     int T1 = (T_mel + 1) / 2, T2 = (T1 + 1) / 2;
     return (T2 + 1) / 2;
