@@ -6,6 +6,12 @@ check the assignment, the long-form windowing of configuration 5, and a
 world-size-2 gloo run in which each rank processes its shard and rank 0
 verifies that every utterance was processed exactly once with the result a
 single process computes.
+
+Failure detection (ReplicaPool) is tested on the host only, with stand-in
+replicas: one whose step raises (as a failed CUDA call surfaces through the
+engine's return code), one whose device status word turns non-zero (as a
+bounded device wait that ran out reports itself), and a pool in which every
+replica fails.  No GPU is faulted or hung.
 """
 import importlib
 import os
@@ -111,3 +117,95 @@ def test_sharded_run_two_ranks_gloo():
     assert all(seen[i] == _work(i, secs[i]) for i in seen)
     a = disp.assign(secs, 2)
     assert sorted(gathered[0]) == [i for i in range(len(secs)) if a[i] == 0]
+
+
+class FakeReplica:
+    """Engine stand-in: one token per live utterance per step; tokens are a
+    function of the utterance id, so any replica gives the same result.
+    fail_after: raise on that step call; bad_status_after: report a non-zero
+    device status word from that step on (a bounded device wait that ran out)."""
+
+    def __init__(self, fail_after=None, bad_status_after=None, delay=0.0):
+        self.live, self.ready, self.steps = {}, {}, 0
+        self.fail_after, self.bad_status_after, self.delay = fail_after, bad_status_after, delay
+        self.seen = []
+
+    def _submit(self, uid, data, forced):
+        self.seen.append(uid)
+        self.live[uid] = [int(forced), 0]
+
+    submit_mel = submit_audio = submit = _submit
+
+    def step(self, n):
+        import time
+        self.steps += 1
+        if self.fail_after is not None and self.steps >= self.fail_after:
+            raise RuntimeError("step failed: -4")
+        time.sleep(self.delay)
+        for uid in list(self.live):
+            f, g = self.live[uid]
+            g = min(f, g + n)
+            if g >= f:
+                self.ready[uid] = (np.arange(f) + uid).astype(np.int32)
+                del self.live[uid]
+            else:
+                self.live[uid][1] = g
+        return len(self.live)
+
+    def poll(self):
+        out, self.ready = self.ready, {}
+        return out
+
+    def status(self):
+        return 1 if self.bad_status_after is not None and self.steps >= self.bad_status_after else 0
+
+
+def _items(n, seed=0):
+    rng = np.random.default_rng(seed)
+    secs = rng.uniform(1.0, 30.0, n)
+    return [(i, "mel", None, int(3 * s) + 1, float(s)) for i, s in enumerate(secs)]
+
+
+def _check(res, items):
+    assert sorted(res) == [it[0] for it in items]
+    for uid, _k, _d, f, _s in items:
+        assert np.array_equal(res[uid], np.arange(f) + uid)
+
+
+def test_pool_without_failures_balances_and_finishes_once():
+    items = _items(200)
+    reps = [FakeReplica() for _ in range(4)]
+    pool = disp.ReplicaPool(reps, steps_per_poll=8, max_in_flight=16)
+    res = pool.run(items)
+    _check(res, items)
+    assert pool.failed == []
+    assert sum(len(r.seen) for r in reps) == 200 and all(r.seen for r in reps)
+
+
+def test_pool_requeues_the_work_of_a_failing_replica():
+    items = _items(120, seed=1)
+    reps = [FakeReplica(delay=0.001), FakeReplica(fail_after=3, delay=0.001), FakeReplica(delay=0.001)]
+    pool = disp.ReplicaPool(reps, steps_per_poll=4, max_in_flight=8)
+    res = pool.run(items)
+    _check(res, items)
+    assert [f[0] for f in pool.failed] == [1] and "step failed" in pool.failed[0][1]
+    # the failed replica's unfinished utterances ran again on the others
+    rerun = set(reps[1].seen) & (set(reps[0].seen) | set(reps[2].seen))
+    assert rerun
+
+
+def test_pool_retires_a_replica_reporting_device_status():
+    items = _items(60, seed=2)
+    reps = [FakeReplica(bad_status_after=2), FakeReplica()]
+    pool = disp.ReplicaPool(reps, steps_per_poll=4, max_in_flight=8)
+    res = pool.run(items)
+    _check(res, items)
+    assert [f[0] for f in pool.failed] == [0] and "device status" in pool.failed[0][1]
+
+
+def test_pool_raises_when_every_replica_fails():
+    items = _items(20, seed=3)
+    pool = disp.ReplicaPool([FakeReplica(fail_after=1), FakeReplica(fail_after=2)], steps_per_poll=1)
+    with pytest.raises(disp.ReplicaFailed, match="every replica failed"):
+        pool.run(items)
+    assert sorted(f[0] for f in pool.failed) == [0, 1]
