@@ -471,6 +471,9 @@ def main():
     s_end = eng.stats()
     status = eng.status()
     launches = int(s_end["kernel_launches"] - s_start["kernel_launches"])
+    n_steps = s_end["steps"] - s_start["steps"]
+    # batch occupancy of the timed region: packed query rows per step (prefill rows included)
+    rows_per_step = (s_end["rows"] - s_start["rows"]) / n_steps if n_steps > 0 else None
     config4 = None
     if with_s:   # configuration 4, after the timed legs (its own wall-clock measurement)
         stream = importlib.import_module("cohere-transcribe_b200.stream")
@@ -596,7 +599,8 @@ def main():
             "p50_step_ms": statistics.median(step_times) if step_times else None,
             "config2": config2_summary(dev_c, wall_c, step_times_c, K) if with_c else None,
             ("config5" if args.stream_config == 5 else "config4"): config4,
-            "gpu_launches": launches, "roofline": roof, "rooflines": rooflines,
+            "gpu_launches": launches, "rows_per_step": rows_per_step, "steps_timed": int(n_steps),
+            "roofline": roof, "rooflines": rooflines,
             "profiled_step_breakdown": breakdown, "clocks": clk.summary(), "device_status": status,
             "precision": "bf16 weights, activations as bf16 hi+lo planes, fp32 accumulate" if args.precision else
             "bf16 weights and activations, fp32 accumulate"}

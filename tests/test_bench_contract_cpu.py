@@ -111,6 +111,7 @@ def test_bench_line_keys_and_units(bench_mod, capsys, monkeypatch):
     assert set(d["e2e"]) >= {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"}
     assert d["e2e"]["h2d_bytes_per_step"] > 0 and d["e2e"]["d2h_bytes_per_step"] > 0
     assert d["gpu_launches"] > 0
+    assert d["steps_timed"] > 0 and d["rows_per_step"] is not None
     r = d["roofline"]
     assert set(r) >= {"bound", "achieved", "peak", "unit", "frac", "traffic"}
     assert r["frac"] == pytest.approx(r["achieved"] / r["peak"])
