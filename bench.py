@@ -210,9 +210,14 @@ class ReferenceCPU:
     """The reference's CPU path (its model.h driving its backends/cpu/backend.c,
     prebuilt as oracle/_ref/libref_decode_cpu.so) on bounded samples of the
     workload, one utterance per host thread (as run_files_parallel does with one
-    CPU "device" per core), on the first n_threads utterances:
-      decode      cross K/V + 10-row prefill + greedy decode from the workload's
-                  encoder rows to min(forced length, cap) tokens -> tokens/s
+    CPU "device" per core):
+      decode      the n_threads utterances nearest the workload's mean forced
+                  length and mean T_enc: cross K/V + 10-row prefill + greedy
+                  decode from the workload's encoder rows to each utterance's
+                  forced length (cap > 0 caps it) -> tokens/s.  The sample's
+                  tokens per utterance then average the workload's, so the
+                  per-utterance cross-K/V and prefill cost is spread over as
+                  many tokens as in the GPU run.
       transcribe  encoder + decode of the first CPU_CUT_S seconds of each
                   utterance's log-mel, to min(forced, CPU_CUT_TOKENS) tokens
                   -> RTFx (audio seconds / wall seconds)."""
@@ -231,12 +236,18 @@ class ReferenceCPU:
         self.ws = W.weights_struct(self.wb)
         self.L.refh_bind_weights(ctypes.addressof(self.ws))
         n = n_threads
-        idx = np.arange(n) % len(case["T_enc"])
+        f_all, te_all = case["forced_len"].astype(np.float64), case["T_enc"].astype(np.float64)
+        # distance to the means, the forced length weighted 3x: the threads then
+        # finish close together (wall time = the longest thread)
+        near = 3.0 * np.abs(f_all - f_all.mean()) / f_all.mean() + np.abs(te_all - te_all.mean()) / te_all.mean()
+        idx = np.resize(np.argsort(near, kind="stable"), n)
         self.n = n
         self.T_enc = np.ascontiguousarray(case["T_enc"][idx], dtype=np.int32)
         self.Tm = int(self.T_enc.max())
         self.enc = np.ascontiguousarray(enc[idx, :self.Tm], dtype=np.float32)
-        self.forced = np.ascontiguousarray(np.minimum(case["forced_len"][idx], cap), dtype=np.int32)
+        forced = case["forced_len"][idx]
+        self.forced = np.ascontiguousarray(np.minimum(forced, cap) if cap > 0 else forced, dtype=np.int32)
+        self.workload_mean_tokens = float(f_all.mean())
         self.prompt = np.array(_in.ctb.PROMPT_FULL, np.int32)
         cut = _in.ctb.t_mel_of_seconds(CPU_CUT_S)
         self.T_mel_cut = np.full(n, cut, np.int32)
@@ -244,21 +255,33 @@ class ReferenceCPU:
         self.M = ctypes.CDLL(os.path.join(po.REF_DIR, "libref_mel.so"))
         self.M.refmel_compute.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
         self.forced_cut = np.ascontiguousarray(np.minimum(case["forced_len"][idx], CPU_CUT_TOKENS), dtype=np.int32)
-        self.sample = (f"first {n} utterances of the workload (T_enc {int(self.T_enc.min())}-{int(self.T_enc.max())}),"
-                       f" each cross-K/V + 10-token prefill + greedy decode to min(forced length, {cap}) tokens"
+        self.sample = (f"{n} utterances of the workload nearest its mean forced length and mean T_enc (T_enc "
+                       f"{int(self.T_enc.min())}-{int(self.T_enc.max())}, mean {self.T_enc.mean():.0f}; forced "
+                       f"{int(self.forced.min())}-{int(self.forced.max())} tokens, mean {self.forced.mean():.0f} "
+                       f"against the workload's {self.workload_mean_tokens:.0f}), each cross-K/V + 10-token prefill"
+                       f" + greedy decode to its forced length" + (f" capped at {cap}" if cap > 0 else "") +
                        f" ({int(self.forced.sum())} tokens), one utterance per host thread")
         self.sample_rtfx = (f"first {n} utterances of the workload cut to their first {CPU_CUT_S:g} s of audio,"
                             f" each log-mel front-end + encoder (48 layers) + prefill + greedy decode to"
                             f" {CPU_CUT_TOKENS} tokens, one utterance per host thread")
 
-    def decode(self):
+    def decode(self, warm: bool = False):
+        """One timed sample (tokens, seconds).  warm: a short untimed pass (two
+        tokens per thread on the shortest encoder rows) that pages in the code
+        and the weights."""
         po = self.po
         tokens = np.zeros((self.n, 1024), np.int32)
         n_tok = np.zeros(self.n, np.int32)
-        secs = self.L.refh_parallel_decode(self.n, self.n, po.fp(self.enc), po.ip(self.T_enc), self.Tm,
-                                           po.ip(self.prompt), len(self.prompt), po.ip(self.forced),
+        forced, T_enc, Tm, enc = self.forced, self.T_enc, self.Tm, self.enc
+        if warm:
+            forced = np.full(self.n, 2, np.int32)
+            T_enc = np.full(self.n, int(self.T_enc.min()), np.int32)
+            Tm = int(T_enc[0])
+            enc = np.ascontiguousarray(self.enc[:, :Tm])
+        secs = self.L.refh_parallel_decode(self.n, self.n, po.fp(enc), po.ip(T_enc), Tm,
+                                           po.ip(self.prompt), len(self.prompt), po.ip(forced),
                                            po.ip(tokens), po.ip(n_tok))
-        return int(self.forced.sum()), secs
+        return int(forced.sum()), secs
 
     def transcribe(self):
         po = self.po
@@ -297,7 +320,8 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-tokens", type=int, default=32, help="token cap per utterance of the CPU decode sample")
+    ap.add_argument("--cpu-tokens", type=int, default=0,
+                    help="token cap per utterance of the CPU decode sample (0 = each utterance's forced length)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--precision", type=int, default=1)
     ap.add_argument("--batch", type=int, default=BATCH, help="utterances per GPU per step (profiling cases)")
@@ -340,8 +364,7 @@ def main():
             return
         ref = ReferenceCPU(case, enc, audio, ncores, args.cpu_tokens)
         for _ in range(args.warmup):
-            ref.decode()
-            ref.transcribe()
+            ref.decode(warm=True)
         toks, secs, aud, tsecs = 0, 0.0, 0.0, 0.0
         for _ in range(args.steps):
             t, s_ = ref.decode()
@@ -356,7 +379,9 @@ def main():
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
                 "data": "synthetic", "config": cfg,
                 "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": ncores, "kind": "reference",
-                                 "sample": ref.sample},
+                                 "sample": ref.sample, "sample_tokens": int(ref.forced.sum()),
+                                 "sample_mean_tokens": float(ref.forced.mean()),
+                                 "workload_mean_tokens": ref.workload_mean_tokens},
                 "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                 "rtfx": {"value": aud / tsecs, "e2e": aud / tsecs, "unit": "audio s / s", "cores": ncores,
                          "sample": ref.sample_rtfx}}
@@ -609,7 +634,10 @@ def main():
         t, s_ = ref.decode()
         a_, s2 = ref.transcribe()
         line["cpu_baseline"] = {"value": t / s_, "unit": "tokens/s", "cores": ncores, "kind": "reference",
-                                "sample": ref.sample, "rtfx": a_ / s2, "rtfx_sample": ref.sample_rtfx}
+                                "sample": ref.sample, "sample_tokens": int(ref.forced.sum()),
+                                "sample_mean_tokens": float(ref.forced.mean()),
+                                "workload_mean_tokens": ref.workload_mean_tokens,
+                                "rtfx": a_ / s2, "rtfx_sample": ref.sample_rtfx}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

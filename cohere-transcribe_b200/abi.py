@@ -62,6 +62,7 @@ SIGNATURES = {
     "backend_sdp_attn_batch_decode_ca": (None, [_vp, _vp, _vp, _vp, _int, _int, _vp]),
     # extensions
     "ct_device_status": (_int, []),
+    "ct_selftest_bounded_wait": (_int, [_int, _int]),
     "ct_sdp_attn_batch_decode_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
     # engine (include/ct_engine.h)
     "ct_engine_create": (_int, [_vp, _int, _vp, _sz, _vp, _vp]),
@@ -80,6 +81,7 @@ SIGNATURES = {
     "ct_engine_log_mel": (_int, [_vp, _int, _vp, _vp, _vp]),
     "ct_engine_step_times": (_int, [_vp, _vp, _int]),
     "ct_engine_set_prompt": (_int, [_vp, _vp, _int]),
+    "ct_engine_last_logits": (_int, [_vp, _vp, _vp, _vp, _int]),
 }
 
 
@@ -204,6 +206,16 @@ class Engine:
         if n < 0:
             raise RuntimeError(f"poll failed: {n}")
         return {res[i].utt_id: toks[i, :res[i].n_tokens].copy() for i in range(n)}
+
+    def last_logits(self, vocab=16384, max_seqs=1024):
+        """Logits of the most recent step: {utt_id: (generated-token index, fp32 [vocab])}."""
+        lg = np.empty((max_seqs, vocab), np.float32)
+        ids = np.empty(max_seqs, np.int64)
+        gi = np.empty(max_seqs, np.int32)
+        n = self.lib.ct_engine_last_logits(self.h, lg.ctypes.data, ids.ctypes.data, gi.ctypes.data, max_seqs)
+        if n < 0:
+            raise RuntimeError(f"last_logits failed: {n}")
+        return {int(ids[i]): (int(gi[i]), lg[i].copy()) for i in range(n)}
 
     def stats(self):
         s = EngineStats()

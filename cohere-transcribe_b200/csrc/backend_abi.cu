@@ -528,6 +528,36 @@ extern "C" int ct_device_status(void) {
     return v;
 }
 
+// Extension (not in the reference ABI): one thread waits on an mbarrier phase
+// that nothing completes, with a budget of limit_ns, through the bounded wait
+// the pipelines use; it records `code` and returns when the budget runs out.
+__global__ void selftest_wait_kernel(uint64_t limit_ns, int code, unsigned long long *elapsed_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    const uint64_t t0 = globaltimer();
+    const bool arrived = mbar_wait_for(&bar, 0, code, limit_ns);
+    *elapsed_ns = arrived ? 0ull : (unsigned long long)(globaltimer() - t0);
+}
+
+extern "C" int ct_selftest_bounded_wait(int limit_us, int code) {
+    if (limit_us < 1 || limit_us > 1000000 || code < 1 || code > 255) return -1;
+    unsigned long long *el = nullptr;
+    if (cudaMallocHost(&el, sizeof(*el)) != cudaSuccess) return -4;
+    *el = 0;
+    int v = 0, zero = 0;
+    cudaError_t e = cudaSuccess;
+    selftest_wait_kernel<<<1, 32>>>((uint64_t)limit_us * 1000ull, code, el);
+    if ((e = cudaGetLastError()) == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_ct_status, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_ct_status, &zero, sizeof(int));
+    // the wait must have lasted its budget (the timer is checked every 256 polls)
+    if (e == cudaSuccess && v == code && *el < (unsigned long long)limit_us * 1000ull) v = -4;
+    cudaFreeHost(el);
+    return e == cudaSuccess ? v : -4;
+}
+
 // Extension (not in the reference ABI): the library's tensor-core GEMM on
 // caller-held bf16 activation planes; Y = act(X W^T + b), fp32 out.
 extern "C" int ct_linear_bf16(float *Y, int ldy, const uint16_t *X_hi, const uint16_t *X_lo, const uint16_t *W,

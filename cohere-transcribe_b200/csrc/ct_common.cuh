@@ -93,17 +93,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-// Bounded wait; returns false (and records `code`) on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code) {
+// Bounded wait of at most budget_ns; returns false (and records `code`) on timeout.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, int code, uint64_t budget_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 0;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 255u && globaltimer() - t0 > CT_WAIT_NS) {
+        if ((it & 255u) == 255u && globaltimer() - t0 > budget_ns) {
             set_status(code);
             return false;
         }
     }
+}
+// Bounded wait with the library's budget (CT_WAIT_NS).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code) {
+    return mbar_wait_for(bar, parity, code, CT_WAIT_NS);
 }
 
 // ---- TMA --------------------------------------------------------------------

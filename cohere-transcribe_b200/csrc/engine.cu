@@ -1403,6 +1403,28 @@ extern "C" int ct_engine_step_times(ct_engine *e, float *out, int max) {
     return n;
 }
 
+extern "C" int ct_engine_last_logits(ct_engine *e, float *logits, long long *utt_ids, int *gen_index, int max) {
+    if (!e || max < 0 || (max > 0 && (!logits || !utt_ids || !gen_index))) return CT_EINVAL;
+    if (e->n_steps == 0 || max == 0) return 0;
+    EK(cudaSetDevice(e->device));
+    EK(cudaStreamSynchronize(e->st));
+    int n = 0;
+    EK(cudaMemcpy(&n, e->ds.n_seqs, sizeof(int), cudaMemcpyDeviceToHost));
+    n = std::min(n, max);
+    if (n <= 0) return 0;
+    std::vector<int> qs(n), gen(e->cfg.max_slots);
+    EK(cudaMemcpy(qs.data(), e->ds.q_slot, sizeof(int) * n, cudaMemcpyDeviceToHost));
+    EK(cudaMemcpy(gen.data(), e->ds.gen, sizeof(int) * e->cfg.max_slots, cudaMemcpyDeviceToHost));
+    EK(cudaMemcpy(logits, e->logits, sizeof(float) * (size_t)n * V, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < n; ++i) {
+        const int slot = qs[i];
+        if (slot < 0 || slot >= e->cfg.max_slots) return CT_EDEVICE;
+        utt_ids[i] = e->slot_id[slot];
+        gen_index[i] = gen[slot] - 1;   // the argmax kernel counted this step's token
+    }
+    return n;
+}
+
 extern "C" int ct_engine_status(ct_engine *e) {
     if (!e) return CT_EINVAL;
     EK(cudaSetDevice(e->device));

@@ -133,9 +133,13 @@ void make_rel_pos_emb(cudaStream_t st, float *pe, int T, int D) {
 // ---------------------------------------------------------------- attention
 static constexpr int ACH = 128;   // keys per chunk (one per thread)
 
+// Keys of row r.  A length above len_max is clamped to it and one of zero or
+// less leaves the row with no keys (attn_chunk_kernel writes zeros); both set
+// CT_STATUS_BAD_ARG in the device status word.
 __device__ __forceinline__ int attn_len(const AttnRows &a, int r) {
     int L = a.len_arr ? a.len_arr[r] : (a.len_dev ? *a.len_dev : a.len_const);
     if (L > a.len_max) { set_status(CT_STATUS_BAD_ARG); L = a.len_max; }
+    if (L <= 0) { set_status(CT_STATUS_BAD_ARG); L = 0; }
     return L;
 }
 
@@ -147,6 +151,10 @@ __global__ void __launch_bounds__(ACH) attn_chunk_kernel(const AttnRows a, float
     const int r = blockIdx.z, h = blockIdx.y, c = blockIdx.x;
     const int L = attn_len(a, r);
     const int nck = (L + ACH - 1) / ACH;
+    if (L == 0 && c == 0) {   // no keys (a bad length): the output row is defined as zero
+        for (int d = threadIdx.x; d < a.DK; d += ACH) a.out[(size_t)r * a.ldo + h * a.DK + d] = 0.0f;
+        return;
+    }
     if (c >= nck) return;
     const int DK = a.DK, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     for (int d = tid; d < DK; d += ACH) qs[d] = a.Q[(size_t)r * a.ldq + h * DK + d];

@@ -43,6 +43,14 @@ extern "C" int ct_sdp_attn_batch_decode_noalloc(float *out, const float *Q, cons
         if (!g_noalloc_dev_ptr[dev]) {
             void *p = nullptr;
             if (cudaGetSymbolAddress(&p, g_noalloc_attn_scratch) != cudaSuccess || !p) return CT_NOALLOC_ECUDA;
+            // With lazy module loading a kernel is loaded at its first launch,
+            // which may allocate or synchronise; querying both kernels here
+            // loads them now, so a later call (e.g. the first one long enough
+            // to need the combine kernel) loads nothing.
+            cudaFuncAttributes fa;
+            if (cudaFuncGetAttributes(&fa, attn_chunk_kernel) != cudaSuccess ||
+                cudaFuncGetAttributes(&fa, attn_combine_kernel) != cudaSuccess)
+                return CT_NOALLOC_ECUDA;
             g_noalloc_dev_ptr[dev] = static_cast<float *>(p);
         }
         scratch = g_noalloc_dev_ptr[dev];
@@ -53,6 +61,9 @@ extern "C" int ct_sdp_attn_batch_decode_noalloc(float *out, const float *Q, cons
     a.mask = nullptr; a.mask_ld = 0; a.out = out; a.ldo = DEC_D;
     a.R = B; a.H = DEC_H; a.DK = DEC_DK; a.scale = 1.0f / sqrtf((float)DEC_DK);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // an error left pending by unrelated earlier work stays for its owner to
+    // read; this call launches nothing and reports it
+    if (cudaPeekAtLastError() != cudaSuccess) return CT_NOALLOC_ECUDA;
     const int nck = (T_k_stride + 127) / 128;
     attn_chunk_kernel<<<dim3(nck, DEC_H, B), 128, 0, st>>>(a, scratch, nck);
     if (cudaGetLastError() != cudaSuccess) return CT_NOALLOC_ECUDA;

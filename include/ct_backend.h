@@ -118,6 +118,18 @@ void backend_sdp_attn_batch_decode_ca(float *out, const float *Q,
  * in the reference. */
 int ct_device_status(void);
 
+/* Self-test of the bounded device waits.  No counterpart in the reference
+ * (its kernels never wait on one another).  Launches one small kernel on the
+ * current device that waits, through the same bounded mbarrier wait every
+ * pipeline of this library uses, on a barrier phase that nothing ever
+ * completes; after limit_us microseconds (1 .. 1000000) the wait gives up,
+ * records `code` (1 .. 255) in the device status word and the kernel returns.
+ * The call synchronises, then reads and clears the status word and returns
+ * it, so a caller sees `code` when the wait expired as designed; -1 for bad
+ * arguments, -4 when a CUDA call failed.  Needs no backend_init and leaves the
+ * context usable. */
+int ct_selftest_bounded_wait(int limit_us, int code);
+
 /* Batched decode attention that allocates nothing.  No counterpart in the
  * reference: it is the no-allocation form of backend_sdp_attn_batch_decode_sa
  * / _ca for callers that cannot call cudaMalloc -- code running under CUDA
@@ -133,9 +145,15 @@ int ct_device_status(void);
  * must fit in it (e.g. B <= 64 with T_k_stride <= MAX_SEQ), else the call
  * returns CT_NOALLOC_ETOOBIG and launches nothing.  The first call on a device
  * looks up the array's device address (once per device, with that device
- * current), so make that first call before any stream capture.  Calls share
- * the array: calls that overlap on the GPU race and must be serialised.
- * Returns 0, CT_NOALLOC_EINVAL, CT_NOALLOC_ETOOBIG or CT_NOALLOC_ECUDA. */
+ * current) and loads both of its kernels, so make that first call before any
+ * stream capture.  Calls share the array: calls that overlap on the GPU race
+ * and must be serialised.  A lens[b] above T_k_stride is clamped to it; one of
+ * zero or less gives item b an all-zero output row; both set the library's
+ * device status word, which ct_device_status reads and clears (that reader
+ * needs backend_init on the calling thread).  Returns 0, CT_NOALLOC_EINVAL,
+ * CT_NOALLOC_ETOOBIG or CT_NOALLOC_ECUDA; ECUDA is also returned, with nothing
+ * launched, when an earlier CUDA error is already pending on the calling
+ * thread (that error is left in place for the code that caused it). */
 #define CT_NOALLOC_ATTN_SCRATCH_FLOATS (64 * DEC_H * ((MAX_SEQ + 127) / 128) * (DEC_DK + 2))
 #define CT_NOALLOC_EINVAL (-1)
 #define CT_NOALLOC_ETOOBIG (-2)

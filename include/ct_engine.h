@@ -149,6 +149,16 @@ int ct_engine_step_times(ct_engine *e, float *out, int max);
  * Returns the JSON length (written truncated to cap - 1 bytes). */
 int ct_engine_profile_report(ct_engine *e, char *buf, int cap);
 
+/* Logits of the most recent packed step, for checking them against a
+ * reference (model.h:721-744 computes the same [B, VOCAB] logits before its
+ * argmax, backend_lm_head_batch, backends/backend.h:192-194).  For each
+ * sequence of that step, up to max: its VOCAB fp32 logits at
+ * logits + i * VOCAB (the row the greedy argmax chose from), its utterance id
+ * in utt_ids[i] and, in gen_index[i], which generated token they chose (0 =
+ * the token after the prompt).  Call it after ct_engine_step(e, 1), before the
+ * next step.  Returns the number of sequences written. */
+int ct_engine_last_logits(ct_engine *e, float *logits, long long *utt_ids, int *gen_index, int max);
+
 /* Read (and clear) the device status word; 0 when no kernel reported a problem. */
 int ct_engine_status(ct_engine *e);
 

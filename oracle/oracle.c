@@ -521,11 +521,14 @@ void orc_decoder_step_decode_batch(const ct_dims *d, const Weights *W,
 }
 
 /* transcribe.c:686-795 (per-item prefill then the joint decode loop), driven
- * from encoder outputs, with forced-EOS lengths and optional teacher forcing. */
-int orc_decode_batch(const ct_dims *d, const Weights *W, int B, const int *T_enc, int T_enc_stride,
-                     const float *enc_h_batch, const int *prompt, int n_prompt,
-                     const int *forced_len, const int *force_tokens,
-                     int *tokens, int *n_tok, int *am, float *margin) {
+ * from encoder outputs, with forced-EOS lengths and optional teacher forcing.
+ * logits_out (optional, [B][logits_cap][V]) receives the logits that chose
+ * generated token g of sequence b, for g < logits_cap (g = 0: the prefill's). */
+int orc_decode_batch_logits(const ct_dims *d, const Weights *W, int B, const int *T_enc, int T_enc_stride,
+                            const float *enc_h_batch, const int *prompt, int n_prompt,
+                            const int *forced_len, const int *force_tokens,
+                            int *tokens, int *n_tok, int *am, float *margin,
+                            float *logits_out, int logits_cap) {
     const int D = d->dec_d, L = d->dec_n, MS = d->max_seq, V = d->vocab;
     float **ca_k = XMALLOC(sizeof(float *) * L), **ca_v = XMALLOC(sizeof(float *) * L);
     float **sa_k = XMALLOC(sizeof(float *) * L), **sa_v = XMALLOC(sizeof(float *) * L);
@@ -560,6 +563,7 @@ int orc_decode_batch(const ct_dims *d, const Weights *W, int B, const int *T_enc
         orc_top2(lg, V, &id, &mg);
         if (am) am[(size_t)b * MS + n_prompt] = id;
         if (margin) margin[(size_t)b * MS + n_prompt] = mg;
+        if (logits_out && logits_cap > 0) memcpy(logits_out + (size_t)b * logits_cap * V, lg, sizeof(float) * V);
         gen[b] = 1;
         if (force_tokens) id = force_tokens[(size_t)b * MS + n_prompt];
         if (gen[b] >= forced_len[b]) id = CT_TOK_EOS;
@@ -583,6 +587,8 @@ int orc_decode_batch(const ct_dims *d, const Weights *W, int B, const int *T_enc
             orc_top2(lg + (size_t)b * V, V, &id, &mg);
             if (am) am[(size_t)b * MS + S[b]] = id;
             if (margin) margin[(size_t)b * MS + S[b]] = mg;
+            if (logits_out && gen[b] < logits_cap)
+                memcpy(logits_out + ((size_t)b * logits_cap + gen[b]) * V, lg + (size_t)b * V, sizeof(float) * V);
             gen[b]++;
             if (force_tokens) id = force_tokens[(size_t)b * MS + S[b]];
             if (gen[b] >= forced_len[b]) id = CT_TOK_EOS;
@@ -596,6 +602,14 @@ int orc_decode_batch(const ct_dims *d, const Weights *W, int B, const int *T_enc
     free(ca_k); free(ca_v); free(sa_k); free(sa_v); free(lg); free(h); free(S); free(S_dev);
     free(active); free(cur); free(next); free(gen); free(cak_b); free(cav_b); free(sak_b); free(sav_b);
     return 0;
+}
+
+int orc_decode_batch(const ct_dims *d, const Weights *W, int B, const int *T_enc, int T_enc_stride,
+                     const float *enc_h_batch, const int *prompt, int n_prompt,
+                     const int *forced_len, const int *force_tokens,
+                     int *tokens, int *n_tok, int *am, float *margin) {
+    return orc_decode_batch_logits(d, W, B, T_enc, T_enc_stride, enc_h_batch, prompt, n_prompt, forced_len,
+                                   force_tokens, tokens, n_tok, am, margin, NULL, 0);
 }
 
 /* ------------------------------------------------------------------ */

@@ -99,6 +99,15 @@ int orc_decode_batch(const ct_dims *d, const Weights *W, int B, const int *T_enc
                      const int *forced_len, const int *force_tokens,
                      int *tokens, int *n_tok, int *am, float *margin);
 
+/* orc_decode_batch that also returns logits: logits_out [B, logits_cap, vocab]
+ * holds the logits that chose generated token g of sequence b, for
+ * g < logits_cap (g = 0 is the prefill's token). */
+int orc_decode_batch_logits(const ct_dims *d, const Weights *W, int B, const int *T_enc, int T_enc_stride,
+                            const float *enc_h_batch, const int *prompt, int n_prompt,
+                            const int *forced_len, const int *force_tokens,
+                            int *tokens, int *n_tok, int *am, float *margin,
+                            float *logits_out, int logits_cap);
+
 /* top-1 index and (top1 - top2) over n logits */
 void orc_top2(const float *lg, int n, int *idx, float *margin);
 

@@ -5,6 +5,8 @@
   _ref/libref_decode_cpu.so the reference's model.h driven by ref_harness.c on
                             the reference CPU backend (full-size dims)
   _ref/libref_decode_tiny.so the same at the tiny configuration's dims
+  _ref/libref_decode_cuda.so the reference's model.h on its own CUDA backend
+                            (backends/cuda/backend.cu, sm_100a; GPU host only)
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU legs import this module.
 """
@@ -93,12 +95,14 @@ def lib() -> ctypes.CDLL:
             "orc_encoder_forward_batch": [D, _vp, _f, ctypes.c_int, ctypes.c_int, _i, _i, ctypes.c_int, _f],
             "orc_decode_batch": [D, _vp, ctypes.c_int, _i, ctypes.c_int, _f, _i, ctypes.c_int, _i, _i,
                                  _i, _i, _i, _f],
+            "orc_decode_batch_logits": [D, _vp, ctypes.c_int, _i, ctypes.c_int, _f, _i, ctypes.c_int, _i, _i,
+                                        _i, _i, _i, _f, _f, ctypes.c_int],
             "orc_compute_mel": [_f, ctypes.c_int, _f],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)
             fn.argtypes = args
-            fn.restype = ctypes.c_int if name in ("orc_argmax", "orc_decode_batch") else None
+            fn.restype = ctypes.c_int if name in ("orc_argmax", "orc_decode_batch", "orc_decode_batch_logits") else None
         _lib = L
     return _lib
 
@@ -128,6 +132,9 @@ def bind_ref_decode(L: ctypes.CDLL) -> ctypes.CDLL:
         L.refh_parallel_transcribe.argtypes = [ctypes.c_int, ctypes.c_int, _f, ctypes.c_int, _i, _i, ctypes.c_int,
                                                _i, _i, _i]
         L.refh_parallel_transcribe.restype = ctypes.c_double
+    if hasattr(L, "refh_capture_logits"):
+        L.refh_capture_logits.argtypes = [_f, ctypes.c_int]
+        L.refh_capture_logits.restype = None
     for fn in ("backend_weights_upload_blob",):
         getattr(L, fn).argtypes = [_vp, ctypes.c_size_t]
         getattr(L, fn).restype = None
@@ -147,9 +154,11 @@ def null_f():
 
 
 def decode_batch(dims: dict, wstruct, enc_h: np.ndarray, T_enc: np.ndarray, prompt,
-                 forced_len, force_tokens=None, want_margin=True):
+                 forced_len, force_tokens=None, want_margin=True, logits_cap: int = 0):
     """Run orc_decode_batch.  enc_h: [B, T_enc_stride, dec_d] float32.
-    Returns (tokens [B,max_seq], n_tok [B], argmax [B,max_seq], margin [B,max_seq])."""
+    Returns (tokens [B,max_seq], n_tok [B], argmax [B,max_seq], margin [B,max_seq]);
+    with logits_cap > 0 also logits [B, logits_cap, vocab] of generated tokens
+    0 .. logits_cap - 1 (orc_decode_batch_logits)."""
     L = lib()
     d = dims_struct(dims)
     B, stride, _ = enc_h.shape
@@ -162,10 +171,14 @@ def decode_batch(dims: dict, wstruct, enc_h: np.ndarray, T_enc: np.ndarray, prom
     am = np.full((B, ms), -1, np.int32)
     mg = np.full((B, ms), np.nan, np.float32)
     ft = None if force_tokens is None else np.ascontiguousarray(force_tokens, dtype=np.int32)
-    L.orc_decode_batch(ctypes.byref(d), ctypes.addressof(wstruct), B, ip(T_enc), stride,
-                       fp(np.ascontiguousarray(enc_h, dtype=np.float32)), ip(prompt), len(prompt),
-                       ip(forced), ip(ft) if ft is not None else null_i(), ip(tokens), ip(n_tok),
-                       ip(am), fp(mg) if want_margin else null_f())
+    lg = np.zeros((B, logits_cap, dims["vocab"]), np.float32) if logits_cap > 0 else None
+    L.orc_decode_batch_logits(ctypes.byref(d), ctypes.addressof(wstruct), B, ip(T_enc), stride,
+                              fp(np.ascontiguousarray(enc_h, dtype=np.float32)), ip(prompt), len(prompt),
+                              ip(forced), ip(ft) if ft is not None else null_i(), ip(tokens), ip(n_tok),
+                              ip(am), fp(mg) if want_margin else null_f(),
+                              fp(lg) if lg is not None else null_f(), logits_cap)
+    if lg is not None:
+        return tokens, n_tok, am, mg, lg
     return tokens, n_tok, am, mg
 
 

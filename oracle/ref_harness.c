@@ -28,6 +28,14 @@ int verbose = 0;
 /* Copy a table of host weight pointers (same struct as model.h's W). */
 void refh_bind_weights(const Weights *w) { W = *w; }
 
+/* Optional logits capture of the next decode calls on this thread: buf
+ * [count][cap][VOCAB] receives the logits that chose generated token g of item
+ * b for g < cap (g = 0: the prefill's token).  Needs am or margin (the logits
+ * are read back only then).  cap = 0 switches it off. */
+static __thread float *g_lg_buf = NULL;
+static __thread int g_lg_cap = 0;
+void refh_capture_logits(float *buf, int cap) { g_lg_buf = buf; g_lg_cap = buf ? cap : 0; }
+
 #ifndef EMBEDDED_MODEL
 #include <unistd.h>
 /* The reference's own model-file loader (model.h load_weights: sf_load of
@@ -138,6 +146,7 @@ static void decode_loop(Arena *a, int count, const int *T_mel, const int *T_enc,
         if (am || margin) {
             float mg; int i2;
             backend_dtoh(lg_host, a->work, VOCAB * sizeof(float));
+            if (g_lg_cap > 0) memcpy(g_lg_buf + (size_t)b * g_lg_cap * VOCAB, lg_host, sizeof(float) * VOCAB);
             top2(lg_host, &i2, &mg);
             if (am) am[(size_t)b * MAX_SEQ + n_prompt] = i2;
             if (margin) margin[(size_t)b * MAX_SEQ + n_prompt] = mg;
@@ -170,6 +179,9 @@ static void decode_loop(Arena *a, int count, const int *T_mel, const int *T_enc,
             if (am || margin) {
                 float mg; int i2;
                 top2(lg_host + (size_t)b * VOCAB, &i2, &mg);
+                if (gen[b] < g_lg_cap)
+                    memcpy(g_lg_buf + ((size_t)b * g_lg_cap + gen[b]) * VOCAB, lg_host + (size_t)b * VOCAB,
+                           sizeof(float) * VOCAB);
                 if (am) am[(size_t)b * MAX_SEQ + S[b]] = id;
                 if (margin) margin[(size_t)b * MAX_SEQ + S[b]] = mg;
             }

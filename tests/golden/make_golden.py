@@ -131,4 +131,7 @@ def make_longform_fixture() -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CT_REFERENCE_DIR", "/root/reference"))
+    ref_dir = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CT_REFERENCE_DIR", "")
+    if not ref_dir:
+        sys.exit("usage: make_golden.py <reference tree> (or set CT_REFERENCE_DIR)")
+    main(ref_dir)

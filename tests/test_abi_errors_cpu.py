@@ -120,3 +120,12 @@ def test_linear_bf16_rejects_bad_shapes_and_alignment(lib):
     assert call(W=a + 2) == -1         # TMA bases are 16-byte aligned
     assert call(X_lo=a + 8) == -1
     assert call(Y=None) == -1
+
+
+def test_bounded_wait_selftest_rejects_bad_arguments(lib):
+    """ct_selftest_bounded_wait checks its budget (1 us .. 1 s) and code
+    (1 .. 255) before any CUDA call."""
+    assert lib.ct_selftest_bounded_wait(0, 1) == CT_EINVAL
+    assert lib.ct_selftest_bounded_wait(100, 0) == CT_EINVAL
+    assert lib.ct_selftest_bounded_wait(100, 256) == CT_EINVAL
+    assert lib.ct_selftest_bounded_wait(2000000, 1) == CT_EINVAL

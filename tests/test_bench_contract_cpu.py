@@ -133,9 +133,11 @@ def test_reference_arm_line(bench_mod, capsys, monkeypatch):
     class StandInReference:
         def __init__(self, case, enc, audio, n, cap):
             self.sample, self.sample_rtfx = "stand-in", "stand-in"
+            self.forced = np.array([40, 60], np.int32)
+            self.workload_mean_tokens = 50.0
 
-        def decode(self):
-            return 100, 2.0
+        def decode(self, warm=False):
+            return (4, 0.5) if warm else (100, 2.0)
 
         def transcribe(self):
             return 8.0, 4.0
@@ -147,6 +149,7 @@ def test_reference_arm_line(bench_mod, capsys, monkeypatch):
     assert d["cpu_baseline"]["kind"] == "reference" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["rtfx"]["value"] == pytest.approx(2.0)
+    assert d["cpu_baseline"]["sample_tokens"] == 100 and d["cpu_baseline"]["sample_mean_tokens"] == 50.0
 
 
 def test_stream_leg_summary(bench_mod, capsys, monkeypatch):

@@ -78,6 +78,62 @@ def test_encoder_ragged_batch_vs_oracle(abi, full_model, wmod):
         assert err <= ENC_TOL, (b, err)
 
 
+def test_encoder_long_vs_reference(abi, full_model):
+    """The benchmark's lengths: 30 s, 10 s and 1.3 s (T_enc 376, 126 and 17)
+    packed in one encoder batch, against the reference's own encoder
+    (model.h:573-609 on backends/cpu/backend.c, compiled from the reference
+    sources; tests/golden/make_encoder_long.py recorded its rows).  376 and
+    126 rows cover several 64-key tiles of the relative-position attention:
+    the online-softmax rescaling across tiles, position-table rows
+    k - q + T_max - 1 far from the diagonal, and the depthwise-convolution
+    halo between tiles.  Same weights as the other tests of this module
+    (seed 21)."""
+    import make_encoder_long as mel_long
+    gold = np.load(po.os.path.join(po.os.path.dirname(inputs.__file__), "encoder_long_ref.npz"))
+    mel, T_mel = mel_long.case()
+    assert mel_long.WEIGHT_SEED == 21
+    T_enc = t_enc_of(T_mel)
+    assert list(T_enc) == [376, 126, 17]
+    for b in range(len(T_mel)):
+        assert np.isclose(mel[b, :, :T_mel[b]].astype(np.float64).sum(), float(gold[f"checksum{b}"]))
+    eng = make_engine(abi, full_model)
+    try:
+        got = eng.encode(mels_of(mel, T_mel))
+        assert eng.status() == 0
+    finally:
+        eng.close()
+    errs = []
+    for b in range(len(T_mel)):
+        ref = gold[f"enc{b}"]
+        assert got[b].shape == ref.shape
+        err = float(np.max(np.abs(got[b] - ref)) / np.max(np.abs(ref)))
+        errs.append(err)
+        # per 64-row tile as well, so an error confined to a later key tile shows
+        for r0 in range(0, ref.shape[0], 64):
+            e_t = float(np.max(np.abs(got[b][r0:r0 + 64] - ref[r0:r0 + 64])) / np.max(np.abs(ref)))
+            assert e_t <= ENC_TOL, (b, r0, e_t)
+    print("encoder max error / output scale per utterance (T_enc 376, 126, 17):", errs)
+    assert max(errs) <= ENC_TOL, errs
+
+
+def test_encoder_batch_invariance_long(abi, full_model):
+    """Utterances past one 64-row tile (T_enc 376, 251, 126, 70, 17) encoded
+    together equal their runs alone."""
+    mel, T_mel = inputs.mel_batch([30.0, 20.0, 10.0, 5.55, 1.3], seed=703)
+    assert t_enc_of(T_mel).min() < 64 < t_enc_of(T_mel).max()
+    mels = mels_of(mel, T_mel)
+    eng = make_engine(abi, full_model)
+    try:
+        together = eng.encode(mels)
+        alone = [eng.encode([m])[0] for m in mels]
+        assert eng.status() == 0
+    finally:
+        eng.close()
+    for b in range(len(mels)):
+        err = float(np.max(np.abs(together[b] - alone[b])))
+        assert err <= 1e-6 * float(np.max(np.abs(alone[b]))), (b, err)
+
+
 def test_encoder_batch_invariance(abi, full_model):
     """An utterance's encoder rows do not depend on the other utterances of
     the packed batch (row-wise GEMMs without K splits; attention and the
