@@ -70,6 +70,7 @@ BATCH = 64
 CPU_CUT_S = 1.0        # seconds of log-mel per utterance in the CPU transcription sample
 CPU_CUT_TOKENS = 8     # generated-token cap per utterance in the CPU transcription sample
 CFG2_SECONDS, CFG2_TOKENS = 30.0, 200   # configuration 2: one 30 s utterance, EOS forced at the 200th token
+CUDA_REF_SAMPLE = 16   # utterances in the reference CUDA backend's decode sample
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one ncu capture
 # per kernel class, on a smaller case than the bench's, with the units that
@@ -91,16 +92,27 @@ NCU_TRAFFIC = {
 }
 
 
+# Sharding weight of a generated token against an audio second: on one B200
+# the packed encoder takes ~0.14 ms per audio second (156 ms for 1,110 s) and
+# a 64-sequence decode step ~0.0105 ms per sequence (0.675 ms), so about 13
+# generated tokens cost as much as one second of audio.
+DECODE_TOKENS_PER_AUDIO_S = 13.0
+
+
 def workload(seed: int = 0, batch: int = BATCH, rank: int = 0, world: int = 1):
     """Configuration 3: seconds ~ U(5, 30), forced lengths ~ U{20..220}; log-mel
     N(0, 1) [128, 100 s + 1] per utterance; encoder rows N(0, 1) [T_enc, 1024].
-    With world > 1 the job is batch * world utterances, dispatched by queued
-    audio seconds; this rank's shard is returned (inputs seeded per utterance,
-    so a shard is generated alone)."""
+    With world > 1 the job is batch * world utterances, dispatched least
+    queued work first, where an utterance's work is its audio seconds plus its
+    forced token count / DECODE_TOKENS_PER_AUDIO_S (the forced lengths are
+    drawn independently of the durations, so audio seconds alone would leave
+    the ranks' decode work unequal); this rank's shard is returned (inputs
+    seeded per utterance, so a shard is generated alone)."""
     import inputs
     disp = importlib.import_module("cohere-transcribe_b200.dispatch")
     full = inputs.ragged_decode_case(batch * world, seed=seed, t_lo=5.0, t_hi=30.0, l_lo=20, l_hi=220)
-    idx = np.array([i for i, _ in disp.shard(list(range(batch * world)), full["seconds"], rank, world)], np.int64)
+    work = full["seconds"] + full["forced_len"] / DECODE_TOKENS_PER_AUDIO_S
+    idx = np.array([i for i, _ in disp.shard(list(range(batch * world)), work, rank, world)], np.int64)
     case = {k: (v[idx] if isinstance(v, np.ndarray) else v) for k, v in full.items()}
     case["index"] = idx
     T_enc = case["T_enc"]
@@ -298,6 +310,66 @@ class ReferenceCPU:
         return self.n * CPU_CUT_S, secs
 
 
+class ReferenceCUDA:
+    """The reference's own CUDA backend on this GPU: backends/cuda/backend.cu
+    compiled from the reference sources for sm_100a (oracle/Makefile
+    `ref-cuda`), driven by the reference's model.h decode loop through
+    oracle/ref_harness.c -- the kernels this repository replaces, on the same
+    B200 and inputs.  Measured on bounded samples (wall time of the harness
+    call: encoder-row upload, cross K/V precompute, per-utterance prefill and
+    the batched decode loop with its host argmax, as model.h runs them):
+      decode    the n utterances of the workload nearest its mean forced length
+                and mean T_enc (the CPU sample's rule), decoded together to
+                their forced lengths -> tokens/s;
+      config2   one 30 s utterance's encoder rows (T_enc 376), 200 tokens at
+                batch 1 -> tokens/s and ms per token."""
+
+    def __init__(self, ws, case, enc, n: int):
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import pyoracle as po
+        self.po = po
+        L = po.ref_lib("libref_decode_cuda.so")
+        self.L = po.bind_ref_decode(L) if L is not None else None
+        self.ws = ws
+        f_all, te_all = case["forced_len"].astype(np.float64), case["T_enc"].astype(np.float64)
+        near = 3.0 * np.abs(f_all - f_all.mean()) / f_all.mean() + np.abs(te_all - te_all.mean()) / te_all.mean()
+        idx = np.sort(np.argsort(near, kind="stable")[:n])
+        self.T_enc = np.ascontiguousarray(case["T_enc"][idx], dtype=np.int32)
+        self.Tm = int(self.T_enc.max())
+        self.enc = np.ascontiguousarray(enc[idx, :self.Tm], dtype=np.float32)
+        self.forced = np.ascontiguousarray(case["forced_len"][idx], dtype=np.int32)
+        self.sample = (f"{len(idx)} utterances of the workload nearest its mean forced length and mean T_enc "
+                       f"(T_enc {int(self.T_enc.min())}-{self.Tm}, forced {int(self.forced.min())}-"
+                       f"{int(self.forced.max())} tokens, {int(self.forced.sum())} in all) decoded as one batch")
+
+    def _decode(self, wb, enc, T_enc, forced):
+        po, L = self.po, self.L
+        import inputs as _in
+        B = len(T_enc)
+        prompt = np.array(_in.ctb.PROMPT_FULL, np.int32)
+        tokens = np.zeros((B, 1024), np.int32)
+        n_tok = np.zeros(B, np.int32)
+        L.backend_weights_upload_blob(wb.ptr(), wb.nbytes)
+        L.refh_bind_weights(ctypes.addressof(self.ws))
+        L.backend_init(0)
+        secs = L.refh_decode_from_enc(B, po.fp(enc), po.ip(T_enc), enc.shape[1], po.ip(prompt), len(prompt),
+                                      po.ip(forced), po.null_i(), po.ip(tokens), po.ip(n_tok), po.null_i(),
+                                      po.null_f())
+        L.backend_destroy()
+        return int(forced.sum()), secs
+
+    def run(self, wb):
+        if self.L is None:
+            return None
+        t, s_ = self._decode(wb, self.enc, self.T_enc, self.forced)
+        enc2 = np.random.default_rng([0, 620]).standard_normal((1, 376, 1024), dtype=np.float32)
+        t2, s2 = self._decode(wb, enc2, np.array([376], np.int32), np.array([CFG2_TOKENS], np.int32))
+        return {"value": t / s_, "unit": "tokens/s", "kind": "reference CUDA backend (backends/cuda/backend.cu, "
+                "sm_100a) on this B200", "sample": self.sample, "sample_tokens": t,
+                "config2": {"tokens_per_s": t2 / s2, "ms_per_token": 1000.0 * s2 / t2,
+                            "sample": f"one utterance of T_enc 376 (30 s) from encoder rows, {t2} tokens"}}
+
+
 def config2_summary(dev, wall_s, step_times, K):
     """Configuration 2 (batch 1, one 30 s utterance, 200 tokens) from K timed runs:
     device times from the engine's CUDA events (encoder, admission, steps),
@@ -323,6 +395,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=0,
                     help="token cap per utterance of the CPU decode sample (0 = each utterance's forced length)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cuda-ref", action="store_true", help="skip the reference CUDA backend leg")
     ap.add_argument("--precision", type=int, default=1)
     ap.add_argument("--batch", type=int, default=BATCH, help="utterances per GPU per step (profiling cases)")
     ap.add_argument("--kv-pages", type=int, default=0, help="page-pool size (0 = engine default)")
@@ -638,6 +711,8 @@ def main():
                                 "sample_mean_tokens": float(ref.forced.mean()),
                                 "workload_mean_tokens": ref.workload_mean_tokens,
                                 "rtfx": a_ / s2, "rtfx_sample": ref.sample_rtfx}
+    if rank == 0 and world == 1 and not args.no_cuda_ref:
+        line["cuda_baseline"] = ReferenceCUDA(ws, case, enc, CUDA_REF_SAMPLE).run(wb)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

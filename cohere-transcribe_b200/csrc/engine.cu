@@ -34,7 +34,6 @@ constexpr int PR = kPageRows;
 constexpr int SELF_PAGES = MAX_SEQ / PR;     // 64
 constexpr int CROSS_PAGES = 64;              // T_enc <= 1024
 constexpr long long PAGE_ELEMS = (long long)NL * 2 * PR * D;
-enum { S_FREE = 0, S_PREFILL = 1, S_DECODE = 2, S_DONE = 3 };
 constexpr int PROMPT_MAX = 96;                 // longest prompt (the reference's long-form prompts reach 2 + 64 + 16)
 constexpr int AW = 8;                          // consumer warps per attention CTA (one per head)
 constexpr int ANST = 3;                        // page stages in the attention pipeline
@@ -117,19 +116,19 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     __shared__ int4 seq_b[1024];   // per sequence: first self entry, first cross entry, first self / cross group
     __shared__ int seq_te[1024];   // per sequence: encoder rows
     const int i = threadIdx.x;
-    const int st = i < s.max_slots ? s.state[i] : S_FREE;
-    const int nr = st == S_PREFILL ? s.plen[i] : st == S_DECODE ? 1 : 0;
+    const int st = i < s.max_slots ? s.state[i] : SEQ_FREE;
+    const int nr = st == SEQ_PREFILL ? s.plen[i] : st == SEQ_DECODE ? 1 : 0;
     const int te = nr > 0 ? s.tenc[i] : 0;
-    const int pos = st == S_DECODE ? s.pos[i] : -1;
+    const int pos = st == SEQ_DECODE ? s.pos[i] : -1;
     const int cross_np = (te + PR - 1) / PR;
     int self_np = 0, self_ng = 0;   // self-attention pages and groups over the slot's rows
-    if (st == S_PREFILL) {
+    if (st == SEQ_PREFILL) {
         for (int j = 0; j < nr; ++j) {
             const int np = (j + 1 + PR - 1) / PR;
             self_np += np;
             self_ng += (np + GP - 1) / GP;
         }
-    } else if (st == S_DECODE) {
+    } else if (st == SEQ_DECODE) {
         self_np = (pos + 1 + PR - 1) / PR;
         self_ng = (self_np + GP - 1) / GP;
     }
@@ -146,10 +145,10 @@ __global__ void __launch_bounds__(1024) build_rows_kernel(DevState s, int row_ca
     }
     for (int j = 0; j < nr; ++j) {
         const int r = base + j;
-        const int p = st == S_PREFILL ? j : pos;
+        const int p = st == SEQ_PREFILL ? j : pos;
         s.r_slot[r] = i;
         s.r_pos[r] = p;
-        s.r_tok[r] = st == S_PREFILL ? s.prompt[i * PROMPT_MAX + j] : s.tok[i];
+        s.r_tok[r] = st == SEQ_PREFILL ? s.prompt[i * PROMPT_MAX + j] : s.tok[i];
         const int page = (p >= 0 && p < MAX_SEQ) ? s.self_pt[i * SELF_PAGES + p / PR] : -1;
         s.r_off[r] = page >= 0 ? (long long)page * PAGE_ELEMS + (long long)(p % PR) * D : -1;
     }
@@ -553,62 +552,6 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
     }
 }
 
-// next[q] = argmax over the vocabulary of sequence q's logits (first max).
-// Greedy argmax of each sequence's logits (first index of the maximum), then
-// that sequence's bookkeeping: append the token (EOS when the forced length is
-// reached), advance its position, retire it on EOS / forced length / MAX_SEQ
-// (done_map tells the host).  One CTA per sequence; sequences are independent.
-__global__ void __launch_bounds__(256) argmax_update_kernel(DevState s, const float *logits, int *next) {
-    pdl_wait();
-    pdl_trigger();
-    __shared__ float bv[256];
-    __shared__ int bi[256];
-    const int q = blockIdx.x;
-    if (q >= *s.n_seqs) return;
-    const float *x = logits + (size_t)q * V;
-    float best = -INFINITY;
-    int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += 256) {
-        const float v = x[i];
-        if (v > best) { best = v; idx = i; }
-    }
-    bv[threadIdx.x] = best;
-    bi[threadIdx.x] = idx;
-    __syncthreads();
-    for (int st = 128; st > 0; st >>= 1) {
-        if (threadIdx.x < st) {
-            const float ov = bv[threadIdx.x + st];
-            const int oi = bi[threadIdx.x + st];
-            if (ov > bv[threadIdx.x] || (ov == bv[threadIdx.x] && oi < bi[threadIdx.x])) {
-                bv[threadIdx.x] = ov;
-                bi[threadIdx.x] = oi;
-            }
-        }
-        __syncthreads();
-    }
-    if (threadIdx.x != 0) return;
-    int tok = bi[0] == 0x7fffffff ? 0 : bi[0];
-    next[q] = tok;
-    const int slot = s.q_slot[q];
-    const int st = s.state[slot];
-    const int gen = s.gen[slot] + 1;
-    const int forced = s.forced[slot];
-    if (forced > 0 && gen >= forced) tok = CT_TOK_EOS;
-    if (gen - 1 < MAX_SEQ) s.out_tok[(size_t)slot * MAX_SEQ + gen - 1] = tok;
-    s.gen[slot] = gen;
-    s.pos[slot] += st == S_PREFILL ? s.plen[slot] : 1;
-    s.tok[slot] = tok;
-    const bool done = (forced > 0 ? gen >= forced : tok == CT_TOK_EOS) || s.plen[slot] + gen >= MAX_SEQ;
-    if (done) {
-        s.state[slot] = S_DONE;
-        volatile int *dm = s.done_map;
-        dm[slot] = gen;
-        __threadfence_system();
-    } else {
-        s.state[slot] = S_DECODE;
-    }
-}
-
 // ------------------------------------------------------------ host --------
 // Pinned host ring: contiguous blocks allocated at submission and released
 // in submission order, so inputs are copied once from the caller and uploaded
@@ -697,6 +640,8 @@ struct ct_engine {
     int attn_ctas = 148;             // attention grid (one CTA per SM; set from the device)
     bf16 *xa[2], *xb[2], *xm[2], *lm[2];
     int *next = nullptr;
+    unsigned long long *amax_best = nullptr;   // LM head -> argmax: each sequence's argmax key
+    unsigned *amax_ticket = nullptr; // per 32-sequence block of the LM head: vocabulary tiles finished
     size_t attn_ws_floats = 0;
     // admission staging
     float *enc_dev = nullptr;
@@ -906,13 +851,18 @@ static void encode_step(ct_engine *e, int rows) {
     launch_pdl(st, dim3(seqs), dim3(256), ln_rows_kernel, (const int *)s.n_seqs, (const int *)s.q_row, (const float *)e->h,
                e->dlnw, e->dlnb, e->lm[0], lm_lo);
     mark(e, "layernorm_final");
+    // LM head with the greedy argmax, the token append and the retirement in
+    // its epilogue (logits stored only when the caller keeps them)
     GemmEpilogue lh;
-    lh.bias = e->hdb; lh.Y = e->logits; lh.ldy = V; lh.T_dev = s.n_seqs;
+    lh.bias = e->hdb; lh.Y = e->cfg.keep_logits ? e->logits : nullptr; lh.ldy = V; lh.T_dev = s.n_seqs;
     lh.split = 1;   // 128 vocabulary tiles, one wave: each CTA streams its 128 x 1024 slice of the table
+    ArgmaxSink &sk = lh.amax;
+    sk.best = e->amax_best; sk.ticket = e->amax_ticket; sk.next = e->next;
+    sk.q_slot = s.q_slot; sk.forced = s.forced; sk.plen = s.plen;
+    sk.state = s.state; sk.gen = s.gen; sk.pos = s.pos; sk.tok = s.tok; sk.out_tok = s.out_tok;
+    sk.done_map = s.done_map; sk.max_seq = MAX_SEQ; sk.eos = CT_TOK_EOS;
     egemm(e, e->etw, V, D, e->lm[0], lm_lo, seqs, e->cfg.max_slots, lh, true);
-    mark(e, "gemm_lm_head");
-    launch_pdl(st, dim3(seqs), dim3(256), argmax_update_kernel, s, (const float *)e->logits, e->next);
-    mark(e, "argmax_update");
+    mark(e, "gemm_lm_head_argmax");
 }
 
 static Bucket *bucket_for(ct_engine *e, int rows_needed) {
@@ -1002,7 +952,7 @@ static int admit(ct_engine *e) {
         int *rec = e->slot_stage + (size_t)n_rec * REC_INTS;
         ++n_rec;
         rec[REC_SLOT] = slot;
-        rec[REC_STATE] = S_PREFILL; rec[REC_TOK] = 0; rec[REC_POS] = 0; rec[REC_GEN] = 0;
+        rec[REC_STATE] = SEQ_PREFILL; rec[REC_TOK] = 0; rec[REC_POS] = 0; rec[REC_GEN] = 0;
         rec[REC_FORCED] = p.forced; rec[REC_TENC] = p.T_enc;
         int *spt = rec + REC_N, *cpt = spt + SELF_PAGES;
         for (int j = 0; j < SELF_PAGES; ++j) spt[j] = j < self_need ? pages[j] : -1;
@@ -1061,7 +1011,7 @@ static int harvest(ct_engine *e) {
         if (ng <= 0) continue;
         EK(cudaMemcpyAsync(e->tok_stage + (size_t)i * MAX_SEQ, e->ds.out_tok + (size_t)i * MAX_SEQ, sizeof(int) * ng,
                            cudaMemcpyDeviceToHost, e->st));
-        EK(cudaMemsetAsync(e->ds.state + i, 0, sizeof(int), e->st));   // S_FREE
+        EK(cudaMemsetAsync(e->ds.state + i, 0, sizeof(int), e->st));   // SEQ_FREE
         done.push_back({i, ng});
     }
     if (done.empty()) return 0;
@@ -1405,6 +1355,7 @@ extern "C" int ct_engine_step_times(ct_engine *e, float *out, int max) {
 
 extern "C" int ct_engine_last_logits(ct_engine *e, float *logits, long long *utt_ids, int *gen_index, int max) {
     if (!e || max < 0 || (max > 0 && (!logits || !utt_ids || !gen_index))) return CT_EINVAL;
+    if (!e->cfg.keep_logits) return CT_EINVAL;   // the LM head stored none
     if (e->n_steps == 0 || max == 0) return 0;
     EK(cudaSetDevice(e->device));
     EK(cudaStreamSynchronize(e->st));
@@ -1448,7 +1399,7 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
                     e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.pid_self, e->ds.pid_cross, e->ds.rp_self,
                     e->ds.rp_cross, e->ds.n_grp, e->ds.grp_self, e->ds.grp_cross, e->ds.n_wself, e->ds.n_wcross,
                     e->ds.crange, e->rec_dev,
-                    e->mel_rows, e->ln_stats};
+                    e->mel_rows, e->ln_stats, e->amax_best, e->amax_ticket};
     for (void *p : ptrs) cudaFree(p);
     for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
     cudaFreeHost(e->h_done);
@@ -1598,8 +1549,11 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         dalloc(&e->xa[1], (size_t)R * D) || dalloc(&e->xb[0], (size_t)R * D) || dalloc(&e->xb[1], (size_t)R * D) ||
         dalloc(&e->xm[0], (size_t)R * FF) || dalloc(&e->xm[1], (size_t)R * FF) || dalloc(&e->lm[0], (size_t)S * D) ||
         dalloc(&e->lm[1], (size_t)S * D) || dalloc(&e->logits, (size_t)S * V) || dalloc(&e->next, S) ||
-        dalloc(&e->ln_stats, (size_t)R * (D / 128))) { ct_engine_destroy(e); return CT_ENOMEM; }
+        dalloc(&e->ln_stats, (size_t)R * (D / 128)) || dalloc(&e->amax_best, S) ||
+        dalloc(&e->amax_ticket, S)) { ct_engine_destroy(e); return CT_ENOMEM; }
     EK(cudaMemset(e->ln_stats, 0, sizeof(float2) * (size_t)R * (D / 128)));
+    EK(cudaMemset(e->amax_ticket, 0, sizeof(unsigned) * S));
+    EK(cudaMemset(e->amax_best, 0, sizeof(unsigned long long) * S));
     e->attn_ws_floats = (size_t)R * SEG_MAX * (2 * H + D);
     if (dalloc(&e->attn_ws, e->attn_ws_floats) || dalloc(&e->tickets, (size_t)R * H)) {
         ct_engine_destroy(e);

@@ -437,6 +437,75 @@ __device__ __forceinline__ void ln_fill(const GemmEpilogue &ep, uint8_t *xs, int
     }
 }
 
+// Greedy-argmax order of (value, index) candidates: the larger value, and the
+// lower index among equal values, so the winner is the first index of the
+// maximum.  Candidates that are NaN or -inf never win (index INT_MAX).
+__device__ __forceinline__ void amax_take(float &bv, int &bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+}
+
+// Transposing warp reduction: on entry lane l holds one candidate per token j
+// (v[j], ix[j]) for its own feature; on exit v[0], ix[0] of lane l is the
+// best of the warp's 32 features for token l.  Five exchange rounds: in the
+// round of distance s each lane keeps the half of its tokens selected by bit
+// s of its lane id and folds in the partner's copy of that half.
+__device__ __forceinline__ void warp_amax_transpose(float (&v)[32], int (&ix)[32], int lane) {
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        const bool upper = (lane & s) != 0;
+#pragma unroll
+        for (int i = 0; i < s; ++i) {
+            const float send_v = upper ? v[i] : v[i + s];
+            const int send_i = upper ? ix[i] : ix[i + s];
+            float keep_v = upper ? v[i + s] : v[i];
+            int keep_i = upper ? ix[i + s] : ix[i];
+            const float rv = __shfl_xor_sync(0xffffffffu, send_v, s);
+            const int ri = __shfl_xor_sync(0xffffffffu, send_i, s);
+            amax_take(keep_v, keep_i, rv, ri);
+            v[i] = keep_v;
+            ix[i] = keep_i;
+        }
+    }
+}
+
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Greedy hand-off of the LM head (ArgmaxSink, no K split): the 128 epilogue
+// threads (et = 0..127) merge the four warps' per-token maxima (red, warp
+// order = feature order) into one candidate per token row of this CTA's
+// vocabulary tile and fold it into the row's key (atomicMax), then take a
+// ticket of the row block; the CTA that completes the block reads the keys
+// and appends each row's token.  Nothing waits on another CTA.
+template <int BN>
+__device__ __forceinline__ void argmax_tail(const ArgmaxSink &sk, const float2 *red, int *flag, int t0, int T_eff,
+                                            int et) {
+    for (int j = et; j < BN; j += 128) {
+        if (t0 + j >= T_eff) break;
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float2 c = red[(j >> 5) * 128 + w * 32 + (j & 31)];
+            amax_take(bv, bi, c.x, __float_as_int(c.y));
+        }
+        if (bi != 0x7fffffff) atomicMax(&sk.best[t0 + j], argmax_key(bv, bi));
+    }
+    __threadfence();
+    epi_bar_sync();
+    if (et == 0) *flag = atomicAdd(&sk.ticket[blockIdx.y], 1u) == gridDim.x - 1;
+    epi_bar_sync();
+    if (!*flag) return;
+    __threadfence();
+    for (int j = et; j < BN; j += 128) {
+        const int t = t0 + j;
+        if (t >= T_eff) break;
+        const unsigned long long key = __ldcg(&sk.best[t]);
+        sk.best[t] = 0ull;   // ready for the next step's launch
+        decode_append(sk, t, key ? (int)(0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFull)) : 0);
+    }
+    if (et == 0) sk.ticket[blockIdx.y] = 0u;
+}
+
 template <int BN, bool TWO>
 __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
                                                            const __grid_constant__ CUtensorMap tmXh,
@@ -564,19 +633,40 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
     const float bias = (epi_warp && n < p.N && p.ep.bias) ? bf2f(p.ep.bias[n]) : 0.0f;
     const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
     if (!split) {
-        if (epi_warp && ok) {
+        const bool amx = p.ep.amax.best != nullptr;
+        // argmax hand-off: per-token maxima of each epilogue warp, [BN/32][4][32],
+        // in the stage buffers (idle once the accumulator is complete)
+        float2 *red = reinterpret_cast<float2 *>(smem);
+        if (epi_warp) {
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 if (t0 + c >= T_eff) break;   // warp-uniform
                 float v[32];
-                tmem_ld32(tbase + (uint32_t)c, v);
-                if (n < p.N) {
+                if (ok) tmem_ld32(tbase + (uint32_t)c, v);
+                if (ok && n < p.N) {
                     const int tl = min(32, T_eff - (t0 + c));
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] += bias;
-                    epilogue16(p.ep, t0 + c, min(16, tl), n, v);
-                    if (tl > 16) epilogue16(p.ep, t0 + c + 16, tl - 16, n, v + 16);
+                    if (p.ep.Y || p.ep.epi != EPI_STORE) {   // EPI_STORE without Y: argmax hand-off only
+                        epilogue16(p.ep, t0 + c, min(16, tl), n, v);
+                        if (tl > 16) epilogue16(p.ep, t0 + c + 16, tl - 16, n, v + 16);
+                    }
                 }
+                if (amx) {
+                    int ix[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const bool cand = ok && n < p.N && v[j] > -INFINITY;
+                        ix[j] = cand ? n : 0x7fffffff;
+                        v[j] = cand ? v[j] : -INFINITY;
+                    }
+                    warp_amax_transpose(v, ix, lane);
+                    red[(c >> 5) * 128 + q * 32 + lane] = make_float2(v[0], __int_as_float(ix[0]));
+                }
+            }
+            if (amx) {
+                epi_bar_sync();
+                argmax_tail<BN>(p.ep.amax, red, reinterpret_cast<int *>(red + BN * 4), t0, T_eff, threadIdx.x - 64);
             }
         }
     } else {
@@ -998,6 +1088,10 @@ void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, c
         CT_FATAL("LayerNorm-input GEMM needs K = 1024, row statistics and 16-byte aligned LN weights");
     if (ep.stats_out && (ep.epi != EPI_FMADD || ep.row_mask || N % BM || nsplit < 2))
         CT_FATAL("row statistics need EPI_FMADD with a K split, no row mask and N a multiple of %d", BM);
+    if (ep.amax.best && (ep.epi != EPI_STORE || ep.row_mask || nsplit != 1 || pers || ep.ln_x || !ep.amax.ticket ||
+                         !ep.amax.next || !ep.T_dev))
+        CT_FATAL("the argmax hand-off needs EPI_STORE without a K split, a device row count and its ticket buffers");
+    if (ep.epi == EPI_STORE && !ep.Y && !ep.amax.best) CT_FATAL("GEMM without an output");
     const CUtensorMap &mw = tmap_bf16(c, W, N, K, BM);
     const CUtensorMap &mh = tmap_bf16(c, X_hi, xrows, K, BN);
     const CUtensorMap &ml = two ? tmap_bf16(c, X_lo, xrows, K, BN) : mh;

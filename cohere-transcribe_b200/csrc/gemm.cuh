@@ -28,6 +28,64 @@ enum Epi : int {
 // Paged KV pool geometry: page = [DEC_N layers][K,V][kPageRows rows][1024].
 constexpr int kPageRows = 16;
 
+// Sequence states of the engine's slot table.
+enum SeqState : int { SEQ_FREE = 0, SEQ_PREFILL = 1, SEQ_DECODE = 2, SEQ_DONE = 3 };
+
+// Greedy-decode hand-off of the LM-head GEMM.  With ArgmaxSink::best set, the
+// epilogue reduces each token row's logits over the CTA's 128-entry
+// vocabulary tile (first index of the maximum, warp shuffles) and folds the
+// result into the row's 64-bit key with one atomicMax: the key orders by the
+// value, then by the lower index, so the fold is independent of the order in
+// which the tiles arrive and the winner is the first index of the maximum over
+// the whole vocabulary, as the reference's argmax
+// (backends/cpu/backend.c:446-456).  The CTA that takes the last ticket of a
+// row block (no waiting) reads the keys, appends each row's token to its
+// sequence (decode_append) and clears the keys.
+struct ArgmaxSink {
+    unsigned long long *best = nullptr;   // [rows]: argmax key (0 = no candidate; cleared after use)
+    unsigned *ticket = nullptr;           // [row blocks]: tiles finished (the last one resets it to 0)
+    int *next = nullptr;                  // [rows]: chosen token (before the forced-EOS rule)
+    // slot table (row q belongs to slot q_slot[q])
+    const int *q_slot = nullptr, *forced = nullptr, *plen = nullptr;
+    int *state = nullptr, *gen = nullptr, *pos = nullptr, *tok = nullptr, *out_tok = nullptr;
+    int *done_map = nullptr;    // host-mapped: generated count of a finished slot
+    int max_seq = 0, eos = 0;
+};
+
+// Argmax key of a candidate (value v, index i < 2^31): the float's bits mapped
+// to an unsigned order (larger value, larger key) in the high word, the
+// complement of the index in the low word (lower index, larger key).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    const unsigned b = v == 0.0f ? 0u : __float_as_uint(v);   // -0 ties with +0, as the float comparison does
+    const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
+}
+
+// Append the greedy token of row q to its sequence: EOS when the forced length
+// is reached, advance the position (the prompt on the prefill step), retire
+// on EOS / forced length / max_seq (done_map tells the host).
+__device__ __forceinline__ void decode_append(const ArgmaxSink &s, int q, int tok) {
+    s.next[q] = tok;
+    const int slot = s.q_slot[q];
+    const int st = s.state[slot];
+    const int gen = s.gen[slot] + 1;
+    const int forced = s.forced[slot];
+    if (forced > 0 && gen >= forced) tok = s.eos;
+    if (gen - 1 < s.max_seq) s.out_tok[(size_t)slot * s.max_seq + gen - 1] = tok;
+    s.gen[slot] = gen;
+    s.pos[slot] += st == SEQ_PREFILL ? s.plen[slot] : 1;
+    s.tok[slot] = tok;
+    const bool done = (forced > 0 ? gen >= forced : tok == s.eos) || s.plen[slot] + gen >= s.max_seq;
+    if (done) {
+        s.state[slot] = SEQ_DONE;
+        volatile int *dm = s.done_map;
+        dm[slot] = gen;
+        __threadfence_system();
+    } else {
+        s.state[slot] = SEQ_DECODE;
+    }
+}
+
 struct GemmEpilogue {
     int epi = EPI_STORE;
     float scale = 1.0f;
@@ -66,6 +124,9 @@ struct GemmEpilogue {
     const float2 *ln_stats = nullptr;
     const bf16 *ln_g = nullptr;
     const bf16 *ln_b = nullptr;
+    // Greedy argmax of each token row over N (EPI_STORE without a K split;
+    // Y may then be null, in which case no logits are stored).
+    ArgmaxSink amax;
 };
 
 // Per-thread GEMM context: stream, workspaces, tensor-map cache.

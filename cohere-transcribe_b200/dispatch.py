@@ -34,7 +34,9 @@ def t_mel_of_seconds(sec: float) -> int:
 
 
 def assign(seconds, n_replicas: int) -> list[int]:
-    """Replica index for every utterance: least queued audio seconds first."""
+    """Replica index for every utterance: least queued audio seconds first.
+    Any non-negative per-utterance work measure may stand in for the seconds
+    (bench.py weighs audio seconds and forced decode tokens together)."""
     if n_replicas < 1:
         raise ValueError("n_replicas must be >= 1")
     heap = [(0.0, r) for r in range(n_replicas)]

