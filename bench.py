@@ -402,6 +402,8 @@ def main():
     ap.add_argument("--max-len", type=int, default=0, help="cap the forced lengths (profiling cases)")
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel-class profiling pass")
     ap.add_argument("--no-pdl", action="store_true", help="launch step kernels without programmatic dependent launch")
+    ap.add_argument("--fused-step", type=int, default=0, choices=[0, 1],
+                    help="1 = each decode step as one persistent kernel (0 = separate kernels)")
     ap.add_argument("--legs", default="ABC", help="A = decode leg, B = transcription leg, C = configuration 2 "
                     "(batch 1), E = encoder only (profiling cases)")
     ap.add_argument("--max-slots", type=int, default=256, help="engine slots (profiling cases)")
@@ -485,6 +487,7 @@ def main():
     def make_engine(profile=0):
         return abi.Engine(lib, dev, wb, ws, max_slots=args.max_slots, max_rows=1024, precision=args.precision,
                           kv_pages=args.kv_pages, no_pdl=int(args.no_pdl), profile=profile,
+                          fused_step=args.fused_step,
                           enc_max_utts=enc_utts if (with_enc or with_c or with_s) else -1,
                           enc_max_frames=enc_frames)
 

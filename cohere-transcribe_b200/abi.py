@@ -88,7 +88,8 @@ SIGNATURES = {
 class EngineConfig(ctypes.Structure):
     _fields_ = [("max_slots", _int), ("max_rows", _int), ("kv_pages", _int), ("precision", _int),
                 ("n_prompt", _int), ("prompt", _vp), ("profile", _int), ("no_pdl", _int),
-                ("enc_max_utts", _int), ("enc_max_frames", _int), ("keep_logits", _int)]
+                ("enc_max_utts", _int), ("enc_max_frames", _int), ("keep_logits", _int),
+                ("fused_step", _int)]
 
 
 class EngineStats(ctypes.Structure):
@@ -109,12 +110,12 @@ class Engine:
     """Thin owner of a ct_engine* (one per GPU, driven by one thread)."""
 
     def __init__(self, lib, device, wb, wstruct, max_slots=256, max_rows=1024, precision=1, kv_pages=0, profile=0,
-                 no_pdl=0, enc_max_utts=0, enc_max_frames=0, keep_logits=0):
+                 no_pdl=0, enc_max_utts=0, enc_max_frames=0, keep_logits=0, fused_step=0):
         self.lib = lib
         self.wb = wb            # keeps the host blob alive (the engine copies it at creation)
         self.ws = wstruct
         cfg = EngineConfig(max_slots, max_rows, kv_pages, precision, 0, None, profile, no_pdl, enc_max_utts,
-                           enc_max_frames, keep_logits)
+                           enc_max_frames, keep_logits, fused_step)
         h = ctypes.c_void_p()
         rc = lib.ct_engine_create(ctypes.byref(h), device, wb.ptr(), wb.nbytes, ctypes.addressof(wstruct),
                                   ctypes.byref(cfg))

@@ -41,6 +41,7 @@ enum {
     CT_STATUS_TIMEOUT_MMA = 2,   // an MMA commit never arrived
     CT_STATUS_TIMEOUT_FREE = 3,  // a stage was never released
     CT_STATUS_BAD_ARG = 4,       // a kernel saw an out-of-range index and skipped it
+    CT_STATUS_TIMEOUT_GRID = 5,  // a grid barrier or a split-K tile counter of the persistent step never filled
 };
 // Defined here: the library is built as one translation unit (ct_b200.cu).
 __device__ int g_ct_status = 0;
@@ -104,6 +105,34 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, in
             return false;
         }
     }
+}
+// Acquire loads of global words (spins on counters other CTAs release).
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Release adds (order the writes that happen before them, the CTA's other
+// threads' included through a preceding CTA barrier); return the old value.
+__device__ __forceinline__ unsigned long long atom_add_release_u64(unsigned long long *p, unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ unsigned atom_add_release_u32(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+// L2 prefetch of `bytes` (a multiple of 16) at a 16-byte aligned global address.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+                 : "memory");
 }
 // Bounded wait with the library's budget (CT_WAIT_NS).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code) {

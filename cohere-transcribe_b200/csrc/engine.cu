@@ -552,6 +552,8 @@ __global__ void __launch_bounds__((AW + 1) * 32, 1) attn_paged_kernel(DevState s
     }
 }
 
+#include "step.cuh"
+
 // ------------------------------------------------------------ host --------
 // Pinned host ring: contiguous blocks allocated at submission and released
 // in submission order, so inputs are copied once from the caller and uploaded
@@ -642,6 +644,19 @@ struct ct_engine {
     int *next = nullptr;
     unsigned long long *amax_best = nullptr;   // LM head -> argmax: each sequence's argmax key
     unsigned *amax_ticket = nullptr; // per 32-sequence block of the LM head: vocabulary tiles finished
+    // persistent step kernel (cfg.fused_step): one plan per token tile (32, 64, 128)
+    struct StepPlan {
+        StepPhase *ph = nullptr;
+        StepGemm *gm = nullptr;
+        CUtensorMap *maps = nullptr;
+        int n_ph = 0, n_gm = 0;
+        std::vector<std::string> labels;   // per phase (profile mode)
+    } plans[3];
+    float *step_part = nullptr;      // split-K partial tiles (shared by the phases)
+    unsigned *step_cnt = nullptr;    // per GEMM phase and (token tile, feature tile): arrival counters
+    unsigned long long *step_gbar = nullptr;     // grid barrier: arrivals, failed-launch marker
+    unsigned long long *step_stamps = nullptr;   // profile mode: per phase and CTA stamps (ns)
+    int last_plan = -1;                          // plan of the last fused step launched (profile mode)
     size_t attn_ws_floats = 0;
     // admission staging
     float *enc_dev = nullptr;
@@ -788,81 +803,252 @@ static void launch_attn(cudaStream_t st, int ctas, const DevState &s, const floa
     CT_CHECK(cudaLaunchKernelEx(&cfg, attn_paged_kernel, s, q, pool, layer, cross, hi, lo, ws, tickets));
 }
 
+// The GEMMs of a decode step with their epilogues, shared by the
+// separate-kernel step (encode_step launches them one by one) and the
+// persistent step kernel (which runs them as phases), so both compute the same.
+enum StepGemmKind { G_QKV = 0, G_O, G_QC, G_OC, G_F1, G_F2, G_LM };
+
+struct GemmSpec {
+    const bf16 *W;
+    int N, K;
+    const bf16 *xh, *xl;   // activation planes (LayerNorm-input mode: shape of the tensor maps only)
+    long x_rows;           // their capacity in rows
+    GemmEpilogue ep;
+};
+
+static GemmSpec gemm_spec(ct_engine *e, int l, int kind) {
+    const DevState &s = e->ds;
+    const bool two = two_planes(e);
+    GemmSpec g{};
+    GemmEpilogue &ep = g.ep;
+    // The pre-LayerNorms of the QKV (layers 1..7), cross-query and FFN1
+    // projections run inside those GEMMs: each residual GEMM (EPI_FMADD) leaves
+    // per-row (mean, M2) partials of its 128-feature tiles in ln_stats, and the
+    // next GEMM normalises its own K slice of h into shared memory.  Layer 0's
+    // self-attention LayerNorm is fused into the embedding, which writes planes.
+    auto ln_input = [&](const bf16 *w, const bf16 *b) {
+        ep.ln_x = e->h; ep.ln_stats = e->ln_stats; ep.ln_g = w; ep.ln_b = b;
+        g.xh = e->xa[0]; g.xl = two ? e->xa[1] : nullptr;
+    };
+    g.x_rows = e->cfg.max_rows;
+    ep.T_dev = s.n_rows;
+    if (kind == G_LM) {
+        // LM head with the greedy argmax, the token append and the retirement in
+        // its epilogue (logits stored only when the caller keeps them)
+        g.W = e->etw; g.N = V; g.K = D;
+        g.xh = e->lm[0]; g.xl = two ? e->lm[1] : nullptr; g.x_rows = e->cfg.max_slots;
+        ep.bias = e->hdb; ep.Y = e->cfg.keep_logits ? e->logits : nullptr; ep.ldy = V; ep.T_dev = s.n_seqs;
+        ep.split = 1;   // 128 vocabulary tiles, one wave: each CTA streams its 128 x 1024 slice of the table
+        ArgmaxSink &sk = ep.amax;
+        sk.best = e->amax_best; sk.ticket = e->amax_ticket; sk.next = e->next;
+        sk.q_slot = s.q_slot; sk.forced = s.forced; sk.plen = s.plen;
+        sk.state = s.state; sk.gen = s.gen; sk.pos = s.pos; sk.tok = s.tok; sk.out_tok = s.out_tok;
+        sk.done_map = s.done_map; sk.max_seq = MAX_SEQ; sk.eos = CT_TOK_EOS;
+        return g;
+    }
+    const auto &Ly = e->L[l];
+    switch (kind) {
+    case G_QKV:
+        g.W = Ly.qkv_w; g.N = 3 * D; g.K = D;
+        g.xh = e->xa[0]; g.xl = two ? e->xa[1] : nullptr;
+        ep.epi = EPI_QKV_PAGED; ep.bias = Ly.qkv_b; ep.Y = e->q; ep.ldy = D; ep.qdim = D;
+        ep.kv_pool = e->pool; ep.row_off = s.r_off; ep.layer = l;
+        if (l > 0) ln_input(Ly.sa_lnw, Ly.sa_lnb);
+        break;
+    case G_O:
+    case G_OC:
+        g.W = kind == G_O ? Ly.sa_ow : Ly.ca_ow; g.N = D; g.K = D;
+        g.xh = e->xb[0]; g.xl = two ? e->xb[1] : nullptr;
+        ep.epi = EPI_FMADD; ep.scale = 1.0f; ep.bias = kind == G_O ? Ly.sa_ob : Ly.ca_ob; ep.Y = e->h; ep.ldy = D;
+        ep.stats_out = e->ln_stats;
+        break;
+    case G_QC:
+        g.W = Ly.ca_qw; g.N = D; g.K = D;
+        ep.bias = Ly.ca_qb; ep.Y = e->q; ep.ldy = D;
+        ln_input(Ly.ca_lnw, Ly.ca_lnb);
+        break;
+    case G_F1:
+        g.W = Ly.ffn_w1; g.N = FF; g.K = D;
+        ep.epi = EPI_BF16; ep.act = 2; ep.bias = Ly.ffn_b1; ep.Ybf = e->xm[0]; ep.Ybf_lo = two ? e->xm[1] : nullptr;
+        ep.ldy = FF;
+        ln_input(Ly.ffn_lnw, Ly.ffn_lnb);
+        break;
+    case G_F2:
+        g.W = Ly.ffn_w2; g.N = D; g.K = FF;
+        g.xh = e->xm[0]; g.xl = two ? e->xm[1] : nullptr;
+        ep.epi = EPI_FMADD; ep.scale = 1.0f; ep.bias = Ly.ffn_b2; ep.Y = e->h; ep.ldy = D;
+        ep.stats_out = e->ln_stats;
+        break;
+    default: break;
+    }
+    return g;
+}
+
+static void launch_gemm_spec(ct_engine *e, const GemmSpec &g, int T) {
+    egemm(e, g.W, g.N, g.K, g.xh, g.xl, T, g.x_rows, g.ep, true);
+}
+
+// Token tile of the persistent step kernel for a bucket of `rows` rows.
+static int step_bn(int rows) { return rows <= 32 ? 32 : rows <= 64 ? 64 : 128; }
+
 // Encode one step for capacity `rows` (seqs capacity = min(rows, max_slots)) on e->st.
 static void encode_step(ct_engine *e, int rows) {
     const int seqs = std::min(rows, e->cfg.max_slots);
     DevState s = e->ds;
     cudaStream_t st = e->st;
     const bool two = two_planes(e);
-    bf16 *xa_lo = two ? e->xa[1] : nullptr, *xb_lo = two ? e->xb[1] : nullptr, *xm_lo = two ? e->xm[1] : nullptr;
-    bf16 *lm_lo = two ? e->lm[1] : nullptr;
+    bf16 *xa_lo = two ? e->xa[1] : nullptr;
     e->mark_label.clear();
     mark(e, "start");
     build_rows_kernel<<<1, 1024, 0, st>>>(s, rows, seqs);
     mark(e, "build_rows");
+    if (e->cfg.fused_step) {
+        const int bn = step_bn(rows);
+        const int slot = bn == 32 ? 0 : bn == 64 ? 1 : 2;
+        const auto &pl = e->plans[slot];
+        StepParams sp{};
+        sp.s = s; sp.ph = pl.ph; sp.n_ph = pl.n_ph; sp.gm = pl.gm; sp.n_gm = pl.n_gm;
+        sp.etw = e->etw; sp.epw = e->epw; sp.elnw = e->elnw; sp.elnb = e->elnb;
+        sp.ln1w = e->L[0].sa_lnw; sp.ln1b = e->L[0].sa_lnb; sp.h = e->h; sp.xa_hi = e->xa[0]; sp.xa_lo = xa_lo;
+        sp.q = e->q; sp.pool = e->pool; sp.xb_hi = e->xb[0]; sp.xb_lo = two ? e->xb[1] : nullptr;
+        sp.attn_ws = e->attn_ws; sp.tickets = e->tickets;
+        sp.dlnw = e->dlnw; sp.dlnb = e->dlnb; sp.lm_hi = e->lm[0]; sp.lm_lo = two ? e->lm[1] : nullptr;
+        sp.gbar = e->step_gbar;
+        sp.stamps = e->cfg.profile ? e->step_stamps : nullptr;
+        e->last_plan = slot;
+        void (*k)(StepParams) = nullptr;
+        if (two) k = bn == 32 ? step_kernel<32, true> : bn == 64 ? step_kernel<64, true> : step_kernel<128, true>;
+        else k = bn == 32 ? step_kernel<32, false> : bn == 64 ? step_kernel<64, false> : step_kernel<128, false>;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(e->ds.n_cta);
+        cfg.blockDim = dim3(SP_THREADS);
+        cfg.dynamicSmemBytes = SP_SMEM;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeCooperative;   // every CTA resident: the grid barriers need it
+        at[0].val.cooperative = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        CT_CHECK(cudaLaunchKernelEx(&cfg, k, sp));
+        mark(e, "step_fused");
+        return;
+    }
     launch_pdl(st, dim3(rows), dim3(256), embed_rows_kernel, s, e->etw, e->epw, e->elnw, e->elnb, e->L[0].sa_lnw,
                e->L[0].sa_lnb, e->h, e->xa[0], xa_lo);
     mark(e, "embed_ln");
-    // The pre-LayerNorms of the QKV (layers 1..7), cross-query and FFN1
-    // projections run inside those GEMMs: each residual GEMM (EPI_FMADD) leaves
-    // per-row (mean, M2) partials of its 128-feature tiles in ln_stats, and the
-    // next GEMM normalises its own K slice of h into shared memory.  Layer 0's
-    // self-attention LayerNorm is fused into the embedding, which writes planes.
-    auto ln_input = [&](GemmEpilogue &g, const bf16 *w, const bf16 *b) {
-        g.ln_x = e->h; g.ln_stats = e->ln_stats; g.ln_g = w; g.ln_b = b;
-    };
     for (int l = 0; l < NL; ++l) {
-        const auto &Ly = e->L[l];
-        GemmEpilogue qkv;
-        qkv.epi = EPI_QKV_PAGED; qkv.bias = Ly.qkv_b; qkv.Y = e->q; qkv.ldy = D; qkv.qdim = D;
-        qkv.kv_pool = e->pool; qkv.row_off = s.r_off; qkv.layer = l; qkv.T_dev = s.n_rows;
-        if (l > 0) ln_input(qkv, Ly.sa_lnw, Ly.sa_lnb);
-        egemm(e, Ly.qkv_w, 3 * D, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, qkv, true);
+        launch_gemm_spec(e, gemm_spec(e, l, G_QKV), rows);
         mark(e, "gemm_qkv");
-        launch_attn(st, e->attn_ctas, s, e->q, e->pool, l, 0, e->xb[0], xb_lo, e->attn_ws, e->tickets);
+        launch_attn(st, e->attn_ctas, s, e->q, e->pool, l, 0, e->xb[0], two ? e->xb[1] : nullptr, e->attn_ws,
+                    e->tickets);
         mark(e, "attn_self");
-        GemmEpilogue o;
-        o.epi = EPI_FMADD; o.scale = 1.0f; o.bias = Ly.sa_ob; o.Y = e->h; o.ldy = D; o.T_dev = s.n_rows;
-        o.stats_out = e->ln_stats;
-        egemm(e, Ly.sa_ow, D, D, e->xb[0], xb_lo, rows, e->cfg.max_rows, o, true);
+        launch_gemm_spec(e, gemm_spec(e, l, G_O), rows);
         mark(e, "gemm_o");
-        GemmEpilogue qc;
-        qc.bias = Ly.ca_qb; qc.Y = e->q; qc.ldy = D; qc.T_dev = s.n_rows;
-        ln_input(qc, Ly.ca_lnw, Ly.ca_lnb);
-        egemm(e, Ly.ca_qw, D, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, qc, true);
+        launch_gemm_spec(e, gemm_spec(e, l, G_QC), rows);
         mark(e, "gemm_q_cross");
-        launch_attn(st, e->attn_ctas, s, e->q, e->pool, l, 1, e->xb[0], xb_lo, e->attn_ws, e->tickets);
+        launch_attn(st, e->attn_ctas, s, e->q, e->pool, l, 1, e->xb[0], two ? e->xb[1] : nullptr, e->attn_ws,
+                    e->tickets);
         mark(e, "attn_cross");
-        GemmEpilogue oc = o;
-        oc.bias = Ly.ca_ob;
-        egemm(e, Ly.ca_ow, D, D, e->xb[0], xb_lo, rows, e->cfg.max_rows, oc, true);
+        launch_gemm_spec(e, gemm_spec(e, l, G_OC), rows);
         mark(e, "gemm_o");
-        GemmEpilogue f1;
-        f1.epi = EPI_BF16; f1.act = 2; f1.bias = Ly.ffn_b1; f1.Ybf = e->xm[0]; f1.Ybf_lo = xm_lo; f1.ldy = FF;
-        f1.T_dev = s.n_rows;
-        ln_input(f1, Ly.ffn_lnw, Ly.ffn_lnb);
-        egemm(e, Ly.ffn_w1, FF, D, e->xa[0], xa_lo, rows, e->cfg.max_rows, f1, true);
+        launch_gemm_spec(e, gemm_spec(e, l, G_F1), rows);
         mark(e, "gemm_ffn1");
-        GemmEpilogue f2 = o;
-        f2.bias = Ly.ffn_b2;
-        egemm(e, Ly.ffn_w2, D, FF, e->xm[0], xm_lo, rows, e->cfg.max_rows, f2, true);
+        launch_gemm_spec(e, gemm_spec(e, l, G_F2), rows);
         mark(e, "gemm_ffn2");
     }
     launch_pdl(st, dim3(seqs), dim3(256), ln_rows_kernel, (const int *)s.n_seqs, (const int *)s.q_row, (const float *)e->h,
-               e->dlnw, e->dlnb, e->lm[0], lm_lo);
+               e->dlnw, e->dlnb, e->lm[0], two ? e->lm[1] : nullptr);
     mark(e, "layernorm_final");
-    // LM head with the greedy argmax, the token append and the retirement in
-    // its epilogue (logits stored only when the caller keeps them)
-    GemmEpilogue lh;
-    lh.bias = e->hdb; lh.Y = e->cfg.keep_logits ? e->logits : nullptr; lh.ldy = V; lh.T_dev = s.n_seqs;
-    lh.split = 1;   // 128 vocabulary tiles, one wave: each CTA streams its 128 x 1024 slice of the table
-    ArgmaxSink &sk = lh.amax;
-    sk.best = e->amax_best; sk.ticket = e->amax_ticket; sk.next = e->next;
-    sk.q_slot = s.q_slot; sk.forced = s.forced; sk.plen = s.plen;
-    sk.state = s.state; sk.gen = s.gen; sk.pos = s.pos; sk.tok = s.tok; sk.out_tok = s.out_tok;
-    sk.done_map = s.done_map; sk.max_seq = MAX_SEQ; sk.eos = CT_TOK_EOS;
-    egemm(e, e->etw, V, D, e->lm[0], lm_lo, seqs, e->cfg.max_slots, lh, true);
+    launch_gemm_spec(e, gemm_spec(e, 0, G_LM), seqs);
     mark(e, "gemm_lm_head_argmax");
+}
+
+static int dalloc_bytes(void **p, size_t bytes) { return cudaMalloc(p, bytes) == cudaSuccess ? 0 : 1; }
+
+// Phase table and GEMM descriptors of the persistent step kernel for token
+// tile bn (written once, at engine creation: no allocation during capture).
+static int build_step_plan(ct_engine *e, int slot, int bn) {
+    auto &pl = e->plans[slot];
+    std::vector<StepPhase> ph;
+    std::vector<GemmSpec> specs;
+    static const char *gname[] = {"gemm_qkv", "gemm_o", "gemm_q_cross", "gemm_o_cross", "gemm_ffn1", "gemm_ffn2",
+                                  "gemm_lm_head_argmax"};
+    pl.labels.clear();
+    auto add_gemm = [&](int l, int kind) {
+        specs.push_back(gemm_spec(e, l, kind));
+        ph.push_back({SP_GEMM, (int)specs.size() - 1, -1, -1});
+        pl.labels.push_back(std::string("fused:") + gname[kind]);
+    };
+    auto add = [&](int kind, int arg, const char *label) {
+        ph.push_back({kind, arg, -1, -1});
+        pl.labels.push_back(label);
+    };
+    add(SP_EMBED, 0, "fused:embed_ln");
+    for (int l = 0; l < NL; ++l) {
+        add_gemm(l, G_QKV);
+        add(SP_ATTN, l * 2 + 0, "fused:attn_self");
+        add_gemm(l, G_O);
+        add_gemm(l, G_QC);
+        add(SP_ATTN, l * 2 + 1, "fused:attn_cross");
+        add_gemm(l, G_OC);
+        add_gemm(l, G_F1);
+        add_gemm(l, G_F2);
+    }
+    add(SP_FINAL_LN, 0, "fused:layernorm_final");
+    add_gemm(0, G_LM);
+    for (size_t i = 0; i < ph.size(); ++i) {
+        for (size_t j = i + 1; j < ph.size(); ++j)
+            if (ph[j].kind == SP_GEMM) { ph[i].next_gemm = ph[j].arg; break; }
+        if (i + 1 < ph.size() && ph[i + 1].kind == SP_ATTN) ph[i].next_attn = ph[i + 1].arg;
+    }
+    if ((int)ph.size() > SP_MAX_PH || (int)specs.size() > SP_MAX_GEMM) return CT_EINVAL;
+    // tensor maps: W (box 128 rows) and X planes (box bn rows) of every GEMM
+    std::vector<CUtensorMap> maps(specs.size() * 3);
+    std::vector<StepGemm> gm(specs.size());
+    const size_t cnt_per = (size_t)(e->cfg.max_rows / 32 + 1) * (V / 128);
+    const int planes = two_planes(e) ? 2 : 1;
+    for (size_t i = 0; i < specs.size(); ++i) {
+        const GemmSpec &g = specs[i];
+        maps[3 * i] = gemm_tmap(g.W, g.N, g.K, 128);
+        const bool lnx = g.ep.ln_x != nullptr;
+        if (!lnx) {
+            maps[3 * i + 1] = gemm_tmap(g.xh, g.x_rows, g.K, bn);
+            if (g.xl) maps[3 * i + 2] = gemm_tmap(g.xl, g.x_rows, g.K, bn);
+        }
+        StepGemm &d = gm[i];
+        d.W = g.W; d.N = g.N; d.K = g.K;
+        d.S = gemm_nsplit(g.N, g.K, bn, g.ep.split);
+        if (g.N % 128 || g.K % 64 || (g.K / 64) % d.S || bn % d.S ||
+            (d.S > 1 && d.S != 2 && d.S != 4 && d.S != 8 && d.S != 16))
+            return CT_EINVAL;
+        // two feature tiles per item when one tile per item would take more
+        // than one wave of CTAs and the stages still fit
+        const int tiles = g.N / 128, kbps = g.K / 64 / d.S;
+        const size_t xbytes = lnx ? (size_t)kbps * planes * bn * 128 : 0;
+        const size_t stage1 = 16384 + (lnx ? 0 : (size_t)planes * bn * 128);
+        const size_t stage2 = 2 * 16384 + (lnx ? 0 : (size_t)planes * bn * 128);
+        if (SP_NSTG * stage1 + xbytes > SP_RING) return CT_EINVAL;
+        d.TG = (d.S > 1 && tiles % 2 == 0 && tiles * d.S > e->ds.n_cta && SP_NSTG * stage2 + xbytes <= SP_RING) ? 2 : 1;
+        d.ep = g.ep;
+        d.part = e->step_part;
+        d.cnt = e->step_cnt + (size_t)(slot * SP_MAX_GEMM + i) * cnt_per;
+    }
+    if (dalloc_bytes((void **)&pl.maps, maps.size() * sizeof(CUtensorMap)) ||
+        dalloc_bytes((void **)&pl.gm, gm.size() * sizeof(StepGemm)) ||
+        dalloc_bytes((void **)&pl.ph, ph.size() * sizeof(StepPhase)))
+        return CT_ENOMEM;
+    for (size_t i = 0; i < specs.size(); ++i) {
+        gm[i].tmW = pl.maps + 3 * i;
+        const bool lnx = specs[i].ep.ln_x != nullptr;
+        gm[i].tmXh = lnx ? nullptr : pl.maps + 3 * i + 1;
+        gm[i].tmXl = (lnx || !specs[i].xl) ? nullptr : pl.maps + 3 * i + 2;
+    }
+    EK(cudaMemcpy(pl.maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
+    EK(cudaMemcpy(pl.gm, gm.data(), gm.size() * sizeof(StepGemm), cudaMemcpyHostToDevice));
+    EK(cudaMemcpy(pl.ph, ph.data(), ph.size() * sizeof(StepPhase), cudaMemcpyHostToDevice));
+    pl.n_ph = (int)ph.size();
+    pl.n_gm = (int)gm.size();
+    return CT_OK;
 }
 
 static Bucket *bucket_for(ct_engine *e, int rows_needed) {
@@ -1101,6 +1287,70 @@ static int encode_pending(ct_engine *e) {
     return 0;
 }
 
+// Profile mode of the persistent step: per phase, the span from the first
+// CTA's start to the last CTA's finish, then the barrier from that finish to
+// the first release; for the GEMM phases also the median over the CTAs with
+// work of start -> accumulator ready -> split-K partials counted in -> done,
+// and the spread of the start times.
+static int collect_step_stamps(ct_engine *e) {
+    const auto &pl = e->plans[e->last_plan];
+    const int G = e->ds.n_cta;
+    const int NS = SP_NSTAMP;
+    std::vector<unsigned long long> st((size_t)(pl.n_ph + 1) * G * NS);
+    EK(cudaMemcpy(st.data(), e->step_stamps, st.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+    // a CTA without a GEMM item in a phase writes no middle stamps next time
+    EK(cudaMemset(e->step_stamps, 0, st.size() * sizeof(unsigned long long)));
+    auto at = [&](int ph, int c, int k) { return st[((size_t)ph * G + c) * NS + k]; };
+    auto lo = [&](int ph, int k) {
+        unsigned long long v = ~0ull;
+        for (int c = 0; c < G; ++c) v = std::min(v, at(ph, c, k));
+        return v;
+    };
+    auto hi = [&](int ph, int k) {
+        unsigned long long v = 0;
+        for (int c = 0; c < G; ++c) v = std::max(v, at(ph, c, k));
+        return v;
+    };
+    auto median = [](std::vector<double> v) {
+        if (v.empty()) return 0.0;
+        std::nth_element(v.begin(), v.begin() + v.size() / 2, v.end());
+        return v[v.size() / 2];
+    };
+    auto add_ms = [&](const std::string &k, double v) {
+        auto &x = e->mark_ms[k];
+        x.first += v;
+        x.second += 1;
+    };
+    for (int ph = 0; ph < pl.n_ph; ++ph) {
+        const unsigned long long s0 = lo(ph, 0), d1 = hi(ph, 3);
+        const double work = d1 > s0 ? (d1 - s0) * 1e-6 : 0.0;
+        add_ms(pl.labels[ph], work);
+        if (pl.labels[ph] == "fused:attn_self") e->st_acc.self_attn_ms += work;
+        else if (pl.labels[ph] == "fused:attn_cross") e->st_acc.cross_attn_ms += work;
+        else if (pl.labels[ph].rfind("fused:gemm_ffn", 0) == 0) e->st_acc.ffn_ms += work;
+        std::vector<double> m1, m2, m3;
+        for (int c = 0; c < G; ++c) {
+            const unsigned long long t0 = at(ph, c, 0), t1 = at(ph, c, 1), t2 = at(ph, c, 2), t3 = at(ph, c, 3);
+            if (t1 > t0) {
+                m1.push_back((t1 - t0) * 1e-6);
+                if (t2 > t1) m2.push_back((t2 - t1) * 1e-6);
+                m3.push_back((t3 - (t2 > t1 ? t2 : t1)) * 1e-6);
+            }
+        }
+        if (!m1.empty()) {
+            add_ms(pl.labels[ph] + "/cta_to_accumulator", median(m1));
+            add_ms(pl.labels[ph] + "/cta_partials_wait", median(m2));
+            add_ms(pl.labels[ph] + "/cta_reduce_epilogue", median(m3));
+            add_ms(pl.labels[ph] + "/start_spread", (hi(ph, 0) - s0) * 1e-6);
+        }
+        if (ph + 1 < pl.n_ph) {
+            const unsigned long long s1 = lo(ph + 1, 0);
+            add_ms("fused:barrier", s1 > d1 ? (s1 - d1) * 1e-6 : 0.0);
+        }
+    }
+    return 0;
+}
+
 extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
     if (!e) return CT_EINVAL;
     EK(cudaSetDevice(e->device));
@@ -1168,6 +1418,10 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
                 if (b->labels[i] == "attn_self") e->st_acc.self_attn_ms += t;
                 else if (b->labels[i] == "attn_cross") e->st_acc.cross_attn_ms += t;
                 else if (b->labels[i].rfind("gemm_ffn", 0) == 0) e->st_acc.ffn_ms += t;
+            }
+            if (e->cfg.fused_step && e->step_stamps && e->last_plan >= 0) {
+                const int rc = collect_step_stamps(e);
+                if (rc) return rc;
             }
         }
         e->st_acc.self_kv_bytes += NL * self_b;
@@ -1399,7 +1653,10 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
                     e->tickets, e->ds.w_self, e->ds.w_cross, e->ds.pid_self, e->ds.pid_cross, e->ds.rp_self,
                     e->ds.rp_cross, e->ds.n_grp, e->ds.grp_self, e->ds.grp_cross, e->ds.n_wself, e->ds.n_wcross,
                     e->ds.crange, e->rec_dev,
-                    e->mel_rows, e->ln_stats, e->amax_best, e->amax_ticket};
+                    e->mel_rows, e->ln_stats, e->amax_best, e->amax_ticket, e->step_part, e->step_cnt,
+                    e->step_gbar, e->step_stamps, e->plans[0].ph, e->plans[0].gm, e->plans[0].maps,
+                    e->plans[1].ph, e->plans[1].gm, e->plans[1].maps, e->plans[2].ph, e->plans[2].gm,
+                    e->plans[2].maps};
     for (void *p : ptrs) cudaFree(p);
     for (int l = 0; l < NL; ++l) { cudaFree(e->L[l].qkv_w); cudaFree(e->L[l].qkv_b); }
     cudaFreeHost(e->h_done);
@@ -1560,6 +1817,38 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         return CT_ENOMEM;
     }
     EK(cudaMemset(e->tickets, 0, sizeof(int) * (size_t)R * H));
+    if (cfg.fused_step) {
+        // persistent step kernel: split-K partial tiles (the largest phase:
+        // rows in whole 128-row tiles x N x S floats), tile counters, grid
+        // barrier, profile stamps, phase plans
+        const size_t Rp = ((size_t)R + 127) / 128 * 128;
+        size_t part = 0;
+        for (int kind = G_QKV; kind <= G_F2; ++kind) {
+            const GemmSpec g = gemm_spec(e, 0, kind);
+            part = std::max(part, Rp * g.N * gemm_nsplit(g.N, g.K, 32, g.ep.split));
+        }
+        const size_t cnt = (size_t)3 * SP_MAX_GEMM * (R / 32 + 1) * (V / 128);
+        if (dalloc(&e->step_part, part) || dalloc(&e->step_cnt, cnt) || dalloc(&e->step_gbar, 2) ||
+            (cfg.profile && dalloc(&e->step_stamps, (size_t)(SP_MAX_PH + 1) * e->ds.n_cta * SP_NSTAMP))) {
+            ct_engine_destroy(e);
+            return CT_ENOMEM;
+        }
+        EK(cudaMemset(e->step_cnt, 0, sizeof(unsigned) * cnt));
+        EK(cudaMemset(e->step_gbar, 0, sizeof(unsigned long long) * 2));
+        if (e->step_stamps)
+            EK(cudaMemset(e->step_stamps, 0, sizeof(unsigned long long) * (SP_MAX_PH + 1) * e->ds.n_cta * SP_NSTAMP));
+        for (auto k : {step_kernel<32, true>, step_kernel<64, true>, step_kernel<128, true>, step_kernel<32, false>,
+                       step_kernel<64, false>, step_kernel<128, false>})
+            EK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SP_SMEM));
+        int per_sm = 0;
+        EK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel<128, true>, SP_THREADS, SP_SMEM));
+        if (per_sm < 1) { ct_engine_destroy(e); return CT_EDEVICE; }
+        const int bns[3] = {32, 64, 128};
+        for (int i = 0; i < 3; ++i) {
+            const int rc = build_step_plan(e, i, bns[i]);
+            if (rc != CT_OK) { ct_engine_destroy(e); return rc; }
+        }
+    }
     // admission staging: up to 64 utterances of 30 s worth of encoder rows
     e->enc_rows_cap = 64 * 400;
     if (dalloc(&e->enc_dev, (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_pl[0], (size_t)e->enc_rows_cap * D) ||

@@ -367,13 +367,14 @@ __device__ __forceinline__ void splitk_reduce(const KernelParams &p, int t0, int
 // BN * 128.  The row's mean and variance merge the eight (mean, M2) partials
 // of its 128-feature tiles in tile order (equal counts of 128); rows past the
 // device row count are zero.
-template <int BN, bool TWO>
+template <int BN, bool TWO, int NT = 128>
 __device__ __forceinline__ void ln_fill(const GemmEpilogue &ep, uint8_t *xs, int t0, int T_eff, int kb0, int nkb,
                                         int et) {
     constexpr int K = 1024;
-    constexpr int TPR = BN >= 128 ? 1 : 128 / BN;   // threads per row
+    constexpr int TPR = BN >= NT ? 1 : NT / BN;     // threads per row
+    static_assert(TPR <= 8, "at most eight threads per row (one 16-byte chunk each)");
     constexpr int CPT = 8 / TPR;                    // 16-byte chunks per thread and k-block
-    constexpr int RSTEP = 128 / TPR;                // rows per pass of the 128 threads
+    constexpr int RSTEP = NT / TPR;                 // rows per pass of the NT threads
     constexpr uint32_t TILE = BN * 128;
     for (int r = et / TPR; r < BN; r += RSTEP) {
         const int t = t0 + r;
@@ -468,18 +469,20 @@ __device__ __forceinline__ void warp_amax_transpose(float (&v)[32], int (&ix)[32
     }
 }
 
-__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier 1 over the NT epilogue threads (the producer and MMA warps do not take part).
+template <int NT = 128>
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
 
-// Greedy hand-off of the LM head (ArgmaxSink, no K split): the 128 epilogue
-// threads (et = 0..127) merge the four warps' per-token maxima (red, warp
-// order = feature order) into one candidate per token row of this CTA's
-// vocabulary tile and fold it into the row's key (atomicMax), then take a
-// ticket of the row block; the CTA that completes the block reads the keys
-// and appends each row's token.  Nothing waits on another CTA.
-template <int BN>
+// Greedy hand-off of the LM head (ArgmaxSink, no K split): the NT epilogue
+// threads (et = 0..NT-1) merge the four TMEM lane quarters' per-token maxima
+// (red, quarter order = feature order) into one candidate per token row of
+// this CTA's vocabulary tile and fold it into the row's key (atomicMax), then
+// take ticket rb (the row block) of `tiles`; the CTA that completes the block
+// reads the keys and appends each row's token.  Nothing waits on another CTA.
+template <int BN, int NT = 128>
 __device__ __forceinline__ void argmax_tail(const ArgmaxSink &sk, const float2 *red, int *flag, int t0, int T_eff,
-                                            int et) {
-    for (int j = et; j < BN; j += 128) {
+                                            int et, int tiles, int rb) {
+    for (int j = et; j < BN; j += NT) {
         if (t0 + j >= T_eff) break;
         float bv = -INFINITY;
         int bi = 0x7fffffff;
@@ -491,19 +494,19 @@ __device__ __forceinline__ void argmax_tail(const ArgmaxSink &sk, const float2 *
         if (bi != 0x7fffffff) atomicMax(&sk.best[t0 + j], argmax_key(bv, bi));
     }
     __threadfence();
-    epi_bar_sync();
-    if (et == 0) *flag = atomicAdd(&sk.ticket[blockIdx.y], 1u) == gridDim.x - 1;
-    epi_bar_sync();
+    epi_bar_sync<NT>();
+    if (et == 0) *flag = atomicAdd(&sk.ticket[rb], 1u) == (unsigned)(tiles - 1);
+    epi_bar_sync<NT>();
     if (!*flag) return;
     __threadfence();
-    for (int j = et; j < BN; j += 128) {
+    for (int j = et; j < BN; j += NT) {
         const int t = t0 + j;
         if (t >= T_eff) break;
         const unsigned long long key = __ldcg(&sk.best[t]);
         sk.best[t] = 0ull;   // ready for the next step's launch
         decode_append(sk, t, key ? (int)(0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFull)) : 0);
     }
-    if (et == 0) sk.ticket[blockIdx.y] = 0u;
+    if (et == 0) sk.ticket[rb] = 0u;
 }
 
 template <int BN, bool TWO>
@@ -666,7 +669,8 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
             }
             if (amx) {
                 epi_bar_sync();
-                argmax_tail<BN>(p.ep.amax, red, reinterpret_cast<int *>(red + BN * 4), t0, T_eff, threadIdx.x - 64);
+                argmax_tail<BN>(p.ep.amax, red, reinterpret_cast<int *>(red + BN * 4), t0, T_eff, threadIdx.x - 64,
+                                gridDim.x, blockIdx.y);
             }
         }
     } else {
@@ -966,6 +970,19 @@ int split_factor(int N, int K) {
     return s;
 }
 
+int gemm_nsplit(int N, int K, int BN, int requested) {
+    const int kb_total = (K + BK - 1) / BK;
+    int nsplit = requested > 0 ? std::min(requested, 16) : split_factor(N, K);
+    while (nsplit > 1 && BN % nsplit) nsplit >>= 1;
+    const int kbps = (kb_total + nsplit - 1) / nsplit;
+    if ((kb_total + kbps - 1) / kbps != nsplit) nsplit = 1;   // every split must own >= 1 block
+    return nsplit;
+}
+
+CUtensorMap gemm_tmap(const void *ptr, long rows, long cols, long box_rows) {
+    return tmap_bf16(gemm_ctx(), ptr, rows, cols, box_rows);
+}
+
 template <int BN, bool TWO>
 static void launch_tc(cudaStream_t st, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml,
                       KernelParams p, bool pdl) {
@@ -1074,10 +1091,8 @@ void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, c
     const bool two = X_lo != nullptr;
     int BN = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : (two ? 128 : 256);
     const int kb_total = (K + BK - 1) / BK;
-    int nsplit = allow_split ? (ep.split > 0 ? std::min(ep.split, 16) : split_factor(N, K)) : 1;
-    while (nsplit > 1 && BN % nsplit) nsplit >>= 1;
+    const int nsplit = allow_split ? gemm_nsplit(N, K, BN, ep.split) : 1;
     const int kbps = (kb_total + nsplit - 1) / nsplit;
-    if ((kb_total + kbps - 1) / kbps != nsplit) nsplit = 1;   // every split must own >= 1 block
     const int kbps_final = nsplit > 1 ? kbps : kb_total;
     // X maps use the scratch capacity (or the caller's buffer rows) as the row count
     const long xrows = (X_hi == c->xhi || X_hi == c->xlo) ? (long)(c->x_elems / K) : (ep.x_rows > 0 ? ep.x_rows : (long)T);

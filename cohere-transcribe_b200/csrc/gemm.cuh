@@ -155,6 +155,14 @@ void linear_fp32(cudaStream_t st, const bf16 *W, int N, int K, const float *X, i
 
 int split_factor(int N, int K);
 
+// K-split factor gemm_bf16 uses for an N x K weight at token tile BN
+// (`requested` = ep.split: 0 = by shape, 1 = none).
+int gemm_nsplit(int N, int K, int BN, int requested);
+
+// Tensor map of a bf16 [rows, cols] operand with a box of 64 x box_rows
+// (128-byte swizzle), as the GEMMs load it.
+CUtensorMap gemm_tmap(const void *ptr, long rows, long cols, long box_rows);
+
 // Called whenever a per-thread scratch buffer moves, so that cached CUDA graphs
 // holding its old address are dropped (defined by the ABI layer).
 void scratch_moved();

@@ -56,6 +56,9 @@ typedef struct {
     int enc_max_frames;  /* encoder batch: log-mel frames in total (default 64 x 3001, 30 s each) */
     int keep_logits;     /* 1 = also store every step's fp32 logits for ct_engine_last_logits; 0 (default):
                             the LM head hands only per-tile maxima to the greedy argmax in its epilogue */
+    int fused_step;      /* 1 = run each decode step as one persistent kernel (one CTA per SM, grid
+                            barriers between its phases) instead of ~70 separate launches; same
+                            results bit for bit.  Needs the whole GPU: one such engine per device */
 } ct_engine_config;
 
 typedef struct {

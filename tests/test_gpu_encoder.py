@@ -6,7 +6,10 @@ Tolerance: the encoder runs its GEMMs on bf16 tensor cores with the
 activations split into bf16 hi + lo planes (about 16 mantissa bits) and fp32
 accumulation; the oracle is fp32 throughout.  Over 48 layers the difference
 stays near 1e-4 of the output scale; ENC_TOL = 2e-3 (max |engine - oracle|
-over max |oracle|, per utterance) leaves an order of magnitude.
+over max |oracle|, per utterance) leaves an order of magnitude.  With plain
+bf16 activations (precision 0: one plane, every GEMM input rounded to 8
+mantissa bits, fp32 accumulation) the error grows with depth; ENC_TOL_BF16
+is the stated tolerance for that mode.
 """
 import ctypes
 import importlib
@@ -19,6 +22,7 @@ import pyoracle as po
 
 pytestmark = pytest.mark.gpu
 ENC_TOL = 2e-3
+ENC_TOL_BF16 = 5e-2
 E2E_MARGIN_TOL = 0.05
 
 
@@ -78,7 +82,8 @@ def test_encoder_ragged_batch_vs_oracle(abi, full_model, wmod):
         assert err <= ENC_TOL, (b, err)
 
 
-def test_encoder_long_vs_reference(abi, full_model):
+@pytest.mark.parametrize("precision,tol", [(1, ENC_TOL), (0, ENC_TOL_BF16)])
+def test_encoder_long_vs_reference(abi, full_model, precision, tol):
     """The benchmark's lengths: 30 s, 10 s and 1.3 s (T_enc 376, 126 and 17)
     packed in one encoder batch, against the reference's own encoder
     (model.h:573-609 on backends/cpu/backend.c, compiled from the reference
@@ -87,7 +92,8 @@ def test_encoder_long_vs_reference(abi, full_model):
     the online-softmax rescaling across tiles, position-table rows
     k - q + T_max - 1 far from the diagonal, and the depthwise-convolution
     halo between tiles.  Same weights as the other tests of this module
-    (seed 21)."""
+    (seed 21).  Both activation precisions: hi+lo planes (the default) and
+    plain bf16."""
     import make_encoder_long as mel_long
     gold = np.load(po.os.path.join(po.os.path.dirname(inputs.__file__), "encoder_long_ref.npz"))
     mel, T_mel = mel_long.case()
@@ -96,7 +102,7 @@ def test_encoder_long_vs_reference(abi, full_model):
     assert list(T_enc) == [376, 126, 17]
     for b in range(len(T_mel)):
         assert np.isclose(mel[b, :, :T_mel[b]].astype(np.float64).sum(), float(gold[f"checksum{b}"]))
-    eng = make_engine(abi, full_model)
+    eng = make_engine(abi, full_model, precision=precision)
     try:
         got = eng.encode(mels_of(mel, T_mel))
         assert eng.status() == 0
@@ -111,9 +117,9 @@ def test_encoder_long_vs_reference(abi, full_model):
         # per 64-row tile as well, so an error confined to a later key tile shows
         for r0 in range(0, ref.shape[0], 64):
             e_t = float(np.max(np.abs(got[b][r0:r0 + 64] - ref[r0:r0 + 64])) / np.max(np.abs(ref)))
-            assert e_t <= ENC_TOL, (b, r0, e_t)
-    print("encoder max error / output scale per utterance (T_enc 376, 126, 17):", errs)
-    assert max(errs) <= ENC_TOL, errs
+            assert e_t <= tol, (b, r0, e_t)
+    print(f"precision {precision}: encoder max error / output scale per utterance (T_enc 376, 126, 17):", errs)
+    assert max(errs) <= tol, errs
 
 
 def test_encoder_batch_invariance_long(abi, full_model):
