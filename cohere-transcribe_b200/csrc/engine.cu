@@ -690,6 +690,7 @@ struct ct_engine {
     std::map<std::string, std::pair<double, long long>> mark_ms;   // label -> (total ms, count)
     cudaEvent_t aev0 = nullptr, aev1 = nullptr;
     std::vector<int> slot_steps;     // steps run since admission (host mirror of the KV length)
+    std::vector<int> slot_limit;     // steps after which the slot's sequence has certainly finished
     enc::State *enc = nullptr;       // packed encoder (null when the blob has no encoder weights)
     // queued utterance: log-mel [N_MELS][T_mel] or 16 kHz samples (n_samples > 0)
     // input in job_ring (ring_off >= 0, float offset) or in the vector (ring full)
@@ -1132,6 +1133,7 @@ static int admit(ct_engine *e) {
         e->slot_id[slot] = p.id;
         e->slot_pages[slot] = pages;
         e->slot_steps[slot] = 0;
+        e->slot_limit[slot] = p.forced > 0 ? std::min(p.forced, MAX_SEQ - plen) : MAX_SEQ - plen;
         e->slot_tenc[slot] = p.T_enc;
         ++e->st_acc.admitted;
         // slot record + page tables (copied for all admissions at once below)
@@ -1355,6 +1357,17 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
     if (!e) return CT_EINVAL;
     EK(cudaSetDevice(e->device));
     int inflight = 0;   // steps launched since the last synchronisation
+    auto sync_inflight = [&]() -> int {
+        EK(cudaEventSynchronize(e->sev1[inflight - 1]));
+        for (int j = 0; j < inflight; ++j) {
+            float ms = 0.0f;
+            EK(cudaEventElapsedTime(&ms, e->sev0[j], e->sev1[j]));
+            e->step_ms += ms;
+            e->step_log.push_back(ms);
+        }
+        inflight = 0;
+        return 0;
+    };
     for (int it = 0; it < n_steps; ++it) {
         if (inflight == 0) {   // harvest and admit only at synchronisation points
             if (e->pending.empty() && !e->mel_pending.empty()) {
@@ -1369,6 +1382,18 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
         if (e->n_live == 0) {
             if (!e->pending.empty()) return CT_EBUSY;   // nothing live and nothing admissible
             break;
+        }
+        // A sequence has certainly finished on the device once it has run its
+        // forced length of steps (or MAX_SEQ minus its prompt).  When every
+        // live sequence has, the queued steps already retired them: collect
+        // them instead of launching a step over no rows.
+        bool any_active = false;
+        for (int i = 0; i < e->cfg.max_slots && !any_active; ++i)
+            any_active = e->slot_live[i] && e->slot_steps[i] < e->slot_limit[i];
+        if (!any_active && inflight > 0) {
+            const int rc = sync_inflight();
+            if (rc) return rc;
+            continue;
         }
         int rows = 0;
         double self_b = 0.0, cross_b = 0.0;
@@ -1396,14 +1421,8 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
         // ends; the host synchronises every kStepRing steps, at the last step,
         // and for every step in profile mode.
         if (inflight == ct_engine::kStepRing || it == n_steps - 1 || e->cfg.profile) {
-            EK(cudaEventSynchronize(e->sev1[inflight - 1]));
-            for (int j = 0; j < inflight; ++j) {
-                float ms = 0.0f;
-                EK(cudaEventElapsedTime(&ms, e->sev0[j], e->sev1[j]));
-                e->step_ms += ms;
-                e->step_log.push_back(ms);
-            }
-            inflight = 0;
+            const int rc = sync_inflight();
+            if (rc) return rc;
         }
         e->st_acc.kernel_launches += b->kernels;
         ++e->n_steps;
@@ -1864,6 +1883,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     e->slot_id.assign(S, -1);
     e->slot_pages.assign(S, {});
     e->slot_steps.assign(S, 0);
+    e->slot_limit.assign(S, 0);
     e->slot_tenc.assign(S, 0);
     e->slot_plen.assign(S, cfg.n_prompt);
     EK(cudaEventCreate(&e->eev0));

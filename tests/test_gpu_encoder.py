@@ -8,8 +8,9 @@ accumulation; the oracle is fp32 throughout.  Over 48 layers the difference
 stays near 1e-4 of the output scale; ENC_TOL = 2e-3 (max |engine - oracle|
 over max |oracle|, per utterance) leaves an order of magnitude.  With plain
 bf16 activations (precision 0: one plane, every GEMM input rounded to 8
-mantissa bits, fp32 accumulation) the error grows with depth; ENC_TOL_BF16
-is the stated tolerance for that mode.
+mantissa bits, fp32 accumulation) the error grows with depth: 7.6e-3 of the
+output scale at 30 s; ENC_TOL_BF16 = 2e-2 is the stated tolerance for that
+mode.
 """
 import ctypes
 import importlib
@@ -22,7 +23,7 @@ import pyoracle as po
 
 pytestmark = pytest.mark.gpu
 ENC_TOL = 2e-3
-ENC_TOL_BF16 = 5e-2
+ENC_TOL_BF16 = 2e-2
 E2E_MARGIN_TOL = 0.05
 
 
