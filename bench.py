@@ -86,6 +86,11 @@ NCU_TRAFFIC = {
     # rows: 31.509504 MB read + 24.338688 MB written.  Unit: packed row.  The
     # 13.1 MB of weights do not grow with the rows, so the scaled figure is an
     # upper bound at larger batches.
+    # profiles/gemm_decode_ffn_lmhead.md: one layer's FFN1 + FFN2 at 64 rows
+    # (18,087,936 algorithmic bytes): 8.760832 + 9.787648 MB read, 0 written.
+    # Unit: algorithmic byte (weights + activation planes of the two launches).
+    "decode FFN GEMMs (tcgen05)": {"bytes": 8.760832e6 + 9.787648e6, "units": 18087936.0,
+                                   "unit": "algorithmic byte", "source": "profiles/gemm_decode_ffn_lmhead.md"},
     "encoder FFN1 GEMM (tcgen05, persistent)": {"bytes": 31.509504e6 + 24.338688e6, "units": 3545.0,
                                                 "unit": "packed row",
                                                 "source": "profiles/gemm_persistent_encoder_ffn1.md"},
