@@ -170,12 +170,16 @@ __global__ void __launch_bounds__(256) ln_enc(const float *x, int R, const bf16 
 // the quad of threads that holds it; the probabilities feed the P.V MMA
 // directly from the score accumulators.  qkv_h / qkv_l rows hold [Q | K | V]
 // (stride 3D); P_h / P_l the projected table of 2*T_max - 1 rows.  Output:
-// bf16 hi/lo planes.
+// bf16 hi/lo planes.  With TWO = false (plain bf16 activations) only the hi
+// planes are staged and every product is one bf16 MMA (fp32 accumulate); the
+// shared-memory footprint then halves and two CTAs share an SM.
 constexpr int RQ = 64, RB = 128, RS = DK + 8;   // query/key tile, CTA band rows, smem row stride (bf16)
+template <bool TWO>
 struct RelposSmem {
-    bf16 qh[RQ][RS], ql[RQ][RS];
-    bf16 kh[RQ][RS], kl[RQ][RS];   // K tile, then the V tile of the same keys
-    bf16 ph[RB][RS], pl[RB][RS];   // P band
+    static constexpr int NP = TWO ? 2 : 1;
+    bf16 q[NP][RQ][RS];
+    bf16 k[NP][RQ][RS];   // K tile, then the V tile of the same keys
+    bf16 p[NP][RB][RS];   // P band
     float uk[RQ], vp[RB];          // u.K[k], v.P[m]
     float bd[4][16][84];           // per warp: its 16 x 80 band tile
 };
@@ -214,36 +218,43 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // Asynchronously copy N rows of DK bf16 values from the hi and lo planes
 // (row i at plane + src_row(i) * ld + col0, or zeros where src_row(i) < 0) into
 // padded shared rows; 16-byte pieces spread over the 128 threads.
-template <int N, class RowOf>
+template <int N, int NP, class RowOf>
 __device__ __forceinline__ void stage_planes(RowOf src_row, const bf16 *ph_g, const bf16 *pl_g, size_t ld, int col0,
                                              bf16 (*hi)[RS], bf16 (*lo)[RS]) {
     constexpr int CH = DK / 8;   // 16-byte pieces per row and plane
-    for (int id = threadIdx.x; id < N * 2 * CH; id += 128) {
-        const int row = id / (2 * CH), rem = id % (2 * CH), plane = rem / CH, c = (rem % CH) * 8;
+    for (int id = threadIdx.x; id < N * NP * CH; id += 128) {
+        const int row = id / (NP * CH), rem = id % (NP * CH), plane = rem / CH, c = (rem % CH) * 8;
         const int sr = src_row(row);
         const bf16 *g = plane ? pl_g : ph_g;
         const bf16 *src = sr >= 0 ? g + (size_t)sr * ld + col0 + c : g;
         cp_async16(plane ? &lo[row][c] : &hi[row][c], src, sr >= 0);
     }
 }
-// dot[i] = bias . (hi[i] + lo[i]) for N rows, 128 / N threads per row.
+// dot[i] = bias . (hi[i] + lo[i]) (lo null: bias . hi[i]) for N rows, 128 / N threads per row.
 template <int N>
 __device__ __forceinline__ void row_dots(const bf16 (*hi)[RS], const bf16 (*lo)[RS], const bf16 *bias, float *dot) {
     constexpr int TPR = 128 / N, PER = DK / TPR;
     const int row = threadIdx.x / TPR, part = threadIdx.x % TPR;
     float acc = 0.0f;
     for (int c = part * PER; c < part * PER + PER; ++c)
-        acc += bf2f(bias[c]) * (__bfloat162float(hi[row][c]) + __bfloat162float(lo[row][c]));
+        acc += bf2f(bias[c]) * (__bfloat162float(hi[row][c]) + (lo ? __bfloat162float(lo[row][c]) : 0.0f));
 #pragma unroll
     for (int o = 1; o < TPR; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (part == 0) dot[row] = acc;
 }
 
-__global__ void __launch_bounds__(128, 1) relpos_tc(const bf16 *qkv_h, const bf16 *qkv_l, const bf16 *P_h,
-                                                    const bf16 *P_l, Batch b, const bf16 *pbu, const bf16 *pbv,
-                                                    bf16 *hi, bf16 *lo) {
+template <bool TWO>
+__global__ void __launch_bounds__(128, TWO ? 1 : 2) relpos_tc(const bf16 *qkv_h, const bf16 *qkv_l, const bf16 *P_h,
+                                                              const bf16 *P_l, Batch b, const bf16 *pbu,
+                                                              const bf16 *pbv, bf16 *hi, bf16 *lo) {
     extern __shared__ __align__(16) uint8_t relpos_raw[];
-    RelposSmem &sm = *reinterpret_cast<RelposSmem *>(relpos_raw);
+    using Smem = RelposSmem<TWO>;
+    constexpr int NP = Smem::NP;
+    Smem &sm = *reinterpret_cast<Smem *>(relpos_raw);
+    // plane views (the lo views alias the hi planes when TWO is false and are never read then)
+    bf16 (*sqh)[RS] = sm.q[0], (*sql)[RS] = sm.q[NP - 1];
+    bf16 (*skh)[RS] = sm.k[0], (*skl)[RS] = sm.k[NP - 1];
+    bf16 (*sph)[RS] = sm.p[0], (*spl)[RS] = sm.p[NP - 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, tig = lane & 3;
     const int h = blockIdx.y;
@@ -256,7 +267,7 @@ __global__ void __launch_bounds__(128, 1) relpos_tc(const bf16 *qkv_h, const bf1
     const size_t ld = (size_t)3 * D;
     const bf16 *ub = pbu + h * DK, *vb = pbv + h * DK;
 
-    stage_planes<RQ>([&](int r) { return q0 + r < T ? base + q0 + r : -1; }, qkv_h, qkv_l, ld, h * DK, sm.qh, sm.ql);
+    stage_planes<RQ, NP>([&](int r) { return q0 + r < T ? base + q0 + r : -1; }, qkv_h, qkv_l, ld, h * DK, sqh, sql);
 
     float o[DK / 8][4];
 #pragma unroll
@@ -267,18 +278,18 @@ __global__ void __launch_bounds__(128, 1) relpos_tc(const bf16 *qkv_h, const bf1
 
     for (int k0 = 0; k0 < T; k0 += RQ) {
         __syncthreads();   // the previous tile's V and band reads are done
-        stage_planes<RQ>([&](int r) { return k0 + r < T ? base + k0 + r : -1; }, qkv_h, qkv_l, ld, D + h * DK, sm.kh,
-                         sm.kl);
+        stage_planes<RQ, NP>([&](int r) { return k0 + r < T ? base + k0 + r : -1; }, qkv_h, qkv_l, ld, D + h * DK, skh,
+                             skl);
         // CTA band row m <-> relative offset (k - q) = (k0 - q0 - 63) + m
         const int prow0 = (k0 - q0) - (RQ - 1) + Tm - 1;
-        stage_planes<RB>([&](int m) {
+        stage_planes<RB, NP>([&](int m) {
             const int pr = prow0 + m;
             return (m < 2 * RQ - 1 && pr >= 0 && pr < PL) ? pr : -1;
-        }, P_h, P_l, (size_t)D, h * DK, sm.ph, sm.pl);
+        }, P_h, P_l, (size_t)D, h * DK, sph, spl);
         cp_async_wait_all();
         __syncthreads();
-        row_dots<RQ>(sm.kh, sm.kl, ub, sm.uk);
-        row_dots<RB>(sm.ph, sm.pl, vb, sm.vp);
+        row_dots<RQ>(skh, TWO ? skl : nullptr, ub, sm.uk);
+        row_dots<RB>(sph, TWO ? spl : nullptr, vb, sm.vp);
         __syncthreads();
 
         float sc[RQ / 8][4], bnd[10][4];
@@ -290,32 +301,40 @@ __global__ void __launch_bounds__(128, 1) relpos_tc(const bf16 *qkv_h, const bf1
         const int brow = (lane & 7) + ((lane >> 4) << 3), bcol = ((lane >> 3) & 1) * 8;
 #pragma unroll 2
         for (int ks = 0; ks < DK / 16; ++ks) {
-            uint32_t ah0, ah1, ah2, ah3, al0, al1, al2, al3;
-            ldsm_x4(&sm.qh[arow][ks * 16 + acol], ah0, ah1, ah2, ah3);
-            ldsm_x4(&sm.ql[arow][ks * 16 + acol], al0, al1, al2, al3);
+            uint32_t ah0, ah1, ah2, ah3, al0 = 0, al1 = 0, al2 = 0, al3 = 0;
+            ldsm_x4(&sqh[arow][ks * 16 + acol], ah0, ah1, ah2, ah3);
+            if (TWO) ldsm_x4(&sql[arow][ks * 16 + acol], al0, al1, al2, al3);
 #pragma unroll
             for (int np = 0; np < RQ / 16; ++np) {   // key n8-tile pairs
-                uint32_t bh0, bh1, bh2, bh3, bl0, bl1, bl2, bl3;
-                ldsm_x4(&sm.kh[np * 16 + brow][ks * 16 + bcol], bh0, bh1, bh2, bh3);
-                ldsm_x4(&sm.kl[np * 16 + brow][ks * 16 + bcol], bl0, bl1, bl2, bl3);
+                uint32_t bh0, bh1, bh2, bh3, bl0 = 0, bl1 = 0, bl2 = 0, bl3 = 0;
+                ldsm_x4(&skh[np * 16 + brow][ks * 16 + bcol], bh0, bh1, bh2, bh3);
+                if (TWO) ldsm_x4(&skl[np * 16 + brow][ks * 16 + bcol], bl0, bl1, bl2, bl3);
                 mma16816(sc[2 * np], ah0, ah1, ah2, ah3, bh0, bh1);
-                mma16816(sc[2 * np], ah0, ah1, ah2, ah3, bl0, bl1);
-                mma16816(sc[2 * np], al0, al1, al2, al3, bh0, bh1);
+                if (TWO) {
+                    mma16816(sc[2 * np], ah0, ah1, ah2, ah3, bl0, bl1);
+                    mma16816(sc[2 * np], al0, al1, al2, al3, bh0, bh1);
+                }
                 mma16816(sc[2 * np + 1], ah0, ah1, ah2, ah3, bh2, bh3);
-                mma16816(sc[2 * np + 1], ah0, ah1, ah2, ah3, bl2, bl3);
-                mma16816(sc[2 * np + 1], al0, al1, al2, al3, bh2, bh3);
+                if (TWO) {
+                    mma16816(sc[2 * np + 1], ah0, ah1, ah2, ah3, bl2, bl3);
+                    mma16816(sc[2 * np + 1], al0, al1, al2, al3, bh2, bh3);
+                }
             }
 #pragma unroll
             for (int np = 0; np < 5; ++np) {         // band n8-tile pairs
-                uint32_t bh0, bh1, bh2, bh3, bl0, bl1, bl2, bl3;
-                ldsm_x4(&sm.ph[mbw + np * 16 + brow][ks * 16 + bcol], bh0, bh1, bh2, bh3);
-                ldsm_x4(&sm.pl[mbw + np * 16 + brow][ks * 16 + bcol], bl0, bl1, bl2, bl3);
+                uint32_t bh0, bh1, bh2, bh3, bl0 = 0, bl1 = 0, bl2 = 0, bl3 = 0;
+                ldsm_x4(&sph[mbw + np * 16 + brow][ks * 16 + bcol], bh0, bh1, bh2, bh3);
+                if (TWO) ldsm_x4(&spl[mbw + np * 16 + brow][ks * 16 + bcol], bl0, bl1, bl2, bl3);
                 mma16816(bnd[2 * np], ah0, ah1, ah2, ah3, bh0, bh1);
-                mma16816(bnd[2 * np], ah0, ah1, ah2, ah3, bl0, bl1);
-                mma16816(bnd[2 * np], al0, al1, al2, al3, bh0, bh1);
+                if (TWO) {
+                    mma16816(bnd[2 * np], ah0, ah1, ah2, ah3, bl0, bl1);
+                    mma16816(bnd[2 * np], al0, al1, al2, al3, bh0, bh1);
+                }
                 mma16816(bnd[2 * np + 1], ah0, ah1, ah2, ah3, bh2, bh3);
-                mma16816(bnd[2 * np + 1], ah0, ah1, ah2, ah3, bl2, bl3);
-                mma16816(bnd[2 * np + 1], al0, al1, al2, al3, bh2, bh3);
+                if (TWO) {
+                    mma16816(bnd[2 * np + 1], ah0, ah1, ah2, ah3, bl2, bl3);
+                    mma16816(bnd[2 * np + 1], al0, al1, al2, al3, bh2, bh3);
+                }
             }
         }
         // band tile -> shared memory, read back along the diagonals
@@ -367,8 +386,8 @@ __global__ void __launch_bounds__(128, 1) relpos_tc(const bf16 *qkv_h, const bf1
         for (int i = 0; i < DK / 8; ++i) { o[i][0] *= c0; o[i][1] *= c0; o[i][2] *= c1; o[i][3] *= c1; }
 
         __syncthreads();   // every warp is done with the K tile: stage V over it
-        stage_planes<RQ>([&](int r) { return k0 + r < T ? base + k0 + r : -1; }, qkv_h, qkv_l, ld, 2 * D + h * DK,
-                         sm.kh, sm.kl);
+        stage_planes<RQ, NP>([&](int r) { return k0 + r < T ? base + k0 + r : -1; }, qkv_h, qkv_l, ld,
+                             2 * D + h * DK, skh, skl);
         cp_async_wait_all();
         __syncthreads();
         // O += P.V, P from the score accumulators (16-key blocks)
@@ -384,15 +403,19 @@ __global__ void __launch_bounds__(128, 1) relpos_tc(const bf16 *qkv_h, const bf1
                            pl3 = pack_bf16(pb2[2] - hv[6], pb2[3] - hv[7]);
 #pragma unroll
             for (int dp = 0; dp < DK / 16; ++dp) {   // dim n8-tile pairs
-                uint32_t vh0, vh1, vh2, vh3, vl0, vl1, vl2, vl3;
-                ldsm_x4_t(&sm.kh[kk * 16 + (lane & 15)][dp * 16 + (lane >> 4) * 8], vh0, vh1, vh2, vh3);
-                ldsm_x4_t(&sm.kl[kk * 16 + (lane & 15)][dp * 16 + (lane >> 4) * 8], vl0, vl1, vl2, vl3);
+                uint32_t vh0, vh1, vh2, vh3, vl0 = 0, vl1 = 0, vl2 = 0, vl3 = 0;
+                ldsm_x4_t(&skh[kk * 16 + (lane & 15)][dp * 16 + (lane >> 4) * 8], vh0, vh1, vh2, vh3);
+                if (TWO) ldsm_x4_t(&skl[kk * 16 + (lane & 15)][dp * 16 + (lane >> 4) * 8], vl0, vl1, vl2, vl3);
                 mma16816(o[2 * dp], ph0, ph1, ph2, ph3, vh0, vh1);
-                mma16816(o[2 * dp], ph0, ph1, ph2, ph3, vl0, vl1);
-                mma16816(o[2 * dp], pl0, pl1, pl2, pl3, vh0, vh1);
+                if (TWO) {
+                    mma16816(o[2 * dp], ph0, ph1, ph2, ph3, vl0, vl1);
+                    mma16816(o[2 * dp], pl0, pl1, pl2, pl3, vh0, vh1);
+                }
                 mma16816(o[2 * dp + 1], ph0, ph1, ph2, ph3, vh2, vh3);
-                mma16816(o[2 * dp + 1], ph0, ph1, ph2, ph3, vl2, vl3);
-                mma16816(o[2 * dp + 1], pl0, pl1, pl2, pl3, vh2, vh3);
+                if (TWO) {
+                    mma16816(o[2 * dp + 1], ph0, ph1, ph2, ph3, vl2, vl3);
+                    mma16816(o[2 * dp + 1], pl0, pl1, pl2, pl3, vh2, vh3);
+                }
             }
         }
     }
@@ -631,7 +654,10 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     int dev = 0;
     CT_CHECK(cudaGetDevice(&dev));
     if (relpos_dev != dev) {
-        CT_CHECK(cudaFuncSetAttribute(relpos_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(RelposSmem)));
+        CT_CHECK(cudaFuncSetAttribute(relpos_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)sizeof(RelposSmem<true>)));
+        CT_CHECK(cudaFuncSetAttribute(relpos_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)sizeof(RelposSmem<false>)));
         relpos_dev = dev;
     }
     const Weights_ &w = st.w;
@@ -685,15 +711,19 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.sa_lnw, L.sa_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
         GemmEpilogue eq;
-        eq.epi = EPI_BF16; eq.bias = L.qkv_b; eq.Ybf = st.qkvp[0]; eq.Ybf_lo = st.qkvp[1]; eq.ldy = 3 * D;
+        eq.epi = EPI_BF16; eq.bias = L.qkv_b; eq.Ybf = st.qkvp[0]; eq.Ybf_lo = st.two ? st.qkvp[1] : nullptr; eq.ldy = 3 * D;
         egemm_enc(s, st, L.qkv_w, 3 * D, D, xap, R3, RT, eq);
         mark(s, st, "enc_gemm_qkv");
         GemmEpilogue ep;
-        ep.epi = EPI_BF16; ep.Ybf = st.Pp[0]; ep.Ybf_lo = st.Pp[1]; ep.ldy = D;
+        ep.epi = EPI_BF16; ep.Ybf = st.Pp[0]; ep.Ybf_lo = st.two ? st.Pp[1] : nullptr; ep.ldy = D;
         egemm_enc(s, st, L.sa_pw, D, D, st.posp, PL, 2 * st.T_cap, ep);
         mark(s, st, "enc_gemm_pos");
-        relpos_tc<<<dim3(NQ, H), 128, sizeof(RelposSmem), s>>>(st.qkvp[0], st.qkvp[1], st.Pp[0], st.Pp[1], bt,
-                                                               L.sa_pbu, L.sa_pbv, st.ap[0], lo_p);
+        if (st.two)
+            relpos_tc<true><<<dim3(NQ, H), 128, sizeof(RelposSmem<true>), s>>>(
+                st.qkvp[0], st.qkvp[1], st.Pp[0], st.Pp[1], bt, L.sa_pbu, L.sa_pbv, st.ap[0], lo_p);
+        else
+            relpos_tc<false><<<dim3(NQ, H), 128, sizeof(RelposSmem<false>), s>>>(
+                st.qkvp[0], nullptr, st.Pp[0], nullptr, bt, L.sa_pbu, L.sa_pbv, st.ap[0], nullptr);
         mark(s, st, "enc_relpos_attn");
         GemmEpilogue eo2;
         eo2.epi = EPI_FMADD; eo2.scale = 1.0f; eo2.bias = L.sa_ob; eo2.Y = st.x; eo2.ldy = D;
