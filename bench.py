@@ -41,6 +41,12 @@ One bench step runs three legs (A and B over that batch, C alone):
      under "config5" with tokens and audio summed over ranks and the worst
      rank's wall time.
 
+Precision: the headline runs --precision 0, bf16 weights and bf16 activations
+with fp32 accumulation (the configurations' "bf16 weights with fp32
+accumulate").  On one GPU legs A and B then run once more at the other
+precision (--precision 1: activations carried as bf16 hi + lo planes, close to
+fp32) on a fresh engine, reported under "precision_compare".
+
 `--impl reference` times the reference's own CPU implementation (its
 backends/cpu/backend.c driven by its model.h, prebuilt under oracle/_ref/) on
 bounded samples of the same workload, one utterance per host thread: greedy
@@ -82,15 +88,15 @@ NCU_TRAFFIC = {
     # written.  Unit: algorithmic byte (the K/V rows the launch must read).
     "paged cross-attention": {"bytes": 59.354368e6 + 0.41216e6, "units": 14080 * 4096.0,
                               "unit": "algorithmic byte", "source": "profiles/attn_paged_decode.md"},
-    # profiles/gemm_persistent_encoder_ffn1.md: layer 0's FFN1 over 3,545 packed
-    # rows: 31.509504 MB read + 24.338688 MB written.  Unit: packed row.  The
-    # 13.1 MB of weights do not grow with the rows, so the scaled figure is an
-    # upper bound at larger batches.
     # profiles/gemm_decode_ffn_lmhead.md: one layer's FFN1 + FFN2 at 64 rows
     # (18,087,936 algorithmic bytes): 8.760832 + 9.787648 MB read, 0 written.
     # Unit: algorithmic byte (weights + activation planes of the two launches).
     "decode FFN GEMMs (tcgen05)": {"bytes": 8.760832e6 + 9.787648e6, "units": 18087936.0,
                                    "unit": "algorithmic byte", "source": "profiles/gemm_decode_ffn_lmhead.md"},
+    # profiles/gemm_persistent_encoder_ffn1.md: layer 0's FFN1 over 3,545 packed
+    # rows: 31.509504 MB read + 24.338688 MB written.  Unit: packed row.  The
+    # 13.1 MB of weights do not grow with the rows, so the scaled figure is an
+    # upper bound at larger batches.
     "encoder FFN1 GEMM (tcgen05, persistent)": {"bytes": 31.509504e6 + 24.338688e6, "units": 3545.0,
                                                 "unit": "packed row",
                                                 "source": "profiles/gemm_persistent_encoder_ffn1.md"},
@@ -401,7 +407,11 @@ def main():
                     help="token cap per utterance of the CPU decode sample (0 = each utterance's forced length)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-cuda-ref", action="store_true", help="skip the reference CUDA backend leg")
-    ap.add_argument("--precision", type=int, default=1)
+    ap.add_argument("--precision", type=int, default=0, choices=[0, 1],
+                    help="0: bf16 activations (the configurations' bf16 / fp32-accumulate contract); "
+                         "1: activations as bf16 hi+lo planes (near-fp32 activations)")
+    ap.add_argument("--no-compare-precision", action="store_true",
+                    help="skip timing legs A and B once more at the other precision (one GPU only)")
     ap.add_argument("--batch", type=int, default=BATCH, help="utterances per GPU per step (profiling cases)")
     ap.add_argument("--kv-pages", type=int, default=0, help="page-pool size (0 = engine default)")
     ap.add_argument("--max-len", type=int, default=0, help="cap the forced lengths (profiling cases)")
@@ -672,7 +682,8 @@ def main():
                 "bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": ach / pk["bf16_tflops"], "ms_per_step": ms_, "launches": n_l,
                 "algorithmic_flops_per_launch": fl, "avg_launch_ms": ms_ / n_l,
-                "note": "activations as bf16 hi+lo planes: the tensor cores execute 2x the algorithmic flops"}
+                "note": ("activations as bf16 hi+lo planes: the tensor cores execute 2x the algorithmic flops"
+                         if args.precision else "plain bf16 activations: executed = algorithmic flops")}
     # the dominant kernel of the whole bench step by device time
     roof = None
     if rooflines:
@@ -710,6 +721,45 @@ def main():
             "profiled_step_breakdown": breakdown, "clocks": clk.summary(), "device_status": status,
             "precision": "bf16 weights, activations as bf16 hi+lo planes, fp32 accumulate" if args.precision else
             "bf16 weights and activations, fp32 accumulate"}
+    if world == 1 and not args.no_compare_precision and ("A" in legs or with_enc):
+        # Legs A and B once more on an engine at the other precision (same
+        # inputs, warm-up and step count), so the line carries both.
+        other = 1 - args.precision
+        e2 = abi.Engine(lib, dev, wb, ws, max_slots=args.max_slots, max_rows=1024, precision=other,
+                        kv_pages=args.kv_pages, no_pdl=int(args.no_pdl), fused_step=args.fused_step,
+                        enc_max_utts=enc_utts if with_enc else -1, enc_max_frames=enc_frames)
+        for _ in range(args.warmup):
+            if "A" in legs:
+                leg_a(e2, [])
+            if with_enc:
+                leg_b(e2)
+        st2, da, wa, db, wb_ = [], 0.0, 0.0, 0.0, 0.0
+        for _ in range(K):
+            if "A" in legs:
+                s0 = e2.stats()
+                t0 = time.perf_counter()
+                leg_a(e2, st2)
+                wa += time.perf_counter() - t0
+                s1 = e2.stats()
+                da += (s1["step_ms"] - s0["step_ms"]) + (s1["admit_ms"] - s0["admit_ms"])
+            if with_enc:
+                s0 = e2.stats()
+                t0 = time.perf_counter()
+                leg_b(e2)
+                wb_ += time.perf_counter() - t0
+                s1 = e2.stats()
+                db += (s1["step_ms"] - s0["step_ms"]) + (s1["admit_ms"] - s0["admit_ms"]) + (s1["enc_ms"] - s0["enc_ms"])
+        st_other = e2.status()
+        e2.close()
+        line["precision_compare"] = {
+            "precision": "bf16 weights, activations as bf16 hi+lo planes, fp32 accumulate" if other else
+            "bf16 weights and activations, fp32 accumulate",
+            "value": tokens_per_step * K / (da / 1000.0) if da > 0 else None,
+            "e2e": tokens_per_step * K / wa if wa > 0 else None, "unit": "tokens/s",
+            "p50_step_ms": statistics.median(st2) if st2 else None,
+            "rtfx": audio_s * K / (db / 1000.0) if db > 0 else None,
+            "rtfx_e2e": audio_s * K / wb_ if wb_ > 0 else None, "device_status": st_other,
+            "note": "legs A and B of the same workload, timed after the headline legs on the same GPU"}
     if rank == 0 and world == 1 and not args.no_cpu:
         ref = ReferenceCPU(case, enc, audio, ncores, args.cpu_tokens)
         t, s_ = ref.decode()

@@ -60,6 +60,13 @@ __device__ __forceinline__ uint64_t globaltimer() {
 
 __device__ __forceinline__ void set_status(int code) { atomicCAS(&g_ct_status, 0, code); }
 
+// x * sigmoid(g) = x / (1 + e^-g) with the hardware exponential and an
+// approximate divide: a few fp32 ulp, and no branch (the IEEE division's
+// slow-path test serialises an otherwise unrolled epilogue).  For g < -88 the
+// denominator is +inf and the result is a signed zero, the limit.
+__device__ __forceinline__ float mul_sigmoid(float x, float g) { return __fdividef(x, 1.0f + __expf(-g)); }
+__device__ __forceinline__ float silu_fast(float x) { return mul_sigmoid(x, x); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

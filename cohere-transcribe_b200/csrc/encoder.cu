@@ -56,54 +56,110 @@ struct Batch {
 };
 
 // ------------------------------------------------------------ kernels -----
-// conv0 3x3 stride 2 pad 1 on the (time, mel) plane of each utterance, 1 -> C
-// channels, ReLU; output rows packed by utterance, channels last [R1][F1][C].
-__global__ void conv0_packed(const float *mel, Batch b, const bf16 *w, const bf16 *bias, float *out) {
-    const size_t n = (size_t)b.R1 * F1 * C;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int c = (int)(i % C), f = (int)((i / C) % F1);
-        const int row = (int)(i / ((size_t)C * F1));
-        const int u = b.row_utt1[row];
-        const int t = row - b.r1_off[u], Tm = b.T_mel[u];
-        const float *m = mel + b.mel_off[u];
-        float s = bf2f(bias[c]);
-        for (int kh = 0; kh < 3; ++kh) {
-            const int ih = 2 * t - 1 + kh;
-            if (ih < 0 || ih >= Tm) continue;
-            for (int kw = 0; kw < 3; ++kw) {
-                const int iw = 2 * f - 1 + kw;
-                if (iw < 0 || iw >= F0) continue;
-                s += m[(size_t)iw * Tm + ih] * bf2f(w[c * 9 + kh * 3 + kw]);
-            }
+// The first two subsampling convolutions fused (backends/cpu/backend.c:188-229:
+// conv0 3x3/s2 1 -> C + ReLU, then the depthwise 3x3/s2), written as the bf16
+// planes the following 1x1 GEMM reads: out[r2 * F2 + f2][c].  One CTA per
+// stage-2 row r2 (time step t2 of utterance u), thread = channel c.  The conv0
+// activations A[t1][f1][c] that the depthwise stencil needs (t1 = 2 t2 - 1 ..
+// 2 t2 + 1, all f1) are recomputed from the 7 log-mel frames 4 t2 - 3 .. 4 t2 + 3
+// staged in shared memory, walking f2 left to right with a 3 x 3 window of A
+// values in registers (two new A columns per step), so the [R1][F1][C]
+// intermediate never reaches memory.  Padding: mel outside the utterance or
+// the bins is 0 (conv0's), A outside [0, T1) x [0, F1) is 0 (the depthwise's).
+// Summation order per output: conv0 taps (kh, kw) row-major, then depthwise
+// taps (kh, kw) row-major, each starting from its bias, as the reference.
+constexpr int SUB_TH = 7;   // mel frames per stage-2 row (4 t2 - 3 .. 4 t2 + 3)
+__global__ void __launch_bounds__(C) conv0_dw_planes(const float *mel, Batch b, const bf16 *w0, const bf16 *b0,
+                                                     const bf16 *w2, const bf16 *b2, bf16 *hi, bf16 *lo) {
+    __shared__ float ms[SUB_TH][F0 + 4];   // [frame][bin + 2]: bins -2 .. F0 + 1, zero outside
+    const int r2 = blockIdx.x;
+    const int c = threadIdx.x;
+    const int u = b.row_utt2[r2];
+    const int t2 = r2 - b.r2_off[u];
+    const int T1 = b.r1_off[u + 1] - b.r1_off[u], Tm = b.T_mel[u];
+    const float *m = mel + b.mel_off[u];
+    for (int i = threadIdx.x; i < SUB_TH * (F0 + 4); i += blockDim.x) {
+        const int fr = i / (F0 + 4), bin = i % (F0 + 4) - 2;
+        const int t = 4 * t2 - 3 + fr;
+        ms[fr][bin + 2] = (t >= 0 && t < Tm && bin >= 0 && bin < F0) ? m[(size_t)bin * Tm + t] : 0.0f;
+    }
+    float k0[9], k2[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) { k0[i] = bf2f(w0[c * 9 + i]); k2[i] = bf2f(w2[c * 9 + i]); }
+    const float bias0 = bf2f(b0[c]), bias2 = bf2f(b2[c]);
+    bool rv[3];   // A rows t1 = 2 t2 - 1 + j inside the utterance
+#pragma unroll
+    for (int j = 0; j < 3; ++j) { const int t1 = 2 * t2 - 1 + j; rv[j] = t1 >= 0 && t1 < T1; }
+    __syncthreads();
+    // A[j][f1] for row j (t1 = 2 t2 - 1 + j) uses frames 2 j .. 2 j + 2 of ms
+    // and bins 2 f1 - 1 .. 2 f1 + 1 (ms columns 2 f1 + 1 .. 2 f1 + 3)
+    auto a_val = [&](int j, int f1) -> float {
+        if (!rv[j] || f1 < 0 || f1 >= F1) return 0.0f;
+        float s = bias0;
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) s += ms[2 * j + kh][2 * f1 + 1 + kw] * k0[kh * 3 + kw];
+        return s > 0.0f ? s : 0.0f;
+    };
+    float a[3][3];   // A[j][2 f2 - 1 + i]
+#pragma unroll
+    for (int j = 0; j < 3; ++j) a[j][2] = a_val(j, -1);
+    const size_t row0 = (size_t)r2 * F2;
+#pragma unroll 1
+    for (int f2 = 0; f2 < F2; ++f2) {
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            a[j][0] = a[j][2];
+            a[j][1] = a_val(j, 2 * f2);
+            a[j][2] = a_val(j, 2 * f2 + 1);
         }
-        out[i] = s > 0.0f ? s : 0.0f;
+        float s = bias2;
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) s += a[kh][kw] * k2[kh * 3 + kw];
+        const size_t i = (row0 + f2) * C + c;
+        const bf16 hb = __float2bfloat16_rn(s);
+        hi[i] = hb;
+        if (lo) lo[i] = __float2bfloat16_rn(s - __bfloat162float(hb));
     }
 }
 
-// depthwise 3x3 stride 2 pad 1, channels last, per utterance: input rows of
-// utterance u are [in_off[u], in_off[u+1]) with Fi bins, output rows
-// [out_off[u], out_off[u+1]) with (Fi+1)/2 bins.
-__global__ void dw_packed(const float *in, int Fi, const int *in_off, const int *out_off, const int *row_utt_out,
-                          int R_out, const bf16 *w, const bf16 *bias, float *out) {
+// depthwise 3x3 stride 2 pad 1 (the second one), channels last, fp32 input
+// rows [in_off[u], in_off[u+1]) of utterance u with Fi bins; output as bf16
+// planes [R_out * Fo][C] for the following 1x1 GEMM.  One CTA per output row,
+// thread = channel.
+__global__ void __launch_bounds__(C) dw_planes(const float *in, int Fi, const int *in_off, const int *out_off,
+                                               const int *row_utt_out, const bf16 *w, const bf16 *bias, bf16 *hi,
+                                               bf16 *lo) {
     const int Fo = (Fi + 1) / 2;
-    const size_t n = (size_t)R_out * Fo * C;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int c = (int)(i % C), f = (int)((i / C) % Fo);
-        const int row = (int)(i / ((size_t)C * Fo));
-        const int u = row_utt_out[row];
-        const int t = row - out_off[u];
-        const int base = in_off[u], Ti = in_off[u + 1] - base;
-        float s = bf2f(bias[c]);
+    const int row = blockIdx.x, c = threadIdx.x;
+    const int u = row_utt_out[row];
+    const int t = row - out_off[u];
+    const int base = in_off[u], Ti = in_off[u + 1] - base;
+    float k[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) k[i] = bf2f(w[c * 9 + i]);
+    const float b0 = bf2f(bias[c]);
+#pragma unroll 1
+    for (int f = 0; f < Fo; ++f) {
+        float s = b0;
+#pragma unroll
         for (int kh = 0; kh < 3; ++kh) {
             const int ih = 2 * t - 1 + kh;
             if (ih < 0 || ih >= Ti) continue;
+#pragma unroll
             for (int kw = 0; kw < 3; ++kw) {
                 const int iw = 2 * f - 1 + kw;
                 if (iw < 0 || iw >= Fi) continue;
-                s += in[((size_t)(base + ih) * Fi + iw) * C + c] * bf2f(w[c * 9 + kh * 3 + kw]);
+                s += in[((size_t)(base + ih) * Fi + iw) * C + c] * k[kh * 3 + kw];
             }
         }
-        out[i] = s;
+        const size_t i = ((size_t)row * Fo + f) * C + c;
+        const bf16 hb = __float2bfloat16_rn(s);
+        hi[i] = hb;
+        if (lo) lo[i] = __float2bfloat16_rn(s - __bfloat162float(hb));
     }
 }
 
@@ -458,7 +514,7 @@ __global__ void __launch_bounds__(256) glu_dw_packed(const float *pw1, Batch b, 
         if (row >= 0 && row < b.R3) {
             const float a = pw1[(size_t)row * 2 * D + c];
             const float g = pw1[(size_t)row * 2 * D + D + c];
-            gv = a / (1.0f + expf(-g));
+            gv = mul_sigmoid(a, g);
         }
         g_s[hr][tc] = gv;
     }
@@ -480,7 +536,7 @@ __global__ void __launch_bounds__(256) glu_dw_packed(const float *pw1, Batch b, 
             if (ti >= lo_row && ti < hi_row) sum += wk[k] * g_s[rr + k][tc];
         }
         float v = (sum - bn_mean) * bn_scale + bn_b;
-        v = v / (1.0f + expf(-v));
+        v = silu_fast(v);
         const size_t i = (size_t)row * D + c;
         const bf16 hb = __float2bfloat16_rn(v);
         hi[i] = hb;
@@ -494,7 +550,7 @@ struct State {
     int max_utts = 0, max_frames = 0;     // capacity: utterances and log-mel frames per batch
     int R1_max = 0, R2_max = 0, R3_max = 0, T_cap = 0;
     bool two = true;                       // activations as hi+lo bf16 planes
-    float *mel = nullptr, *s1 = nullptr, *s2 = nullptr, *x = nullptr, *qkv = nullptr, *pos = nullptr;
+    float *mel = nullptr, *s1 = nullptr, *x = nullptr, *qkv = nullptr, *pos = nullptr;
     float *enc_h = nullptr;
     bf16 *xa[2] = {nullptr, nullptr}, *hid[2] = {nullptr, nullptr}, *ap[2] = {nullptr, nullptr};
     bf16 *posp[2] = {nullptr, nullptr};
@@ -545,10 +601,10 @@ static bool state_alloc(State &st, int max_utts, int max_frames, bool two) {
     st.R2_max = st.R1_max / 2 + max_utts;
     st.R3_max = st.R2_max / 2 + max_utts;
     st.T_cap = st.R3_max;
-    const size_t s1 = std::max({(size_t)st.R1_max * F1 * C, (size_t)st.R2_max * F2 * C, (size_t)st.R3_max * C * F3});
-    const size_t s2 = std::max((size_t)st.R2_max * F2 * C, (size_t)st.R3_max * F3 * C);
+    // fp32 outputs of the two 1x1 subsampling GEMMs ([R2 * F2][C], [R3][C * F3])
+    const size_t s1 = std::max((size_t)st.R2_max * F2 * C, (size_t)st.R3_max * C * F3);
     const size_t R = st.R3_max;
-    bool ok = ealloc(st, &st.mel, (size_t)max_frames * F0) && ealloc(st, &st.s1, s1) && ealloc(st, &st.s2, s2) &&
+    bool ok = ealloc(st, &st.mel, (size_t)max_frames * F0) && ealloc(st, &st.s1, s1) &&
               ealloc(st, &st.x, R * D) && ealloc(st, &st.qkv, R * 3 * D) && ealloc(st, &st.enc_h, R * DEC_D) &&
               ealloc(st, &st.pos, (size_t)(2 * st.T_cap) * D) && ealloc(st, &st.qkvp[0], R * 3 * D) &&
               ealloc(st, &st.qkvp[1], R * 3 * D) && ealloc(st, &st.Pp[0], (size_t)(2 * st.T_cap) * D) &&
@@ -567,11 +623,6 @@ static void state_free(State &st) {
     fe::front_free(st.fe);
     for (cudaEvent_t e : st.ev) cudaEventDestroy(e);
     st.ev.clear();
-}
-
-static inline int grid_of(size_t n) {
-    size_t b = (n + 255) / 256;
-    return (int)std::min<size_t>(std::max<size_t>(b, 1), 148 * 16);
 }
 
 static void egemm_enc(cudaStream_t s, const State &st, const bf16 *W, int N, int K, bf16 *const *xp, int T, long x_rows,
@@ -667,16 +718,12 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         mark(s, st, "");
     }
     // ---- subsampling (backends/cpu/backend.c:188-229), channels last ----
-    conv0_packed<<<grid_of((size_t)R1 * F1 * C), 256, 0, s>>>(st.mel, bt, w.s0w, w.s0b, st.s1);
-    dw_packed<<<grid_of((size_t)R2 * F2 * C), 256, 0, s>>>(st.s1, F1, bt.r1_off, bt.r2_off, bt.row_utt2, R2, w.s2w,
-                                                           w.s2b, st.s2);
-    split_fp32_to_bf16(s, st.s2, R2 * F2, C, C, hidp[0], st.two ? hidp[1] : nullptr, C);
+    conv0_dw_planes<<<R2, C, 0, s>>>(st.mel, bt, w.s0w, w.s0b, w.s2w, w.s2b, hidp[0], st.two ? hidp[1] : nullptr);
     GemmEpilogue e3;
     e3.epi = EPI_RELU; e3.bias = w.s3b; e3.Y = st.s1; e3.ldy = C;
     egemm_enc(s, st, w.s3w, C, C, hidp, R2 * F2, (long)st.R2_max * F2, e3);
-    dw_packed<<<grid_of((size_t)R3 * F3 * C), 256, 0, s>>>(st.s1, F2, bt.r2_off, bt.r3_off, bt.row_utt3, R3, w.s5w,
-                                                           w.s5b, st.s2);
-    split_fp32_to_bf16(s, st.s2, R3 * F3, C, C, hidp[0], st.two ? hidp[1] : nullptr, C);
+    dw_planes<<<R3, C, 0, s>>>(st.s1, F2, bt.r2_off, bt.r3_off, bt.row_utt3, w.s5w, w.s5b, hidp[0],
+                               st.two ? hidp[1] : nullptr);
     GemmEpilogue e6;
     e6.epi = EPI_RELU_FLAT; e6.bias = w.s6b; e6.Y = st.s1; e6.ldy = C * F3; e6.flat_f = F3;
     egemm_enc(s, st, w.s6w, C, C, hidp, R3 * F3, (long)st.R3_max * F3, e6);

@@ -40,7 +40,7 @@ __device__ __forceinline__ void store_epilogue(const GemmEpilogue &ep, int t, in
     case EPI_RELU: ep.Y[(size_t)t * ep.ldy + n] = v > 0.0f ? v : 0.0f; break;
     case EPI_BF16: {
         float a = v;
-        if (ep.act == 1) a = v / (1.0f + expf(-v));
+        if (ep.act == 1) a = silu_fast(v);
         else if (ep.act == 2) a = v > 0.0f ? v : 0.0f;
         const bf16 hb = __float2bfloat16_rn(a);
         ep.Ybf[(size_t)t * ep.ldy + n] = hb;
@@ -131,7 +131,7 @@ __device__ __forceinline__ void epilogue16(const GemmEpilogue &ep, int t0, int t
         float a[16];
         if (ep.act == 1) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) a[j] = v[j] / (1.0f + expf(-v[j]));
+            for (int j = 0; j < 16; ++j) a[j] = silu_fast(v[j]);
         } else if (ep.act == 2) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) a[j] = fmaxf(v[j], 0.0f);
@@ -250,7 +250,7 @@ __device__ __forceinline__ void epilogue_f4_post(const GemmEpilogue &ep, int t, 
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             a[i] = v[i];
-            if (ep.act == 1) a[i] = v[i] / (1.0f + expf(-v[i]));
+            if (ep.act == 1) a[i] = silu_fast(v[i]);
             else if (ep.act == 2) a[i] = v[i] > 0.0f ? v[i] : 0.0f;
         }
         const size_t idx = (size_t)t * ep.ldy + nf;

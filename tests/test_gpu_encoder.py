@@ -123,13 +123,14 @@ def test_encoder_long_vs_reference(abi, full_model, precision, tol):
     assert max(errs) <= tol, errs
 
 
-def test_encoder_batch_invariance_long(abi, full_model):
+@pytest.mark.parametrize("precision", [1, 0])
+def test_encoder_batch_invariance_long(abi, full_model, precision):
     """Utterances past one 64-row tile (T_enc 376, 251, 126, 70, 17) encoded
-    together equal their runs alone."""
+    together equal their runs alone, with both activation precisions."""
     mel, T_mel = inputs.mel_batch([30.0, 20.0, 10.0, 5.55, 1.3], seed=703)
     assert t_enc_of(T_mel).min() < 64 < t_enc_of(T_mel).max()
     mels = mels_of(mel, T_mel)
-    eng = make_engine(abi, full_model)
+    eng = make_engine(abi, full_model, precision=precision)
     try:
         together = eng.encode(mels)
         alone = [eng.encode([m])[0] for m in mels]

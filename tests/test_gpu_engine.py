@@ -173,17 +173,18 @@ def test_engine_batch_invariance(abi, dec_model):
         assert np.array_equal(alone[b], together[b]), b
 
 
-def test_engine_batch_invariance_config3(abi, dec_model):
+@pytest.mark.parametrize("precision", [1, 0])
+def test_engine_batch_invariance_config3(abi, dec_model, precision):
     """Configuration 3's shape: 64 ragged utterances of U(5, 30) s (T_enc
     63-376) with EOS forced at U{20..220} tokens, decoded as one static batch;
     every sequence's tokens equal its batch-1 run on the same engine (the
     reference's tests/batch_correctness.sh:7-32 compares --batch-size 1 with
-    --batch-size 64 the same way)."""
+    --batch-size 64 the same way), with both activation precisions."""
     case = inputs.ragged_decode_case(64, seed=450)
     T_enc, forced = case["T_enc"], case["forced_len"]
     enc = inputs.enc_outputs(T_enc, case["enc_seed"])
     wb, ws = dec_model
-    eng = abi.Engine(abi.load(), 0, wb, ws, max_slots=64)
+    eng = abi.Engine(abi.load(), 0, wb, ws, max_slots=64, precision=precision)
     try:
         for b in range(64):
             eng.submit(b, enc[b, :T_enc[b]], forced[b])
@@ -199,7 +200,7 @@ def test_engine_batch_invariance_config3(abi, dec_model):
         eng.close()
     assert T_enc.max() > 300 and forced.max() > 180
     diff = [b for b in range(64) if not np.array_equal(alone[b], together[b])]
-    assert not diff, f"{len(diff)}/64 sequences differ from their batch-1 run: {diff}"
+    assert not diff, f"precision {precision}: {len(diff)}/64 sequences differ from their batch-1 run: {diff}"
 
 
 def test_engine_continuous_admission(abi, dec_model):
