@@ -53,6 +53,8 @@ struct Batch {
     int T_max;                     // max T_enc of the batch
     const int *qtile;              // relative-position attention work list: utterance << 16 | first query row
     int n_qtiles;
+    const int *qtile2;             // the same with 128-row query tiles (tensor-memory kernel)
+    int n_qtiles2;
 };
 
 // ------------------------------------------------------------ kernels -----
@@ -493,6 +495,8 @@ __global__ void __launch_bounds__(128, TWO ? 1 : 2) relpos_tc(const bf16 *qkv_h,
     }
 }
 
+#include "relpos_umma.cuh"
+
 // GLU(pw1) -> depthwise conv (kernel CK, same padding inside the utterance) ->
 // eval BatchNorm -> SiLU (backends/cpu/backend.c:304-334); output bf16 planes.
 // Block = GR packed rows x GC channels: the GLU of rows [r0 - pad, r0 + GR +
@@ -555,6 +559,7 @@ struct State {
     bf16 *xa[2] = {nullptr, nullptr}, *hid[2] = {nullptr, nullptr}, *ap[2] = {nullptr, nullptr};
     bf16 *posp[2] = {nullptr, nullptr};
     bf16 *qkvp[2] = {nullptr, nullptr}, *Pp[2] = {nullptr, nullptr};   // Q|K|V and P as bf16 hi/lo planes
+    float *ukg = nullptr, *vpg = nullptr;  // u.K per packed row and head, v.P per table row and head
     int *tab = nullptr;                    // device tables
     std::vector<int> htab;
     std::vector<void *> owned;
@@ -609,7 +614,9 @@ static bool state_alloc(State &st, int max_utts, int max_frames, bool two) {
               ealloc(st, &st.pos, (size_t)(2 * st.T_cap) * D) && ealloc(st, &st.qkvp[0], R * 3 * D) &&
               ealloc(st, &st.qkvp[1], R * 3 * D) && ealloc(st, &st.Pp[0], (size_t)(2 * st.T_cap) * D) &&
               ealloc(st, &st.Pp[1], (size_t)(2 * st.T_cap) * D) &&
-              ealloc(st, &st.tab, (size_t)9 * max_utts + 8 + st.R1_max + st.R2_max + st.R3_max + st.R3_max / RQ + 1);
+              ealloc(st, &st.ukg, (size_t)st.R3_max * H) && ealloc(st, &st.vpg, (size_t)(2 * st.T_cap) * H) &&
+              ealloc(st, &st.tab, (size_t)9 * max_utts + 8 + st.R1_max + st.R2_max + st.R3_max + st.R3_max / RQ +
+                                      st.R3_max / UQ + 2);
     const size_t hidn = std::max((size_t)R * FF, (size_t)st.R2_max * F2 * C);
     for (int k = 0; k < (two ? 2 : 1); ++k)
         ok = ok && ealloc(st, &st.xa[k], R * D) && ealloc(st, &st.hid[k], hidn) && ealloc(st, &st.ap[k], R * D) &&
@@ -657,7 +664,8 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     const int R1 = r1[n], R2 = r2[n], R3 = r3[n];
     // device table layout: T_mel[n] mel_off[n] r1[n+1] r2[n+1] r3[n+1] utt1[R1] utt2[R2] utt3[R3]
     // attention work list: query tiles, longest utterances first
-    std::vector<int> qt;
+    // (64-row tiles for the warp-MMA kernel, then 128-row tiles for the tensor-memory kernel)
+    std::vector<int> qt, qt2;
     {
         std::vector<int> order(n);
         for (int b = 0; b < n; ++b) order[b] = b;
@@ -665,10 +673,12 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
                          [&](int a, int c) { return r3[a + 1] - r3[a] > r3[c + 1] - r3[c]; });
         for (int b : order)
             for (int q0 = 0; q0 < r3[b + 1] - r3[b]; q0 += RQ) qt.push_back(b << 16 | q0);
+        for (int b : order)
+            for (int q0 = 0; q0 < r3[b + 1] - r3[b]; q0 += UQ) qt2.push_back(b << 16 | q0);
     }
-    const int NQ = (int)qt.size();
+    const int NQ = (int)qt.size(), NQ2 = (int)qt2.size();
     std::vector<int> &h = st.htab;
-    h.assign((size_t)5 * n + 3 + R1 + R2 + R3 + NQ, 0);
+    h.assign((size_t)5 * n + 3 + R1 + R2 + R3 + NQ + NQ2, 0);
     int *hp = h.data();
     memcpy(hp, T_mel, sizeof(int) * n);
     memcpy(hp + n, mel_off.data(), sizeof(int) * n);
@@ -682,6 +692,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         for (int r = r3[b]; r < r3[b + 1]; ++r) u3[r] = b;
     }
     memcpy(u3 + R3, qt.data(), sizeof(int) * NQ);
+    memcpy(u3 + R3 + NQ, qt2.data(), sizeof(int) * NQ2);
     CT_CHECK(cudaMemcpyAsync(st.tab, hp, sizeof(int) * h.size(), cudaMemcpyHostToDevice, s));
     if (mel)
         for (int b = 0; b < n; ++b)
@@ -701,6 +712,8 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     bt.T_max = T_max;
     bt.qtile = bt.row_utt3 + R3;
     bt.n_qtiles = NQ;
+    bt.qtile2 = bt.qtile + NQ;
+    bt.n_qtiles2 = NQ2;
     static thread_local int relpos_dev = -1;
     int dev = 0;
     CT_CHECK(cudaGetDevice(&dev));
@@ -709,6 +722,8 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
                                       (int)sizeof(RelposSmem<true>)));
         CT_CHECK(cudaFuncSetAttribute(relpos_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)sizeof(RelposSmem<false>)));
+        CT_CHECK(cudaFuncSetAttribute(relpos_umma, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)sizeof(RelposUmmaSmem) + 1024));
         relpos_dev = dev;
     }
     const Weights_ &w = st.w;
@@ -740,6 +755,19 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     bf16 *xap[2] = {st.xa[0], st.xa[1]}, *app[2] = {st.ap[0], st.ap[1]};
     bf16 *lo_a = st.two ? st.xa[1] : nullptr, *lo_h = st.two ? st.hid[1] : nullptr, *lo_p = st.two ? st.ap[1] : nullptr;
     const int RT = st.R3_max;
+    // tensor-memory rel-pos attention (plain bf16): operand maps over this batch's rows
+    // (the maps span the buffers' capacity, at least one box: rows past this
+    // batch only reach query rows that are not stored and keys that are masked)
+    const bool umma = !st.two && st.R3_max >= UQ;
+    CUtensorMap tmQ{}, tmK{}, tmP{};
+    RelposUmmaArgs ua{};
+    if (umma) {
+        tmQ = gemm_tmap(st.qkvp[0], st.R3_max, 3 * D, UQ);
+        tmK = gemm_tmap(st.qkvp[0], st.R3_max, 3 * D, UK);
+        tmP = gemm_tmap(st.Pp[0], 2 * st.T_cap, D, UB);
+        ua.qkv = st.qkvp[0]; ua.ukg = st.ukg; ua.vpg = st.vpg; ua.qtile = bt.qtile2; ua.r3_off = bt.r3_off;
+        ua.T_max = T_max; ua.PL = PL; ua.out = st.ap[0];
+    }
     // ---- Conformer layers (model.h:276-314) ----
     for (int l = 0; l < NL; ++l) {
         const Layer &L = w.L[l];
@@ -768,9 +796,14 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         if (st.two)
             relpos_tc<true><<<dim3(NQ, H), 128, sizeof(RelposSmem<true>), s>>>(
                 st.qkvp[0], st.qkvp[1], st.Pp[0], st.Pp[1], bt, L.sa_pbu, L.sa_pbv, st.ap[0], lo_p);
-        else
+        else if (!umma)
             relpos_tc<false><<<dim3(NQ, H), 128, sizeof(RelposSmem<false>), s>>>(
                 st.qkvp[0], nullptr, st.Pp[0], nullptr, bt, L.sa_pbu, L.sa_pbv, st.ap[0], nullptr);
+        else {
+            relpos_bias_dots<<<(R3 * H + PL * H + 7) / 8, 256, 0, s>>>(st.qkvp[0], nullptr, st.Pp[0], nullptr, R3, PL,
+                                                                        L.sa_pbu, L.sa_pbv, st.ukg, st.vpg);
+            relpos_umma<<<dim3(bt.n_qtiles2, H), U_THREADS, sizeof(RelposUmmaSmem) + 1024, s>>>(tmQ, tmK, tmP, ua);
+        }
         mark(s, st, "enc_relpos_attn");
         GemmEpilogue eo2;
         eo2.epi = EPI_FMADD; eo2.scale = 1.0f; eo2.bias = L.sa_ob; eo2.Y = st.x; eo2.ldy = D;

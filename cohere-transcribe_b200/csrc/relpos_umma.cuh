@@ -1,0 +1,383 @@
+// relpos_umma.cuh -- encoder relative-position attention on the 5th-generation
+// tensor cores (tcgen05 MMAs into TMEM), plain bf16 operands.  Included by
+// encoder.cu inside namespace ct::enc (uses its D, H, DK, Batch).
+//
+// Per (utterance u, head h, 128-query tile q0) one CTA computes, for queries q
+// of the tile and keys k < T = T_enc[u] (backends/cpu/backend.c:262-295):
+//   score[q][k] = ((Q[q] + u_h) . K[k] + (Q[q] + v_h) . P[k - q + T_max - 1]) / sqrt(DK)
+//   out[q]      = softmax_k(score[q]) . V
+// The bias terms u_h . K[k] and v_h . P[m] are per-key / per-table-row scalars,
+// computed once per layer for the whole batch (relpos_bias_dots).  Key tiles of
+// 64, walked with an online softmax:
+//   S  = Q . K_tile^T        (M 128, N 64,  K 160)  -> TMEM columns [0, 64)
+//   BD = Q . P_band^T        (M 128, N 192, K 160)  -> TMEM columns [64, 256)
+//        P_band = table rows m0 .. m0 + 191, m0 = k0 - q0 - 127 + T_max - 1:
+//        every (q, k) pair of the tile has its relative row inside the band.
+//   O += probs . V_tile      (M 128, N 160, K 64)   -> TMEM columns [256, 416)
+// TMEM lane = query row, so each softmax thread owns one whole score row (no
+// cross-thread reductions).  Row q needs BD at band column k - k0 + 127 - (q - q0):
+// a window that slides with the row.  A warp loads the 96 band columns its 32
+// rows can reach, each thread writes its 64 needed values (plus v.P of their
+// table rows) to its own shared-memory row at aligned positions, and reads them
+// back in key order.
+// Operands: Q, K and P tiles by TMA with the 128-byte swizzle (K-major, three
+// 64-column atoms cover DK = 160; the MMAs use the first 160 columns); V is
+// transposed into a K-major [160 d][64 keys] tile by the staging warps; the
+// probabilities are written by the softmax threads as the K-major A operand of
+// the P.V MMA.
+// Warps: 0 TMA producer, 1 MMA issuer (TMEM owner), 2..5 softmax (TMEM lane
+// quarters 2, 3, 0, 1), 6..9 V / bias staging.  Every wait is bounded.
+
+constexpr int UQ = 128, UK = 64, UB = 192, UKA = 3;     // query tile, key tile, band rows, k atoms
+constexpr int U_THREADS = 320;
+constexpr int U_SKEW = 68;                              // floats per skew row (conflict-free writes, float4 reads)
+constexpr uint32_t U_COL_S = 0, U_COL_BD = 64, U_COL_O = 256, U_TMEM_COLS = 512;
+static_assert(DK == 160, "the atom layout below assumes a 160-wide head");
+
+struct RelposUmmaSmem {
+    uint8_t q[UKA][UQ * 128];    // Q tile, three 64-column atoms (SW128, 1024-aligned)
+    uint8_t k[UKA][UK * 128];    // K tile
+    uint8_t p[UKA][UB * 128];    // P band
+    uint8_t vt[DK * 128];        // V^T [160 d][64 keys]
+    uint8_t pr[UQ * 128];        // probabilities [128 q][64 keys] bf16
+    float skew[UQ][U_SKEW];      // per row: BD + v.P at the row's 64 key positions
+    float uk[2][UK];             // u.K of the tile's keys (double-buffered by tile parity)
+    float vp[2][UB];             // v.P of the band rows
+    uint64_t qfull, kfull, kfree, sfull, sfree, bfull, vfull, pfull, pvdone;
+    uint32_t tmem_slot;
+};
+
+static_assert(sizeof(RelposUmmaSmem) + 1024 <= 227 * 1024, "rel-pos tile exceeds the shared memory of a CTA");
+
+struct RelposUmmaArgs {
+    const bf16 *qkv;      // [R3][3 D]: Q | K | V
+    const float *ukg;     // [R3][H]: u_h . K[r]
+    const float *vpg;     // [PL][H]: v_h . P[m]
+    const int *qtile;     // utterance << 16 | first query row (128-row tiles)
+    const int *r3_off;
+    int T_max, PL;        // PL = 2 T_max - 1 table rows
+    bf16 *out;            // [R3][D]
+};
+
+// Bounded wait that also gives up as soon as the device status word is set
+// (by a wait of this launch that ran out, or an earlier error): a failed launch
+// then ends within one wait budget instead of one per CTA and wait.
+__device__ __forceinline__ bool u_wait(uint64_t *bar, uint32_t parity, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u) {
+            if (*reinterpret_cast<volatile int *>(&g_ct_status) != 0) return false;
+            if (globaltimer() - t0 > CT_WAIT_NS) {
+                set_status(code);
+                return false;
+            }
+        }
+    }
+}
+
+// byte offset of element (row, col) in a K-major SW128 tile of 64-element rows
+__device__ __forceinline__ uint32_t sw128_off(int row, int col) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((col >> 3) ^ row) & 7) << 4) + (col & 7) * 2);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+          "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+          "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+          "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+          "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+          "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+          "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+          "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+          "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+          "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// u_h . K[r] and v_h . P[m] for every packed row r and table row m, head h
+// (fp32 sums of the bf16 hi (+ lo) planes).  One warp per (row, head).
+__global__ void __launch_bounds__(256) relpos_bias_dots(const bf16 *qkv_h, const bf16 *qkv_l, const bf16 *P_h,
+                                                        const bf16 *P_l, int R3, int PL, const bf16 *pbu,
+                                                        const bf16 *pbv, float *ukg, float *vpg) {
+    const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int n_uk = R3 * H;
+    if (w >= n_uk + PL * H) return;
+    const bool is_k = w < n_uk;
+    const int idx = is_k ? w : w - n_uk;
+    const int r = idx / H, h = idx % H;
+    const bf16 *bias = (is_k ? pbu : pbv) + h * DK;
+    const size_t base = is_k ? (size_t)r * 3 * D + D + h * DK : (size_t)r * D + h * DK;
+    const bf16 *hi = is_k ? qkv_h : P_h, *lo = is_k ? qkv_l : P_l;
+    float acc = 0.0f;
+    for (int c = lane; c < DK; c += 32)
+        acc += bf2f(bias[c]) * (bf2f(hi[base + c]) + (lo ? bf2f(lo[base + c]) : 0.0f));
+    acc = warp_sum(acc);
+    if (lane == 0) (is_k ? ukg : vpg)[idx] = acc;
+}
+
+__global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constant__ CUtensorMap tmQ,
+                                                            const __grid_constant__ CUtensorMap tmK,
+                                                            const __grid_constant__ CUtensorMap tmP,
+                                                            const RelposUmmaArgs a) {
+    extern __shared__ __align__(1024) uint8_t umma_raw[];
+    RelposUmmaSmem &sm =
+        *reinterpret_cast<RelposUmmaSmem *>((reinterpret_cast<uintptr_t>(umma_raw) + 1023) & ~(uintptr_t)1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.y;
+    const int wq = a.qtile[blockIdx.x];
+    const int u = wq >> 16, q0 = wq & 0xFFFF;
+    const int base = a.r3_off[u];
+    const int T = a.r3_off[u + 1] - base;
+    const int Tm = a.T_max;
+    const int nkt = (T + UK - 1) / UK;   // >= 1: the host lists tiles of non-empty utterances only
+    if (threadIdx.x == 0) {
+        mbar_init(&sm.qfull, 1);
+        mbar_init(&sm.kfull, 1);
+        mbar_init(&sm.kfree, 1);
+        mbar_init(&sm.sfull, 1);
+        mbar_init(&sm.sfree, 4);
+        mbar_init(&sm.bfull, 128);
+        mbar_init(&sm.vfull, 128);
+        mbar_init(&sm.pfull, 128);
+        mbar_init(&sm.pvdone, 1);
+        fence_mbar_init();
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmP);
+    }
+    if (warp == 1) { tmem_alloc(&sm.tmem_slot, U_TMEM_COLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------- producer
+        if (lane == 0) {
+            mbar_expect_tx(&sm.qfull, UKA * UQ * 128);
+            for (int kb = 0; kb < UKA; ++kb) tma_load_2d(sm.q[kb], &tmQ, &sm.qfull, h * DK + kb * 64, base + q0);
+            for (int i = 0; i < nkt; ++i) {
+                // the K tile and band of tile i - 1 are free once its S / BD MMAs completed
+                if (i > 0 && !u_wait(&sm.kfree, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_FREE)) break;
+                const int k0 = i * UK, m0 = k0 - q0 - (UQ - 1) + Tm - 1;
+                mbar_expect_tx(&sm.kfull, UKA * (UK + UB) * 128);
+                for (int kb = 0; kb < UKA; ++kb) {
+                    tma_load_2d(sm.k[kb], &tmK, &sm.kfull, D + h * DK + kb * 64, base + k0);
+                    tma_load_2d(sm.p[kb], &tmP, &sm.kfull, h * DK + kb * 64, m0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t id_s = idesc_bf16(UQ, UK), id_bd = idesc_bf16(UQ, UB), id_o = idesc_bf16(UQ, DK);
+            bool ok = u_wait(&sm.qfull, 0, CT_STATUS_TIMEOUT_TMA);
+            for (int i = 0; i <= nkt && ok; ++i) {
+                if (i < nkt) {
+                    // S and BD of tile i, once its operands landed and the softmax
+                    // threads have read tile i - 1's out of TMEM
+                    ok = u_wait(&sm.kfull, (uint32_t)i & 1u, CT_STATUS_TIMEOUT_TMA);
+                    if (ok && i > 0) ok = u_wait(&sm.sfree, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_MMA);
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kb = 0; kb < UKA; ++kb) {
+                        const uint64_t qd = sw128_desc(smem_u32(sm.q[kb]));
+                        const uint64_t kd = sw128_desc(smem_u32(sm.k[kb]));
+                        const uint64_t pd = sw128_desc(smem_u32(sm.p[kb]));
+                        const int nks = kb < UKA - 1 ? 4 : (DK - 128) / 16;   // 160 = 64 + 64 + 32
+                        for (int k = 0; k < nks; ++k) {
+                            const uint32_t acc = (kb | k) ? 1u : 0u;
+                            mma_bf16(tmem + U_COL_S, qd + 2 * k, kd + 2 * k, id_s, acc);
+                            mma_bf16(tmem + U_COL_BD, qd + 2 * k, pd + 2 * k, id_bd, acc);
+                        }
+                    }
+                    mma_commit(&sm.sfull);
+                    mma_commit(&sm.kfree);
+                }
+                if (i > 0) {
+                    // P.V of tile i - 1
+                    const int j = i - 1;
+                    ok = u_wait(&sm.pfull, (uint32_t)j & 1u, CT_STATUS_TIMEOUT_MMA) &&
+                         u_wait(&sm.vfull, (uint32_t)j & 1u, CT_STATUS_TIMEOUT_TMA);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint64_t ad = sw128_desc(smem_u32(sm.pr)), vd = sw128_desc(smem_u32(sm.vt));
+#pragma unroll
+                    for (int k = 0; k < UK / 16; ++k)
+                        mma_bf16(tmem + U_COL_O, ad + 2 * k, vd + 2 * k, id_o, (j | k) ? 1u : 0u);
+                    mma_commit(&sm.pvdone);
+                }
+            }
+        }
+    } else if (warp >= 6) {
+        // ------------------------------------------ V^T and bias staging (128 threads)
+        const int t = threadIdx.x - 192;
+        const int kp = t & 31, cq = t >> 5;   // key pair (2 kp, 2 kp + 1), chunk phase
+        for (int i = 0; i < nkt; ++i) {
+            const int k0 = i * UK, m0 = k0 - q0 - (UQ - 1) + Tm - 1;
+            float *ukb = sm.uk[i & 1], *vpb = sm.vp[i & 1];
+            // buffer i & 1 was last read by the softmax of tile i - 2, finished
+            // before P.V of tile i - 2, which this thread saw complete last tile
+            if (t < UK) ukb[t] = k0 + t < T ? a.ukg[(size_t)(base + k0 + t) * H + h] : 0.0f;
+            for (int j = t; j < UB; j += 128) {
+                const int m = m0 + j;
+                vpb[j] = (m >= 0 && m < a.PL) ? a.vpg[(size_t)m * H + h] : 0.0f;
+            }
+            mbar_arrive(&sm.bfull);
+            // V^T of tile i overwrites tile i - 1's, read by its P.V
+            if (i > 0 && !u_wait(&sm.pvdone, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_MMA)) break;
+            const int ka = 2 * kp;
+            const bf16 *va_p = a.qkv + (size_t)(base + k0 + ka) * 3 * D + 2 * D + h * DK;
+            const bool va_ok = k0 + ka < T, vb_ok = k0 + ka + 1 < T;
+            for (int ch = cq; ch < DK / 8; ch += 4) {
+                uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
+                if (va_ok) va = *reinterpret_cast<const uint4 *>(va_p + ch * 8);
+                if (vb_ok) vb = *reinterpret_cast<const uint4 *>(va_p + (size_t)3 * D + ch * 8);
+                const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    // d = ch * 8 + e: (V[ka][d], V[ka + 1][d]) as one 32-bit pair
+                    const uint32_t lo16 = (wa[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu;
+                    const uint32_t hi16 = (wb[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu;
+                    *reinterpret_cast<uint32_t *>(sm.vt + sw128_off(ch * 8 + e, ka)) = lo16 | (hi16 << 16);
+                }
+            }
+            fence_proxy_async_smem();   // the MMA reads V^T through the async proxy
+            mbar_arrive(&sm.vfull);
+        }
+    } else {
+        // ------------------------------------------------- softmax (warps 2..5)
+        const int qw = warp & 3;
+        const int ql = qw * 32 + lane;           // query row in the tile = TMEM lane
+        const uint32_t trow = tmem + ((uint32_t)(qw * 32) << 16);
+        const int c0w = 96 - 32 * qw;            // first band column this warp reads
+        const int woff = 31 - lane;              // loaded column index of this row's key 0
+        const float scale = 1.0f / sqrtf((float)DK);
+        float *skr = sm.skew[ql];
+        float m = -INFINITY, l = 0.0f;
+        bool ok = true;
+        for (int i = 0; i < nkt; ++i) {
+            const int k0 = i * UK;
+            ok = ok && u_wait(&sm.sfull, (uint32_t)i & 1u, CT_STATUS_TIMEOUT_MMA) &&
+                 u_wait(&sm.bfull, (uint32_t)i & 1u, CT_STATUS_TIMEOUT_TMA);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+            const float *ukb = sm.uk[i & 1], *vpb = sm.vp[i & 1];
+            float v[32];
+            // BD: this row's 64 band values (+ v.P of their table rows), aligned by key
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                tmem_ld32(trow + U_COL_BD + (uint32_t)(c0w + 32 * c), v);
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const int pos = 32 * c + jj - woff;
+                    if (pos >= 0 && pos < UK) skr[pos] = v[jj] + vpb[c0w + 32 * c + jj];
+                }
+            }
+            float sc[UK];
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                tmem_ld32(trow + U_COL_S + (uint32_t)(32 * c), v);
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) sc[32 * c + jj] = v[jj];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.sfree);   // S / BD may be overwritten
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < UK; j += 4) {
+                const float4 bd = *reinterpret_cast<const float4 *>(skr + j);
+                const float b4[4] = {bd.x, bd.y, bd.z, bd.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float x = (sc[j + e] + ukb[j + e] + b4[e]) * scale;
+                    if (k0 + j + e >= T) x = -INFINITY;
+                    sc[j + e] = x;
+                    mx = fmaxf(mx, x);
+                }
+            }
+            const float mn = fmaxf(m, mx);           // finite: key k0 < T
+            const float corr = __expf(m - mn);       // 0 on the first tile (m = -inf)
+            float ls = 0.0f;
+#pragma unroll
+            for (int j = 0; j < UK; ++j) {
+                const float p = __expf(sc[j] - mn);
+                sc[j] = p;
+                ls += p;
+            }
+            l = l * corr + ls;
+            m = mn;
+            if (i > 0) {
+                // P.V of tile i - 1 done: O may be rescaled and the probability tile reused
+                ok = u_wait(&sm.pvdone, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_MMA);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, corr != 1.0f)) {
+#pragma unroll 1
+                    for (int c = 0; c < DK / 32; ++c) {
+                        tmem_ld32(trow + U_COL_O + (uint32_t)(32 * c), v);
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj) v[jj] *= corr;
+                        tmem_st32(trow + U_COL_O + (uint32_t)(32 * c), v);
+                    }
+                }
+            }
+            // probabilities -> bf16 A operand of the P.V MMA (row ql, keys 0..63)
+#pragma unroll
+            for (int ch = 0; ch < UK / 8; ++ch) {
+                uint32_t w4[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const __nv_bfloat162 pr2 = __floats2bfloat162_rn(sc[ch * 8 + 2 * e], sc[ch * 8 + 2 * e + 1]);
+                    w4[e] = *reinterpret_cast<const uint32_t *>(&pr2);
+                }
+                *reinterpret_cast<uint4 *>(sm.pr + sw128_off(ql, ch * 8)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(&sm.pfull);
+        }
+        // ------------------------------------------------------------ epilogue
+        if (ok) ok = u_wait(&sm.pvdone, (uint32_t)(nkt - 1) & 1u, CT_STATUS_TIMEOUT_MMA);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+            tc_fence_after();
+            const float inv = 1.0f / l;
+            const bool store = q0 + ql < T;
+            bf16 *dst = a.out + (size_t)(base + q0 + ql) * D + h * DK;
+#pragma unroll 1
+            for (int c = 0; c < DK / 32; ++c) {
+                float v[32];
+                tmem_ld32(trow + U_COL_O + (uint32_t)(32 * c), v);
+                if (store) {
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        uint32_t w4[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const __nv_bfloat162 o2 =
+                                __floats2bfloat162_rn(v[8 * g + 2 * e] * inv, v[8 * g + 2 * e + 1] * inv);
+                            w4[e] = *reinterpret_cast<const uint32_t *>(&o2);
+                        }
+                        *reinterpret_cast<uint4 *>(dst + 32 * c + 8 * g) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, U_TMEM_COLS);
+}
