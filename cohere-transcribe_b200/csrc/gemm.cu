@@ -65,12 +65,13 @@ __device__ __forceinline__ void epilogue16(const GemmEpilogue &ep, int t0, int t
     for (int j = 0; j < 16; ++j) keep[j] = j < tl && (!ep.row_mask || ep.row_mask[t0 + j]);
     switch (ep.epi) {
     case EPI_FMADD: {
-        float old[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) old[j] = keep[j] ? ep.Y[(size_t)(t0 + j) * ep.ldy + n] : 0.0f;
+        // Y += scale * v as a reduction into memory: no load round trip per
+        // chunk.  Each element has exactly one writer in the launch, so the
+        // sum is the load / add / store result (atom and red .add.f32 round to
+        // nearest; they also flush subnormals, which these residuals never reach).
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-            if (keep[j]) ep.Y[(size_t)(t0 + j) * ep.ldy + n] = old[j] + ep.scale * v[j];
+            if (keep[j]) atomicAdd(ep.Y + (size_t)(t0 + j) * ep.ldy + n, ep.scale * v[j]);
         break;
     }
     case EPI_KVCACHE: {

@@ -43,7 +43,10 @@ struct RelposUmmaSmem {
     float skew[UQ][U_SKEW];      // per row: BD + v.P at the row's 64 key positions
     float uk[2][UK];             // u.K of the tile's keys (double-buffered by tile parity)
     float vp[2][UB];             // v.P of the band rows
-    uint64_t qfull, kfull, kfree, sfull, sfree, bfull, vfull, pfull, pvdone;
+    uint64_t qfull, kfull, kfree, sfull, sfree, vfull, pfull, pvdone;
+    // bias tiles, one barrier per buffer: the staging warps may run a tile
+    // ahead of the softmax, and one barrier would then alias its phases
+    uint64_t bfull[2];
     uint32_t tmem_slot;
 };
 
@@ -102,6 +105,35 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 64 consecutive TMEM columns (32 per load) from taddr, one wait for all.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]),"=r"(r[1]),"=r"(r[2]),"=r"(r[3]),"=r"(r[4]),"=r"(r[5]),"=r"(r[6]),"=r"(r[7]),"=r"(r[8]),"=r"(r[9]),"=r"(r[10]),"=r"(r[11]),"=r"(r[12]),"=r"(r[13]),"=r"(r[14]),"=r"(r[15]),"=r"(r[16]),"=r"(r[17]),"=r"(r[18]),"=r"(r[19]),"=r"(r[20]),"=r"(r[21]),"=r"(r[22]),"=r"(r[23]),"=r"(r[24]),"=r"(r[25]),"=r"(r[26]),"=r"(r[27]),"=r"(r[28]),"=r"(r[29]),"=r"(r[30]),"=r"(r[31]),"=r"(r[32]),"=r"(r[33]),"=r"(r[34]),"=r"(r[35]),"=r"(r[36]),"=r"(r[37]),"=r"(r[38]),"=r"(r[39]),"=r"(r[40]),"=r"(r[41]),"=r"(r[42]),"=r"(r[43]),"=r"(r[44]),"=r"(r[45]),"=r"(r[46]),"=r"(r[47]),"=r"(r[48]),"=r"(r[49]),"=r"(r[50]),"=r"(r[51]),"=r"(r[52]),"=r"(r[53]),"=r"(r[54]),"=r"(r[55]),"=r"(r[56]),"=r"(r[57]),"=r"(r[58]),"=r"(r[59]),"=r"(r[60]),"=r"(r[61]),"=r"(r[62]),"=r"(r[63])
+        : "r"(taddr + 0u), "r"(taddr + 32u)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 96 consecutive TMEM columns (32 per load) from taddr, one wait for all.
+__device__ __forceinline__ void tmem_ld96(uint32_t taddr, float (&v)[96]) {
+    uint32_t r[96];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%96];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%97];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95}, [%98];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]),"=r"(r[1]),"=r"(r[2]),"=r"(r[3]),"=r"(r[4]),"=r"(r[5]),"=r"(r[6]),"=r"(r[7]),"=r"(r[8]),"=r"(r[9]),"=r"(r[10]),"=r"(r[11]),"=r"(r[12]),"=r"(r[13]),"=r"(r[14]),"=r"(r[15]),"=r"(r[16]),"=r"(r[17]),"=r"(r[18]),"=r"(r[19]),"=r"(r[20]),"=r"(r[21]),"=r"(r[22]),"=r"(r[23]),"=r"(r[24]),"=r"(r[25]),"=r"(r[26]),"=r"(r[27]),"=r"(r[28]),"=r"(r[29]),"=r"(r[30]),"=r"(r[31]),"=r"(r[32]),"=r"(r[33]),"=r"(r[34]),"=r"(r[35]),"=r"(r[36]),"=r"(r[37]),"=r"(r[38]),"=r"(r[39]),"=r"(r[40]),"=r"(r[41]),"=r"(r[42]),"=r"(r[43]),"=r"(r[44]),"=r"(r[45]),"=r"(r[46]),"=r"(r[47]),"=r"(r[48]),"=r"(r[49]),"=r"(r[50]),"=r"(r[51]),"=r"(r[52]),"=r"(r[53]),"=r"(r[54]),"=r"(r[55]),"=r"(r[56]),"=r"(r[57]),"=r"(r[58]),"=r"(r[59]),"=r"(r[60]),"=r"(r[61]),"=r"(r[62]),"=r"(r[63]),"=r"(r[64]),"=r"(r[65]),"=r"(r[66]),"=r"(r[67]),"=r"(r[68]),"=r"(r[69]),"=r"(r[70]),"=r"(r[71]),"=r"(r[72]),"=r"(r[73]),"=r"(r[74]),"=r"(r[75]),"=r"(r[76]),"=r"(r[77]),"=r"(r[78]),"=r"(r[79]),"=r"(r[80]),"=r"(r[81]),"=r"(r[82]),"=r"(r[83]),"=r"(r[84]),"=r"(r[85]),"=r"(r[86]),"=r"(r[87]),"=r"(r[88]),"=r"(r[89]),"=r"(r[90]),"=r"(r[91]),"=r"(r[92]),"=r"(r[93]),"=r"(r[94]),"=r"(r[95])
+        : "r"(taddr + 0u), "r"(taddr + 32u), "r"(taddr + 64u)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 96; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // u_h . K[r] and v_h . P[m] for every packed row r and table row m, head h
 // (fp32 sums of the bf16 hi (+ lo) planes).  One warp per (row, head).
 __global__ void __launch_bounds__(256) relpos_bias_dots(const bf16 *qkv_h, const bf16 *qkv_l, const bf16 *P_h,
@@ -144,7 +176,8 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
         mbar_init(&sm.kfree, 1);
         mbar_init(&sm.sfull, 1);
         mbar_init(&sm.sfree, 4);
-        mbar_init(&sm.bfull, 128);
+        mbar_init(&sm.bfull[0], 128);
+        mbar_init(&sm.bfull[1], 128);
         mbar_init(&sm.vfull, 128);
         mbar_init(&sm.pfull, 128);
         mbar_init(&sm.pvdone, 1);
@@ -220,29 +253,44 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
         }
     } else if (warp >= 6) {
         // ------------------------------------------ V^T and bias staging (128 threads)
+        // Each tile's global loads are issued one tile ahead into registers,
+        // so only the shared-memory stores wait for the previous P.V.
         const int t = threadIdx.x - 192;
-        const int kp = t & 31, cq = t >> 5;   // key pair (2 kp, 2 kp + 1), chunk phase
-        for (int i = 0; i < nkt; ++i) {
+        const int ka = 2 * (t & 31), cq = t >> 5;   // keys (ka, ka + 1), chunks cq, cq + 4, ...
+        constexpr int NCH = DK / 8 / 4;              // 16-byte chunks per key and thread
+        uint4 va[NCH], vb[NCH];
+        float uk_r = 0.0f, vp_r0 = 0.0f, vp_r1 = 0.0f;
+        auto load_tile = [&](int i) {
             const int k0 = i * UK, m0 = k0 - q0 - (UQ - 1) + Tm - 1;
-            float *ukb = sm.uk[i & 1], *vpb = sm.vp[i & 1];
-            // buffer i & 1 was last read by the softmax of tile i - 2, finished
-            // before P.V of tile i - 2, which this thread saw complete last tile
-            if (t < UK) ukb[t] = k0 + t < T ? a.ukg[(size_t)(base + k0 + t) * H + h] : 0.0f;
-            for (int j = t; j < UB; j += 128) {
-                const int m = m0 + j;
-                vpb[j] = (m >= 0 && m < a.PL) ? a.vpg[(size_t)m * H + h] : 0.0f;
+            const bf16 *src = a.qkv + (size_t)(base + k0 + ka) * 3 * D + 2 * D + h * DK;
+            const bool oka = k0 + ka < T, okb = k0 + ka + 1 < T;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                const int ch = cq + 4 * c;
+                va[c] = oka ? *reinterpret_cast<const uint4 *>(src + ch * 8) : make_uint4(0, 0, 0, 0);
+                vb[c] = okb ? *reinterpret_cast<const uint4 *>(src + (size_t)3 * D + ch * 8) : make_uint4(0, 0, 0, 0);
             }
-            mbar_arrive(&sm.bfull);
+            uk_r = (t < UK && k0 + t < T) ? a.ukg[(size_t)(base + k0 + t) * H + h] : 0.0f;
+            const int m1 = m0 + t, m2 = m0 + t + 128;
+            vp_r0 = (m1 >= 0 && m1 < a.PL) ? a.vpg[(size_t)m1 * H + h] : 0.0f;
+            vp_r1 = (t + 128 < UB && m2 >= 0 && m2 < a.PL) ? a.vpg[(size_t)m2 * H + h] : 0.0f;
+        };
+        load_tile(0);
+        for (int i = 0; i < nkt; ++i) {
+            // bias buffer i & 1 was last read by the softmax of tile i - 2, which
+            // finished before P.V of tile i - 2 (seen complete last iteration)
+            float *ukb = sm.uk[i & 1], *vpb = sm.vp[i & 1];
+            if (t < UK) ukb[t] = uk_r;
+            vpb[t] = vp_r0;
+            if (t + 128 < UB) vpb[t + 128] = vp_r1;
+            mbar_arrive(&sm.bfull[i & 1]);
             // V^T of tile i overwrites tile i - 1's, read by its P.V
             if (i > 0 && !u_wait(&sm.pvdone, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_MMA)) break;
-            const int ka = 2 * kp;
-            const bf16 *va_p = a.qkv + (size_t)(base + k0 + ka) * 3 * D + 2 * D + h * DK;
-            const bool va_ok = k0 + ka < T, vb_ok = k0 + ka + 1 < T;
-            for (int ch = cq; ch < DK / 8; ch += 4) {
-                uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
-                if (va_ok) va = *reinterpret_cast<const uint4 *>(va_p + ch * 8);
-                if (vb_ok) vb = *reinterpret_cast<const uint4 *>(va_p + (size_t)3 * D + ch * 8);
-                const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                const int ch = cq + 4 * c;
+                const uint32_t wa[4] = {va[c].x, va[c].y, va[c].z, va[c].w};
+                const uint32_t wb[4] = {vb[c].x, vb[c].y, vb[c].z, vb[c].w};
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     // d = ch * 8 + e: (V[ka][d], V[ka + 1][d]) as one 32-bit pair
@@ -253,9 +301,15 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
             }
             fence_proxy_async_smem();   // the MMA reads V^T through the async proxy
             mbar_arrive(&sm.vfull);
+            if (i + 1 < nkt) load_tile(i + 1);
         }
     } else {
         // ------------------------------------------------- softmax (warps 2..5)
+        // The exponent reference m of a row moves only when the tile maximum
+        // exceeds it by more than U_RESCALE (probabilities then stay below
+        // e^U_RESCALE), so the O accumulator is rescaled in TMEM only on
+        // those tiles; the final division by l is exact either way.
+        constexpr float U_RESCALE = 8.0f;
         const int qw = warp & 3;
         const int ql = qw * 32 + lane;           // query row in the tile = TMEM lane
         const uint32_t trow = tmem + ((uint32_t)(qw * 32) << 16);
@@ -268,37 +322,38 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
         for (int i = 0; i < nkt; ++i) {
             const int k0 = i * UK;
             ok = ok && u_wait(&sm.sfull, (uint32_t)i & 1u, CT_STATUS_TIMEOUT_MMA) &&
-                 u_wait(&sm.bfull, (uint32_t)i & 1u, CT_STATUS_TIMEOUT_TMA);
+                 u_wait(&sm.bfull[i & 1], (uint32_t)(i >> 1) & 1u, CT_STATUS_TIMEOUT_TMA);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
             const float *ukb = sm.uk[i & 1], *vpb = sm.vp[i & 1];
-            float v[32];
-            // BD: this row's 64 band values (+ v.P of their table rows), aligned by key
+            {
+                // BD: this row's 64 band values (+ v.P of their table rows), aligned by key
+                float bd[64];
+                tmem_ld64(trow + U_COL_BD + (uint32_t)c0w, bd);
 #pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                tmem_ld32(trow + U_COL_BD + (uint32_t)(c0w + 32 * c), v);
+                for (int jj = 0; jj < 64; ++jj) {
+                    const int pos = jj - woff;
+                    if (pos >= 0) skr[pos] = bd[jj] + vpb[c0w + jj];   // pos < 64 here
+                }
+                float bd2[32];
+                tmem_ld32(trow + U_COL_BD + (uint32_t)(c0w + 64), bd2);
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) {
-                    const int pos = 32 * c + jj - woff;
-                    if (pos >= 0 && pos < UK) skr[pos] = v[jj] + vpb[c0w + 32 * c + jj];
+                    const int pos = 64 + jj - woff;
+                    if (pos < UK) skr[pos] = bd2[jj] + vpb[c0w + 64 + jj];   // pos >= 33 here
                 }
             }
             float sc[UK];
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                tmem_ld32(trow + U_COL_S + (uint32_t)(32 * c), v);
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) sc[32 * c + jj] = v[jj];
-            }
+            tmem_ld64(trow + U_COL_S, sc);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.sfree);   // S / BD may be overwritten
             float mx = -INFINITY;
 #pragma unroll
             for (int j = 0; j < UK; j += 4) {
-                const float4 bd = *reinterpret_cast<const float4 *>(skr + j);
-                const float b4[4] = {bd.x, bd.y, bd.z, bd.w};
+                const float4 bd4 = *reinterpret_cast<const float4 *>(skr + j);
+                const float b4[4] = {bd4.x, bd4.y, bd4.z, bd4.w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     float x = (sc[j + e] + ukb[j + e] + b4[e]) * scale;
@@ -307,14 +362,16 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
                     mx = fmaxf(mx, x);
                 }
             }
-            const float mn = fmaxf(m, mx);           // finite: key k0 < T
-            const float corr = __expf(m - mn);       // 0 on the first tile (m = -inf)
+            // mx is finite: key k0 < T
+            const bool move = mx > m + U_RESCALE;      // always on the first tile (m = -inf)
+            const float mn = move ? mx : m;
+            const float corr = move ? __expf(m - mn) : 1.0f;   // 0 on the first tile
             float ls = 0.0f;
 #pragma unroll
             for (int j = 0; j < UK; ++j) {
-                const float p = __expf(sc[j] - mn);
-                sc[j] = p;
-                ls += p;
+                const float pj = __expf(sc[j] - mn);
+                sc[j] = pj;
+                ls += pj;
             }
             l = l * corr + ls;
             m = mn;
@@ -324,13 +381,14 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, corr != 1.0f)) {
+                if (__any_sync(0xffffffffu, move)) {
 #pragma unroll 1
-                    for (int c = 0; c < DK / 32; ++c) {
-                        tmem_ld32(trow + U_COL_O + (uint32_t)(32 * c), v);
+                    for (int c = 0; c < DK; c += 32) {
+                        float o32[32];
+                        tmem_ld32(trow + U_COL_O + (uint32_t)c, o32);
 #pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) v[jj] *= corr;
-                        tmem_st32(trow + U_COL_O + (uint32_t)(32 * c), v);
+                        for (int jj = 0; jj < 32; ++jj) o32[jj] *= corr;
+                        tmem_st32(trow + U_COL_O + (uint32_t)c, o32);
                     }
                 }
             }
