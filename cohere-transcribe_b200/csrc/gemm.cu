@@ -59,11 +59,15 @@ __device__ __forceinline__ void store_epilogue(const GemmEpilogue &ep, int t, in
 // offsets, the old values of an FMADD -- is issued before the first store:
 // the stores may alias those addresses as far as the compiler knows, so
 // interleaving loads and stores would serialise one memory round trip per token.
+// E >= 0 fixes the epilogue kind at compile time (the persistent kernel's
+// instantiations: one switch arm of code instead of all of them, no dispatch
+// per chunk); E = -1 dispatches on ep.epi.
+template <int E = -1>
 __device__ __forceinline__ void epilogue16(const GemmEpilogue &ep, int t0, int tl, int n, const float *v) {
     bool keep[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) keep[j] = j < tl && (!ep.row_mask || ep.row_mask[t0 + j]);
-    switch (ep.epi) {
+    switch (E >= 0 ? E : ep.epi) {
     case EPI_FMADD: {
         // Y += scale * v as a reduction into memory: no load round trip per
         // chunk.  Each element has exactly one writer in the launch, so the
@@ -726,7 +730,7 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
 // bit-identical results.
 static constexpr int kThreadsP = 320;   // persistent kernel: TMA warp, MMA warp, 8 epilogue warps
 
-template <int BN, bool TWO>
+template <int BN, bool TWO, int EPI>
 __global__ void __launch_bounds__(kThreadsP, 1) gemm_pers_kernel(const __grid_constant__ CUtensorMap tmW,
                                                                 const __grid_constant__ CUtensorMap tmXh,
                                                                 const __grid_constant__ CUtensorMap tmXl,
@@ -841,8 +845,8 @@ __global__ void __launch_bounds__(kThreadsP, 1) gemm_pers_kernel(const __grid_co
                     const int tl = min(32, p.T - (t0 + c));
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] += bias;
-                    epilogue16(p.ep, t0 + c, min(16, tl), n, v);
-                    if (tl > 16) epilogue16(p.ep, t0 + c + 16, tl - 16, n, v + 16);
+                    epilogue16<EPI>(p.ep, t0 + c, min(16, tl), n, v);
+                    if (tl > 16) epilogue16<EPI>(p.ep, t0 + c + 16, tl - 16, n, v + 16);
                 }
             }
             tc_fence_before();
@@ -1051,7 +1055,7 @@ static void launch_tc(cudaStream_t st, const CUtensorMap &mw, const CUtensorMap 
     CT_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, TWO>, mw, mh, ml, p));
 }
 
-template <int BN, bool TWO>
+template <int BN, bool TWO, int EPI>
 static void launch_pers(cudaStream_t st, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml,
                         KernelParams p, bool pdl) {
     constexpr int STAGE = BM * BK * 2 + BN * BK * 2 * (TWO ? 2 : 1);
@@ -1064,7 +1068,7 @@ static void launch_pers(cudaStream_t st, const CUtensorMap &mw, const CUtensorMa
     CT_CHECK(cudaGetDevice(&dev));
     static thread_local int n_sm = 0;
     if (configured_dev != dev) {
-        CT_CHECK(cudaFuncSetAttribute(gemm_pers_kernel<BN, TWO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CT_CHECK(cudaFuncSetAttribute(gemm_pers_kernel<BN, TWO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       kSmemBudget));
         CT_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
         configured_dev = dev;
@@ -1080,7 +1084,22 @@ static void launch_pers(cudaStream_t st, const CUtensorMap &mw, const CUtensorMa
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    CT_CHECK(cudaLaunchKernelEx(&cfg, gemm_pers_kernel<BN, TWO>, mw, mh, ml, p));
+    CT_CHECK(cudaLaunchKernelEx(&cfg, gemm_pers_kernel<BN, TWO, EPI>, mw, mh, ml, p));
+}
+
+// The persistent kernel compiled per epilogue kind the encoder and admission use.
+template <int BN, bool TWO>
+static void launch_pers_epi(cudaStream_t st, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &ml,
+                            const KernelParams &p, bool pdl) {
+    switch (p.ep.epi) {
+    case EPI_STORE: launch_pers<BN, TWO, EPI_STORE>(st, mw, mh, ml, p, pdl); break;
+    case EPI_RELU: launch_pers<BN, TWO, EPI_RELU>(st, mw, mh, ml, p, pdl); break;
+    case EPI_FMADD: launch_pers<BN, TWO, EPI_FMADD>(st, mw, mh, ml, p, pdl); break;
+    case EPI_BF16: launch_pers<BN, TWO, EPI_BF16>(st, mw, mh, ml, p, pdl); break;
+    case EPI_RELU_FLAT: launch_pers<BN, TWO, EPI_RELU_FLAT>(st, mw, mh, ml, p, pdl); break;
+    case EPI_CAKV_PAGED: launch_pers<BN, TWO, EPI_CAKV_PAGED>(st, mw, mh, ml, p, pdl); break;
+    default: launch_pers<BN, TWO, -1>(st, mw, mh, ml, p, pdl); break;
+    }
 }
 
 void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, const bf16 *X_lo, int T,
@@ -1116,7 +1135,7 @@ void gemm_bf16(cudaStream_t st, const bf16 *W, int N, int K, const bf16 *X_hi, c
     p.nsplit = nsplit; p.bar_off = 0;
     p.ep = ep;
     if (pers) {
-        two ? launch_pers<128, true>(st, mw, mh, ml, p, ep.pdl) : launch_pers<256, false>(st, mw, mh, ml, p, ep.pdl);
+        two ? launch_pers_epi<128, true>(st, mw, mh, ml, p, ep.pdl) : launch_pers_epi<256, false>(st, mw, mh, ml, p, ep.pdl);
         return;
     }
     switch (BN) {
