@@ -764,7 +764,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     if (umma) {
         tmQ = gemm_tmap(st.qkvp[0], st.R3_max, 3 * D, UQ);
         tmK = gemm_tmap(st.qkvp[0], st.R3_max, 3 * D, UK);
-        tmP = gemm_tmap(st.Pp[0], 2 * st.T_cap, D, UB);
+        tmP = gemm_tmap(st.Pp[0], 2 * st.T_cap, D, UK);   // 64-row band blocks
         ua.qkv = st.qkvp[0]; ua.ukg = st.ukg; ua.vpg = st.vpg; ua.qtile = bt.qtile2; ua.r3_off = bt.r3_off;
         ua.T_max = T_max; ua.PL = PL; ua.out = st.ap[0];
     }

@@ -17,33 +17,33 @@
 // TMEM lane = query row, so each softmax thread owns one whole score row (no
 // cross-thread reductions).  Row q needs BD at band column k - k0 + 127 - (q - q0):
 // a window that slides with the row.  A warp loads the 96 band columns its 32
-// rows can reach, each thread writes its 64 needed values (plus v.P of their
-// table rows) to its own shared-memory row at aligned positions, and reads them
-// back in key order.
+// rows can reach, and each thread shifts its 64 needed values into place with
+// a five-stage register barrel shift (by 16, 8, 4, 2, 1 as the row offset's
+// bits say).
 // Operands: Q, K and P tiles by TMA with the 128-byte swizzle (K-major, three
-// 64-column atoms cover DK = 160; the MMAs use the first 160 columns); V is
-// transposed into a K-major [160 d][64 keys] tile by the staging warps; the
-// probabilities are written by the softmax threads as the K-major A operand of
-// the P.V MMA.
+// 64-column atoms cover DK = 160; the MMAs use the first 160 columns).  K is
+// double-buffered; the band lives in a ring of three 64-row blocks (tile i
+// reads blocks i, i + 1, i + 2, so each tile loads one new block, and BD is
+// three N = 64 MMAs, the new block's last).  V is transposed into a K-major
+// [160 d][64 keys] tile by the staging warps; the probabilities are written by
+// the softmax threads as the K-major A operand of the P.V MMA.
 // Warps: 0 TMA producer, 1 MMA issuer (TMEM owner), 2..5 softmax (TMEM lane
 // quarters 2, 3, 0, 1), 6..9 V / bias staging.  Every wait is bounded.
 
 constexpr int UQ = 128, UK = 64, UB = 192, UKA = 3;     // query tile, key tile, band rows, k atoms
 constexpr int U_THREADS = 320;
-constexpr int U_SKEW = 68;                              // floats per skew row (conflict-free writes, float4 reads)
 constexpr uint32_t U_COL_S = 0, U_COL_BD = 64, U_COL_O = 256, U_TMEM_COLS = 512;
 static_assert(DK == 160, "the atom layout below assumes a 160-wide head");
 
 struct RelposUmmaSmem {
     uint8_t q[UKA][UQ * 128];    // Q tile, three 64-column atoms (SW128, 1024-aligned)
-    uint8_t k[UKA][UK * 128];    // K tile
-    uint8_t p[UKA][UB * 128];    // P band
+    uint8_t k[2][UKA][UK * 128]; // K tiles (by tile parity)
+    uint8_t p[3][UKA][UK * 128]; // band ring: block b (table rows m_base + 64 b ..) in slot b % 3
     uint8_t vt[DK * 128];        // V^T [160 d][64 keys]
     uint8_t pr[UQ * 128];        // probabilities [128 q][64 keys] bf16
-    float skew[UQ][U_SKEW];      // per row: BD + v.P at the row's 64 key positions
     float uk[2][UK];             // u.K of the tile's keys (double-buffered by tile parity)
     float vp[2][UB];             // v.P of the band rows
-    uint64_t qfull, kfull, kfree, sfull, sfree, vfull, pfull, pvdone;
+    uint64_t qfull, kfull[2], pfull3[3], kfree, sfull, sfree, vfull, pfull, pvdone;
     // bias tiles, one barrier per buffer: the staging warps may run a tile
     // ahead of the softmax, and one barrier would then alias its phases
     uint64_t bfull[2];
@@ -172,7 +172,8 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
     const int nkt = (T + UK - 1) / UK;   // >= 1: the host lists tiles of non-empty utterances only
     if (threadIdx.x == 0) {
         mbar_init(&sm.qfull, 1);
-        mbar_init(&sm.kfull, 1);
+        for (int b = 0; b < 2; ++b) mbar_init(&sm.kfull[b], 1);
+        for (int b = 0; b < 3; ++b) mbar_init(&sm.pfull3[b], 1);
         mbar_init(&sm.kfree, 1);
         mbar_init(&sm.sfull, 1);
         mbar_init(&sm.sfree, 4);
@@ -191,48 +192,69 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_slot;
+    const int mb0 = -q0 - (UQ - 1) + Tm - 1;   // first table row of band block 0 (tile 0's band start)
 
     if (warp == 0) {
         // ------------------------------------------------------------- producer
         if (lane == 0) {
+            auto load_k = [&](int i) {   // K tile i into buffer i & 1
+                mbar_expect_tx(&sm.kfull[i & 1], UKA * UK * 128);
+                for (int kb = 0; kb < UKA; ++kb)
+                    tma_load_2d(sm.k[i & 1][kb], &tmK, &sm.kfull[i & 1], D + h * DK + kb * 64, base + i * UK);
+            };
+            auto load_p = [&](int b) {   // band block b into slot b % 3
+                mbar_expect_tx(&sm.pfull3[b % 3], UKA * UK * 128);
+                for (int kb = 0; kb < UKA; ++kb)
+                    tma_load_2d(sm.p[b % 3][kb], &tmP, &sm.pfull3[b % 3], h * DK + kb * 64, mb0 + b * UK);
+            };
             mbar_expect_tx(&sm.qfull, UKA * UQ * 128);
             for (int kb = 0; kb < UKA; ++kb) tma_load_2d(sm.q[kb], &tmQ, &sm.qfull, h * DK + kb * 64, base + q0);
-            for (int i = 0; i < nkt; ++i) {
-                // the K tile and band of tile i - 1 are free once its S / BD MMAs completed
-                if (i > 0 && !u_wait(&sm.kfree, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_FREE)) break;
-                const int k0 = i * UK, m0 = k0 - q0 - (UQ - 1) + Tm - 1;
-                mbar_expect_tx(&sm.kfull, UKA * (UK + UB) * 128);
-                for (int kb = 0; kb < UKA; ++kb) {
-                    tma_load_2d(sm.k[kb], &tmK, &sm.kfull, D + h * DK + kb * 64, base + k0);
-                    tma_load_2d(sm.p[kb], &tmP, &sm.kfull, h * DK + kb * 64, m0);
-                }
+            load_k(0);
+            for (int b = 0; b < 3; ++b) load_p(b);
+            if (nkt > 1) load_k(1);
+            for (int i = 1; i < nkt; ++i) {
+                // S / BD of tile i - 1 complete: band block i - 1's slot and K
+                // buffer (i + 1) & 1 (tile i - 1's) are free
+                if (!u_wait(&sm.kfree, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_FREE)) break;
+                load_p(i + 2);
+                if (i + 1 < nkt) load_k(i + 1);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t id_s = idesc_bf16(UQ, UK), id_bd = idesc_bf16(UQ, UB), id_o = idesc_bf16(UQ, DK);
+            constexpr uint32_t id_s = idesc_bf16(UQ, UK), id_o = idesc_bf16(UQ, DK);
             bool ok = u_wait(&sm.qfull, 0, CT_STATUS_TIMEOUT_TMA);
+            // Q . X^T over the 160 head columns (three atoms, the last one half used)
+            auto qx = [&](uint32_t dcol, const uint8_t (*x)[UK * 128]) {
+#pragma unroll
+                for (int kb = 0; kb < UKA; ++kb) {
+                    const uint64_t qd = sw128_desc(smem_u32(sm.q[kb]));
+                    const uint64_t xd = sw128_desc(smem_u32(x[kb]));
+                    const int nks = kb < UKA - 1 ? 4 : (DK - 128) / 16;   // 160 = 64 + 64 + 32
+                    for (int k = 0; k < nks; ++k)
+                        mma_bf16(tmem + dcol, qd + 2 * k, xd + 2 * k, id_s, (kb | k) ? 1u : 0u);
+                }
+            };
             for (int i = 0; i <= nkt && ok; ++i) {
                 if (i < nkt) {
-                    // S and BD of tile i, once its operands landed and the softmax
-                    // threads have read tile i - 1's out of TMEM
-                    ok = u_wait(&sm.kfull, (uint32_t)i & 1u, CT_STATUS_TIMEOUT_TMA);
+                    // S and the band blocks i, i + 1 of tile i once K_i landed and the
+                    // softmax threads have read tile i - 1 out of TMEM; block i + 2
+                    // (the one loaded last) after it lands
+                    ok = u_wait(&sm.kfull[i & 1], (uint32_t)(i >> 1) & 1u, CT_STATUS_TIMEOUT_TMA);
+                    if (ok && i == 0)
+                        ok = u_wait(&sm.pfull3[0], 0, CT_STATUS_TIMEOUT_TMA) &&
+                             u_wait(&sm.pfull3[1], 0, CT_STATUS_TIMEOUT_TMA);
                     if (ok && i > 0) ok = u_wait(&sm.sfree, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_MMA);
                     if (!ok) break;
                     tc_fence_after();
-#pragma unroll
-                    for (int kb = 0; kb < UKA; ++kb) {
-                        const uint64_t qd = sw128_desc(smem_u32(sm.q[kb]));
-                        const uint64_t kd = sw128_desc(smem_u32(sm.k[kb]));
-                        const uint64_t pd = sw128_desc(smem_u32(sm.p[kb]));
-                        const int nks = kb < UKA - 1 ? 4 : (DK - 128) / 16;   // 160 = 64 + 64 + 32
-                        for (int k = 0; k < nks; ++k) {
-                            const uint32_t acc = (kb | k) ? 1u : 0u;
-                            mma_bf16(tmem + U_COL_S, qd + 2 * k, kd + 2 * k, id_s, acc);
-                            mma_bf16(tmem + U_COL_BD, qd + 2 * k, pd + 2 * k, id_bd, acc);
-                        }
-                    }
+                    qx(U_COL_S, sm.k[i & 1]);
+                    qx(U_COL_BD, sm.p[i % 3]);
+                    qx(U_COL_BD + UK, sm.p[(i + 1) % 3]);
+                    const int b2 = i + 2;
+                    if (!u_wait(&sm.pfull3[b2 % 3], (uint32_t)(b2 / 3) & 1u, CT_STATUS_TIMEOUT_TMA)) { ok = false; break; }
+                    tc_fence_after();
+                    qx(U_COL_BD + 2 * UK, sm.p[b2 % 3]);
                     mma_commit(&sm.sfull);
                     mma_commit(&sm.kfree);
                 }
@@ -316,7 +338,6 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
         const int c0w = 96 - 32 * qw;            // first band column this warp reads
         const int woff = 31 - lane;              // loaded column index of this row's key 0
         const float scale = 1.0f / sqrtf((float)DK);
-        float *skr = sm.skew[ql];
         float m = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int i = 0; i < nkt; ++i) {
@@ -327,23 +348,22 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
             if (!ok) break;
             tc_fence_after();
             const float *ukb = sm.uk[i & 1], *vpb = sm.vp[i & 1];
-            {
-                // BD: this row's 64 band values (+ v.P of their table rows), aligned by key
-                float bd[64];
-                tmem_ld64(trow + U_COL_BD + (uint32_t)c0w, bd);
+            // BD: the 96 band columns this warp reaches, + v.P of their table rows,
+            // shifted left by this row's offset woff so that bd[j] is key k0 + j's
+            float bd[96];
+            tmem_ld96(trow + U_COL_BD + (uint32_t)c0w, bd);
 #pragma unroll
-                for (int jj = 0; jj < 64; ++jj) {
-                    const int pos = jj - woff;
-                    if (pos >= 0) skr[pos] = bd[jj] + vpb[c0w + jj];   // pos < 64 here
-                }
-                float bd2[32];
-                tmem_ld32(trow + U_COL_BD + (uint32_t)(c0w + 64), bd2);
+            for (int jj = 0; jj < 96; ++jj) bd[jj] += vpb[c0w + jj];
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
-                    const int pos = 64 + jj - woff;
-                    if (pos < UK) skr[pos] = bd2[jj] + vpb[c0w + 64 + jj];   // pos >= 33 here
-                }
-            }
+            for (int j = 0; j < 80; ++j) bd[j] = (woff & 16) ? bd[j + 16] : bd[j];
+#pragma unroll
+            for (int j = 0; j < 72; ++j) bd[j] = (woff & 8) ? bd[j + 8] : bd[j];
+#pragma unroll
+            for (int j = 0; j < 68; ++j) bd[j] = (woff & 4) ? bd[j + 4] : bd[j];
+#pragma unroll
+            for (int j = 0; j < 66; ++j) bd[j] = (woff & 2) ? bd[j + 2] : bd[j];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) bd[j] = (woff & 1) ? bd[j + 1] : bd[j];
             float sc[UK];
             tmem_ld64(trow + U_COL_S, sc);
             tc_fence_before();
@@ -351,16 +371,11 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
             if (lane == 0) mbar_arrive(&sm.sfree);   // S / BD may be overwritten
             float mx = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < UK; j += 4) {
-                const float4 bd4 = *reinterpret_cast<const float4 *>(skr + j);
-                const float b4[4] = {bd4.x, bd4.y, bd4.z, bd4.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    float x = (sc[j + e] + ukb[j + e] + b4[e]) * scale;
-                    if (k0 + j + e >= T) x = -INFINITY;
-                    sc[j + e] = x;
-                    mx = fmaxf(mx, x);
-                }
+            for (int j = 0; j < UK; ++j) {
+                float x = (sc[j] + ukb[j] + bd[j]) * scale;
+                if (k0 + j >= T) x = -INFINITY;
+                sc[j] = x;
+                mx = fmaxf(mx, x);
             }
             // mx is finite: key k0 < T
             const bool move = mx > m + U_RESCALE;      // always on the first tile (m = -inf)
