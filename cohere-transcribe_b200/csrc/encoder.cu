@@ -512,15 +512,22 @@ __global__ void __launch_bounds__(256) glu_dw_packed(const float *pw1, Batch b, 
     const int r0 = blockIdx.x * GR, c0 = blockIdx.y * GC;
     const int tc = threadIdx.x & (GC - 1), tr = threadIdx.x / GC;   // 2 row lanes x 128 channels
     const int c = c0 + tc;
-    for (int hr = tr; hr < HR; hr += 256 / GC) {
-        const int row = r0 - pad + hr;
-        float gv = 0.0f;
-        if (row >= 0 && row < b.R3) {
-            const float a = pw1[(size_t)row * 2 * D + c];
-            const float g = pw1[(size_t)row * 2 * D + D + c];
-            gv = mul_sigmoid(a, g);
-        }
-        g_s[hr][tc] = gv;
+    // every load of the thread's rows issued before the first use (memory-level
+    // parallelism: the kernel streams 2560 fp32 per row)
+    constexpr int NH = HR / (256 / GC);
+    static_assert(HR % (256 / GC) == 0, "halo rows split evenly over the row lanes");
+    float av[NH], gw[NH];
+#pragma unroll
+    for (int k = 0; k < NH; ++k) {
+        const int row = r0 - pad + tr + k * (256 / GC);
+        const bool in = row >= 0 && row < b.R3;
+        av[k] = in ? pw1[(size_t)row * 2 * D + c] : 0.0f;
+        gw[k] = in ? pw1[(size_t)row * 2 * D + D + c] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < NH; ++k) {
+        const int row = r0 - pad + tr + k * (256 / GC);
+        g_s[tr + k * (256 / GC)][tc] = (row >= 0 && row < b.R3) ? mul_sigmoid(av[k], gw[k]) : 0.0f;
     }
     float wk[CK];
 #pragma unroll

@@ -38,7 +38,8 @@ static_assert(DK == 160, "the atom layout below assumes a 160-wide head");
 struct RelposUmmaSmem {
     uint8_t q[UKA][UQ * 128];    // Q tile, three 64-column atoms (SW128, 1024-aligned)
     uint8_t k[2][UKA][UK * 128]; // K tiles (by tile parity)
-    uint8_t p[3][UKA][UK * 128]; // band ring: block b (table rows m_base + 64 b ..) in slot b % 3
+    uint8_t p[UKA][3][UK * 128]; // band ring per atom: block b (table rows m_base + 64 b ..) in slot b % 3;
+                                 // the slots of an atom are adjacent, so slots s, s + 1 form one N = 128 operand
     uint8_t vt[DK * 128];        // V^T [160 d][64 keys]
     uint8_t pr[UQ * 128];        // probabilities [128 q][64 keys] bf16
     float uk[2][UK];             // u.K of the tile's keys (double-buffered by tile parity)
@@ -205,7 +206,7 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
             auto load_p = [&](int b) {   // band block b into slot b % 3
                 mbar_expect_tx(&sm.pfull3[b % 3], UKA * UK * 128);
                 for (int kb = 0; kb < UKA; ++kb)
-                    tma_load_2d(sm.p[b % 3][kb], &tmP, &sm.pfull3[b % 3], h * DK + kb * 64, mb0 + b * UK);
+                    tma_load_2d(sm.p[kb][b % 3], &tmP, &sm.pfull3[b % 3], h * DK + kb * 64, mb0 + b * UK);
             };
             mbar_expect_tx(&sm.qfull, UKA * UQ * 128);
             for (int kb = 0; kb < UKA; ++kb) tma_load_2d(sm.q[kb], &tmQ, &sm.qfull, h * DK + kb * 64, base + q0);
@@ -223,17 +224,19 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t id_s = idesc_bf16(UQ, UK), id_o = idesc_bf16(UQ, DK);
+            constexpr uint32_t id_o = idesc_bf16(UQ, DK);
             bool ok = u_wait(&sm.qfull, 0, CT_STATUS_TIMEOUT_TMA);
             // Q . X^T over the 160 head columns (three atoms, the last one half used)
-            auto qx = [&](uint32_t dcol, const uint8_t (*x)[UK * 128]) {
+            // for an X of n rows whose atom kb starts at x(kb)
+            auto qx = [&](uint32_t dcol, int n, auto x) {
+                const uint32_t id = idesc_bf16(UQ, n);
 #pragma unroll
                 for (int kb = 0; kb < UKA; ++kb) {
                     const uint64_t qd = sw128_desc(smem_u32(sm.q[kb]));
-                    const uint64_t xd = sw128_desc(smem_u32(x[kb]));
+                    const uint64_t xd = sw128_desc(smem_u32(x(kb)));
                     const int nks = kb < UKA - 1 ? 4 : (DK - 128) / 16;   // 160 = 64 + 64 + 32
                     for (int k = 0; k < nks; ++k)
-                        mma_bf16(tmem + dcol, qd + 2 * k, xd + 2 * k, id_s, (kb | k) ? 1u : 0u);
+                        mma_bf16(tmem + dcol, qd + 2 * k, xd + 2 * k, id, (kb | k) ? 1u : 0u);
                 }
             };
             for (int i = 0; i <= nkt && ok; ++i) {
@@ -248,13 +251,17 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
                     if (ok && i > 0) ok = u_wait(&sm.sfree, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_MMA);
                     if (!ok) break;
                     tc_fence_after();
-                    qx(U_COL_S, sm.k[i & 1]);
-                    qx(U_COL_BD, sm.p[i % 3]);
-                    qx(U_COL_BD + UK, sm.p[(i + 1) % 3]);
-                    const int b2 = i + 2;
+                    const int kbuf = i & 1, r = i % 3, b2 = i + 2;
+                    qx(U_COL_S, UK, [&](int kb) { return sm.k[kbuf][kb]; });
+                    // band positions 0, 1, 2 are slots r, r + 1, r + 2 (mod 3); slots
+                    // adjacent in memory go as one MMA, the new block (position 2) last
+                    if (r == 1) qx(U_COL_BD, 2 * UK, [&](int kb) { return sm.p[kb][1]; });
+                    if (r == 2) qx(U_COL_BD, UK, [&](int kb) { return sm.p[kb][2]; });
                     if (!u_wait(&sm.pfull3[b2 % 3], (uint32_t)(b2 / 3) & 1u, CT_STATUS_TIMEOUT_TMA)) { ok = false; break; }
                     tc_fence_after();
-                    qx(U_COL_BD + 2 * UK, sm.p[b2 % 3]);
+                    if (r == 0) qx(U_COL_BD, 3 * UK, [&](int kb) { return sm.p[kb][0]; });
+                    if (r == 1) qx(U_COL_BD + 2 * UK, UK, [&](int kb) { return sm.p[kb][0]; });
+                    if (r == 2) qx(U_COL_BD + UK, 2 * UK, [&](int kb) { return sm.p[kb][0]; });
                     mma_commit(&sm.sfull);
                     mma_commit(&sm.kfree);
                 }
