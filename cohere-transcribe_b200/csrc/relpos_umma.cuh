@@ -32,19 +32,19 @@
 
 constexpr int UQ = 128, UK = 64, UB = 192, UKA = 3;     // query tile, key tile, band rows, k atoms
 constexpr int U_THREADS = 320;
-constexpr uint32_t U_COL_S = 0, U_COL_BD = 64, U_COL_O = 256, U_TMEM_COLS = 512;
+constexpr uint32_t U_COL_S = 0, U_COL_BD = 64, U_COL_O = 256, U_COL_P = 416, U_TMEM_COLS = 512;
+constexpr int U_SLOTS = 4;   // band ring slots: block b + 2 is loaded while tile b - 1 still reads slot (b - 2) % 4
 static_assert(DK == 160, "the atom layout below assumes a 160-wide head");
 
 struct RelposUmmaSmem {
     uint8_t q[UKA][UQ * 128];    // Q tile, three 64-column atoms (SW128, 1024-aligned)
     uint8_t k[2][UKA][UK * 128]; // K tiles (by tile parity)
-    uint8_t p[UKA][3][UK * 128]; // band ring per atom: block b (table rows m_base + 64 b ..) in slot b % 3;
-                                 // the slots of an atom are adjacent, so slots s, s + 1 form one N = 128 operand
+    uint8_t p[UKA][U_SLOTS][UK * 128];   // band ring per atom: block b (table rows m_base + 64 b ..) in
+                                         // slot b % 4; adjacent slots form one wider MMA operand
     uint8_t vt[DK * 128];        // V^T [160 d][64 keys]
-    uint8_t pr[UQ * 128];        // probabilities [128 q][64 keys] bf16
     float uk[2][UK];             // u.K of the tile's keys (double-buffered by tile parity)
     float vp[2][UB];             // v.P of the band rows
-    uint64_t qfull, kfull[2], pfull3[3], kfree, sfull, sfree, vfull, pfull, pvdone;
+    uint64_t qfull, kfull[2], pslot[U_SLOTS], kfree, sfull, sfree, vfull, pfull, pvdone;
     // bias tiles, one barrier per buffer: the staging warps may run a tile
     // ahead of the softmax, and one barrier would then alias its phases
     uint64_t bfull[2];
@@ -84,6 +84,18 @@ __device__ __forceinline__ bool u_wait(uint64_t *bar, uint32_t parity, int code)
 // byte offset of element (row, col) in a K-major SW128 tile of 64-element rows
 __device__ __forceinline__ uint32_t sw128_off(int row, int col) {
     return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((col >> 3) ^ row) & 7) << 4) + (col & 7) * 2);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16: A (M rows = TMEM lanes, K packed two
+// bf16 per 32-bit column from a_tmem) is read from tensor memory.
+__device__ __forceinline__ void mma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
@@ -174,7 +186,7 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
     if (threadIdx.x == 0) {
         mbar_init(&sm.qfull, 1);
         for (int b = 0; b < 2; ++b) mbar_init(&sm.kfull[b], 1);
-        for (int b = 0; b < 3; ++b) mbar_init(&sm.pfull3[b], 1);
+        for (int b = 0; b < U_SLOTS; ++b) mbar_init(&sm.pslot[b], 1);
         mbar_init(&sm.kfree, 1);
         mbar_init(&sm.sfull, 1);
         mbar_init(&sm.sfree, 4);
@@ -203,22 +215,23 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
                 for (int kb = 0; kb < UKA; ++kb)
                     tma_load_2d(sm.k[i & 1][kb], &tmK, &sm.kfull[i & 1], D + h * DK + kb * 64, base + i * UK);
             };
-            auto load_p = [&](int b) {   // band block b into slot b % 3
-                mbar_expect_tx(&sm.pfull3[b % 3], UKA * UK * 128);
+            auto load_p = [&](int b) {   // band block b into slot b % 4
+                const int sl = b % U_SLOTS;
+                mbar_expect_tx(&sm.pslot[sl], UKA * UK * 128);
                 for (int kb = 0; kb < UKA; ++kb)
-                    tma_load_2d(sm.p[kb][b % 3], &tmP, &sm.pfull3[b % 3], h * DK + kb * 64, mb0 + b * UK);
+                    tma_load_2d(sm.p[kb][sl], &tmP, &sm.pslot[sl], h * DK + kb * 64, mb0 + b * UK);
             };
             mbar_expect_tx(&sm.qfull, UKA * UQ * 128);
             for (int kb = 0; kb < UKA; ++kb) tma_load_2d(sm.q[kb], &tmQ, &sm.qfull, h * DK + kb * 64, base + q0);
             load_k(0);
             for (int b = 0; b < 3; ++b) load_p(b);
-            if (nkt > 1) load_k(1);
-            for (int i = 1; i < nkt; ++i) {
-                // S / BD of tile i - 1 complete: band block i - 1's slot and K
-                // buffer (i + 1) & 1 (tile i - 1's) are free
+            if (nkt > 1) { load_k(1); load_p(3); }
+            for (int i = 1; i + 1 < nkt; ++i) {
+                // S / BD of tile i - 1 complete: band block i - 1's slot (block
+                // i + 3's) and K buffer (i + 1) & 1 (tile i - 1's) are free
                 if (!u_wait(&sm.kfree, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_FREE)) break;
-                load_p(i + 2);
-                if (i + 1 < nkt) load_k(i + 1);
+                load_k(i + 1);
+                load_p(i + 3);
             }
         }
     } else if (warp == 1) {
@@ -241,27 +254,29 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
             };
             for (int i = 0; i <= nkt && ok; ++i) {
                 if (i < nkt) {
-                    // S and the band blocks i, i + 1 of tile i once K_i landed and the
-                    // softmax threads have read tile i - 1 out of TMEM; block i + 2
-                    // (the one loaded last) after it lands
+                    // S and BD of tile i once K_i landed and the softmax threads have
+                    // read tile i - 1 out of TMEM
                     ok = u_wait(&sm.kfull[i & 1], (uint32_t)(i >> 1) & 1u, CT_STATUS_TIMEOUT_TMA);
-                    if (ok && i == 0)
-                        ok = u_wait(&sm.pfull3[0], 0, CT_STATUS_TIMEOUT_TMA) &&
-                             u_wait(&sm.pfull3[1], 0, CT_STATUS_TIMEOUT_TMA);
                     if (ok && i > 0) ok = u_wait(&sm.sfree, (uint32_t)(i - 1) & 1u, CT_STATUS_TIMEOUT_MMA);
                     if (!ok) break;
+                    // band blocks i, i + 1, i + 2 (loaded a tile ahead): wait for the ones not seen yet
+                    for (int b = (i == 0 ? 0 : i + 2); b <= i + 2 && ok; ++b)
+                        ok = u_wait(&sm.pslot[b % U_SLOTS], (uint32_t)(b / U_SLOTS) & 1u, CT_STATUS_TIMEOUT_TMA);
+                    if (!ok) break;
                     tc_fence_after();
-                    const int kbuf = i & 1, r = i % 3, b2 = i + 2;
+                    const int kbuf = i & 1, r = i % U_SLOTS;
                     qx(U_COL_S, UK, [&](int kb) { return sm.k[kbuf][kb]; });
-                    // band positions 0, 1, 2 are slots r, r + 1, r + 2 (mod 3); slots
-                    // adjacent in memory go as one MMA, the new block (position 2) last
-                    if (r == 1) qx(U_COL_BD, 2 * UK, [&](int kb) { return sm.p[kb][1]; });
-                    if (r == 2) qx(U_COL_BD, UK, [&](int kb) { return sm.p[kb][2]; });
-                    if (!u_wait(&sm.pfull3[b2 % 3], (uint32_t)(b2 / 3) & 1u, CT_STATUS_TIMEOUT_TMA)) { ok = false; break; }
-                    tc_fence_after();
-                    if (r == 0) qx(U_COL_BD, 3 * UK, [&](int kb) { return sm.p[kb][0]; });
-                    if (r == 1) qx(U_COL_BD + 2 * UK, UK, [&](int kb) { return sm.p[kb][0]; });
-                    if (r == 2) qx(U_COL_BD + UK, 2 * UK, [&](int kb) { return sm.p[kb][0]; });
+                    // band positions 0, 1, 2 are slots r, r + 1, r + 2 (mod 4); runs of
+                    // slots adjacent in memory go as one MMA
+                    if (r <= 1) {
+                        qx(U_COL_BD, 3 * UK, [&](int kb) { return sm.p[kb][r]; });
+                    } else if (r == 2) {
+                        qx(U_COL_BD, 2 * UK, [&](int kb) { return sm.p[kb][2]; });
+                        qx(U_COL_BD + 2 * UK, UK, [&](int kb) { return sm.p[kb][0]; });
+                    } else {
+                        qx(U_COL_BD, UK, [&](int kb) { return sm.p[kb][3]; });
+                        qx(U_COL_BD + UK, 2 * UK, [&](int kb) { return sm.p[kb][0]; });
+                    }
                     mma_commit(&sm.sfull);
                     mma_commit(&sm.kfree);
                 }
@@ -272,10 +287,10 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
                          u_wait(&sm.vfull, (uint32_t)j & 1u, CT_STATUS_TIMEOUT_TMA);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint64_t ad = sw128_desc(smem_u32(sm.pr)), vd = sw128_desc(smem_u32(sm.vt));
+                    const uint64_t vd = sw128_desc(smem_u32(sm.vt));
 #pragma unroll
-                    for (int k = 0; k < UK / 16; ++k)
-                        mma_bf16(tmem + U_COL_O, ad + 2 * k, vd + 2 * k, id_o, (j | k) ? 1u : 0u);
+                    for (int k = 0; k < UK / 16; ++k)   // A = the probabilities in TMEM (16 bf16 = 8 columns a step)
+                        mma_bf16_ta(tmem + U_COL_O, tmem + U_COL_P + 8u * k, vd + 2 * k, id_o, (j | k) ? 1u : 0u);
                     mma_commit(&sm.pvdone);
                 }
             }
@@ -414,18 +429,17 @@ __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constan
                     }
                 }
             }
-            // probabilities -> bf16 A operand of the P.V MMA (row ql, keys 0..63)
+            // probabilities -> the P.V MMA's A operand in TMEM: row ql, keys 2c, 2c + 1
+            // packed in column c as bf16 (lower key in the low half)
+            {
+                float pk[32];
 #pragma unroll
-            for (int ch = 0; ch < UK / 8; ++ch) {
-                uint32_t w4[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const __nv_bfloat162 pr2 = __floats2bfloat162_rn(sc[ch * 8 + 2 * e], sc[ch * 8 + 2 * e + 1]);
-                    w4[e] = *reinterpret_cast<const uint32_t *>(&pr2);
+                for (int c = 0; c < UK / 2; ++c) {
+                    const __nv_bfloat162 pr2 = __floats2bfloat162_rn(sc[2 * c], sc[2 * c + 1]);
+                    pk[c] = __uint_as_float(*reinterpret_cast<const uint32_t *>(&pr2));
                 }
-                *reinterpret_cast<uint4 *>(sm.pr + sw128_off(ql, ch * 8)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                tmem_st32(trow + U_COL_P, pk);
             }
-            fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&sm.pfull);
         }
