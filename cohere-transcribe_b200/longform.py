@@ -122,9 +122,12 @@ class LongFormScheduler:
         self.step_block = step_block
         self.files = {}
 
-    def add(self, file_id: int, samples: np.ndarray) -> None:
+    def add(self, file_id: int, samples: np.ndarray, single: bool = False) -> None:
+        """Queue an input; `single` decodes it in one pass (transcribe_chunk)
+        instead of cutting it at silences."""
         x = np.ascontiguousarray(samples, dtype=np.float32)
-        self.files[file_id] = {"x": x, "bounds": chunk_bounds(x, *self.opts), "next": 0, "carry": [], "out": []}
+        bounds = [(0, len(x))] if single else chunk_bounds(x, *self.opts)
+        self.files[file_id] = {"x": x, "bounds": bounds, "next": 0, "carry": [], "out": []}
 
     def _submit_next(self, fid: int) -> bool:
         f = self.files[fid]

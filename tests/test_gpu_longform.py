@@ -79,3 +79,46 @@ def test_long_form_chunks_with_carried_context(model, wmod):
             assert out[g] == am[0, n_p + g], g
             checked += 1
     assert checked > 0.7 * (forced[0] - 1)
+
+
+def test_folder_mode_matches_direct_calls(model, tmp_path):
+    """The input-folder mode (audio_files.run_folder, transcribe.c:1108-1228) on
+    16 kHz PCM WAV files: a short file decodes in one pass and a 48 s file in
+    silence-split chunks; the transcripts written equal the vocabulary printout
+    of the tokens the engine gives the same samples directly."""
+    import wave
+    abi = importlib.import_module("cohere-transcribe_b200.abi")
+    lf = importlib.import_module("cohere-transcribe_b200.longform")
+    af = importlib.import_module("cohere-transcribe_b200.audio_files")
+    wb, ws = model
+    prompt = list(inputs.ctb.PROMPT_FULL)
+    src, dst = tmp_path / "in", tmp_path / "out"
+    src.mkdir(); dst.mkdir()
+    xs = {"a_short": inputs.speech_like(6.0, 1401), "b_long": inputs.speech_like(48.0, 1302)}
+    pcm = {}
+    for name, x in xs.items():
+        q = np.clip(np.round(x * 32768.0), -32768, 32767).astype("<i2")
+        pcm[name] = (q.astype(np.float64) / 32768.0).astype(np.float32)   # what the file decodes to
+        with wave.open(str(src / f"{name}.wav"), "wb") as w:
+            w.setnchannels(1); w.setsampwidth(2); w.setframerate(16000); w.writeframes(q.tobytes())
+    vocab = [f"▁t{i}" for i in range(16384)]
+    vocab[3] = "<|endoftext|>"
+    eng = abi.Engine(abi.load(), 0, wb, ws, enc_max_utts=4, enc_max_frames=16000)
+    try:
+        written = af.run_folder(eng, str(src), str(dst), vocab, prompt, forced_len=_forced)
+        # direct: the short file in one pass, the long one through the chunk scheduler
+        eng.set_prompt(lf.chunk_prompt(prompt, []))
+        eng.submit_audio(9000, pcm["a_short"], _forced(len(pcm["a_short"])))
+        eng.set_prompt(None)
+        eng.run()
+        short = eng.poll()[9000]
+        sch = lf.LongFormScheduler(eng, prompt, forced_len=_forced)
+        sch.add(1, pcm["b_long"])
+        long_chunks = sch.run()[1]
+        assert eng.status() == 0
+    finally:
+        eng.close()
+    assert [p.rsplit("/", 1)[-1] for p in written] == ["a_short.txt", "b_long.txt"]
+    assert (dst / "a_short.txt").read_text() == af.detokenize(short, vocab)
+    assert len(long_chunks) >= 2
+    assert (dst / "b_long.txt").read_text() == "".join(af.detokenize(t, vocab) for t in long_chunks)
