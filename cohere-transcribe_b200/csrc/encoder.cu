@@ -167,47 +167,68 @@ __global__ void __launch_bounds__(C) dw_planes(const float *in, int Fi, const in
 
 // LayerNorm (eps 1e-5, biased variance; backends/cpu/backend.c:109-122) of
 // packed rows of width D, one warp per row (40 values per lane in registers):
-// optional fp32 output y (may alias x) and bf16 hi/lo planes.
+// optional fp32 output y (may alias x) and bf16 hi/lo planes.  With w2 the
+// planes are those of a second LayerNorm (w2, b2) applied to the first one's
+// output (a layer's final LayerNorm followed by the next layer's first): y
+// holds the first, the planes the second, from one read of x.
+__device__ __forceinline__ void ln_row_stats(const float4 (&v)[D / 128], float &mean, float &inv) {
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < D / 128; ++j) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    mean = warp_sum(s) / D;
+    float var = 0.0f;
+#pragma unroll
+    for (int j = 0; j < D / 128; ++j) {
+        const float a = v[j].x - mean, b2 = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
+        var += (a * a + b2 * b2) + (c * c + d * d);
+    }
+    inv = 1.0f / sqrtf(warp_sum(var) / D + 1e-5f);
+}
+__device__ __forceinline__ void ln_row_apply(float4 (&v)[D / 128], float mean, float inv, const bf16 *w,
+                                             const bf16 *b, int lane) {
+#pragma unroll
+    for (int j = 0; j < D / 128; ++j) {
+        const int k = 4 * (lane + 32 * j);
+        v[j] = make_float4((v[j].x - mean) * inv * bf2f(w[k]) + bf2f(b[k]),
+                           (v[j].y - mean) * inv * bf2f(w[k + 1]) + bf2f(b[k + 1]),
+                           (v[j].z - mean) * inv * bf2f(w[k + 2]) + bf2f(b[k + 2]),
+                           (v[j].w - mean) * inv * bf2f(w[k + 3]) + bf2f(b[k + 3]));
+    }
+}
 __global__ void __launch_bounds__(256) ln_enc(const float *x, int R, const bf16 *w, const bf16 *b, float *y,
-                                              bf16 *hi, bf16 *lo) {
+                                              bf16 *hi, bf16 *lo, const bf16 *w2 = nullptr,
+                                              const bf16 *b2 = nullptr) {
     constexpr int NV = D / 128;   // float4 per lane
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.x * 8 + warp;
     if (r >= R) return;
     const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)r * D);
     float4 v[NV];
-    float s = 0.0f;
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        v[j] = xr[lane + 32 * j];
-        s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-    }
-    const float mean = warp_sum(s) / D;
-    float var = 0.0f;
+    for (int j = 0; j < NV; ++j) v[j] = xr[lane + 32 * j];
+    float mean, inv;
+    ln_row_stats(v, mean, inv);
+    ln_row_apply(v, mean, inv, w, b, lane);
+    if (y)
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const float a = v[j].x - mean, b2 = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
-        var += (a * a + b2 * b2) + (c * c + d * d);
+        for (int j = 0; j < NV; ++j) reinterpret_cast<float4 *>(y + (size_t)r * D)[lane + 32 * j] = v[j];
+    if (w2) {
+        ln_row_stats(v, mean, inv);
+        ln_row_apply(v, mean, inv, w2, b2, lane);
     }
-    const float inv = 1.0f / sqrtf(warp_sum(var) / D + 1e-5f);
+    if (!hi) return;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
         const int k = 4 * (lane + 32 * j);
-        const float o[4] = {(v[j].x - mean) * inv * bf2f(w[k]) + bf2f(b[k]),
-                            (v[j].y - mean) * inv * bf2f(w[k + 1]) + bf2f(b[k + 1]),
-                            (v[j].z - mean) * inv * bf2f(w[k + 2]) + bf2f(b[k + 2]),
-                            (v[j].w - mean) * inv * bf2f(w[k + 3]) + bf2f(b[k + 3])};
-        if (y) *reinterpret_cast<float4 *>(y + (size_t)r * D + k) = make_float4(o[0], o[1], o[2], o[3]);
-        if (hi) {
-            bf16 h4[4], l4[4];
+        const float o[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+        bf16 h4[4], l4[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                h4[e] = __float2bfloat16_rn(o[e]);
-                l4[e] = __float2bfloat16_rn(o[e] - __bfloat162float(h4[e]));
-            }
-            *reinterpret_cast<uint2 *>(hi + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(h4);
-            if (lo) *reinterpret_cast<uint2 *>(lo + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(l4);
+        for (int e = 0; e < 4; ++e) {
+            h4[e] = __float2bfloat16_rn(o[e]);
+            l4[e] = __float2bfloat16_rn(o[e] - __bfloat162float(h4[e]));
         }
+        *reinterpret_cast<uint2 *>(hi + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(h4);
+        if (lo) *reinterpret_cast<uint2 *>(lo + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(l4);
     }
 }
 
@@ -504,7 +525,10 @@ __global__ void __launch_bounds__(128, TWO ? 1 : 2) relpos_tc(const bf16 *qkv_h,
 // each output sums its CK taps from there, skipping taps outside its own
 // utterance.
 constexpr int GR = 32, GC = 128;
-__global__ void __launch_bounds__(256) glu_dw_packed(const float *pw1, Batch b, const bf16 *dww, const bf16 *dwb,
+__device__ __forceinline__ float ld_act(const float *p) { return *p; }
+__device__ __forceinline__ float ld_act(const bf16 *p) { return __bfloat162float(*p); }
+template <typename TIn>   // the pw1 output: fp32, or bf16 with plain bf16 activations
+__global__ void __launch_bounds__(256) glu_dw_packed(const TIn *pw1, Batch b, const bf16 *dww, const bf16 *dwb,
                                                      const bf16 *bnw, const bf16 *bnb, const bf16 *bnm,
                                                      const bf16 *bnv, bf16 *hi, bf16 *lo) {
     constexpr int pad = (CK - 1) / 2, HR = GR + CK - 1;
@@ -521,8 +545,8 @@ __global__ void __launch_bounds__(256) glu_dw_packed(const float *pw1, Batch b, 
     for (int k = 0; k < NH; ++k) {
         const int row = r0 - pad + tr + k * (256 / GC);
         const bool in = row >= 0 && row < b.R3;
-        av[k] = in ? pw1[(size_t)row * 2 * D + c] : 0.0f;
-        gw[k] = in ? pw1[(size_t)row * 2 * D + D + c] : 0.0f;
+        av[k] = in ? ld_act(pw1 + (size_t)row * 2 * D + c) : 0.0f;
+        gw[k] = in ? ld_act(pw1 + (size_t)row * 2 * D + D + c) : 0.0f;
     }
 #pragma unroll
     for (int k = 0; k < NH; ++k) {
@@ -779,8 +803,10 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     for (int l = 0; l < NL; ++l) {
         const Layer &L = w.L[l];
         // FFN1: x += 0.5 * W2 silu(W1 LN(x) + b1) + b2
-        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.ff1_lnw, L.ff1_lnb, nullptr, st.xa[0], lo_a);
-        mark(s, st, "enc_layernorm");
+        if (l == 0) {   // later layers get these planes from the previous layer's final LayerNorm
+            ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.ff1_lnw, L.ff1_lnb, nullptr, st.xa[0], lo_a);
+            mark(s, st, "enc_layernorm");
+        }
         GemmEpilogue f1;
         f1.epi = EPI_BF16; f1.act = 1; f1.bias = L.ff1_b1; f1.Ybf = st.hid[0]; f1.Ybf_lo = lo_h; f1.ldy = FF;
         egemm_enc(s, st, L.ff1_w1, FF, D, xap, R3, RT, f1);
@@ -819,12 +845,22 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         // conv module: x += pw2(silu(bn(dw(glu(pw1(LN(x)))))))
         ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.cv_lnw, L.cv_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
+        // pw1 output: fp32 with hi+lo planes, bf16 with plain bf16 activations
+        // (half the bytes written and read back by the GLU)
         GemmEpilogue e1;
-        e1.bias = L.cv_pw1b; e1.Y = st.qkv; e1.ldy = 2 * D;
+        e1.bias = L.cv_pw1b; e1.ldy = 2 * D;
+        bf16 *pw1_bf = reinterpret_cast<bf16 *>(st.qkv);
+        if (st.two) e1.Y = st.qkv;
+        else { e1.epi = EPI_BF16; e1.Ybf = pw1_bf; }
         egemm_enc(s, st, L.cv_pw1w, 2 * D, D, xap, R3, RT, e1);
         mark(s, st, "enc_gemm_pw1");
-        glu_dw_packed<<<dim3((R3 + GR - 1) / GR, D / GC), 256, 0, s>>>(st.qkv, bt, L.cv_dww, L.cv_dwb, L.cv_bnw, L.cv_bnb,
-                                                              L.cv_bnm, L.cv_bnv, st.ap[0], lo_p);
+        const dim3 ggrid((R3 + GR - 1) / GR, D / GC);
+        if (st.two)
+            glu_dw_packed<float><<<ggrid, 256, 0, s>>>(st.qkv, bt, L.cv_dww, L.cv_dwb, L.cv_bnw, L.cv_bnb, L.cv_bnm,
+                                                       L.cv_bnv, st.ap[0], lo_p);
+        else
+            glu_dw_packed<bf16><<<ggrid, 256, 0, s>>>(pw1_bf, bt, L.cv_dww, L.cv_dwb, L.cv_bnw, L.cv_bnb, L.cv_bnm,
+                                                      L.cv_bnv, st.ap[0], lo_p);
         mark(s, st, "enc_glu_dwconv");
         GemmEpilogue e2;
         e2.epi = EPI_FMADD; e2.scale = 1.0f; e2.bias = L.cv_pw2b; e2.Y = st.x; e2.ldy = D;
@@ -841,8 +877,13 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         g2.bias = L.ff2_b2;
         egemm_enc(s, st, L.ff2_w2, D, FF, hidp, R3, RT, g2);
         mark(s, st, "enc_gemm_ffn2");
-        // x = LN_out(x); its planes feed the next layer's nothing / the projection
-        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a);
+        // x = LN_out(x), and the planes of the next layer's FFN1 LayerNorm of it
+        // (after the last layer: the planes of x itself, for the projection)
+        if (l + 1 < NL)
+            ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a,
+                                                 w.L[l + 1].ff1_lnw, w.L[l + 1].ff1_lnb);
+        else
+            ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
     }
     // ---- encoder -> decoder projection (model.h:607) ----
