@@ -15,10 +15,13 @@
 // sequence counts from device memory, so one captured graph per capacity
 // bucket serves every step.
 #include <algorithm>
+#include <condition_variable>
 #include <deque>
 #include <map>
+#include <mutex>
 #include <string>
 #include <string.h>
+#include <thread>
 #include <vector>
 
 #include "../../include/ct_engine.h"
@@ -607,6 +610,81 @@ struct Bucket {
 using namespace ct;
 using namespace ct::eng;
 
+// Host copies into the pinned staging rings (submissions of encoder rows,
+// log-mel or audio): a copy of 1 MiB or more is split over a few persistent
+// worker threads, since one thread's memcpy into pinned memory (~10 GB/s)
+// would otherwise be the longest part of a submission.  copy() returns once
+// every part has landed.
+class CopyPool {
+  public:
+    explicit CopyPool(int n) {
+        for (int i = 0; i < n; ++i) workers_.emplace_back([this] { loop(); });
+    }
+    ~CopyPool() {
+        {
+            std::lock_guard<std::mutex> g(m_);
+            stop_ = true;
+        }
+        cv_.notify_all();
+        for (auto &t : workers_) t.join();
+    }
+    void copy(void *dst, const void *src, size_t bytes) {
+        const size_t parts = workers_.size() + 1;
+        if (bytes < (1u << 20) || workers_.empty()) {
+            memcpy(dst, src, bytes);
+            return;
+        }
+        const size_t chunk = ((bytes + parts - 1) / parts + 63) & ~(size_t)63;
+        {
+            std::lock_guard<std::mutex> g(m_);
+            dst_ = static_cast<char *>(dst);
+            src_ = static_cast<const char *>(src);
+            bytes_ = bytes;
+            chunk_ = chunk;
+            next_ = 1;   // part 0 is the caller's
+            left_ = parts - 1;
+            ++gen_;
+        }
+        cv_.notify_all();
+        memcpy(dst, src, std::min(chunk, bytes));
+        std::unique_lock<std::mutex> g(m_);
+        done_cv_.wait(g, [this] { return left_ == 0; });
+    }
+
+  private:
+    void loop() {
+        unsigned long long seen = 0;
+        std::unique_lock<std::mutex> g(m_);
+        for (;;) {
+            cv_.wait(g, [&] { return stop_ || gen_ != seen; });
+            if (stop_) return;
+            seen = gen_;
+            while (next_ < workers_.size() + 1 && left_ > 0) {
+                const size_t part = next_++;
+                const size_t off = part * chunk_;
+                const size_t n = off < bytes_ ? std::min(chunk_, bytes_ - off) : 0;
+                g.unlock();
+                if (n) memcpy(dst_ + off, src_ + off, n);
+                g.lock();
+                if (--left_ == 0) done_cv_.notify_one();
+            }
+        }
+    }
+    std::vector<std::thread> workers_;
+    std::mutex m_;
+    std::condition_variable cv_, done_cv_;
+    char *dst_ = nullptr;
+    const char *src_ = nullptr;
+    size_t bytes_ = 0, chunk_ = 0, next_ = 0, left_ = 0;
+    unsigned long long gen_ = 0;
+    bool stop_ = false;
+};
+
+static int copy_threads() {
+    const unsigned hc = std::thread::hardware_concurrency();
+    return (int)std::min<unsigned>(7, hc > 2 ? hc / 2 - 1 : 0);
+}
+
 struct ct_engine {
     int device = -1;
     cudaStream_t st = nullptr;
@@ -663,6 +741,7 @@ struct ct_engine {
     bf16 *enc_pl[2];
     long long *enc_off = nullptr;
     int enc_rows_cap = 0;
+    CopyPool copier{copy_threads()}; // host -> pinned-ring staging copies
     float *enc_stage = nullptr;      // pinned submission ring for host encoder rows (enc_rows_cap rows)
     PinnedRing ring;                 // over enc_stage, in rows
     PinnedRing job_ring;             // over job_stage: queued audio / log-mel inputs, in floats
@@ -1473,7 +1552,7 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
 static void stage_job(ct_engine *e, ct_engine::MelJob &j, const float *src, size_t count) {
     j.count = count;
     j.ring_off = e->job_ring.alloc((long long)count);
-    if (j.ring_off >= 0) memcpy(e->job_stage + j.ring_off, src, sizeof(float) * count);
+    if (j.ring_off >= 0) e->copier.copy(e->job_stage + j.ring_off, src, sizeof(float) * count);
     else j.mel.assign(src, src + count);
 }
 
@@ -1568,7 +1647,7 @@ extern "C" int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const fl
     p.id = utt_id;
     p.prompt = e->next_prompt;
     p.ring_off = ring_alloc(e, T_enc);
-    if (p.ring_off >= 0) memcpy(e->enc_stage + (size_t)p.ring_off * D, enc_h, sizeof(float) * (size_t)T_enc * D);
+    if (p.ring_off >= 0) e->copier.copy(e->enc_stage + (size_t)p.ring_off * D, enc_h, sizeof(float) * (size_t)T_enc * D);
     else p.enc.assign(enc_h, enc_h + (size_t)T_enc * D);
     p.T_enc = T_enc;
     p.forced = forced_len;
