@@ -22,11 +22,12 @@
 // bits say).
 // Operands: Q, K and P tiles by TMA with the 128-byte swizzle (K-major, three
 // 64-column atoms cover DK = 160; the MMAs use the first 160 columns).  K is
-// double-buffered; the band lives in a ring of three 64-row blocks (tile i
-// reads blocks i, i + 1, i + 2, so each tile loads one new block, and BD is
-// three N = 64 MMAs, the new block's last).  V is transposed into a K-major
-// [160 d][64 keys] tile by the staging warps; the probabilities are written by
-// the softmax threads as the K-major A operand of the P.V MMA.
+// double-buffered; the band lives in a ring of four 64-row blocks (tile i
+// reads blocks i, i + 1, i + 2, so each tile needs one new block, loaded a tile
+// ahead; slots adjacent in memory go to one wider MMA).  V is transposed into a
+// K-major [160 d][64 keys] tile by the staging warps; the probabilities are
+// written by the softmax threads into TMEM (columns [416, 448), two bf16 per
+// column) as the A operand of the P.V MMA.
 // Warps: 0 TMA producer, 1 MMA issuer (TMEM owner), 2..5 softmax (TMEM lane
 // quarters 2, 3, 0, 1), 6..9 V / bias staging.  Every wait is bounded.
 
