@@ -525,57 +525,69 @@ __global__ void __launch_bounds__(128, TWO ? 1 : 2) relpos_tc(const bf16 *qkv_h,
 // each output sums its CK taps from there, skipping taps outside its own
 // utterance.
 constexpr int GR = 32, GC = 128;
-__device__ __forceinline__ float ld_act(const float *p) { return *p; }
-__device__ __forceinline__ float ld_act(const bf16 *p) { return __bfloat162float(*p); }
+// two adjacent channels of a pw1 row as float2 (8 B fp32 or 4 B bf16 loads)
+__device__ __forceinline__ float2 ld_act2(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+__device__ __forceinline__ float2 ld_act2(const bf16 *p) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(p));
+}
 template <typename TIn>   // the pw1 output: fp32, or bf16 with plain bf16 activations
 __global__ void __launch_bounds__(256) glu_dw_packed(const TIn *pw1, Batch b, const bf16 *dww, const bf16 *dwb,
                                                      const bf16 *bnw, const bf16 *bnb, const bf16 *bnm,
                                                      const bf16 *bnv, bf16 *hi, bf16 *lo) {
     constexpr int pad = (CK - 1) / 2, HR = GR + CK - 1;
-    __shared__ float g_s[HR][GC];
+    constexpr int TC = GC / 2, RL = 256 / TC;   // 64 channel pairs x 4 row lanes
+    __shared__ float2 g_s[HR][TC];
     const int r0 = blockIdx.x * GR, c0 = blockIdx.y * GC;
-    const int tc = threadIdx.x & (GC - 1), tr = threadIdx.x / GC;   // 2 row lanes x 128 channels
-    const int c = c0 + tc;
+    const int tc = threadIdx.x % TC, tr = threadIdx.x / TC;
+    const int c = c0 + 2 * tc;                  // this thread's channels c, c + 1
     // every load of the thread's rows issued before the first use (memory-level
-    // parallelism: the kernel streams 2560 fp32 per row)
-    constexpr int NH = HR / (256 / GC);
-    static_assert(HR % (256 / GC) == 0, "halo rows split evenly over the row lanes");
-    float av[NH], gw[NH];
+    // parallelism: the kernel streams 2560 values per row)
+    constexpr int NH = HR / RL;
+    static_assert(HR % RL == 0, "halo rows split evenly over the row lanes");
+    float2 av[NH], gw[NH];
 #pragma unroll
     for (int k = 0; k < NH; ++k) {
-        const int row = r0 - pad + tr + k * (256 / GC);
+        const int row = r0 - pad + tr + k * RL;
         const bool in = row >= 0 && row < b.R3;
-        av[k] = in ? ld_act(pw1 + (size_t)row * 2 * D + c) : 0.0f;
-        gw[k] = in ? ld_act(pw1 + (size_t)row * 2 * D + D + c) : 0.0f;
+        av[k] = in ? ld_act2(pw1 + (size_t)row * 2 * D + c) : make_float2(0.0f, 0.0f);
+        gw[k] = in ? ld_act2(pw1 + (size_t)row * 2 * D + D + c) : make_float2(0.0f, 0.0f);
     }
 #pragma unroll
     for (int k = 0; k < NH; ++k) {
-        const int row = r0 - pad + tr + k * (256 / GC);
-        g_s[tr + k * (256 / GC)][tc] = (row >= 0 && row < b.R3) ? mul_sigmoid(av[k], gw[k]) : 0.0f;
+        const int row = r0 - pad + tr + k * RL;
+        const bool in = row >= 0 && row < b.R3;
+        g_s[tr + k * RL][tc] = in ? make_float2(mul_sigmoid(av[k].x, gw[k].x), mul_sigmoid(av[k].y, gw[k].y))
+                                  : make_float2(0.0f, 0.0f);
     }
-    float wk[CK];
+    float wk0[CK], wk1[CK];
 #pragma unroll
-    for (int k = 0; k < CK; ++k) wk[k] = bf2f(dww[c * CK + k]);
-    const float bias = bf2f(dwb[c]);
-    const float bn_scale = bf2f(bnw[c]) / sqrtf(bf2f(bnv[c]) + 1e-5f), bn_mean = bf2f(bnm[c]), bn_b = bf2f(bnb[c]);
+    for (int k = 0; k < CK; ++k) { wk0[k] = bf2f(dww[c * CK + k]); wk1[k] = bf2f(dww[(c + 1) * CK + k]); }
+    const float bias0 = bf2f(dwb[c]), bias1 = bf2f(dwb[c + 1]);
+    const float sc0 = bf2f(bnw[c]) / sqrtf(bf2f(bnv[c]) + 1e-5f), sc1 = bf2f(bnw[c + 1]) / sqrtf(bf2f(bnv[c + 1]) + 1e-5f);
+    const float mu0 = bf2f(bnm[c]), mu1 = bf2f(bnm[c + 1]), be0 = bf2f(bnb[c]), be1 = bf2f(bnb[c + 1]);
     __syncthreads();
-    for (int rr = tr; rr < GR; rr += 256 / GC) {
+    for (int rr = tr; rr < GR; rr += RL) {
         const int row = r0 + rr;
         if (row >= b.R3) break;
         const int u = b.row_utt3[row];
         const int lo_row = b.r3_off[u], hi_row = b.r3_off[u + 1];
-        float sum = bias;
+        float s0 = bias0, s1 = bias1;
 #pragma unroll
         for (int k = 0; k < CK; ++k) {
             const int ti = row - pad + k;
-            if (ti >= lo_row && ti < hi_row) sum += wk[k] * g_s[rr + k][tc];
+            if (ti >= lo_row && ti < hi_row) {
+                const float2 g = g_s[rr + k][tc];
+                s0 += wk0[k] * g.x;
+                s1 += wk1[k] * g.y;
+            }
         }
-        float v = (sum - bn_mean) * bn_scale + bn_b;
-        v = silu_fast(v);
+        const float v0 = silu_fast((s0 - mu0) * sc0 + be0), v1 = silu_fast((s1 - mu1) * sc1 + be1);
         const size_t i = (size_t)row * D + c;
-        const bf16 hb = __float2bfloat16_rn(v);
-        hi[i] = hb;
-        if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(hb));
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+        *reinterpret_cast<__nv_bfloat162 *>(hi + i) = h2;
+        if (lo)
+            *reinterpret_cast<__nv_bfloat162 *>(lo + i) =
+                __floats2bfloat162_rn(v0 - __low2float(h2), v1 - __high2float(h2));
     }
 }
 
