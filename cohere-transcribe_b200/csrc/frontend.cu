@@ -24,6 +24,11 @@ namespace fe {
 
 constexpr int NFFT = 512, WIN = 400, HOP = 160, NM = N_MELS, NB = NFFT / 2 + 1, SR = 16000;
 constexpr int FW = 8;   // frames (warps) per CTA
+// Shared-memory index of FFT element x with one padding float per 32: the
+// bit-reversed stores and the power-of-two butterfly strides then fall in
+// different banks (the values and the arithmetic are unchanged).
+__device__ __forceinline__ int fpad(int x) { return x + (x >> 5); }
+constexpr int NFFT_P = NFFT + NFFT / 32;
 
 struct Front {
     float *hann = nullptr, *twr = nullptr, *twi = nullptr, *fb = nullptr;
@@ -41,7 +46,7 @@ __global__ void __launch_bounds__(FW * 32) mel_power_kernel(const float *samples
                                                             const float *hann, const float *twr, const float *twi,
                                                             const float *fb, const int *fb_lo, const int *fb_hi,
                                                             float *mel) {
-    __shared__ float re_s[FW][NFFT], im_s[FW][NFFT];
+    __shared__ float re_s[FW][NFFT_P], im_s[FW][NFFT_P];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int f = blockIdx.x * FW + warp;
     if (f >= F) return;
@@ -63,15 +68,15 @@ __global__ void __launch_bounds__(FW * 32) mel_power_kernel(const float *samples
             v = sj * hann[i];
         }
         const int r = __brev(i) >> (32 - 9);   // 9-bit bit reversal
-        re[r] = v;
-        im[r] = 0.0f;
+        re[fpad(r)] = v;
+        im[fpad(r)] = 0.0f;
     }
     __syncwarp();
     for (int len = 2; len <= NFFT; len <<= 1) {
         const int half = len >> 1, step = NFFT / len;
         for (int bidx = lane; bidx < NFFT / 2; bidx += 32) {
             const int grp = bidx / half, pos = bidx - grp * half;
-            const int a = grp * len + pos, c = a + half;
+            const int a = fpad(grp * len + pos), c = fpad(grp * len + pos + half);
             const float wr = twr[pos * step], wi = twi[pos * step];
             const float vr = re[c] * wr - im[c] * wi;
             const float vi = re[c] * wi + im[c] * wr;
@@ -81,12 +86,15 @@ __global__ void __launch_bounds__(FW * 32) mel_power_kernel(const float *samples
         }
         __syncwarp();
     }
-    for (int k = lane; k < NB; k += 32) im[k] = re[k] * re[k] + im[k] * im[k];   // power spectrum
+    for (int k = lane; k < NB; k += 32) {   // power spectrum
+        const float r = re[fpad(k)], i = im[fpad(k)];
+        im[fpad(k)] = r * r + i * i;
+    }
     __syncwarp();
     const float guard = 5.9604644775390625e-08f;   // 2^-24
     for (int m = lane; m < NM; m += 32) {
         float v = 0.0f;
-        for (int k = fb_lo[m]; k < fb_hi[m]; ++k) v += fb[m * NB + k] * im[k];
+        for (int k = fb_lo[m]; k < fb_hi[m]; ++k) v += fb[m * NB + k] * im[fpad(k)];
         mel[mel_off[u] + (size_t)m * T + t] = logf(v + guard);
     }
 }
