@@ -98,4 +98,6 @@ def test_submit_audio_end_to_end(engine, full_model, wmod):
             if mg[b, n_p + g] >= E2E_MARGIN_TOL:
                 assert via_audio[b][g] == am[b, n_p + g], (b, g)
                 checked += 1
-    assert checked >= 0.5 * (forced.sum() - 3)
+    total = int(forced.sum()) - 3
+    print(f"token positions checked (oracle margin >= {E2E_MARGIN_TOL}): {checked}/{total}")
+    assert checked >= 0.8 * total, f"checked {checked}/{total}"
