@@ -88,10 +88,11 @@ NCU_TRAFFIC = {
     # written.  Unit: algorithmic byte (the K/V rows the launch must read).
     "paged cross-attention": {"bytes": 59.354368e6 + 0.41216e6, "units": 14080 * 4096.0,
                               "unit": "algorithmic byte", "source": "profiles/attn_paged_decode.md"},
-    # profiles/gemm_decode_ffn_lmhead.md: one layer's FFN1 + FFN2 at 64 rows
-    # (18,087,936 algorithmic bytes): 8.760832 + 9.787648 MB read, 0 written.
-    # Unit: algorithmic byte (weights + activation planes of the two launches).
-    "decode FFN GEMMs (tcgen05)": {"bytes": 8.760832e6 + 9.787648e6, "units": 18087936.0,
+    # profiles/gemm_decode_ffn_lmhead.md: one layer's FFN1 + FFN2 at 64 rows,
+    # bf16 activations (17,432,576 algorithmic bytes): 8.759552 + 9.262848 MB
+    # read, 0 written.  Unit: algorithmic byte (weights + activations of the
+    # two launches).
+    "decode FFN GEMMs (tcgen05)": {"bytes": 8.759552e6 + 9.262848e6, "units": 17432576.0,
                                    "unit": "algorithmic byte", "source": "profiles/gemm_decode_ffn_lmhead.md"},
     # profiles/gemm_persistent_encoder_ffn1.md: layer 0's FFN1 over 3,545 packed
     # rows: 31.509504 MB read + 24.338688 MB written.  Unit: packed row.  The

@@ -1016,16 +1016,8 @@ static void encode_step(ct_engine *e, int rows) {
     launch_pdl(st, dim3(rows), dim3(256), embed_rows_kernel, s, e->etw, e->epw, e->elnw, e->elnb, e->L[0].sa_lnw,
                e->L[0].sa_lnb, e->h, e->xa[0], xa_lo);
     mark(e, "embed_ln");
-    // each GEMM hints the next GEMM's weights into L2 (the step's GEMMs in order)
-    static const int kinds[6] = {G_QKV, G_O, G_QC, G_OC, G_F1, G_F2};
-    auto spec_at = [&](int k) { return k < 6 * NL ? gemm_spec(e, k / 6, kinds[k % 6]) : gemm_spec(e, 0, G_LM); };
-    auto launch_k = [&](int k) {
-        GemmSpec g = spec_at(k);
-        const GemmSpec nx = spec_at(k + 1);
-        g.ep.l2_next = nx.W;
-        g.ep.l2_next_bytes = (unsigned)((size_t)nx.N * nx.K * sizeof(bf16));
-        launch_gemm_spec(e, g, rows);
-    };
+    static const int kinds[6] = {G_QKV, G_O, G_QC, G_OC, G_F1, G_F2};   // the layer's GEMMs in order
+    auto launch_k = [&](int k) { launch_gemm_spec(e, gemm_spec(e, k / 6, kinds[k % 6]), rows); };
     for (int l = 0; l < NL; ++l) {
         launch_k(6 * l + 0);
         mark(e, "gemm_qkv");

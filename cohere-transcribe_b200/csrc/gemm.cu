@@ -574,15 +574,6 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
             mbar_expect_tx(&full[i], stage_bytes);
             tma_load_2d(smem + (size_t)i * stage_bytes, &tmW, &full[i], (kb0 + i) * BK, n0);
         }
-        // this CTA's slice of the next GEMM's weights into L2 (after its own loads)
-        if (p.ep.l2_next) {
-            const unsigned ncta = gridDim.x * gridDim.y * gridDim.z;
-            const unsigned cid = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-            const unsigned chunk = ((p.ep.l2_next_bytes + ncta - 1) / ncta + 15u) & ~15u;
-            const unsigned off = cid * chunk;
-            if (off < p.ep.l2_next_bytes)
-                prefetch_l2(static_cast<const uint8_t *>(p.ep.l2_next) + off, min(chunk, p.ep.l2_next_bytes - off));
-        }
     }
     pdl_wait();
     pdl_trigger();

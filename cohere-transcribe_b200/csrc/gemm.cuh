@@ -127,12 +127,6 @@ struct GemmEpilogue {
     // Greedy argmax of each token row over N (EPI_STORE without a K split;
     // Y may then be null, in which case no logits are stored).
     ArgmaxSink amax;
-    // L2 prefetch hint: the weights of the GEMM that follows this one in a
-    // dependent chain (16-byte aligned, bytes a multiple of 16).  The tile
-    // kernel's CTAs each prefetch an equal slice before their dependency wait,
-    // so the next launch's weight loads hit L2.  Null: none.
-    const void *l2_next = nullptr;
-    unsigned l2_next_bytes = 0;
 };
 
 // Per-thread GEMM context: stream, workspaces, tensor-map cache.
