@@ -105,10 +105,10 @@ NCU_TRAFFIC = {
 
 
 # Sharding weight of a generated token against an audio second: on one B200
-# the packed encoder takes ~0.14 ms per audio second (156 ms for 1,110 s) and
-# a 64-sequence decode step ~0.0105 ms per sequence (0.675 ms), so about 13
+# the packed encoder takes ~0.059 ms per audio second (65 ms for 1,110 s) and
+# a 64-sequence decode step ~0.0102 ms per sequence (0.653 ms), so about 6
 # generated tokens cost as much as one second of audio.
-DECODE_TOKENS_PER_AUDIO_S = 13.0
+DECODE_TOKENS_PER_AUDIO_S = 6.0
 
 
 def workload(seed: int = 0, batch: int = BATCH, rank: int = 0, world: int = 1):
