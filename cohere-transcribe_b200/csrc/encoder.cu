@@ -71,19 +71,23 @@ struct Batch {
 // Summation order per output: conv0 taps (kh, kw) row-major, then depthwise
 // taps (kh, kw) row-major, each starting from its bias, as the reference.
 constexpr int SUB_TH = 7;   // mel frames per stage-2 row (4 t2 - 3 .. 4 t2 + 3)
+// staged bins start at -SUB_LP, so the five bins 4 f2 - 1 .. 4 f2 + 3 that step
+// f2 reads sit at columns 4 f2 + 4 .. 4 f2 + 8: one aligned float4 and one float
+constexpr int SUB_LP = 5, SUB_W = 136;
+static_assert(2 * F2 <= F1 && 4 * (F2 - 1) + 8 < SUB_W && SUB_W % 4 == 0, "staged log-mel columns");
 __global__ void __launch_bounds__(C) conv0_dw_planes(const float *mel, Batch b, const bf16 *w0, const bf16 *b0,
                                                      const bf16 *w2, const bf16 *b2, bf16 *hi, bf16 *lo) {
-    __shared__ float ms[SUB_TH][F0 + 4];   // [frame][bin + 2]: bins -2 .. F0 + 1, zero outside
+    __shared__ __align__(16) float ms[SUB_TH][SUB_W];   // [frame][bin + SUB_LP], zero outside
     const int r2 = blockIdx.x;
     const int c = threadIdx.x;
     const int u = b.row_utt2[r2];
     const int t2 = r2 - b.r2_off[u];
     const int T1 = b.r1_off[u + 1] - b.r1_off[u], Tm = b.T_mel[u];
     const float *m = mel + b.mel_off[u];
-    for (int i = threadIdx.x; i < SUB_TH * (F0 + 4); i += blockDim.x) {
-        const int fr = i / (F0 + 4), bin = i % (F0 + 4) - 2;
+    for (int i = threadIdx.x; i < SUB_TH * SUB_W; i += blockDim.x) {   // frames fastest: a bin's 7 are adjacent
+        const int fr = i % SUB_TH, bin = i / SUB_TH - SUB_LP;
         const int t = 4 * t2 - 3 + fr;
-        ms[fr][bin + 2] = (t >= 0 && t < Tm && bin >= 0 && bin < F0) ? m[(size_t)bin * Tm + t] : 0.0f;
+        ms[fr][bin + SUB_LP] = (t >= 0 && t < Tm && bin >= 0 && bin < F0) ? m[(size_t)bin * Tm + t] : 0.0f;
     }
     float k0[9], k2[9];
 #pragma unroll
@@ -93,28 +97,35 @@ __global__ void __launch_bounds__(C) conv0_dw_planes(const float *mel, Batch b, 
 #pragma unroll
     for (int j = 0; j < 3; ++j) { const int t1 = 2 * t2 - 1 + j; rv[j] = t1 >= 0 && t1 < T1; }
     __syncthreads();
-    // A[j][f1] for row j (t1 = 2 t2 - 1 + j) uses frames 2 j .. 2 j + 2 of ms
-    // and bins 2 f1 - 1 .. 2 f1 + 1 (ms columns 2 f1 + 1 .. 2 f1 + 3)
-    auto a_val = [&](int j, int f1) -> float {
-        if (!rv[j] || f1 < 0 || f1 >= F1) return 0.0f;
-        float s = bias0;
+    // A[j][f1] for row j (t1 = 2 t2 - 1 + j) uses frames 2 j .. 2 j + 2 and bins
+    // 2 f1 - 1 .. 2 f1 + 1; at step f2, f1 = 2 f2 takes bins x[0..2] and
+    // f1 = 2 f2 + 1 takes x[2..4] of the frame's five bins x = 4 f2 - 1 .. 4 f2 + 3
+    float a[3][3];   // A[j][2 f2 - 1 + i]; A[j][-1] = 0 (the depthwise's padding)
 #pragma unroll
-        for (int kh = 0; kh < 3; ++kh)
-#pragma unroll
-            for (int kw = 0; kw < 3; ++kw) s += ms[2 * j + kh][2 * f1 + 1 + kw] * k0[kh * 3 + kw];
-        return s > 0.0f ? s : 0.0f;
-    };
-    float a[3][3];   // A[j][2 f2 - 1 + i]
-#pragma unroll
-    for (int j = 0; j < 3; ++j) a[j][2] = a_val(j, -1);
+    for (int j = 0; j < 3; ++j) a[j][2] = 0.0f;
     const size_t row0 = (size_t)r2 * F2;
 #pragma unroll 1
     for (int f2 = 0; f2 < F2; ++f2) {
+        float x[SUB_TH][5];
+#pragma unroll
+        for (int fr = 0; fr < SUB_TH; ++fr) {
+            const float4 q = *reinterpret_cast<const float4 *>(&ms[fr][4 * f2 + 4]);
+            x[fr][0] = q.x; x[fr][1] = q.y; x[fr][2] = q.z; x[fr][3] = q.w;
+            x[fr][4] = ms[fr][4 * f2 + 8];
+        }
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
+            float s0 = bias0, s1 = bias0;   // conv0 taps (kh, kw) row-major, from the bias
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    s0 += x[2 * j + kh][kw] * k0[kh * 3 + kw];
+                    s1 += x[2 * j + kh][kw + 2] * k0[kh * 3 + kw];
+                }
             a[j][0] = a[j][2];
-            a[j][1] = a_val(j, 2 * f2);
-            a[j][2] = a_val(j, 2 * f2 + 1);
+            a[j][1] = rv[j] && s0 > 0.0f ? s0 : 0.0f;
+            a[j][2] = rv[j] && s1 > 0.0f ? s1 : 0.0f;
         }
         float s = bias2;
 #pragma unroll
@@ -537,6 +548,7 @@ __global__ void __launch_bounds__(256) glu_dw_packed(const TIn *pw1, Batch b, co
     constexpr int pad = (CK - 1) / 2, HR = GR + CK - 1;
     constexpr int TC = GC / 2, RL = 256 / TC;   // 64 channel pairs x 4 row lanes
     __shared__ float2 g_s[HR][TC];
+    __shared__ int lo_s[GR], hi_s[GR];          // the utterance row range of each output row
     const int r0 = blockIdx.x * GR, c0 = blockIdx.y * GC;
     const int tc = threadIdx.x % TC, tr = threadIdx.x / TC;
     const int c = c0 + 2 * tc;                  // this thread's channels c, c + 1
@@ -552,6 +564,13 @@ __global__ void __launch_bounds__(256) glu_dw_packed(const TIn *pw1, Batch b, co
         av[k] = in ? ld_act2(pw1 + (size_t)row * 2 * D + c) : make_float2(0.0f, 0.0f);
         gw[k] = in ? ld_act2(pw1 + (size_t)row * 2 * D + D + c) : make_float2(0.0f, 0.0f);
     }
+    // (dependent index loads once per CTA, while the activation loads are in flight)
+    if (threadIdx.x < GR) {
+        const int row = min(r0 + (int)threadIdx.x, b.R3 - 1);
+        const int u = b.row_utt3[row];
+        lo_s[threadIdx.x] = b.r3_off[u];
+        hi_s[threadIdx.x] = b.r3_off[u + 1];
+    }
 #pragma unroll
     for (int k = 0; k < NH; ++k) {
         const int row = r0 - pad + tr + k * RL;
@@ -566,11 +585,11 @@ __global__ void __launch_bounds__(256) glu_dw_packed(const TIn *pw1, Batch b, co
     const float sc0 = bf2f(bnw[c]) / sqrtf(bf2f(bnv[c]) + 1e-5f), sc1 = bf2f(bnw[c + 1]) / sqrtf(bf2f(bnv[c + 1]) + 1e-5f);
     const float mu0 = bf2f(bnm[c]), mu1 = bf2f(bnm[c + 1]), be0 = bf2f(bnb[c]), be1 = bf2f(bnb[c + 1]);
     __syncthreads();
+#pragma unroll
     for (int rr = tr; rr < GR; rr += RL) {
         const int row = r0 + rr;
         if (row >= b.R3) break;
-        const int u = b.row_utt3[row];
-        const int lo_row = b.r3_off[u], hi_row = b.r3_off[u + 1];
+        const int lo_row = lo_s[rr], hi_row = hi_s[rr];
         float s0 = bias0, s1 = bias1;
 #pragma unroll
         for (int k = 0; k < CK; ++k) {
@@ -845,7 +864,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
             relpos_tc<false><<<dim3(NQ, H), 128, sizeof(RelposSmem<false>), s>>>(
                 st.qkvp[0], nullptr, st.Pp[0], nullptr, bt, L.sa_pbu, L.sa_pbv, st.ap[0], nullptr);
         else {
-            relpos_bias_dots<<<(R3 * H + PL * H + 7) / 8, 256, 0, s>>>(st.qkvp[0], nullptr, st.Pp[0], nullptr, R3, PL,
+            relpos_bias_dots<<<(R3 + PL + 7) / 8, 256, 0, s>>>(st.qkvp[0], nullptr, st.Pp[0], nullptr, R3, PL,
                                                                         L.sa_pbu, L.sa_pbv, st.ukg, st.vpg);
             relpos_umma<<<dim3(bt.n_qtiles2, H), U_THREADS, sizeof(RelposUmmaSmem) + 1024, s>>>(tmQ, tmK, tmP, ua);
         }

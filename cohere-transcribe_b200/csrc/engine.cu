@@ -15,6 +15,8 @@
 // sequence counts from device memory, so one captured graph per capacity
 // bucket serves every step.
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <deque>
 #include <map>
@@ -611,10 +613,13 @@ using namespace ct;
 using namespace ct::eng;
 
 // Host copies into the pinned staging rings (submissions of encoder rows,
-// log-mel or audio): a copy of 1 MiB or more is split over a few persistent
+// log-mel or audio): a copy of 256 KB or more is split over a few persistent
 // worker threads, since one thread's memcpy into pinned memory (~10 GB/s)
 // would otherwise be the longest part of a submission.  copy() returns once
-// every part has landed.
+// every part has landed.  Submissions come in bursts of small copies (one
+// utterance is ~0.2-2 MB), so a worker keeps polling for the next copy for
+// kSpinUs after its last part before it sleeps: a futex wake-up per copy cost
+// more than the copy's own parts.
 class CopyPool {
   public:
     explicit CopyPool(int n) {
@@ -624,60 +629,99 @@ class CopyPool {
         {
             std::lock_guard<std::mutex> g(m_);
             stop_ = true;
+            stop_flag_ = true;
         }
         cv_.notify_all();
         for (auto &t : workers_) t.join();
     }
     void copy(void *dst, const void *src, size_t bytes) {
-        const size_t parts = workers_.size() + 1;
-        if (bytes < (1u << 20) || workers_.empty()) {
+        // parts of at least 128 KB: below that one thread's memcpy beats handing parts out
+        const size_t parts = std::min(workers_.size() + 1, bytes / (128u << 10));
+        if (parts <= 1) {
             memcpy(dst, src, bytes);
             return;
         }
         const size_t chunk = ((bytes + parts - 1) / parts + 63) & ~(size_t)63;
-        {
-            std::lock_guard<std::mutex> g(m_);
-            dst_ = static_cast<char *>(dst);
-            src_ = static_cast<const char *>(src);
-            bytes_ = bytes;
-            chunk_ = chunk;
-            next_ = 1;   // part 0 is the caller's
-            left_ = parts - 1;
-            ++gen_;
+        const unsigned long long g = gen_.load() + 1;
+        dst_ = static_cast<char *>(dst);
+        src_ = static_cast<const char *>(src);
+        bytes_ = bytes;
+        chunk_ = chunk;
+        parts_ = parts;
+        left_ = parts - 1;
+        claim_ = (g << kPartBits) | 1;   // part 0 is the caller's
+        gen_ = g;
+        if (sleepers_.load() > 0) {
+            std::lock_guard<std::mutex> lk(m_);
+            cv_.notify_all();
         }
-        cv_.notify_all();
         memcpy(dst, src, std::min(chunk, bytes));
-        std::unique_lock<std::mutex> g(m_);
-        done_cv_.wait(g, [this] { return left_ == 0; });
+        run_parts(g);   // help with the parts no worker has taken yet
+        while (left_.load() != 0) cpu_relax();
     }
 
   private:
+    static constexpr int kSpinUs = 500;
+    static constexpr int kPartBits = 16;
+    static constexpr unsigned long long kPartMask = (1ull << kPartBits) - 1;
+    static void cpu_relax() {
+#if defined(__x86_64__) || defined(__i386__)
+        __builtin_ia32_pause();
+#endif
+    }
+    // Take and copy parts of copy g until none is left.  A part is claimed by a
+    // compare-and-swap on (generation, next part), so a thread still holding an
+    // earlier copy's generation can never take a part of a later copy, and a
+    // copy's fields stay fixed while any of its parts is being copied (copy()
+    // returns only when all are done).
+    void run_parts(unsigned long long g) {
+        for (;;) {
+            unsigned long long v = claim_.load();
+            for (;;) {
+                if ((v >> kPartBits) != g || (v & kPartMask) >= parts_.load()) return;
+                if (claim_.compare_exchange_weak(v, v + 1)) break;
+            }
+            const size_t part = (size_t)(v & kPartMask);
+            const size_t off = part * chunk_.load(), bytes = bytes_.load();
+            const size_t n = off < bytes ? std::min(chunk_.load(), bytes - off) : 0;
+            if (n) memcpy(dst_.load() + off, src_.load() + off, n);
+            left_.fetch_sub(1);
+        }
+    }
     void loop() {
         unsigned long long seen = 0;
-        std::unique_lock<std::mutex> g(m_);
         for (;;) {
-            cv_.wait(g, [&] { return stop_ || gen_ != seen; });
-            if (stop_) return;
-            seen = gen_;
-            while (next_ < workers_.size() + 1 && left_ > 0) {
-                const size_t part = next_++;
-                const size_t off = part * chunk_;
-                const size_t n = off < bytes_ ? std::min(chunk_, bytes_ - off) : 0;
-                g.unlock();
-                if (n) memcpy(dst_ + off, src_ + off, n);
-                g.lock();
-                if (--left_ == 0) done_cv_.notify_one();
+            // poll for a new copy for kSpinUs, then sleep until one is posted
+            const auto t0 = std::chrono::steady_clock::now();
+            unsigned long long g = gen_.load();
+            for (int i = 0; g == seen && !stop_flag_.load(); ++i) {
+                cpu_relax();
+                if ((i & 255) == 255 &&
+                    std::chrono::steady_clock::now() - t0 > std::chrono::microseconds(kSpinUs)) {
+                    std::unique_lock<std::mutex> lk(m_);
+                    sleepers_.fetch_add(1);
+                    cv_.wait(lk, [&] { return stop_ || gen_.load() != seen; });
+                    sleepers_.fetch_sub(1);
+                    if (stop_) return;
+                }
+                g = gen_.load();
             }
+            if (stop_flag_.load()) return;
+            seen = g;
+            run_parts(g);
         }
     }
     std::vector<std::thread> workers_;
     std::mutex m_;
-    std::condition_variable cv_, done_cv_;
-    char *dst_ = nullptr;
-    const char *src_ = nullptr;
-    size_t bytes_ = 0, chunk_ = 0, next_ = 0, left_ = 0;
-    unsigned long long gen_ = 0;
-    bool stop_ = false;
+    std::condition_variable cv_;
+    // the current copy (written by copy() before gen_ is bumped, read by the parts' takers)
+    std::atomic<char *> dst_{nullptr};
+    std::atomic<const char *> src_{nullptr};
+    std::atomic<size_t> bytes_{0}, chunk_{0}, parts_{0}, left_{0};
+    std::atomic<unsigned long long> claim_{0}, gen_{0};
+    std::atomic<int> sleepers_{0};
+    std::atomic<bool> stop_flag_{false};
+    bool stop_ = false;   // guarded by m_
 };
 
 static int copy_threads() {
@@ -690,7 +734,8 @@ struct ct_engine {
     cudaStream_t st = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     // step graphs in flight between host synchronisations: their start / end events
-    static constexpr int kStepRing = 8;
+    static constexpr int kStepRing = 32;    // steps queued before the host synchronises
+    static constexpr int kAdmitRing = 8;    // ... while utterances wait for admission
     cudaEvent_t sev0[kStepRing] = {}, sev1[kStepRing] = {};
     std::vector<float> step_log;      // device time of each step since the last ct_engine_step_times
     ct_engine_config cfg;
@@ -744,6 +789,13 @@ struct ct_engine {
     CopyPool copier{copy_threads()}; // host -> pinned-ring staging copies
     float *enc_stage = nullptr;      // pinned submission ring for host encoder rows (enc_rows_cap rows)
     PinnedRing ring;                 // over enc_stage, in rows
+    // device mirror of enc_stage (same offsets): a submission's rows are
+    // uploaded on the copy stream as soon as they are staged, and admission
+    // waits for the uploads (upload_ev, recorded after the latest) before it
+    // gathers the admitted rows from the mirror
+    float *enc_ring_dev = nullptr;
+    cudaStream_t cst = nullptr;
+    cudaEvent_t upload_ev = nullptr;
     PinnedRing job_ring;             // over job_stage: queued audio / log-mel inputs, in floats
     float *job_stage = nullptr;
     int *tok_stage = nullptr;        // pinned [max_slots][MAX_SEQ]: harvested tokens
@@ -1193,6 +1245,7 @@ static int admit(ct_engine *e) {
     for (int i = 0; i < e->cfg.max_slots; ++i) live_rows += e->slot_live[i] ? 1 : 0;
     int enc_rows = 0, n_rec = 0;
     std::vector<std::pair<long long, int>> ring_release;   // ring blocks of the admitted utterances
+    if (!e->pending.empty()) EK(cudaStreamWaitEvent(e->st, e->upload_ev, 0));   // submitted rows uploaded
     while (!e->pending.empty()) {
         Pending &p = e->pending.front();
         if (enc_rows + p.T_enc > e->enc_rows_cap) break;
@@ -1234,8 +1287,8 @@ static int admit(ct_engine *e) {
         const size_t bytes = sizeof(float) * (size_t)p.T_enc * D;
         if (p.dev_rows) {
             EK(cudaMemcpyAsync(dst, p.dev_rows, bytes, cudaMemcpyDeviceToDevice, e->st));
-        } else if (p.ring_off >= 0) {   // pinned: asynchronous; the ring space is released after the sync below
-            EK(cudaMemcpyAsync(dst, e->enc_stage + (size_t)p.ring_off * D, bytes, cudaMemcpyHostToDevice, e->st));
+        } else if (p.ring_off >= 0) {   // uploaded at submission; the ring space is released after the sync below
+            EK(cudaMemcpyAsync(dst, e->enc_ring_dev + (size_t)p.ring_off * D, bytes, cudaMemcpyDeviceToDevice, e->st));
             ring_release.push_back({p.ring_off, p.T_enc});
         } else {                        // pageable: the call returns once the source has been staged
             EK(cudaMemcpyAsync(dst, p.enc.data(), bytes, cudaMemcpyHostToDevice, e->st));
@@ -1499,9 +1552,13 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
         ++inflight;
         // The next step's rows come from the device state (finished sequences
         // drop out there), so further graphs can be queued before this one
-        // ends; the host synchronises every kStepRing steps, at the last step,
-        // and for every step in profile mode.
-        if (inflight == ct_engine::kStepRing || it == n_steps - 1 || e->cfg.profile) {
+        // ends; the host synchronises every kStepRing steps (every kAdmitRing
+        // while utterances wait for admission, which happens only at
+        // synchronisation points), at the last step, and for every step in
+        // profile mode.
+        const bool waiting = !e->pending.empty() || !e->mel_pending.empty();
+        if (inflight == ct_engine::kStepRing || (waiting && inflight >= ct_engine::kAdmitRing) ||
+            it == n_steps - 1 || e->cfg.profile) {
             const int rc = sync_inflight();
             if (rc) return rc;
         }
@@ -1639,8 +1696,15 @@ extern "C" int ct_engine_submit_encoded(ct_engine *e, long long utt_id, const fl
     p.id = utt_id;
     p.prompt = e->next_prompt;
     p.ring_off = ring_alloc(e, T_enc);
-    if (p.ring_off >= 0) e->copier.copy(e->enc_stage + (size_t)p.ring_off * D, enc_h, sizeof(float) * (size_t)T_enc * D);
-    else p.enc.assign(enc_h, enc_h + (size_t)T_enc * D);
+    if (p.ring_off >= 0) {
+        const size_t off = (size_t)p.ring_off * D, bytes = sizeof(float) * (size_t)T_enc * D;
+        e->copier.copy(e->enc_stage + off, enc_h, bytes);
+        EK(cudaSetDevice(e->device));
+        EK(cudaMemcpyAsync(e->enc_ring_dev + off, e->enc_stage + off, bytes, cudaMemcpyHostToDevice, e->cst));
+        EK(cudaEventRecord(e->upload_ev, e->cst));
+    } else {
+        p.enc.assign(enc_h, enc_h + (size_t)T_enc * D);
+    }
     p.T_enc = T_enc;
     p.forced = forced_len;
     e->pending.push_back(std::move(p));
@@ -1743,10 +1807,11 @@ extern "C" int ct_engine_status(ct_engine *e) {
 extern "C" void ct_engine_destroy(ct_engine *e) {
     if (!e) return;
     cudaSetDevice(e->device);
+    if (e->cst) cudaStreamSynchronize(e->cst);
     cudaStreamSynchronize(e->st);
     for (auto &b : e->buckets) { cudaGraphExecDestroy(b.exec); cudaGraphDestroy(b.graph); }
     void *ptrs[] = {e->blob, e->pool, e->cakv_w, e->cakv_b, e->h, e->q, e->attn_ws, e->logits, e->xa[0], e->xa[1],
-                    e->xb[0], e->xb[1], e->xm[0], e->xm[1], e->lm[0], e->lm[1], e->next, e->enc_dev, e->enc_pl[0],
+                    e->xb[0], e->xb[1], e->xm[0], e->xm[1], e->lm[0], e->lm[1], e->next, e->enc_dev, e->enc_ring_dev, e->enc_pl[0],
                     e->enc_pl[1], e->enc_off, e->ds.state, e->ds.tok, e->ds.pos, e->ds.gen, e->ds.forced,
                     e->ds.tenc, e->ds.self_pt, e->ds.cross_pt, e->ds.out_tok, e->ds.prompt, e->ds.plen, e->ds.r_slot,
                     e->ds.r_pos, e->ds.r_tok, e->ds.r_off, e->ds.q_row, e->ds.q_slot, e->ds.n_rows, e->ds.n_seqs,
@@ -1782,6 +1847,8 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
         delete e->enc;
     }
     cudaStreamDestroy(e->st);
+    if (e->cst) cudaStreamDestroy(e->cst);
+    if (e->upload_ev) cudaEventDestroy(e->upload_ev);
     for (void *p : e->owned) cudaFree(p);
     delete e;
 }
@@ -1816,6 +1883,8 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     e->device = device;
     if (cudaSetDevice(device) != cudaSuccess) { delete e; return CT_EDEVICE; }
     EK(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
+    EK(cudaStreamCreateWithFlags(&e->cst, cudaStreamNonBlocking));
+    EK(cudaEventCreateWithFlags(&e->upload_ev, cudaEventDisableTiming));
     EK(cudaEventCreate(&e->ev0));
     for (int j = 0; j < ct_engine::kStepRing; ++j) {
         EK(cudaEventCreate(&e->sev0[j]));
@@ -1951,7 +2020,8 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
     }
     // admission staging: up to 64 utterances of 30 s worth of encoder rows
     e->enc_rows_cap = 64 * 400;
-    if (dalloc(&e->enc_dev, (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_pl[0], (size_t)e->enc_rows_cap * D) ||
+    if (dalloc(&e->enc_dev, (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_ring_dev, (size_t)e->enc_rows_cap * D) ||
+        dalloc(&e->enc_pl[0], (size_t)e->enc_rows_cap * D) ||
         dalloc(&e->enc_pl[1], (size_t)e->enc_rows_cap * D) || dalloc(&e->enc_off, e->enc_rows_cap)) { ct_engine_destroy(e); return CT_ENOMEM; }
     EK(cudaHostAlloc(&e->enc_stage, sizeof(float) * (size_t)e->enc_rows_cap * D, cudaHostAllocDefault));
     EK(cudaHostAlloc(&e->tok_stage, sizeof(int) * (size_t)cfg.max_slots * MAX_SEQ, cudaHostAllocDefault));
@@ -1991,7 +2061,8 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
             L.sa_lnw = ew(e, s.sa_lnw); L.sa_lnb = ew(e, s.sa_lnb);
             L.sa_pw = ew_matrix(e, s.sa_pw, (size_t)ED * ED);
             L.sa_ow = ew_matrix(e, s.sa_ow, (size_t)ED * ED); L.sa_ob = ew(e, s.sa_ob);
-            L.sa_pbu = ew(e, s.sa_pbu); L.sa_pbv = ew(e, s.sa_pbv);
+            // 16-byte vector loads in the rel-pos bias dots: aligned copies when the blob's are not
+            L.sa_pbu = ew_matrix(e, s.sa_pbu, (size_t)ED); L.sa_pbv = ew_matrix(e, s.sa_pbv, (size_t)ED);
             L.cv_lnw = ew(e, s.cv_lnw); L.cv_lnb = ew(e, s.cv_lnb);
             L.cv_pw1w = ew_matrix(e, s.cv_pw1w, (size_t)2 * ED * ED); L.cv_pw1b = ew(e, s.cv_pw1b);
             L.cv_dww = ew(e, s.cv_dww); L.cv_dwb = ew(e, s.cv_dwb);

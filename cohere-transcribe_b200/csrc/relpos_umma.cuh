@@ -148,25 +148,48 @@ __device__ __forceinline__ void tmem_ld96(uint32_t taddr, float (&v)[96]) {
     for (int i = 0; i < 96; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// u_h . K[r] and v_h . P[m] for every packed row r and table row m, head h
-// (fp32 sums of the bf16 hi (+ lo) planes).  One warp per (row, head).
+// u_h . K[r] and v_h . P[m] for every packed row r and table row m, all heads
+// (fp32 sums of the bf16 hi (+ lo) planes).  One warp per row: lane l takes
+// head l / 4, dims (l % 4) * 40 .. + 40 as five 16-byte loads, sums them in
+// order, and the four lanes of a head add their sums by two butterfly steps.
+static_assert(H * 4 == 32 && DK == 4 * 40, "four lanes per head, 40 dims each");
+__device__ __forceinline__ float dot8_bf16(const uint4 &a, const uint4 &w, float acc) {
+    const __nv_bfloat162 *a2 = reinterpret_cast<const __nv_bfloat162 *>(&a);
+    const __nv_bfloat162 *w2 = reinterpret_cast<const __nv_bfloat162 *>(&w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(w2[i]);
+        acc += y.x * x.x;
+        acc += y.y * x.y;
+    }
+    return acc;
+}
 __global__ void __launch_bounds__(256) relpos_bias_dots(const bf16 *qkv_h, const bf16 *qkv_l, const bf16 *P_h,
                                                         const bf16 *P_l, int R3, int PL, const bf16 *pbu,
                                                         const bf16 *pbv, float *ukg, float *vpg) {
     const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    const int n_uk = R3 * H;
-    if (w >= n_uk + PL * H) return;
-    const bool is_k = w < n_uk;
-    const int idx = is_k ? w : w - n_uk;
-    const int r = idx / H, h = idx % H;
-    const bf16 *bias = (is_k ? pbu : pbv) + h * DK;
-    const size_t base = is_k ? (size_t)r * 3 * D + D + h * DK : (size_t)r * D + h * DK;
-    const bf16 *hi = is_k ? qkv_h : P_h, *lo = is_k ? qkv_l : P_l;
+    if (w >= R3 + PL) return;
+    const bool is_k = w < R3;
+    const int r = is_k ? w : w - R3;
+    const int h = lane >> 2, d0 = h * DK + (lane & 3) * 40;
+    const size_t base = (is_k ? (size_t)r * 3 * D + D : (size_t)r * D) + d0;
+    const uint4 *hi = reinterpret_cast<const uint4 *>((is_k ? qkv_h : P_h) + base);
+    const bf16 *lo_p = is_k ? qkv_l : P_l;
+    const uint4 *bias = reinterpret_cast<const uint4 *>((is_k ? pbu : pbv) + d0);
+    uint4 x[5], bv[5];
+#pragma unroll
+    for (int j = 0; j < 5; ++j) { x[j] = hi[j]; bv[j] = bias[j]; }
     float acc = 0.0f;
-    for (int c = lane; c < DK; c += 32)
-        acc += bf2f(bias[c]) * (bf2f(hi[base + c]) + (lo ? bf2f(lo[base + c]) : 0.0f));
-    acc = warp_sum(acc);
-    if (lane == 0) (is_k ? ukg : vpg)[idx] = acc;
+#pragma unroll
+    for (int j = 0; j < 5; ++j) acc = dot8_bf16(x[j], bv[j], acc);
+    if (lo_p) {
+        const uint4 *lo = reinterpret_cast<const uint4 *>(lo_p + base);
+#pragma unroll
+        for (int j = 0; j < 5; ++j) acc = dot8_bf16(lo[j], bv[j], acc);
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if ((lane & 3) == 0) (is_k ? ukg : vpg)[(size_t)r * H + h] = acc;
 }
 
 __global__ void __launch_bounds__(U_THREADS, 1) relpos_umma(const __grid_constant__ CUtensorMap tmQ,

@@ -111,9 +111,9 @@ int ct_engine_log_mel(ct_engine *e, int n, const float *const *samples, const in
 
 /* Run up to n_steps packed steps (admitting queued utterances when slots and
  * pages allow).  Step graphs are queued back to back and the host synchronises
- * every 8 steps (and after the last), harvesting finished sequences and
- * admitting new ones at those points.  Returns the number of sequences still
- * queued or live, or a negative error. */
+ * every 32 steps (every 8 while utterances wait for admission, and after the
+ * last), harvesting finished sequences and admitting new ones at those points.
+ * Returns the number of sequences still queued or live, or a negative error. */
 int ct_engine_step(ct_engine *e, int n_steps);
 
 /* Run until every submitted utterance has finished. */
