@@ -756,10 +756,10 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
     memcpy(u3 + R3, qt.data(), sizeof(int) * NQ);
     memcpy(u3 + R3 + NQ, qt2.data(), sizeof(int) * NQ2);
     CT_CHECK(cudaMemcpyAsync(st.tab, hp, sizeof(int) * h.size(), cudaMemcpyHostToDevice, s));
-    if (mel)
+    if (mel)   // host or device sources (the engine's job-ring mirror)
         for (int b = 0; b < n; ++b)
-            CT_CHECK(cudaMemcpyAsync(st.mel + mel_off[b], mel[b], sizeof(float) * F0 * T_mel[b],
-                                     cudaMemcpyHostToDevice, s));
+            CT_CHECK(cudaMemcpyAsync(st.mel + mel_off[b], mel[b], sizeof(float) * F0 * T_mel[b], cudaMemcpyDefault,
+                                     s));
     Batch bt;
     bt.n = n;
     bt.T_mel = st.tab;

@@ -798,6 +798,7 @@ struct ct_engine {
     cudaEvent_t upload_ev = nullptr;
     PinnedRing job_ring;             // over job_stage: queued audio / log-mel inputs, in floats
     float *job_stage = nullptr;
+    float *job_ring_dev = nullptr;   // device mirror of job_stage (same offsets), filled at submission
     int *tok_stage = nullptr;        // pinned [max_slots][MAX_SEQ]: harvested tokens
     long long *off_stage = nullptr;  // pinned
     int *slot_stage = nullptr;       // pinned admission records [max_slots][REC_INTS]
@@ -1384,7 +1385,7 @@ static int encode_pending(ct_engine *e) {
     for (auto &j : e->mel_pending) {
         if ((j.n_samples > 0) != audio) break;
         if ((int)mels.size() >= e->enc->max_utts || frames + j.T_mel > e->enc->max_frames) break;
-        mels.push_back(j.ring_off >= 0 ? e->job_stage + j.ring_off : j.mel.data());
+        mels.push_back(j.ring_off >= 0 ? e->job_ring_dev + j.ring_off : j.mel.data());   // device mirror or host
         T_mel.push_back(j.T_mel);
         n_samp.push_back(j.n_samples);
         frames += j.T_mel;
@@ -1392,6 +1393,7 @@ static int encode_pending(ct_engine *e) {
     const int n = (int)mels.size();
     std::vector<int> off(n + 1);
     EK(cudaEventRecord(e->eev0, e->st));
+    EK(cudaStreamWaitEvent(e->st, e->upload_ev, 0));   // inputs staged in the job ring are on the device
     const bool ok = audio ? enc::encode_audio(e->st, *e->enc, n, mels.data(), n_samp.data(), T_mel.data(), off.data())
                           : enc::encode(e->st, *e->enc, n, mels.data(), T_mel.data(), off.data());
     if (!ok) return CT_EINVAL;
@@ -1597,12 +1599,21 @@ extern "C" int ct_engine_step(ct_engine *e, int n_steps) {
 }
 
 // Copy a queued utterance's input once: into the pinned job ring when it has
-// room, else into the job's own (pageable) vector.
-static void stage_job(ct_engine *e, ct_engine::MelJob &j, const float *src, size_t count) {
+// room (and from there at once into the ring's device mirror, on the copy
+// stream), else into the job's own (pageable) vector.
+static int stage_job(ct_engine *e, ct_engine::MelJob &j, const float *src, size_t count) {
     j.count = count;
     j.ring_off = e->job_ring.alloc((long long)count);
-    if (j.ring_off >= 0) e->copier.copy(e->job_stage + j.ring_off, src, sizeof(float) * count);
-    else j.mel.assign(src, src + count);
+    if (j.ring_off < 0) {
+        j.mel.assign(src, src + count);
+        return CT_OK;
+    }
+    e->copier.copy(e->job_stage + j.ring_off, src, sizeof(float) * count);
+    EK(cudaSetDevice(e->device));
+    EK(cudaMemcpyAsync(e->job_ring_dev + j.ring_off, e->job_stage + j.ring_off, sizeof(float) * count,
+                       cudaMemcpyHostToDevice, e->cst));
+    EK(cudaEventRecord(e->upload_ev, e->cst));
+    return CT_OK;
 }
 
 extern "C" int ct_engine_submit_mel(ct_engine *e, long long utt_id, const float *mel, int T_mel, int forced_len) {
@@ -1612,7 +1623,7 @@ extern "C" int ct_engine_submit_mel(ct_engine *e, long long utt_id, const float 
     if (!admissible(e, T_enc, forced_len)) return CT_EINVAL;
     ct_engine::MelJob j;
     j.id = utt_id;
-    stage_job(e, j, mel, (size_t)N_MELS * T_mel);
+    if (const int rc = stage_job(e, j, mel, (size_t)N_MELS * T_mel)) return rc;
     j.T_mel = T_mel;
     j.n_samples = 0;
     j.forced = forced_len;
@@ -1630,7 +1641,7 @@ extern "C" int ct_engine_submit_audio(ct_engine *e, long long utt_id, const floa
     if (!admissible(e, T_enc, forced_len)) return CT_EINVAL;
     ct_engine::MelJob j;
     j.id = utt_id;
-    stage_job(e, j, samples, (size_t)n_samples);
+    if (const int rc = stage_job(e, j, samples, (size_t)n_samples)) return rc;
     j.T_mel = T_mel;
     j.n_samples = n_samples;
     j.forced = forced_len;
@@ -1811,7 +1822,7 @@ extern "C" void ct_engine_destroy(ct_engine *e) {
     cudaStreamSynchronize(e->st);
     for (auto &b : e->buckets) { cudaGraphExecDestroy(b.exec); cudaGraphDestroy(b.graph); }
     void *ptrs[] = {e->blob, e->pool, e->cakv_w, e->cakv_b, e->h, e->q, e->attn_ws, e->logits, e->xa[0], e->xa[1],
-                    e->xb[0], e->xb[1], e->xm[0], e->xm[1], e->lm[0], e->lm[1], e->next, e->enc_dev, e->enc_ring_dev, e->enc_pl[0],
+                    e->xb[0], e->xb[1], e->xm[0], e->xm[1], e->lm[0], e->lm[1], e->next, e->enc_dev, e->enc_ring_dev, e->job_ring_dev, e->enc_pl[0],
                     e->enc_pl[1], e->enc_off, e->ds.state, e->ds.tok, e->ds.pos, e->ds.gen, e->ds.forced,
                     e->ds.tenc, e->ds.self_pt, e->ds.cross_pt, e->ds.out_tok, e->ds.prompt, e->ds.plen, e->ds.r_slot,
                     e->ds.r_pos, e->ds.r_tok, e->ds.r_off, e->ds.q_row, e->ds.q_slot, e->ds.n_rows, e->ds.n_seqs,
@@ -2095,6 +2106,7 @@ extern "C" int ct_engine_create(ct_engine **out, int device, const void *host_bl
         // one encoder batch of audio input (the larger of samples and log-mel)
         e->job_ring.cap = (long long)mf * fe::HOP;
         EK(cudaHostAlloc(&e->job_stage, sizeof(float) * (size_t)e->job_ring.cap, cudaHostAllocDefault));
+        if (dalloc(&e->job_ring_dev, (size_t)e->job_ring.cap)) { ct_engine_destroy(e); return CT_ENOMEM; }
     }
     EK(cudaDeviceSynchronize());
     *out = e;

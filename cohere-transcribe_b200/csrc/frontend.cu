@@ -216,8 +216,8 @@ static bool log_mel(cudaStream_t s, Front &f, int n, const float *const *samples
     for (int b = 0; b < n; ++b)
         for (int t = fo[b]; t < fo[b + 1]; ++t) fu[t] = b;
     CT_CHECK(cudaMemcpyAsync(f.tab, h.data(), sizeof(int) * h.size(), cudaMemcpyHostToDevice, s));
-    for (int b = 0; b < n; ++b)
-        CT_CHECK(cudaMemcpyAsync(f.samples + so[b], samples[b], sizeof(float) * ns[b], cudaMemcpyHostToDevice, s));
+    for (int b = 0; b < n; ++b)   // host or device sources (the engine's job-ring mirror)
+        CT_CHECK(cudaMemcpyAsync(f.samples + so[b], samples[b], sizeof(float) * ns[b], cudaMemcpyDefault, s));
     mel_power_kernel<<<(frames + FW - 1) / FW, FW * 32, 0, s>>>(f.samples, f.tab, n, frames, f.hann, f.twr, f.twi,
                                                                 f.fb, f.fb_lo, f.fb_hi, mel_dev);
     mel_norm_kernel<<<(n * NM + 7) / 8, 256, 0, s>>>(f.tab, n, mel_dev);
