@@ -206,40 +206,52 @@ __device__ __forceinline__ void ln_row_apply(float4 (&v)[D / 128], float mean, f
                            (v[j].w - mean) * inv * bf2f(w[k + 3]) + bf2f(b[k + 3]));
     }
 }
-__global__ void __launch_bounds__(256) ln_enc(const float *x, int R, const bf16 *w, const bf16 *b, float *y,
-                                              bf16 *hi, bf16 *lo, const bf16 *w2 = nullptr,
-                                              const bf16 *b2 = nullptr) {
+// Persistent over rows: warp w takes rows w, w + W, w + 2W, ... (W = warps in
+// the grid) and loads its next row before it reduces and writes the current
+// one, so every SM keeps streaming while rows are normalised.
+__global__ void __launch_bounds__(256, 2) ln_enc(const float *x, int R, const bf16 *w, const bf16 *b, float *y,
+                                                 bf16 *hi, bf16 *lo, const bf16 *w2 = nullptr,
+                                                 const bf16 *b2 = nullptr) {
     constexpr int NV = D / 128;   // float4 per lane
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r = blockIdx.x * 8 + warp;
+    const int lane = threadIdx.x & 31;
+    const int W = gridDim.x * 8;
+    int r = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (r >= R) return;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)r * D);
-    float4 v[NV];
+    float4 v[NV], nx[NV];
 #pragma unroll
-    for (int j = 0; j < NV; ++j) v[j] = xr[lane + 32 * j];
-    float mean, inv;
-    ln_row_stats(v, mean, inv);
-    ln_row_apply(v, mean, inv, w, b, lane);
-    if (y)
+    for (int j = 0; j < NV; ++j) v[j] = reinterpret_cast<const float4 *>(x + (size_t)r * D)[lane + 32 * j];
+    for (; r < R; r += W) {
+        const int rn = r + W;
+        if (rn < R)
 #pragma unroll
-        for (int j = 0; j < NV; ++j) reinterpret_cast<float4 *>(y + (size_t)r * D)[lane + 32 * j] = v[j];
-    if (w2) {
+            for (int j = 0; j < NV; ++j) nx[j] = reinterpret_cast<const float4 *>(x + (size_t)rn * D)[lane + 32 * j];
+        float mean, inv;
         ln_row_stats(v, mean, inv);
-        ln_row_apply(v, mean, inv, w2, b2, lane);
-    }
-    if (!hi) return;
+        ln_row_apply(v, mean, inv, w, b, lane);
+        if (y)
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int k = 4 * (lane + 32 * j);
-        const float o[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-        bf16 h4[4], l4[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            h4[e] = __float2bfloat16_rn(o[e]);
-            l4[e] = __float2bfloat16_rn(o[e] - __bfloat162float(h4[e]));
+            for (int j = 0; j < NV; ++j) reinterpret_cast<float4 *>(y + (size_t)r * D)[lane + 32 * j] = v[j];
+        if (w2) {
+            ln_row_stats(v, mean, inv);
+            ln_row_apply(v, mean, inv, w2, b2, lane);
         }
-        *reinterpret_cast<uint2 *>(hi + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(h4);
-        if (lo) *reinterpret_cast<uint2 *>(lo + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(l4);
+        if (hi) {
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                const int k = 4 * (lane + 32 * j);
+                const float o[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+                bf16 h4[4], l4[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    h4[e] = __float2bfloat16_rn(o[e]);
+                    l4[e] = __float2bfloat16_rn(o[e] - __bfloat162float(h4[e]));
+                }
+                *reinterpret_cast<uint2 *>(hi + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(h4);
+                if (lo) *reinterpret_cast<uint2 *>(lo + (size_t)r * D + k) = *reinterpret_cast<const uint2 *>(l4);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NV; ++j) v[j] = nx[j];
     }
 }
 
@@ -591,13 +603,22 @@ __global__ void __launch_bounds__(256) glu_dw_packed(const TIn *pw1, Batch b, co
         if (row >= b.R3) break;
         const int lo_row = lo_s[rr], hi_row = hi_s[rr];
         float s0 = bias0, s1 = bias1;
+        if (row - pad >= lo_row && row + pad < hi_row) {   // every tap inside the utterance (warp-uniform)
 #pragma unroll
-        for (int k = 0; k < CK; ++k) {
-            const int ti = row - pad + k;
-            if (ti >= lo_row && ti < hi_row) {
+            for (int k = 0; k < CK; ++k) {
                 const float2 g = g_s[rr + k][tc];
                 s0 += wk0[k] * g.x;
                 s1 += wk1[k] * g.y;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < CK; ++k) {
+                const int ti = row - pad + k;
+                if (ti >= lo_row && ti < hi_row) {
+                    const float2 g = g_s[rr + k][tc];
+                    s0 += wk0[k] * g.x;
+                    s1 += wk1[k] * g.y;
+                }
             }
         }
         const float v0 = silu_fast((s0 - mu0) * sc0 + be0), v1 = silu_fast((s1 - mu1) * sc1 + be1);
@@ -614,6 +635,7 @@ __global__ void __launch_bounds__(256) glu_dw_packed(const TIn *pw1, Batch b, co
 struct State {
     Weights_ w;
     int max_utts = 0, max_frames = 0;     // capacity: utterances and log-mel frames per batch
+    int n_sm = 148;                        // SMs of the device (LayerNorm grid)
     int R1_max = 0, R2_max = 0, R3_max = 0, T_cap = 0;
     bool two = true;                       // activations as hi+lo bf16 planes
     float *mel = nullptr, *s1 = nullptr, *x = nullptr, *qkv = nullptr, *pos = nullptr;
@@ -633,6 +655,10 @@ struct State {
     std::vector<const char *> labels;
     int n_marks = 0;
 };
+
+// LayerNorm grid: a warp per row, at most two CTAs of 8 warps per SM (each
+// warp then walks several rows)
+static int ln_grid(const State &st, int R) { return std::max(1, std::min((R + 7) / 8, 2 * st.n_sm)); }
 
 static void mark(cudaStream_t s, State &st, const char *label) {
     if (!st.prof) return;
@@ -664,6 +690,10 @@ static bool state_alloc(State &st, int max_utts, int max_frames, bool two) {
     st.max_utts = max_utts;
     st.max_frames = max_frames;
     st.two = two;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&st.n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || st.n_sm <= 0)
+        return false;
     st.R1_max = max_frames / 2 + max_utts;
     st.R2_max = st.R1_max / 2 + max_utts;
     st.R3_max = st.R2_max / 2 + max_utts;
@@ -835,7 +865,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         const Layer &L = w.L[l];
         // FFN1: x += 0.5 * W2 silu(W1 LN(x) + b1) + b2
         if (l == 0) {   // later layers get these planes from the previous layer's final LayerNorm
-            ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.ff1_lnw, L.ff1_lnb, nullptr, st.xa[0], lo_a);
+            ln_enc<<<ln_grid(st, R3), 256, 0, s>>>(st.x, R3, L.ff1_lnw, L.ff1_lnb, nullptr, st.xa[0], lo_a);
             mark(s, st, "enc_layernorm");
         }
         GemmEpilogue f1;
@@ -847,7 +877,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         egemm_enc(s, st, L.ff1_w2, D, FF, hidp, R3, RT, f2);
         mark(s, st, "enc_gemm_ffn2");
         // relative-position self-attention: x += Wo attn(LN(x)) + bo
-        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.sa_lnw, L.sa_lnb, nullptr, st.xa[0], lo_a);
+        ln_enc<<<ln_grid(st, R3), 256, 0, s>>>(st.x, R3, L.sa_lnw, L.sa_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
         GemmEpilogue eq;
         eq.epi = EPI_BF16; eq.bias = L.qkv_b; eq.Ybf = st.qkvp[0]; eq.Ybf_lo = st.two ? st.qkvp[1] : nullptr; eq.ldy = 3 * D;
@@ -874,7 +904,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         egemm_enc(s, st, L.sa_ow, D, D, app, R3, RT, eo2);
         mark(s, st, "enc_gemm_o");
         // conv module: x += pw2(silu(bn(dw(glu(pw1(LN(x)))))))
-        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.cv_lnw, L.cv_lnb, nullptr, st.xa[0], lo_a);
+        ln_enc<<<ln_grid(st, R3), 256, 0, s>>>(st.x, R3, L.cv_lnw, L.cv_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
         // pw1 output: fp32 with hi+lo planes, bf16 with plain bf16 activations
         // (half the bytes written and read back by the GLU)
@@ -898,7 +928,7 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         egemm_enc(s, st, L.cv_pw2w, D, D, app, R3, RT, e2);
         mark(s, st, "enc_gemm_pw2");
         // FFN2
-        ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.ff2_lnw, L.ff2_lnb, nullptr, st.xa[0], lo_a);
+        ln_enc<<<ln_grid(st, R3), 256, 0, s>>>(st.x, R3, L.ff2_lnw, L.ff2_lnb, nullptr, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
         GemmEpilogue g1 = f1;
         g1.bias = L.ff2_b1;
@@ -911,10 +941,10 @@ static bool encode(cudaStream_t s, State &st, int n, const float *const *mel, co
         // x = LN_out(x), and the planes of the next layer's FFN1 LayerNorm of it
         // (after the last layer: the planes of x itself, for the projection)
         if (l + 1 < NL)
-            ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a,
+            ln_enc<<<ln_grid(st, R3), 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a,
                                                  w.L[l + 1].ff1_lnw, w.L[l + 1].ff1_lnb);
         else
-            ln_enc<<<(R3 + 7) / 8, 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a);
+            ln_enc<<<ln_grid(st, R3), 256, 0, s>>>(st.x, R3, L.out_lnw, L.out_lnb, st.x, st.xa[0], lo_a);
         mark(s, st, "enc_layernorm");
     }
     // ---- encoder -> decoder projection (model.h:607) ----
