@@ -16,6 +16,8 @@
 // bucket serves every step.
 #include <algorithm>
 #include <atomic>
+#include <sched.h>
+#include <stdlib.h>
 #include <chrono>
 #include <condition_variable>
 #include <deque>
@@ -661,7 +663,7 @@ class CopyPool {
     }
 
   private:
-    static constexpr int kSpinUs = 500;
+    static constexpr int kSpinUs = 200;
     static constexpr int kPartBits = 16;
     static constexpr unsigned long long kPartMask = (1ull << kPartBits) - 1;
     static void cpu_relax() {
@@ -724,9 +726,19 @@ class CopyPool {
     bool stop_ = false;   // guarded by m_
 };
 
+// Copy workers: half the CPUs this process may run on, less the calling
+// thread, shared among the engines of one node (torchrun's LOCAL_WORLD_SIZE
+// processes, one per GPU), at most 7.  Polling workers on oversubscribed CPUs
+// would only delay the threads that launch the GPU work.
 static int copy_threads() {
-    const unsigned hc = std::thread::hardware_concurrency();
-    return (int)std::min<unsigned>(7, hc > 2 ? hc / 2 - 1 : 0);
+    int cpus = 0;
+    cpu_set_t set;
+    if (sched_getaffinity(0, sizeof(set), &set) == 0) cpus = CPU_COUNT(&set);
+    if (cpus <= 0) cpus = (int)std::thread::hardware_concurrency();
+    const char *lw = getenv("LOCAL_WORLD_SIZE");
+    const int local = lw ? std::max(1, atoi(lw)) : 1;
+    const int share = cpus / local;
+    return std::max(0, std::min(7, share / 2 - 1));
 }
 
 struct ct_engine {
