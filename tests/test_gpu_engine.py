@@ -216,6 +216,37 @@ def test_engine_continuous_admission(abi, dec_model):
     assert stats["tokens"] == int(case["forced_len"].sum())
 
 
+def test_engine_submission_ring_overflow(abi, dec_model):
+    """More encoder rows queued than the pinned submission ring and one
+    admission hold (25,600 rows): the utterances that do not fit are staged in
+    pageable memory and uploaded at admission, the rest were uploaded at
+    submission, and admission runs in two rounds.  Every result equals the run
+    that submits the same utterances in groups of 8 (bitwise: a sequence's
+    arithmetic does not depend on the batch)."""
+    n = 72
+    T_enc = (376 - np.arange(n) % 8).astype(np.int32)   # 26,820 rows
+    forced = (2 + np.arange(n) % 4).astype(np.int32)
+    enc = inputs.enc_outputs(T_enc, seed=700)
+    assert int(T_enc.sum()) > 25600
+    together, stats = run_engine(abi, dec_model, enc, T_enc, forced, precision=0)
+    wb, ws = dec_model
+    eng = abi.Engine(abi.load(), 0, wb, ws, precision=0)
+    grouped = {}
+    try:
+        for g0 in range(0, n, 8):
+            for b in range(g0, g0 + 8):
+                eng.submit(b, enc[b, :T_enc[b]], forced[b])
+            eng.run()
+            grouped.update(eng.poll())
+        assert eng.status() == 0
+    finally:
+        eng.close()
+    assert set(together) == set(range(n)) and set(grouped) == set(range(n))
+    diff = [b for b in range(n) if not np.array_equal(together[b], grouped[b])]
+    assert not diff, f"{len(diff)}/{n} sequences differ between one submission burst and groups of 8: {diff}"
+    assert stats["tokens"] == int(forced.sum())
+
+
 def test_engine_long_sequences_and_long_cross(abi, dec_model, wmod):
     """Self-attention over > 128 positions (several split-KV chunks and
     several 16-row pages) and cross-attention over 30 s of encoder rows."""
