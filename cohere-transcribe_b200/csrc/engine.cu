@@ -44,7 +44,7 @@ constexpr long long PAGE_ELEMS = (long long)NL * 2 * PR * D;
 constexpr int PROMPT_MAX = 96;                 // longest prompt (the reference's long-form prompts reach 2 + 64 + 16)
 constexpr int AW = 8;                          // consumer warps per attention CTA (one per head)
 constexpr int ANST = 3;                        // page stages in the attention pipeline
-constexpr int GP = 2;                          // pages per attention group: a row's keys are cut into
+constexpr int GP = 4;                          // pages per attention group: a row's keys are cut into
                                                // fixed groups of GP pages, whatever else is in the batch
 constexpr int SEG_MAX = (SELF_PAGES > CROSS_PAGES ? SELF_PAGES : CROSS_PAGES) / GP;   // groups per row
 
