@@ -84,9 +84,9 @@ CUDA_REF_SAMPLE = 16   # utterances in the reference CUDA backend's decode sampl
 # classes whose traffic grows in proportion to them.
 NCU_TRAFFIC = {
     # profiles/attn_paged_decode.md: one cross launch, 64 rows over 14,080
-    # encoder keys (57,671,680 algorithmic bytes): 59.354112 MB read + 0.501248 MB
+    # encoder keys (57,671,680 algorithmic bytes): 59.356672 MB read + 0.566016 MB
     # written.  Unit: algorithmic byte (the K/V rows the launch must read).
-    "paged cross-attention": {"bytes": 59.354112e6 + 0.501248e6, "units": 14080 * 4096.0,
+    "paged cross-attention": {"bytes": 59.356672e6 + 0.566016e6, "units": 14080 * 4096.0,
                               "unit": "algorithmic byte", "source": "profiles/attn_paged_decode.md"},
     # profiles/gemm_decode_ffn_lmhead.md: one layer's FFN1 + FFN2 at 64 rows,
     # bf16 activations (17,432,576 algorithmic bytes): 8.759552 + 9.262848 MB
